@@ -1,0 +1,142 @@
+// Harness around the reference's own ggml CPU ops (TEST INFRASTRUCTURE: parity checker + timed CPU
+// baseline; never linked into the klein_b200 product).
+//
+// Each entry point binds caller-owned host buffers to ggml tensors with exactly the views klein's graph
+// builds, runs one node on ggml's CPU backend and returns. Nothing is copied into ggml-owned memory, so
+// the 262,144-cell KV caches of the long-verify configuration are used in place.
+//
+//   kbref_flash_attn_ext   ggml_flash_attn_ext + ggml_prec_set_acc(F32) as in src/graph.cpp:113-121
+//                          (q [hd, n, nh] permuted view, k/v [hd, n_kv, nkv] permuted cache views);
+//                          CPU op third_party/ggml/src/ggml-cpu/ops.cpp:8842-9574
+//   kbref_gated_delta_net  ggml_gated_delta_net as in src/graph.cpp:169; CPU op ops.cpp:11123-11316
+//   kbref_quantize_q8_0    ggml_quantize_chunk(Q8_0) -> quantize_row_q8_0_ref (ggml-quants.c:276-299)
+//   kbref_set_rows         ggml_set_rows as in src/graph.cpp:111-112; CPU op ops.cpp:5446-5530
+//   kbref_cpy              ggml_cpy f32<->f16 (snapshot write graph.cpp:179-184, rollback state.cpp:162-183)
+//
+// use_ref = 1 selects ggml's vec-only reference path (no split-KV, no tiling; ops.cpp:9487-9550),
+// which makes results independent of the thread count.
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "ggml.h"
+#include "ggml-cpu.h"
+
+namespace {
+
+struct Ctx {
+    ggml_context* ctx = nullptr;
+    explicit Ctx(size_t n_tensors) {
+        ggml_init_params ip{ggml_tensor_overhead() * n_tensors + ggml_graph_overhead() + 4096, nullptr, true};
+        ctx = ggml_init(ip);
+    }
+    ~Ctx() { if (ctx) ggml_free(ctx); }
+};
+
+int compute(ggml_context* ctx, ggml_tensor* out, int n_threads, int use_ref) {
+    ggml_cgraph* gf = ggml_new_graph(ctx);
+    ggml_build_forward_expand(gf, out);
+    ggml_cplan plan = ggml_graph_plan(gf, n_threads > 0 ? n_threads : 1, nullptr);
+    std::vector<uint8_t> work(plan.work_size + 64);
+    plan.work_data = plan.work_size ? work.data() : nullptr;
+    plan.use_ref = use_ref != 0;
+    return ggml_graph_compute(gf, &plan) == GGML_STATUS_SUCCESS ? 0 : 1;
+}
+
+ggml_tensor* bind(ggml_context* ctx, ggml_type t, int64_t n0, int64_t n1, int64_t n2, int64_t n3, const void* data) {
+    ggml_tensor* x = ggml_new_tensor_4d(ctx, t, n0, n1, n2, n3);
+    x->data = const_cast<void*>(data);
+    return x;
+}
+
+bool init_once() {
+    static bool done = [] { ggml_cpu_init(); return true; }();
+    return done;
+}
+
+}  // namespace
+
+extern "C" {
+
+// q    : f32 [n_q][n_head][D]            (token-major, as klein's q projection output)
+// k, v : kv_type rows, row r at k + r*kv_row_bytes, head h at + h*row_size(D)   (klein's cache layout)
+// mask : f16 [n_q][n_kv] or NULL          (klein's dense mask; -inf = not visible)
+// out  : f32 [n_q][n_head][D]
+int kbref_flash_attn_ext(const float* q, int n_q, int n_head, int D, const void* k, const void* v, int kv_type,
+                         int64_t n_kv, int n_head_kv, size_t kv_row_bytes, const uint16_t* mask, float scale,
+                         float max_bias, float softcap, float* out, int n_threads, int use_ref) {
+    init_once();
+    Ctx c(16);
+    const ggml_type kt = (ggml_type) kv_type;
+    ggml_tensor* qt = bind(c.ctx, GGML_TYPE_F32, D, n_head, n_q, 1, q);
+    ggml_tensor* qp = ggml_permute(c.ctx, qt, 0, 2, 1, 3);  // [D, n_q, n_head]
+    const size_t hs = ggml_row_size(kt, D);
+    ggml_tensor* kb = ggml_new_tensor_2d(c.ctx, kt, (int64_t) D * n_head_kv, n_kv);
+    ggml_tensor* vb = ggml_new_tensor_2d(c.ctx, kt, (int64_t) D * n_head_kv, n_kv);
+    kb->data = const_cast<void*>(k);
+    vb->data = const_cast<void*>(v);
+    ggml_tensor* kv3 = ggml_view_3d(c.ctx, kb, D, n_head_kv, n_kv, hs, kv_row_bytes, 0);
+    ggml_tensor* vv3 = ggml_view_3d(c.ctx, vb, D, n_head_kv, n_kv, hs, kv_row_bytes, 0);
+    ggml_tensor* kp = ggml_permute(c.ctx, kv3, 0, 2, 1, 3);  // [D, n_kv, n_head_kv]
+    ggml_tensor* vp = ggml_permute(c.ctx, vv3, 0, 2, 1, 3);
+    ggml_tensor* mt = nullptr;
+    if (mask) mt = bind(c.ctx, GGML_TYPE_F16, n_kv, n_q, 1, 1, mask);
+    ggml_tensor* o = ggml_flash_attn_ext(c.ctx, qp, kp, vp, mt, scale, max_bias, softcap);
+    ggml_prec_set_acc(o, GGML_PREC_F32);
+    o->data = out;  // result [D, n_head, n_q] f32 contiguous == out[n_q][n_head][D]
+    return compute(c.ctx, o, n_threads, use_ref);
+}
+
+// q, k : f32 [n_seqs][T][H_k][S]; v : f32 [n_seqs][T][H_v][S]; g : f32 [n_seqs][T][H_v][kda ? S : 1];
+// beta : f32 [n_seqs][T][H_v]; s0 : f32 [n_seqs][H_v][S][S] (transposed state, row j = column j of S);
+// out  : f32, ggml's packed layout: attn [n_seqs][T][H_v][S] then K slots of [n_seqs][H_v][S][S].
+int kbref_gated_delta_net(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                          const float* s0, int S, int H_k, int H_v, int T, int n_seqs, int kda, int K, float* out,
+                          int n_threads) {
+    init_once();
+    Ctx c(16);
+    ggml_tensor* qt = bind(c.ctx, GGML_TYPE_F32, S, H_k, T, n_seqs, q);
+    ggml_tensor* kt = bind(c.ctx, GGML_TYPE_F32, S, H_k, T, n_seqs, k);
+    ggml_tensor* vt = bind(c.ctx, GGML_TYPE_F32, S, H_v, T, n_seqs, v);
+    ggml_tensor* gt = bind(c.ctx, GGML_TYPE_F32, kda ? S : 1, H_v, T, n_seqs, g);
+    ggml_tensor* bt = bind(c.ctx, GGML_TYPE_F32, 1, H_v, T, n_seqs, beta);
+    ggml_tensor* st = bind(c.ctx, GGML_TYPE_F32, S, S, H_v, n_seqs, s0);
+    ggml_tensor* r = ggml_gated_delta_net(c.ctx, qt, kt, vt, gt, bt, st, K);
+    r->data = out;
+    return compute(c.ctx, r, n_threads, 0);
+}
+
+// ggml_quantize_chunk(Q8_0, ...) -> quantize_row_q8_0_ref; n_per_row must be a multiple of 32.
+size_t kbref_quantize_q8_0(const float* src, void* dst, int64_t nrows, int64_t n_per_row) {
+    init_once();
+    return ggml_quantize_chunk(GGML_TYPE_Q8_0, src, dst, 0, nrows, n_per_row, nullptr);
+}
+
+void kbref_dequantize(int type, const void* src, float* dst, int64_t n) {
+    init_once();
+    ggml_get_type_traits((ggml_type) type)->to_float(src, dst, n);
+}
+
+// ggml_set_rows(dst_cache [row_elems, n_rows] of dst_type, src f32 [row_elems, n_src], idx i64 [n_src])
+int kbref_set_rows(void* dst, int dst_type, int64_t row_elems, int64_t n_rows, const float* src, int64_t n_src,
+                   const int64_t* idx, int n_threads) {
+    init_once();
+    Ctx c(16);
+    ggml_tensor* dt = bind(c.ctx, (ggml_type) dst_type, row_elems, n_rows, 1, 1, dst);
+    ggml_tensor* st = bind(c.ctx, GGML_TYPE_F32, row_elems, n_src, 1, 1, src);
+    ggml_tensor* it = bind(c.ctx, GGML_TYPE_I64, n_src, 1, 1, 1, idx);
+    ggml_tensor* r = ggml_set_rows(c.ctx, dt, st, it);
+    return compute(c.ctx, r, n_threads, 0);
+}
+
+// ggml_cpy of n elements between two contiguous 1-d tensors (f32 <-> f16 / bf16 / f32)
+int kbref_cpy(const void* src, int src_type, void* dst, int dst_type, int64_t n) {
+    init_once();
+    Ctx c(8);
+    ggml_tensor* s = bind(c.ctx, (ggml_type) src_type, n, 1, 1, 1, src);
+    ggml_tensor* d = bind(c.ctx, (ggml_type) dst_type, n, 1, 1, 1, dst);
+    ggml_tensor* r = ggml_cpy(c.ctx, s, d);
+    return compute(c.ctx, r, 1, 0);
+}
+
+}  // extern "C"
