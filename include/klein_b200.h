@@ -1,0 +1,106 @@
+/*
+ * klein_b200 — B200 (sm_100a) kernels for klein's qwen35 attention hot path, behind a C ABI.
+ *
+ * The entry points keep the semantics of the ggml operator nodes klein's graph builds
+ * (reference: src/graph.cpp:87-191), so a patched ggml-cuda backend can forward those nodes here
+ * (the switch in third_party/ggml/src/ggml-cuda/ggml-cuda.cu:2488-2504). Tensors are described the
+ * way ggml describes them: ne[0] is the innermost extent, nb[i] the byte stride of dimension i, data a
+ * device pointer. All calls are asynchronous on the given CUDA stream, allocate nothing, do not
+ * synchronise, and may be captured into a CUDA graph. Scratch memory, where a call needs it, comes from
+ * the caller (as ggml-cuda's pool provides it, ggml-cuda.cu:925-926).
+ *
+ * Errors: ggml aborts (GGML_ASSERT); this library returns a kb_status instead and leaves the outputs
+ * untouched when it rejects a call. A ggml-side shim turns a non-OK status into GGML_ABORT.
+ */
+#ifndef KLEIN_B200_H
+#define KLEIN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum kb_status {
+    KB_OK = 0,
+    KB_ERR_ARG = 1,          /* null pointer or inconsistent argument */
+    KB_ERR_BAD_SHAPE = 2,    /* shapes or strides that the op does not define */
+    KB_ERR_UNSUPPORTED = 3,  /* a valid ggml configuration this library does not implement */
+    KB_ERR_SCRATCH = 4,      /* scratch buffer missing or too small */
+    KB_ERR_CUDA = 5,         /* a CUDA runtime/driver call failed */
+    KB_ERR_TIMEOUT = 6       /* a bounded device-side wait ran out (see kb_device_error) */
+} kb_status;
+
+/* Element types, numbered as enum ggml_type (third_party/ggml/include/ggml.h:389-420). */
+enum {
+    KB_TYPE_F32 = 0,
+    KB_TYPE_F16 = 1,
+    KB_TYPE_Q8_0 = 8, /* blocks of 32: f16 scale d then 32 int8 (ggml-common.h block_q8_0) */
+    KB_TYPE_I32 = 26,
+    KB_TYPE_I64 = 27,
+    KB_TYPE_BF16 = 30
+};
+
+/* A strided device tensor in ggml's conventions (struct ggml_tensor's type/ne/nb/data, ggml.h). */
+typedef struct kb_tensor {
+    int32_t type;
+    int64_t ne[4];
+    size_t nb[4];
+    void* data;
+} kb_tensor;
+
+/*
+ * Parameters of GGML_OP_FLASH_ATTN_EXT. scale/max_bias/logit_softcap are the op_params set by
+ * ggml_flash_attn_ext (third_party/ggml/src/ggml.c:5540-5541); prec is ggml_prec_set_acc's value
+ * (this library always accumulates in f32, which satisfies every precision request).
+ *
+ * Analytic visibility (used only when the dense mask is NULL and causal != 0) states klein's mask rule
+ * (src/engine.cpp:308-326) without materialising the n_kv x n_q f16 mask: query i sits at position
+ * pos0 + i; with ring == 0 it sees cell j iff kv_lo <= j <= pos0 + i; with ring > 0 (the MTP head's
+ * sliding-window ring buffer) slot j holds cell c = end - ((end - j) mod ring), end = pos0 + n_q - 1,
+ * and is visible iff kv_lo <= c <= pos0 + i and c > pos0 + i - ring.
+ */
+typedef struct kb_fa_params {
+    float scale;
+    float max_bias;
+    float logit_softcap;
+    int32_t prec;
+    int32_t causal;
+    int64_t pos0;
+    int64_t kv_lo;
+    int64_t ring;
+} kb_fa_params;
+
+/*
+ * GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext, ggml.h:2476-2495; CPU semantics ops.cpp:8842-9574;
+ * replaces ggml_cuda_flash_attn_ext, ggml-cuda/fattn.cu:758-772).
+ *   q    f32  [D, n_q, H, ne3]       any byte strides (klein passes a permuted view, graph.cpp:118)
+ *   k, v f16/q8_0/bf16 [D, n_kv, H_kv, ne3k]  nb[0] = element size; H % H_kv == 0, ne3 % ne3k == 0
+ *   mask f16  [n_kv, >= n_q, ne32, ne33] contiguous, or NULL; broadcast over heads as in ggml
+ *   dst  f32  [D, H, n_q, ne3]       ("permuted" result); nb[0] = 4
+ * Head h reads KV head h / (H / H_kv). A row whose every cell is masked produces zeros.
+ * scratch: device memory of at least kb_flash_attn_ext_scratch_bytes(...) bytes (may be NULL when that
+ * is 0). Supported here: D = 256, K and V of the same type (f16 or q8_0).
+ */
+kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                            const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                            void* stream);
+
+/* Scratch needed by kb_flash_attn_ext for these operands on the current device
+ * (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
+size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                       const kb_fa_params* params);
+
+/* Device-side error word of the current device: the code of the last bounded wait that ran out
+ * (0 = none). clear != 0 resets it. Synchronous (reads device memory). */
+kb_status kb_device_error(int32_t* code, int clear);
+
+/* Library version string. */
+const char* kb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLEIN_B200_H */

@@ -1,0 +1,173 @@
+"""klein_b200 — B200 (sm_100a) kernels for klein's qwen35 attention hot path.
+
+The product is the C-ABI library ``libklein_b200.so`` declared in ``include/klein_b200.h``. This module
+loads it with ctypes and offers thin torch-facing wrappers with the operator names and argument meaning
+of the ggml nodes klein builds (``flash_attn_ext`` = ``ggml_flash_attn_ext``, ...), so tests and the
+benchmark call exactly the entry points a patched ggml-cuda backend would call.
+
+There is no fallback: when the library is missing, ``lib()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libklein_b200.so")
+
+# element types (numbered as enum ggml_type)
+F32, F16, Q8_0, I32, I64, BF16 = 0, 1, 8, 26, 27, 30
+TYPE_SIZE = {F32: 4, F16: 2, I32: 4, I64: 8, BF16: 2}
+Q8_0_BLOCK_BYTES = 34
+
+KB_OK, KB_ERR_ARG, KB_ERR_BAD_SHAPE, KB_ERR_UNSUPPORTED, KB_ERR_SCRATCH, KB_ERR_CUDA, KB_ERR_TIMEOUT = range(7)
+STATUS_NAMES = ["OK", "ERR_ARG", "ERR_BAD_SHAPE", "ERR_UNSUPPORTED", "ERR_SCRATCH", "ERR_CUDA", "ERR_TIMEOUT"]
+
+# every symbol include/klein_b200.h declares (checked by tests/test_abi.py)
+EXPORTED = [
+    "kb_flash_attn_ext",
+    "kb_flash_attn_ext_scratch_bytes",
+    "kb_device_error",
+    "kb_version",
+]
+
+
+class KbError(RuntimeError):
+    def __init__(self, fn, status):
+        super().__init__(f"{fn} returned {STATUS_NAMES[status] if 0 <= status < len(STATUS_NAMES) else status}")
+        self.status = status
+
+
+class KbTensor(ctypes.Structure):
+    _fields_ = [("type", c_int32), ("ne", c_int64 * 4), ("nb", c_size_t * 4), ("data", c_void_p)]
+
+
+class KbFaParams(ctypes.Structure):
+    _fields_ = [("scale", c_float), ("max_bias", c_float), ("logit_softcap", c_float), ("prec", c_int32),
+                ("causal", c_int32), ("pos0", c_int64), ("kv_lo", c_int64), ("ring", c_int64)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C-ABI library; raises when it has not been built (there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m klein_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER
+        L.kb_flash_attn_ext.restype = c_int32
+        L.kb_flash_attn_ext.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams), P(KbTensor),
+                                        c_void_p, c_size_t, c_void_p]
+        L.kb_flash_attn_ext_scratch_bytes.restype = c_size_t
+        L.kb_flash_attn_ext_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
+        L.kb_device_error.restype = c_int32
+        L.kb_device_error.argtypes = [P(c_int32), c_int32]
+        L.kb_version.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != KB_OK:
+        raise KbError(fn, status)
+
+
+# ------------------------------------------------------------------------------------------------ tensors
+
+def kb_tensor(data_ptr: int, type_: int, ne, nb) -> KbTensor:
+    """A kb_tensor from ggml-order extents ne[0..3] (innermost first) and byte strides nb[0..3]."""
+    ne = list(ne) + [1] * (4 - len(ne))
+    nb = list(nb)
+    while len(nb) < 4:
+        nb.append(nb[-1] * ne[len(nb) - 1])
+    t = KbTensor()
+    t.type = type_
+    for i in range(4):
+        t.ne[i] = int(ne[i])
+        t.nb[i] = int(nb[i])
+    t.data = data_ptr
+    return t
+
+
+def from_torch(x, type_: int | None = None) -> KbTensor:
+    """kb_tensor view of a torch tensor (ggml order: reversed shape and strides)."""
+    import torch
+
+    if type_ is None:
+        type_ = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}[x.dtype]
+    es = x.element_size()
+    ne = list(reversed(x.shape)) + [1] * (4 - x.dim())
+    nb = [s * es for s in reversed(x.stride())]
+    while len(nb) < 4:
+        nb.append(nb[-1] * ne[len(nb) - 1] if nb else es)
+    return kb_tensor(x.data_ptr(), type_, ne, nb)
+
+
+def kv_cache_view(cache, kv_type: int, n_head_kv: int, head_dim: int, n_kv: int | None = None) -> KbTensor:
+    """klein's K or V view of a cache [n_ctx rows][n_head_kv * head_dim elements] (graph.cpp:114-117):
+    ggml tensor [head_dim, n_kv, n_head_kv] with nb1 = row bytes, nb2 = one head's bytes."""
+    rows = cache.shape[0] if n_kv is None else n_kv
+    row_bytes = cache.stride(0) * cache.element_size()
+    if kv_type == Q8_0:
+        head_bytes = head_dim // 32 * Q8_0_BLOCK_BYTES
+        es = Q8_0_BLOCK_BYTES  # nb0 of a q8_0 tensor is the block size
+    else:
+        es = TYPE_SIZE[kv_type]
+        head_bytes = head_dim * es
+    return kb_tensor(cache.data_ptr(), kv_type, [head_dim, rows, n_head_kv, 1],
+                     [es, row_bytes, head_bytes, row_bytes * cache.shape[0]])
+
+
+# ------------------------------------------------------------------------------------------------ ops
+
+def fa_params(scale: float, max_bias=0.0, softcap=0.0, causal=False, pos0=0, kv_lo=0, ring=0) -> KbFaParams:
+    p = KbFaParams()
+    p.scale, p.max_bias, p.logit_softcap, p.prec = scale, max_bias, softcap, 10
+    p.causal, p.pos0, p.kv_lo, p.ring = int(causal), pos0, kv_lo, ring
+    return p
+
+
+def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bias=0.0, softcap=0.0, causal=False,
+                   pos0=0, kv_lo=0, ring=0, out=None, stream=None):
+    """GGML_OP_FLASH_ATTN_EXT through kb_flash_attn_ext.
+
+    q: torch f32 on the GPU, token-major [ne3][n_q][H][D] (or [n_q][H][D]); passed as klein's permuted
+    view [D, n_q, H, ne3]. k, v: kb_tensor cache views (kv_cache_view). mask: torch f16 [n_q'][n_kv] or
+    None. Returns f32 [ne3][n_q][H][D] (ggml's permuted result [D, H, n_q, ne3]).
+    """
+    import torch
+
+    if q.dim() == 3:
+        q = q.unsqueeze(0)
+    ne3, n_q, H, D = q.shape
+    es = 4
+    qt = kb_tensor(q.data_ptr(), F32, [D, n_q, H, ne3],
+                   [es, q.stride(1) * es, q.stride(2) * es, q.stride(0) * es])
+    if out is None:
+        out = torch.empty((ne3, n_q, H, D), dtype=torch.float32, device=q.device)
+    dt = kb_tensor(out.data_ptr(), F32, [D, H, n_q, ne3], [4, D * 4, H * D * 4, n_q * H * D * 4])
+    mt = None
+    if mask is not None:
+        m = mask if mask.dim() == 4 else mask.reshape((1, 1) + tuple(mask.shape[-2:]))
+        mt = from_torch(m, F16)
+    prm = fa_params(scale, max_bias, softcap, causal, pos0, kv_lo, ring)
+    L = lib()
+    nbytes = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(prm))
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
+    rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(mt) if mt is not None else None,
+                             ctypes.byref(prm), ctypes.byref(dt), c_void_p(scratch.data_ptr()), c_size_t(nbytes),
+                             c_void_p(st))
+    check("kb_flash_attn_ext", rc)
+    out._kb_scratch = scratch  # keep alive until the stream has used it
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    code = c_int32(0)
+    check("kb_device_error", lib().kb_device_error(ctypes.byref(code), int(clear)))
+    return code.value

@@ -1,0 +1,398 @@
+// Split-KV streaming attention for decode (1 query token) and the MTP verify step (a few tokens):
+// GGML_OP_FLASH_ATTN_EXT with few query rows over a long KV cache. HBM-bound: every K/V byte is read
+// once, staged by TMA into a 3-deep shared-memory ring, and consumed by warp-level tensor-core MMA.
+//
+// Work split. One CTA per (KV split, KV head, row chunk). The rows of a KV head are its n_q * gqa query
+// rows (query i, head-in-group g -> row i*gqa + g); a CTA takes up to 32 of them as NRG groups of 8.
+// Consumer warp (rg, kg) owns row group rg and keys 16kg..16kg+15 of every 64-key tile, and keeps its own
+// online-softmax state (max, sum, O^T 256x8 in registers) over its keys, so the main loop needs no
+// cross-warp synchronisation: S^T = K Q^T (16 keys x 8 rows) is an m16n8k16 chain over D, P^T goes from
+// the accumulator into the B fragment of O^T += V^T P^T with two movmatrix transposes, and V^T comes from
+// ldmatrix.trans. At the end the 4 key groups merge through shared memory (log-sum-exp), and when the KV
+// range is split over several CTAs a second kernel merges the per-split partials the same way
+// (the combine of ggml's ops.cpp:9370-9438 / fattn-common.cuh:924-978).
+//
+// Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
+// the K dot type (f16 for f16 K, :8960), scores are scaled, soft-capped, masked (-inf cells skipped), and
+// a row with no visible cell yields zeros (:9066). Accumulation is f32 throughout.
+#include "kb_common.cuh"
+#include "kb_internal.h"
+
+namespace kb {
+
+namespace {
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr int D = FA_D;
+constexpr int TILE = FA_TILE;
+constexpr int ST = FA_STAGES;
+constexpr int NKG = FA_NKG;
+constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 keys][64 dims] f16, 128B-swizzled
+constexpr int STAGE_F16 = 2 * KTILE_F16;       // K + V
+constexpr int QSTRIDE = D + 8;                 // f16 elements per staged Q row (padded)
+
+__host__ __device__ constexpr int q_bytes(int nrg) { return nrg * 8 * QSTRIDE * 2; }
+
+__host__ __device__ constexpr size_t smem_f16(int nrg) {
+    return 1024 /* alignment slack */ + (size_t) ST * STAGE_F16 + q_bytes(nrg) + 2 * ST * sizeof(uint64_t);
+}
+
+__device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
+    if (p.max_bias <= 0.0f) return 1.0f;
+    return h < p.n_head_log2 ? powf(p.m0, (float) (h + 1)) : powf(p.m1, (float) (2 * (h - p.n_head_log2) + 1));
+}
+
+// score of one (key, row) pair in log2 units, or -inf when the cell is not visible
+__device__ __forceinline__ float masked_score(const FaStreamParams& p, float x, int64_t key, int qi, int h, int b,
+                                              float slope) {
+    float v = p.has_softcap ? p.softcap_log2 * tanhf(x * p.scale_sc) : x * p.scale_log2;
+    if (key >= p.n_kv || qi >= p.n_q) return -INFINITY;
+    if (p.causal) {
+        const int64_t pos = p.pos0 + qi;
+        int64_t c = key;
+        if (p.ring > 0) {
+            const int64_t end = p.pos0 + p.n_q - 1;
+            c = end - (((end - key) % p.ring) + p.ring) % p.ring;
+            if (c <= pos - p.ring) return -INFINITY;
+        }
+        if (c < p.kv_lo || c > pos) return -INFINITY;
+    }
+    if (p.mask) {
+        const __half mh = *reinterpret_cast<const __half*>(p.mask + key * 2 + qi * p.m_nb1 + (h % p.m_ne2) * p.m_nb2 +
+                                                           (b % p.m_ne3) * p.m_nb3);
+        const float mv = slope * __half2float(mh);
+        if (mv == -INFINITY) return -INFINITY;
+        v += mv * LOG2E;
+    }
+    return v;
+}
+
+template <int NRG>
+__global__ void __launch_bounds__(NRG * NKG * 32)
+    fa_stream_f16_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const FaStreamParams p) {
+    constexpr int NC = NRG * NKG;  // consumer warps; lane 0 of warp 0 also issues the TMA loads
+    constexpr int RPC = NRG * 8;   // rows per CTA
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = smem;
+    __half* Qs = reinterpret_cast<__half*>(smem + ST * STAGE_F16);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * STAGE_F16 + q_bytes(NRG));
+    uint64_t* empty = full + ST;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, hk = blockIdx.y;
+    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
+    const int64_t key_begin = (int64_t) split * p.keys_per_split;
+    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
+    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
+    const int row0 = chunk * RPC;
+    const int rows = min(RPC, p.R - row0);
+    const bool issuer = threadIdx.x == 0;
+    __shared__ int s_failed;
+
+    if (issuer) {
+        s_failed = 0;
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NC);
+        }
+        fence_barrier_init();
+    }
+    // stage Q rows of this CTA as f16 (rounding to the f16 K dot type); padded rows are zero
+    for (int idx = threadIdx.x; idx < RPC * D; idx += blockDim.x) {
+        const int r = idx / D, d = idx % D;
+        float x = 0.0f;
+        if (r < rows) {
+            const int gr = row0 + r;
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            x = *reinterpret_cast<const float*>(p.q + (int64_t) d * 4 + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3);
+        }
+        Qs[r * QSTRIDE + d] = __float2half_rn(x);
+    }
+    __syncthreads();
+
+    // TMA issue state (meaningful in the issuing thread only)
+    int next_issue = 0;
+    uint64_t pol = 0;
+    const int kb3 = b / p.rk3;
+    auto issue = [&](int t) {
+        const int s = t % ST;
+        mbar_arrive_expect_tx(&full[s], STAGE_F16);
+        const int key = (int) (key_begin + (int64_t) t * TILE);
+        uint8_t* kdst = stages + s * STAGE_F16;
+        uint8_t* vdst = kdst + KTILE_F16;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(kdst + c * (TILE * 128), &tmK, &full[s], c * 64, hk, key, kb3, pol);
+            tma_load_4d(vdst + c * (TILE * 128), &tmV, &full[s], c * 64, hk, key, kb3, pol);
+        }
+    };
+    if (issuer && n_tiles > 0) {
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        pol = l2_policy_evict_first();
+        for (; next_issue < min(ST, n_tiles); ++next_issue) issue(next_issue);
+    }
+
+    bool failed = false;
+    float o[16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
+
+    {
+        const int rg = warp / NKG, kg = warp % NKG;
+        const bool active = rg * 8 < rows;
+        const int mi = lane >> 3, rr = lane & 7;
+
+        uint32_t qf[16][2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint32_t r4[4];
+            ldsm_x4(r4, smem_u32(Qs + (8 * rg + rr) * QSTRIDE + 32 * j + 8 * mi));
+            qf[2 * j][0] = r4[0];
+            qf[2 * j][1] = r4[1];
+            qf[2 * j + 1][0] = r4[2];
+            qf[2 * j + 1][1] = r4[3];
+        }
+
+        // this thread's two rows (columns of S^T / O^T): rl0 = 8rg + 2(lane%4), rl1 = rl0 + 1
+        const int gr0 = row0 + 8 * rg + 2 * (lane & 3), gr1 = gr0 + 1;
+        const int qi0 = gr0 / p.gqa, qi1 = gr1 / p.gqa;
+        const int h0 = hk * p.gqa + gr0 % p.gqa, h1 = hk * p.gqa + gr1 % p.gqa;
+        const float slope0 = slope_of(p, h0), slope1 = slope_of(p, h1);
+        // first query row of this CTA: keys up to its position are visible to every row (causal, no ring)
+        const int64_t min_pos = p.pos0 + row0 / p.gqa;
+
+        const int kkey = 16 * kg + (mi & 1) * 8 + rr;  // K tile row addressed by this lane (A fragment)
+        const int kdo = (mi >> 1) * 8;
+        const int vkey = 16 * kg + (mi >> 1) * 8 + rr;  // V tile row addressed by this lane (A^T fragment)
+        const int vdo = (mi & 1) * 8;
+
+        for (int t = 0; t < n_tiles; ++t) {
+            const int s = t % ST;
+            if (issuer) {
+                // tile t must have been issued: wait for its stage to be released by every warp
+                while (next_issue <= t) {
+                    const int si = next_issue % ST;
+                    if (!mbar_wait(&empty[si], ((next_issue / ST) - 1) & 1, p.wait_ns)) {
+                        record_error(p.err, DEV_ERR_WAIT_EMPTY);
+                        failed = true;
+                        break;
+                    }
+                    issue(next_issue++);
+                }
+            }
+            __syncwarp();
+            if (!failed && !mbar_wait(&full[s], (t / ST) & 1, p.wait_ns)) {
+                record_error(p.err, DEV_ERR_WAIT_FULL);
+                failed = true;
+            }
+            if (__any_sync(0xffffffffu, failed)) {
+                failed = true;
+                break;
+            }
+            if (active) {
+                const uint32_t kb = smem_u32(stages + s * STAGE_F16);
+                const uint32_t vb = kb + KTILE_F16;
+                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk) {
+                    const int dim = 16 * kk + kdo;
+                    const uint32_t addr = kb + (dim >> 6) * (TILE * 128) + kkey * 128 + ((((dim & 63) >> 3) ^ (kkey & 7)) << 4);
+                    uint32_t a[4];
+                    ldsm_x4(a, addr);
+                    if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
+                    else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
+                }
+                float x[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
+
+                const int64_t tkey0 = key_begin + (int64_t) t * TILE;
+                const int64_t key0 = tkey0 + 16 * kg + (lane >> 2), key1 = key0 + 8;
+                const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && tkey0 + TILE <= p.n_kv &&
+                                   (!p.causal || (tkey0 >= p.kv_lo && tkey0 + TILE - 1 <= min_pos));
+                float sc[4];
+                if (plain) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sc[e] = x[e] * p.scale_log2;
+                } else {
+                    sc[0] = masked_score(p, x[0], key0, qi0, h0, b, slope0);
+                    sc[1] = masked_score(p, x[1], key0, qi1, h1, b, slope1);
+                    sc[2] = masked_score(p, x[2], key1, qi0, h0, b, slope0);
+                    sc[3] = masked_score(p, x[3], key1, qi1, h1, b, slope1);
+                }
+                // online softmax over this warp's 16 keys, per row (lanes sharing lane%4 share rows)
+                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                }
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                const float ref0 = mn0 == -INFINITY ? 0.0f : mn0, ref1 = mn1 == -INFINITY ? 0.0f : mn1;
+                const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
+                const float p0 = exp2f(sc[0] - ref0), p1 = exp2f(sc[1] - ref1);
+                const float p2 = exp2f(sc[2] - ref0), p3 = exp2f(sc[3] - ref1);
+                l0 = l0 * al0 + (p0 + p2);
+                l1 = l1 * al1 + (p1 + p3);
+                m0 = mn0;
+                m1 = mn1;
+                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+                    for (int mm = 0; mm < 16; ++mm) {
+                        o[mm][0] *= al0;
+                        o[mm][1] *= al1;
+                        o[mm][2] *= al0;
+                        o[mm][3] *= al1;
+                    }
+                }
+                // P^T as the B fragment of O^T += V^T P^T
+                const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
+                const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
+#pragma unroll
+                for (int mm = 0; mm < 16; ++mm) {
+                    const int dim = 16 * mm + vdo;
+                    const uint32_t addr = vb + (dim >> 6) * (TILE * 128) + vkey * 128 + ((((dim & 63) >> 3) ^ (vkey & 7)) << 4);
+                    uint32_t a[4];
+                    ldsm_x4_trans(a, addr);
+                    mma_f16_16816(o[mm], a, pb0, pb1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (issuer) {
+                // refill without blocking: issue every further tile whose stage all warps have released
+                while (next_issue < n_tiles && next_issue < t + 1 + ST) {
+                    const int si = next_issue % ST;
+                    if (!mbar_try_wait(&empty[si], ((next_issue / ST) - 1) & 1)) break;
+                    issue(next_issue++);
+                }
+            }
+        }
+        // row sums over the warp's lanes
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+        }
+    }
+
+    // ---------------------------------------------------------------------- merge the key groups
+    if (failed && lane == 0) atomicExch(&s_failed, 1);
+    __syncthreads();  // every issued stage consumed: the ring is free for the merge buffers
+    if (s_failed) return;  // a bounded wait ran out (error word set): leave the outputs alone
+    float* Ow = reinterpret_cast<float*>(stages);  // [NC][8 rows][D]
+    float* Mw = Ow + NC * 8 * D;                   // [NC][8]
+    float* Lw = Mw + NC * 8;                       // [NC][8]
+    if (warp < NC) {
+        const int ra = 2 * (lane & 3), dl = lane >> 2;
+        float* ow = Ow + warp * 8 * D;
+#pragma unroll
+        for (int mm = 0; mm < 16; ++mm) {
+            ow[ra * D + 16 * mm + dl] = o[mm][0];
+            ow[(ra + 1) * D + 16 * mm + dl] = o[mm][1];
+            ow[ra * D + 16 * mm + 8 + dl] = o[mm][2];
+            ow[(ra + 1) * D + 16 * mm + 8 + dl] = o[mm][3];
+        }
+        if (lane < 4) {
+            Mw[warp * 8 + 2 * lane] = m0;
+            Mw[warp * 8 + 2 * lane + 1] = m1;
+            Lw[warp * 8 + 2 * lane] = l0;
+            Lw[warp * 8 + 2 * lane + 1] = l1;
+        }
+    }
+    __syncthreads();
+
+    const int64_t part_row0 = ((((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits + split) * RPC;
+    for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
+        const int r = idx / D, d = idx % D;
+        const int rg = r >> 3, ri = r & 7;
+        float M = -INFINITY;
+#pragma unroll
+        for (int kg = 0; kg < NKG; ++kg) M = fmaxf(M, Mw[(rg * NKG + kg) * 8 + ri]);
+        float O = 0.0f, L = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int kg = 0; kg < NKG; ++kg) {
+                const int w = rg * NKG + kg;
+                const float f = exp2f(Mw[w * 8 + ri] - M);
+                O += f * Ow[(w * 8 + ri) * D + d];
+                L += f * Lw[w * 8 + ri];
+            }
+        }
+        if (p.n_splits == 1) {
+            const int gr = row0 + r;
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            *reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3) =
+                L > 0.0f ? O / L : 0.0f;
+        } else {
+            p.o_part[(part_row0 + r) * D + d] = O;
+            if (d == 0) {
+                p.ml_part[(part_row0 + r) * 2 + 0] = M;
+                p.ml_part[(part_row0 + r) * 2 + 1] = L;
+            }
+        }
+    }
+}
+
+// Merges the per-split partials of one row (grid: rows x KV heads x ne3, D threads).
+template <int RPC>
+__global__ void __launch_bounds__(D) fa_combine_kernel(const FaStreamParams p) {
+    const int gr = blockIdx.x, hk = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+    const int chunk = gr / RPC, r = gr % RPC;
+    const int64_t base = (((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < p.n_splits; ++s) {
+        const float* ml = p.ml_part + ((base + s) * RPC + r) * 2;
+        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
+    }
+    float O = 0.0f, L = 0.0f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < p.n_splits; ++s) {
+            const float* ml = p.ml_part + ((base + s) * RPC + r) * 2;
+            if (!(ml[1] > 0.0f)) continue;
+            const float f = exp2f(ml[0] - M);
+            O += f * p.o_part[((base + s) * RPC + r) * D + d];
+            L += f * ml[1];
+        }
+    }
+    const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+    *reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3) = L > 0.0f ? O / L : 0.0f;
+}
+
+template <int NRG>
+cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
+    auto kern = fa_stream_f16_kernel<NRG>;
+    const size_t smem = smem_f16(NRG);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
+    kern<<<grid, NRG * NKG * 32, smem, stream>>>(tmK, tmV, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || p.n_splits == 1) return e;
+    dim3 cgrid(p.R, p.n_head_kv, p.ne3);
+    fa_combine_kernel<NRG * 8><<<cgrid, D, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t fa_stream_smem_bytes(int nrg, int kv_type) {
+    (void) kv_type;
+    return smem_f16(nrg);
+}
+
+cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                             cudaStream_t stream) {
+    (void) kv_type;
+    switch (nrg) {
+        case 1: return launch_nrg<1>(p, tmK, tmV, stream);
+        case 2: return launch_nrg<2>(p, tmK, tmV, stream);
+        default: return launch_nrg<3>(p, tmK, tmV, stream);
+    }
+}
+
+}  // namespace kb

@@ -1,0 +1,246 @@
+// C-ABI shim: validates ggml-style tensor descriptors the way ggml's operator constructors and CPU ops do
+// (ggml.c:5506-5548, ops.cpp:8865-8890), plans the kernel launch, builds the TMA descriptors and launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/klein_b200.h"
+#include "kb_internal.h"
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+struct DevInfo {
+    int sm_count = 0;
+};
+
+DevInfo dev_info() {
+    static DevInfo info[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DevInfo{};
+    if (info[dev].sm_count == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        info[dev].sm_count = n;
+    }
+    return info[dev];
+}
+
+uint64_t g_wait_ns = 1000000000ull;  // 1 s budget for every bounded device wait
+
+bool aligned16(size_t x) { return (x & 15) == 0; }
+
+// The split-KV plan of one streaming attention call.
+struct FaPlan {
+    int nrg = 1, n_row_chunks = 1, n_splits = 1;
+    int64_t keys_per_split = 0;
+    size_t scratch = 0;
+};
+
+struct FaShape {
+    int D, n_q, H, ne3, H_kv, ne3k, gqa, R;
+    int64_t n_kv;
+};
+
+kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask, FaShape* s) {
+    if (!q || !k || !v) return KB_ERR_ARG;
+    if (q->type != KB_TYPE_F32) return KB_ERR_UNSUPPORTED;
+    if (k->type != v->type) return KB_ERR_UNSUPPORTED;
+    if (k->type != KB_TYPE_F16) return KB_ERR_UNSUPPORTED;
+    s->D = (int) q->ne[0];
+    s->n_q = (int) q->ne[1];
+    s->H = (int) q->ne[2];
+    s->ne3 = (int) q->ne[3];
+    s->n_kv = k->ne[1];
+    s->H_kv = (int) k->ne[2];
+    s->ne3k = (int) k->ne[3];
+    // ggml_can_mul_mat(k, q) and the CPU op's shape asserts
+    if (k->ne[0] != q->ne[0] || v->ne[0] != k->ne[0]) return KB_ERR_BAD_SHAPE;
+    if (v->ne[1] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return KB_ERR_BAD_SHAPE;
+    if (s->H_kv <= 0 || s->H % s->H_kv != 0 || s->ne3k <= 0 || s->ne3 % s->ne3k != 0) return KB_ERR_BAD_SHAPE;
+    if (s->n_q <= 0 || s->H <= 0 || s->ne3 <= 0 || s->n_kv < 0) return KB_ERR_BAD_SHAPE;
+    if (q->nb[0] != 4 || k->nb[0] != 2 || v->nb[0] != 2) return KB_ERR_BAD_SHAPE;
+    if (s->D != kb::FA_D) return KB_ERR_UNSUPPORTED;
+    if (mask) {
+        if (mask->type != KB_TYPE_F16 || mask->nb[0] != 2) return KB_ERR_UNSUPPORTED;
+        if (mask->ne[0] < s->n_kv || mask->ne[1] < s->n_q) return KB_ERR_BAD_SHAPE;
+        if (mask->ne[2] <= 0 || mask->ne[3] <= 0 || s->H % mask->ne[2] != 0 || s->ne3 % mask->ne[3] != 0)
+            return KB_ERR_BAD_SHAPE;
+    }
+    // TMA: 16-byte aligned base and strides
+    for (const kb_tensor* t : {k, v}) {
+        if (!aligned16(reinterpret_cast<uintptr_t>(t->data)) || !aligned16(t->nb[1]) || !aligned16(t->nb[2]) ||
+            !aligned16(t->nb[3]))
+            return KB_ERR_UNSUPPORTED;
+    }
+    s->gqa = s->H / s->H_kv;
+    s->R = s->n_q * s->gqa;
+    return KB_OK;
+}
+
+FaPlan plan_fa(const FaShape& s) {
+    FaPlan pl;
+    pl.nrg = kb::fa_stream_nrg(s.R);
+    pl.n_row_chunks = (s.R + pl.nrg * 8 - 1) / (pl.nrg * 8);
+    const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
+    const int64_t base = (int64_t) s.H_kv * pl.n_row_chunks * s.ne3;
+    const int64_t tiles = (s.n_kv + kb::FA_TILE - 1) / kb::FA_TILE;
+    int64_t target = sms / base;
+    if (target < 1) target = 1;
+    if (tiles == 0) {
+        pl.n_splits = 1;
+        pl.keys_per_split = kb::FA_TILE;
+    } else {
+        const int64_t tps = (tiles + target - 1) / target;
+        pl.keys_per_split = tps * kb::FA_TILE;
+        pl.n_splits = (int) ((tiles + tps - 1) / tps);
+    }
+    if (pl.n_splits > 1) {
+        const size_t rows = (size_t) base * pl.n_splits * pl.nrg * 8;
+        pl.scratch = rows * kb::FA_D * 4 + 256 + rows * 2 * 4;
+    }
+    return pl;
+}
+
+kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return KB_ERR_CUDA;
+    // dims (innermost first): head dim, KV head, cell, batch; box = 64 dims x 1 head x 64 cells
+    const cuuint64_t dims[4] = {(cuuint64_t) t->ne[0], (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[3]};
+    const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t) kb::FA_TILE, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? KB_OK : KB_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* kb_version(void) { return "klein_b200 0.1"; }
+
+size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                       const kb_fa_params* params) {
+    (void) params;
+    FaShape s;
+    if (check_fa(q, k, v, nullptr, &s) != KB_OK) return 0;
+    return plan_fa(s).scratch;
+}
+
+kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                            const kb_fa_params* prm, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                            void* stream) {
+    if (!prm || !dst) return KB_ERR_ARG;
+    FaShape s;
+    kb_status st = check_fa(q, k, v, mask, &s);
+    if (st != KB_OK) return st;
+    if (dst->type != KB_TYPE_F32 || dst->nb[0] != 4) return KB_ERR_BAD_SHAPE;
+    if (dst->ne[0] != s.D || dst->ne[1] != s.H || dst->ne[2] != s.n_q || dst->ne[3] != s.ne3) return KB_ERR_BAD_SHAPE;
+    if (prm->logit_softcap != 0.0f && !(std::isfinite(prm->logit_softcap))) return KB_ERR_ARG;
+    if (prm->max_bias > 0.0f && !mask) return KB_ERR_ARG;  // ggml: ALiBi needs a mask
+    if (prm->causal && prm->ring < 0) return KB_ERR_ARG;
+
+    if (s.n_kv == 0) {
+        // no cells: every row's softmax sum is 0, so the output is 0 (ops.cpp:9066)
+        const size_t row = (size_t) s.D * 4;
+        if (dst->nb[1] != row || dst->nb[2] != row * s.H || dst->nb[3] != row * s.H * s.n_q) return KB_ERR_UNSUPPORTED;
+        return cudaMemsetAsync(dst->data, 0, row * s.H * s.n_q * s.ne3, static_cast<cudaStream_t>(stream)) == cudaSuccess
+                   ? KB_OK
+                   : KB_ERR_CUDA;
+    }
+    const FaPlan pl = plan_fa(s);
+    if (pl.scratch > 0 && (!scratch || scratch_bytes < pl.scratch)) return KB_ERR_SCRATCH;
+
+    kb::FaStreamParams p{};
+    p.q = static_cast<const char*>(q->data);
+    p.q_nb1 = (int64_t) q->nb[1];
+    p.q_nb2 = (int64_t) q->nb[2];
+    p.q_nb3 = (int64_t) q->nb[3];
+    p.n_q = s.n_q;
+    p.n_head = s.H;
+    p.n_head_kv = s.H_kv;
+    p.gqa = s.gqa;
+    p.ne3 = s.ne3;
+    p.rk3 = s.ne3 / s.ne3k;
+    p.R = s.R;
+    p.n_kv = s.n_kv;
+    if (mask) {
+        p.mask = static_cast<const char*>(mask->data);
+        p.m_nb1 = (int64_t) mask->nb[1];
+        p.m_nb2 = (int64_t) mask->nb[2];
+        p.m_nb3 = (int64_t) mask->nb[3];
+        p.m_ne2 = (int) mask->ne[2];
+        p.m_ne3 = (int) mask->ne[3];
+    }
+    const float log2e = 1.4426950408889634f;
+    p.scale_log2 = prm->scale * log2e;
+    p.has_softcap = prm->logit_softcap != 0.0f;
+    if (p.has_softcap) {
+        p.scale_sc = prm->scale / prm->logit_softcap;
+        p.softcap_log2 = prm->logit_softcap * log2e;
+    }
+    p.max_bias = prm->max_bias;
+    p.n_head_log2 = 1 << (int) std::floor(std::log2((double) s.H));
+    p.m0 = std::pow(2.0f, -(prm->max_bias) / p.n_head_log2);
+    p.m1 = std::pow(2.0f, -(prm->max_bias / 2.0f) / p.n_head_log2);
+    p.causal = prm->causal;
+    p.pos0 = prm->pos0;
+    p.kv_lo = prm->kv_lo;
+    p.ring = prm->causal ? prm->ring : 0;
+    p.n_splits = pl.n_splits;
+    p.keys_per_split = pl.keys_per_split;
+    p.n_row_chunks = pl.n_row_chunks;
+    if (pl.scratch > 0) {
+        const size_t rows = (size_t) s.H_kv * pl.n_row_chunks * s.ne3 * pl.n_splits * pl.nrg * 8;
+        p.o_part = static_cast<float*>(scratch);
+        const uintptr_t ml = (reinterpret_cast<uintptr_t>(scratch) + rows * kb::FA_D * 4 + 255) & ~uintptr_t(255);
+        p.ml_part = reinterpret_cast<float*>(ml);
+    }
+    p.dst = static_cast<char*>(dst->data);
+    p.d_nb1 = (int64_t) dst->nb[1];
+    p.d_nb2 = (int64_t) dst->nb[2];
+    p.d_nb3 = (int64_t) dst->nb[3];
+    p.err = kb::device_error_word();
+    p.wait_ns = g_wait_ns;
+
+    CUtensorMap tmK, tmV;
+    if ((st = encode_kv_map(k, &tmK)) != KB_OK) return st;
+    if ((st = encode_kv_map(v, &tmV)) != KB_OK) return st;
+    cudaError_t e = kb::launch_fa_stream(p, pl.nrg, k->type, tmK, tmV, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_device_error(int32_t* code, int clear) {
+    if (!code) return KB_ERR_ARG;
+    int* w = kb::device_error_word();
+    if (!w) return KB_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return KB_ERR_CUDA;
+    *code = v;
+    if (clear && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return KB_ERR_CUDA;
+    return KB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,58 @@
+// Internal interface between the C-ABI shim (kb_api.cpp) and the kernel launchers (*.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kb {
+
+constexpr int FA_D = 256;            // head dimension of qwen35 full attention (K and V)
+constexpr int FA_TILE = 64;          // keys per pipeline stage
+constexpr int FA_STAGES = 3;         // TMA pipeline depth
+constexpr int FA_NKG = 4;            // key groups (consumer warps per 8-row group)
+
+// Parameters of one streaming (decode / verify) attention launch. Byte strides follow ggml.
+struct FaStreamParams {
+    const char* q;                   // f32 [D, n_q, H, ne3]
+    int64_t q_nb1, q_nb2, q_nb3;
+    int n_q, n_head, n_head_kv, gqa, ne3, rk3;
+    int R;                           // rows per KV head = n_q * gqa
+    int64_t n_kv;
+    // dense f16 mask [n_kv, n_q', ne32, ne33] or null
+    const char* mask;
+    int64_t m_nb1, m_nb2, m_nb3;
+    int m_ne2, m_ne3;
+    float scale_log2;                // scale * log2(e)          (no softcap)
+    float scale_sc;                  // scale / softcap           (softcap)
+    float softcap_log2;              // softcap * log2(e)         (softcap)
+    int has_softcap;
+    float max_bias, m0, m1;
+    int n_head_log2;
+    int causal;
+    int64_t pos0, kv_lo, ring;
+    // KV split
+    int n_splits;
+    int64_t keys_per_split;          // multiple of FA_TILE
+    int n_row_chunks;                // CTAs along the rows of one KV head (24 rows each at most)
+    // outputs
+    float* o_part;                   // scratch: [ne3][H_kv][chunk][split][RPC][D]
+    float* ml_part;                  // scratch: [ne3][H_kv][chunk][split][RPC][2] (max in log2 units, sum)
+    char* dst;                       // f32 [D, H, n_q, ne3]
+    int64_t d_nb1, d_nb2, d_nb3;
+    int* err;                        // device error word
+    uint64_t wait_ns;                // budget of every bounded wait
+};
+
+// rows handled by one CTA for a given row count: 8 * NRG with NRG in 1..3 (more rows -> more CTAs)
+inline int fa_stream_nrg(int R) { return R <= 8 ? 1 : R <= 16 ? 2 : 3; }
+
+size_t fa_stream_smem_bytes(int nrg, int kv_type);
+
+// launches the split-KV streaming kernel (+ the LSE combine when n_splits > 1)
+cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                             cudaStream_t stream);
+
+int* device_error_word();  // address of the current device's error word (null on failure)
+
+}  // namespace kb

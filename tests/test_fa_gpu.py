@@ -1,0 +1,176 @@
+"""GPU parity of kb_flash_attn_ext (decode / verify streaming kernel) against the CPU oracle.
+
+Every case runs the CUDA path through the C ABI and compares it with the exact f64 restatement on the same
+cache contents and, at sizes ggml finishes quickly, with the reference's own ggml CPU op (three-way rule in
+tests/parity.py).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from parity import check_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def exact_np(q, kd, vd, mask=None, scale=1.0 / 16, softcap=0.0):
+    """f64 attention with numpy matmuls (same definition as oracle.rs_flash_attn_f64, faster at large n_kv)."""
+    n_q, H, D = q.shape
+    H_kv = kd.shape[1]
+    G = H // H_kv
+    out = np.zeros((n_q, H, D))
+    for h in range(H):
+        hk = h // G
+        s = (q[:, h, :].astype(np.float64) @ kd[:, hk, :].T.astype(np.float64)) * scale
+        if softcap:
+            s = softcap * np.tanh(s / softcap)
+        if mask is not None:
+            s = s + mask.astype(np.float64)
+        m = s.max(1, keepdims=True)
+        ok = np.isfinite(m)
+        m = np.where(ok, m, 0.0)
+        p = np.exp(s - m)
+        l = p.sum(1, keepdims=True)
+        o = (p @ vd[:, hk, :].astype(np.float64))
+        out[:, h, :] = np.where(l > 0, o / np.where(l > 0, l, 1.0), 0.0)
+    return out
+
+
+def run_gpu(kb, cuda, q, kc, vc, H_kv, scale=1.0 / 16, mask=None, **kw):
+    import torch
+
+    D = q.shape[-1]
+    qt = torch.from_numpy(q).to(cuda)
+    kt = torch.from_numpy(kc).to(cuda)
+    vt = torch.from_numpy(vc).to(cuda)
+    kv_type = kb.F16 if kc.dtype == np.float16 else kb.Q8_0
+    kview = kb.kv_cache_view(kt, kv_type, H_kv, D)
+    vview = kb.kv_cache_view(vt, kv_type, H_kv, D)
+    mt = None if mask is None else torch.from_numpy(mask.astype(np.float16)).to(cuda)
+    out = kb.flash_attn_ext(qt, kview, vview, scale, mask=mt, **kw)
+    torch.cuda.synchronize()
+    assert kb.device_error() == 0
+    return out[0].cpu().numpy()
+
+
+@pytest.mark.parametrize("n_q,n_kv", [(1, 4096), (4, 4096), (1, 1), (1, 17), (4, 63), (4, 64), (4, 65), (1, 1000),
+                                      (4, 4099), (2, 777), (3, 2048), (5, 513), (8, 300)])
+def test_f16_causal_analytic(kb, cuda, n_q, n_kv):
+    q, kc, vc, kd, vd = O.make_fa_inputs(1000 + n_q * 7 + n_kv, n_q, n_kv)
+    pos0 = max(n_kv - n_q, 0)
+    mask = O.rs_visible_mask(n_q, n_kv, pos0)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0)
+    exact = exact_np(O.q_round_f16(q), kd, vd, mask)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, 4, mask=mask.astype(np.float16), n_threads=4, use_ref=False) \
+        if O.ref_available() and n_kv <= 4099 else None
+    check_attention(gpu, exact, ggml)
+
+
+def test_f16_decode_config0(kb, cuda):
+    """config[0]: 1 token, 4096 cells, 24/4 heads, D 256, scale 1/16, no mask."""
+    q, kc, vc, kd, vd = O.make_fa_inputs(1234, 1, 4096)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4)
+    exact = O.rs_flash_attn_f64(O.q_round_f16(q), kd, vd)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, 4, n_threads=8, use_ref=False) if O.ref_available() else None
+    e_gpu, e_cpu, _ = check_attention(gpu, exact, ggml)
+    assert e_gpu < 1e-3
+
+
+def test_f16_dense_mask_matches_analytic(kb, cuda):
+    """klein's dense mask (padded n_kv, engine.cpp:308-326) and the analytic bounds give the same output."""
+    n_q, n_past = 4, 4100
+    n_kv = (n_past + n_q + 255) // 256 * 256  # padded_n_kv
+    q, kc, vc, kd, vd = O.make_fa_inputs(77, n_q, n_kv)
+    mask = O.rs_visible_mask(n_q, n_kv, n_past)
+    g_dense = run_gpu(kb, cuda, q, kc, vc, 4, mask=mask)
+    g_anal = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_past)
+    exact = exact_np(O.q_round_f16(q), kd, vd, mask)
+    check_attention(g_dense, exact)
+    check_attention(g_anal, exact)
+    assert np.abs(g_dense - g_anal).max() <= 1e-6 * np.abs(exact).max()
+
+
+def test_f16_fully_masked_rows_are_zero(kb, cuda):
+    q, kc, vc, kd, vd = O.make_fa_inputs(5, 4, 512)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=100, kv_lo=200)
+    assert np.all(gpu == 0.0)
+
+
+def test_f16_kv_lo_window(kb, cuda):
+    n_q, n_kv = 4, 3000
+    q, kc, vc, kd, vd = O.make_fa_inputs(6, n_q, n_kv)
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q, kv_lo=1234)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q, kv_lo=1234)
+    check_attention(gpu, exact_np(O.q_round_f16(q), kd, vd, mask))
+
+
+def test_f16_ring_window(kb, cuda):
+    """The MTP head's sliding window: a ring of `ring` cells (engine.cpp:304, :317-322)."""
+    ring, n_q, pos0 = 1024, 4, 5000
+    q, kc, vc, kd, vd = O.make_fa_inputs(8, n_q, ring)
+    mask = O.rs_visible_mask(n_q, ring, pos0, ring=ring)
+    g_anal = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0, ring=ring)
+    g_dense = run_gpu(kb, cuda, q, kc, vc, 4, mask=mask)
+    exact = exact_np(O.q_round_f16(q), kd, vd, mask)
+    check_attention(g_anal, exact)
+    check_attention(g_dense, exact)
+
+
+def test_f16_softcap(kb, cuda):
+    q, kc, vc, kd, vd = O.make_fa_inputs(9, 4, 2048)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, softcap=2.0)
+    exact = exact_np(O.q_round_f16(q), kd, vd, softcap=2.0)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, 4, softcap=2.0, n_threads=4, use_ref=True) if O.ref_available() else None
+    check_attention(gpu, exact, ggml)
+
+
+def test_f16_alibi(kb, cuda):
+    n_q, n_kv = 4, 1024
+    q, kc, vc, kd, vd = O.make_fa_inputs(10, n_q, n_kv)
+    rng = np.random.default_rng(3)
+    mask = (rng.standard_normal((n_q, n_kv)) * 0.5).astype(np.float16).astype(np.float32)
+    mask[:, 700:] = -np.inf
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, mask=mask, max_bias=8.0)
+    exact = O.rs_flash_attn_f64(O.q_round_f16(q), kd, vd, mask=mask, max_bias=8.0)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, 4, mask=mask.astype(np.float16), max_bias=8.0, n_threads=4) \
+        if O.ref_available() else None
+    check_attention(gpu, exact, ggml)
+
+
+@pytest.mark.parametrize("H,H_kv", [(8, 8), (32, 4), (16, 2)])
+def test_f16_gqa_shapes(kb, cuda, H, H_kv):
+    q, kc, vc, kd, vd = O.make_fa_inputs(11 + H, 4, 1500, H=H, H_kv=H_kv)
+    gpu = run_gpu(kb, cuda, q, kc, vc, H_kv)
+    check_attention(gpu, exact_np(O.q_round_f16(q), kd, vd))
+
+
+def test_f16_long_verify_262144(kb, cuda):
+    """config[3] shape (f16): 4 tokens, causal among the last 4, 262,144 cells."""
+    n_q, n_kv = 4, 262144
+    q, kc, vc, kd, vd = O.make_fa_inputs(31337, n_q, n_kv)
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q)
+    check_attention(gpu, exact_np(O.q_round_f16(q), kd, vd, mask))
+
+
+def test_scratch_too_small_is_rejected(kb, cuda):
+    import ctypes
+    import torch
+
+    q, kc, vc, kd, vd = O.make_fa_inputs(12, 4, 8192)
+    qt = torch.from_numpy(q).to(cuda).unsqueeze(0)
+    kt = torch.from_numpy(kc).to(cuda)
+    vt = torch.from_numpy(vc).to(cuda)
+    kv = kb.kv_cache_view(kt, kb.F16, 4, 256)
+    vv = kb.kv_cache_view(vt, kb.F16, 4, 256)
+    qv = kb.kb_tensor(qt.data_ptr(), kb.F32, [256, 4, 24, 1], [4, 24 * 256 * 4, 256 * 4, 4 * 24 * 256 * 4])
+    out = torch.zeros((4, 24, 256), device=cuda)
+    dv = kb.from_torch(out.reshape(1, 4, 24, 256))
+    prm = kb.fa_params(1 / 16)
+    need = kb.lib().kb_flash_attn_ext_scratch_bytes(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(prm))
+    assert need > 0
+    rc = kb.lib().kb_flash_attn_ext(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), None, ctypes.byref(prm),
+                                    ctypes.byref(dv), None, 0, None)
+    assert rc == kb.KB_ERR_SCRATCH
+    torch.cuda.synchronize()
+    assert float(out.abs().max()) == 0.0
