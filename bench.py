@@ -1,0 +1,379 @@
+#!/usr/bin/env python
+"""Benchmark of klein's attention hot path on B200.
+
+Headline (BASELINE.json metric "verify-step attention us/layer @262K KV"): the MTP verify step of
+config[3] — 4 query tokens per layer, causal among the 4 new cells, over a 262,144-cell KV cache
+(4 KV heads x 256, f16) in each of 16 full-attention layers. One step = the 16 layers. value = us per
+layer of the whole job (max over ranks), lower is better. With --gpus N the KV sequence of every layer is
+split into N contiguous ranges, one per rank (strong scaling); each rank computes unnormalised partials
+(o, m, l) of its range and the partials are merged with a log-sum-exp combine after an NCCL all-gather.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+--impl reference times the reference's own ggml CPU implementation of the same op (oracle/_ref, built
+from the reference sources) on the host cores, one layer per step, and prints the same JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_KV = 262144
+N_Q = 4
+H, H_KV, D = 24, 4, 256
+LAYERS = 16
+SCALE = 1.0 / 16
+METRIC = "verify-step attention us/layer @262K KV"
+UNIT = "us/layer"
+
+
+def kv_bytes_per_layer(n_kv: int, kv_type: str) -> int:
+    row = H_KV * D * 2 if kv_type == "f16" else H_KV * D // 32 * 34
+    return 2 * n_kv * row
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(name: str):
+    """dram bytes per launch recorded in a committed ncu summary (profiles/<name>.md, line 'traffic_bytes: N')."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes:"):
+                    return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        rows = []
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                rows.append({"sm": float(f[1]), "max": float(f[2]), "util": float(f[4]), "hw": f[6], "hwt": f[7],
+                             "swt": f[8], "pcap": f[9]})
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [r for r in rows if r["util"] > 0] or rows
+        reasons = set()
+        for r in load:
+            if r["hw"] == "Active":
+                reasons.add("hw_slowdown")
+            if r["hwt"] == "Active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"] == "Active":
+                reasons.add("sw_thermal_slowdown")
+            if r["pcap"] == "Active":
+                reasons.add("sw_power_cap")
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["max"] for r in load),
+                "reasons": sorted(reasons), "samples": len(load)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU arm
+
+def cpu_verify_sample(kv_type: str, threads: int, budget_s: float, min_reps: int = 2):
+    """Times ggml's CPU flash attention (the reference build in oracle/_ref) on one layer of the headline
+    workload: 4 tokens over 262,144 cells. Returns (us per layer, reps)."""
+    import numpy as np
+
+    import oracle as O
+
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((N_Q, H, D), dtype=np.float32)
+    if kv_type == "f16":
+        kc = rng.standard_normal((N_KV, H_KV * D), dtype=np.float32).astype(np.float16)
+        vc = rng.standard_normal((N_KV, H_KV * D), dtype=np.float32).astype(np.float16)
+        t = O.GGML_F16
+    else:
+        kc = O.rs_quantize_q8_0(rng.standard_normal((N_KV, H_KV * D), dtype=np.float32))
+        vc = O.rs_quantize_q8_0(rng.standard_normal((N_KV, H_KV * D), dtype=np.float32))
+        t = O.GGML_Q8_0
+    mask = O.rs_visible_mask(N_Q, N_KV, N_KV - N_Q).astype(np.float16)
+    O.ref_flash_attn_ext(q, kc, vc, t, H_KV, mask=mask, n_threads=threads, use_ref=False)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        O.ref_flash_attn_ext(q, kc, vc, t, H_KV, mask=mask, n_threads=threads, use_ref=False)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, len(times)
+
+
+def run_reference(args, rank: int):
+    """--impl reference: the reference's ggml CPU op on the host cores, one layer per step."""
+    if rank != 0:
+        return
+    import oracle as O
+
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference tree absent at build time)"}))
+        return
+    import numpy as np
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((N_Q, H, D), dtype=np.float32)
+    kc = rng.standard_normal((N_KV, H_KV * D), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((N_KV, H_KV * D), dtype=np.float32).astype(np.float16)
+    mask = O.rs_visible_mask(N_Q, N_KV, N_KV - N_Q).astype(np.float16)
+    for _ in range(args.warmup):
+        O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, H_KV, mask=mask, n_threads=threads, use_ref=False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.ref_flash_attn_ext(q, kc, vc, O.GGML_F16, H_KV, mask=mask, n_threads=threads, use_ref=False)
+    dt = time.perf_counter() - t0
+    us = dt * 1e6 / args.steps
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config[3] long verify, one layer per step: 4 tokens, causal among the last 4, "
+                               "262144-cell f16 KV cache, 24 Q / 4 KV heads, D 256 (ggml CPU flash_attn_ext)",
+                   "n_kv": N_KV, "kv_type": "f16", "layers_per_step": 1},
+        "cpu_baseline": {"value": round(us, 2), "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} layers of the headline workload on ggml's CPU backend"},
+        "e2e": {"value": round(us, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU arm
+
+def run_gpu(args, rank: int, world: int, local_rank: int):
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    import klein_b200 as kb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    kb.lib()
+
+    from klein_b200.kv_split import kv_range, local_bounds, packed_part_floats
+
+    lo, hi = kv_range(N_KV, world, rank)  # this rank's contiguous KV range (strong scaling)
+    n_kv = hi - lo
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    layers = []
+    for _ in range(LAYERS):
+        kc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
+        vc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
+        layers.append((kc, vc, kb.kv_cache_view(kc, kb.F16, H_KV, D), kb.kv_cache_view(vc, kb.F16, H_KV, D)))
+    q = torch.randn(1, N_Q, H, D, device=dev, generator=gen)
+    out = torch.empty(1, N_Q, H, D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # causal among the 4 new cells, which sit at the end of the last rank's range
+    pos0, kv_lo = local_bounds(lo, N_KV - N_Q, 0)
+
+    qt = kb.kb_tensor(q.data_ptr(), kb.F32, [D, N_Q, H, 1], [4, H * D * 4, D * 4, N_Q * H * D * 4])
+    dt = kb.kb_tensor(out.data_ptr(), kb.F32, [D, H, N_Q, 1], [4, D * 4, H * D * 4, N_Q * H * D * 4])
+    prm = kb.fa_params(SCALE, causal=True, pos0=pos0, kv_lo=kv_lo)
+    L = kb.lib()
+    need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]), ctypes.byref(layers[0][3]),
+                                             ctypes.byref(prm))
+    scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(scratch.data_ptr())
+    st = ctypes.c_void_p(stream.cuda_stream)
+
+    rows = N_Q * H
+    if world > 1:
+        # per-rank packed partial [o rows x D | (m, l) rows x 2], all-gathered over NCCL, merged by kb_lse_combine
+        pf = packed_part_floats(rows, D)
+        part = torch.empty(pf, device=dev)
+        gathered = torch.empty(world * pf, device=dev)
+        pt = kb.kb_tensor(part.data_ptr(), kb.F32, [D, H, N_Q, 1], [4, D * 4, H * D * 4, N_Q * H * D * 4])
+        ml_ptr = ctypes.c_void_p(part.data_ptr() + rows * D * 4)
+        g_o = ctypes.c_void_p(gathered.data_ptr())
+        g_ml = ctypes.c_void_p(gathered.data_ptr() + rows * D * 4)
+
+    def layer_call(l):
+        if world == 1:
+            rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(layers[l][2]), ctypes.byref(layers[l][3]), None,
+                                     ctypes.byref(prm), ctypes.byref(dt), sp, ctypes.c_size_t(need), st)
+            if rc != 0:
+                raise kb.KbError("kb_flash_attn_ext", rc)
+            return
+        rc = L.kb_flash_attn_ext_partial(ctypes.byref(qt), ctypes.byref(layers[l][2]), ctypes.byref(layers[l][3]), None,
+                                         ctypes.byref(prm), ctypes.byref(pt), ml_ptr, sp, ctypes.c_size_t(need), st)
+        if rc != 0:
+            raise kb.KbError("kb_flash_attn_ext_partial", rc)
+        dist.all_gather_into_tensor(gathered, part)
+        rc = L.kb_lse_combine(g_o, g_ml, ctypes.c_int64(pf), world, ctypes.c_int64(rows), D,
+                              ctypes.c_void_p(out.data_ptr()), st)
+        if rc != 0:
+            raise kb.KbError("kb_lse_combine", rc)
+
+    def step():
+        for l in range(LAYERS):
+            layer_call(l)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    us_per_layer = ms_per_step * 1e3 / LAYERS
+    kernels_per_call = (2 if need > 0 else 1) + (1 if world > 1 else 0)
+    launches = args.steps * LAYERS * kernels_per_call
+
+    # end to end through the C ABI: per layer, pinned host Q -> device, attention, output -> pinned host
+    q_host = torch.randn(LAYERS, N_Q, H, D).pin_memory()
+    o_host = torch.empty(LAYERS, N_Q, H, D).pin_memory()
+    q_dev = torch.empty(LAYERS, N_Q, H, D, device=dev)
+
+    def e2e_step():
+        for l in range(LAYERS):
+            q_dev[l].copy_(q_host[l], non_blocking=True)
+            qt.data = q_dev[l].data_ptr()
+            layer_call(l)
+            o_host[l].copy_(out[0], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    f0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    e2e_ms = max(f0.elapsed_time(f1), t_wall * 1e3)
+    qt.data = q.data_ptr()
+
+    peaks, peak_kind = measured_peaks()
+    bytes_layer = kv_bytes_per_layer(n_kv, "f16")
+    achieved = bytes_layer / (us_per_layer * 1e-6) / 1e9
+    line = {
+        "metric": METRIC, "value": round(us_per_layer, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config[3] long verify: 4 query tokens per layer, causal among the last 4, "
+                               "262144-cell f16 KV cache (4 KV heads x 256), 24 Q heads, 16 layers per step",
+                   "n_kv": N_KV, "kv_type": "f16", "layers_per_step": LAYERS,
+                   "parallelism": f"kv-split{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: each layer streams 1.07 GB of KV"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": peak_kind,
+                     "traffic": ncu_traffic("fa_stream_f16_verify262k"),
+                     "algorithmic_bytes_per_launch": bytes_layer},
+        "gpu_launches": launches,
+        "e2e": {"value": round(e2e_ms * 1e3 / (args.steps * LAYERS), 2), "unit": UNIT,
+                "h2d_bytes_per_step": LAYERS * N_Q * H * D * 4, "d2h_bytes_per_step": LAYERS * N_Q * H * D * 4},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+
+        if O.ref_available():
+            threads = os.cpu_count() or 1
+            us_cpu, reps = cpu_verify_sample("f16", threads, args.cpu_budget)
+            line["cpu_baseline"] = {"value": round(us_cpu, 1), "unit": UNIT, "cores": threads, "kind": "reference",
+                                    "sample": f"{reps} single layers of the headline workload (ggml CPU flash_attn_ext, "
+                                              f"262144 f16 cells, 4 tokens), median"}
+        else:
+            line["cpu_baseline"] = None
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kb", choices=["kb", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
+    ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
+    args = ap.parse_args()
+    global LAYERS
+    LAYERS = args.layers
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_gpu(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

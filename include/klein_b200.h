@@ -87,8 +87,33 @@ kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_ten
                             const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
                             void* stream);
 
-/* Scratch needed by kb_flash_attn_ext for these operands on the current device
- * (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
+/*
+ * The same attention over one contiguous part of the KV sequence, leaving the result unnormalised so that
+ * parts computed on different GPUs can be merged (the per-chunk partials of ggml's split-KV path,
+ * ops.cpp:9489-9520, written out for a cross-device merge):
+ *   o_part  f32 [D, H, n_q, ne3] (dst's layout): sum_j 2^(s_j - m) v_j over this part's visible cells
+ *   ml_part f32 [ne3][n_q][H][2] contiguous: (m, l) with m the row maximum of s_j = score * log2(e) and
+ *           l = sum_j 2^(s_j - m); l == 0 marks a row with no visible cell in this part
+ * Causal/ring bounds in params are in the coordinates of this part's cells (cell 0 = its first cell).
+ */
+kb_status kb_flash_attn_ext_partial(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                    const kb_fa_params* params, const kb_tensor* o_part, float* ml_part, void* scratch,
+                                    size_t scratch_bytes, void* stream);
+
+/*
+ * Log-sum-exp merge of n_parts partials (generalises flash_attn_combine_results, ggml-cuda/fattn-common.cuh:924-978,
+ * and ggml_flash_attn_ext_reduce_partials, ggml-cpu/ops.cpp:9370-9438, to parts from several devices):
+ *   part p's o at o_parts + p * part_stride: f32 [rows][head_dim]; its (m, l) at ml_parts + p * part_stride:
+ *   f32 [rows][2] (as written by kb_flash_attn_ext_partial; rows = ne3 * n_q * H in dst order; part_stride in
+ *   floats, so one all-gathered buffer of [o | ml] per part can be passed as is); dst f32 [rows][head_dim]
+ *   dst[r] = sum_p 2^(m_p - M) o_p[r] / sum_p 2^(m_p - M) l_p[r], M = max over parts with l_p > 0; 0 if none.
+ * Requires 1 <= n_parts <= 1024, head_dim % 8 == 0, part_stride % 4 == 0, o_parts 16-byte aligned.
+ */
+kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t part_stride, int32_t n_parts, int64_t rows,
+                         int32_t head_dim, float* dst, void* stream);
+
+/* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
+ * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                        const kb_fa_params* params);
 

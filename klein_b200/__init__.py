@@ -27,6 +27,8 @@ STATUS_NAMES = ["OK", "ERR_ARG", "ERR_BAD_SHAPE", "ERR_UNSUPPORTED", "ERR_SCRATC
 # every symbol include/klein_b200.h declares (checked by tests/test_abi.py)
 EXPORTED = [
     "kb_flash_attn_ext",
+    "kb_flash_attn_ext_partial",
+    "kb_lse_combine",
     "kb_flash_attn_ext_scratch_bytes",
     "kb_device_error",
     "kb_version",
@@ -62,6 +64,11 @@ def lib():
         L.kb_flash_attn_ext.restype = c_int32
         L.kb_flash_attn_ext.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams), P(KbTensor),
                                         c_void_p, c_size_t, c_void_p]
+        L.kb_flash_attn_ext_partial.restype = c_int32
+        L.kb_flash_attn_ext_partial.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
+                                                P(KbTensor), c_void_p, c_void_p, c_size_t, c_void_p]
+        L.kb_lse_combine.restype = c_int32
+        L.kb_lse_combine.argtypes = [c_void_p, c_void_p, c_int64, c_int32, c_int64, c_int32, c_void_p, c_void_p]
         L.kb_flash_attn_ext_scratch_bytes.restype = c_size_t
         L.kb_flash_attn_ext_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
         L.kb_device_error.restype = c_int32

@@ -67,6 +67,21 @@ __device__ __forceinline__ float masked_score(const FaStreamParams& p, float x, 
     return v;
 }
 
+// final store of one output element: normalised, or (o, m, l) partial for a cross-device combine
+__device__ __forceinline__ void store_row(const FaStreamParams& p, int qi, int h, int b, int d, float O, float M, float L) {
+    float* dst = reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
+    if (p.partial_out) {
+        *dst = O;
+        if (d == 0) {
+            float* ml = p.dst_ml + (((int64_t) b * p.n_q + qi) * p.n_head + h) * 2;
+            ml[0] = M;
+            ml[1] = L;
+        }
+    } else {
+        *dst = L > 0.0f ? O / L : 0.0f;
+    }
+}
+
 template <int NRG>
 __global__ void __launch_bounds__(NRG * NKG * 32)
     fa_stream_f16_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -326,8 +341,7 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
         if (p.n_splits == 1) {
             const int gr = row0 + r;
             const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-            *reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3) =
-                L > 0.0f ? O / L : 0.0f;
+            store_row(p, qi, h, b, d, O, M, L);
         } else {
             p.o_part[(part_row0 + r) * D + d] = O;
             if (d == 0) {
@@ -338,47 +352,131 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
     }
 }
 
-// Merges the per-split partials of one row (grid: rows x KV heads x ne3, D threads).
+// Merge of n partial results (o_s, m_s, l_s) of one row by one 256-thread block:
+// out = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s with M = max over parts with l_s > 0 (0 if none).
+// The (m, l) pairs are reduced across the block, then warp w accumulates parts w, w+8, ... with every lane
+// holding 8 consecutive dims (two float4 loads per part, all in flight), and the 8 warp sums meet in smem.
+constexpr int MERGE_THREADS = 256;
+constexpr int MERGE_MAX_PARTS = 1024;
+
+__device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const float* __restrict__ ml, int64_t ml_stride,
+                          int n, int Dd, float* __restrict__ out_row, int64_t out_stride_elems, float* __restrict__ ml_out) {
+    __shared__ float f[MERGE_MAX_PARTS];
+    __shared__ float red[MERGE_THREADS / 32];
+    __shared__ float acc_s[MERGE_THREADS / 32][256 + 4];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // block max of m over parts with l > 0
+    float mx = -INFINITY;
+    for (int s = tid; s < n; s += MERGE_THREADS) {
+        const float l = ml[s * ml_stride + 1];
+        if (l > 0.0f) mx = fmaxf(mx, ml[s * ml_stride]);
+    }
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < MERGE_THREADS / 32; ++w) M = fmaxf(M, red[w]);
+    __syncthreads();
+    // weights and the weighted sum of l
+    float lsum = 0.0f;
+    for (int s = tid; s < n; s += MERGE_THREADS) {
+        const float l = ml[s * ml_stride + 1];
+        const float w = (l > 0.0f && M != -INFINITY) ? exp2f(ml[s * ml_stride] - M) : 0.0f;
+        f[s] = w;
+        lsum += w * l;
+    }
+    for (int off = 16; off; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    if (lane == 0) red[warp] = lsum;
+    __syncthreads();
+    float L = 0.0f;
+    for (int w = 0; w < MERGE_THREADS / 32; ++w) L += red[w];
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    for (int d0 = 0; d0 < Dd; d0 += 256) {
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int d = d0 + lane * 8;
+        if (d < Dd) {
+#pragma unroll 4
+            for (int s = warp; s < n; s += MERGE_THREADS / 32) {
+                const float w = f[s];
+                const float4* src = reinterpret_cast<const float4*>(o + s * o_stride + d);
+                const float4 x = src[0], y = src[1];
+                a[0] += w * x.x; a[1] += w * x.y; a[2] += w * x.z; a[3] += w * x.w;
+                a[4] += w * y.x; a[5] += w * y.y; a[6] += w * y.z; a[7] += w * y.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc_s[warp][lane * 8 + e] = a[e];
+        }
+        __syncthreads();
+        if (d0 + tid < Dd) {
+            float t = 0.0f;
+#pragma unroll
+            for (int w = 0; w < MERGE_THREADS / 32; ++w) t += acc_s[w][tid];
+            if (ml_out) {
+                out_row[(int64_t) (d0 + tid) * out_stride_elems] = t;  // partial output: unnormalised
+            } else {
+                out_row[(int64_t) (d0 + tid) * out_stride_elems] = t * inv;
+            }
+        }
+        __syncthreads();
+    }
+    if (ml_out && tid == 0) {
+        ml_out[0] = M;
+        ml_out[1] = L;
+    }
+}
+
+// Merges the per-split partials of one row of one KV head (grid: rows x KV heads x ne3).
 template <int RPC>
-__global__ void __launch_bounds__(D) fa_combine_kernel(const FaStreamParams p) {
-    const int gr = blockIdx.x, hk = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+__global__ void __launch_bounds__(MERGE_THREADS) fa_combine_kernel(const FaStreamParams p) {
+    const int gr = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
     const int chunk = gr / RPC, r = gr % RPC;
     const int64_t base = (((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < p.n_splits; ++s) {
-        const float* ml = p.ml_part + ((base + s) * RPC + r) * 2;
-        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
-    }
-    float O = 0.0f, L = 0.0f;
-    if (M != -INFINITY) {
-        for (int s = 0; s < p.n_splits; ++s) {
-            const float* ml = p.ml_part + ((base + s) * RPC + r) * 2;
-            if (!(ml[1] > 0.0f)) continue;
-            const float f = exp2f(ml[0] - M);
-            O += f * p.o_part[((base + s) * RPC + r) * D + d];
-            L += f * ml[1];
-        }
-    }
     const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-    *reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3) = L > 0.0f ? O / L : 0.0f;
+    float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
+    float* ml_out = p.partial_out ? p.dst_ml + (((int64_t) b * p.n_q + qi) * p.n_head + h) * 2 : nullptr;
+    merge_row(p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + (base * RPC + r) * 2, (int64_t) RPC * 2,
+              p.n_splits, D, out, 1, ml_out);
+}
+
+// Merges partial results computed over disjoint KV ranges (e.g. one per GPU), one row per block.
+__global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float* __restrict__ o_parts,
+                                                                    const float* __restrict__ ml_parts, int64_t stride,
+                                                                    int n_parts, int64_t rows, int Dd,
+                                                                    float* __restrict__ dst) {
+    const int64_t r = blockIdx.x;
+    merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, 1, nullptr);
 }
 
 template <int NRG>
 cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
     auto kern = fa_stream_f16_kernel<NRG>;
     const size_t smem = smem_f16(NRG);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    static bool attr_set[64] = {};  // the attribute is per device: set it once on each
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
     kern<<<grid, NRG * NKG * 32, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || p.n_splits == 1) return e;
     dim3 cgrid(p.R, p.n_head_kv, p.ne3);
-    fa_combine_kernel<NRG * 8><<<cgrid, D, 0, stream>>>(p);
+    fa_combine_kernel<NRG * 8><<<cgrid, MERGE_THREADS, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 }  // namespace
+
+cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int Dd,
+                               float* dst, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    lse_combine_kernel<<<(unsigned) rows, MERGE_THREADS, 0, stream>>>(o_parts, ml_parts, stride, n_parts, rows, Dd, dst);
+    return cudaGetLastError();
+}
 
 size_t fa_stream_smem_bytes(int nrg, int kv_type) {
     (void) kv_type;

@@ -149,9 +149,13 @@ size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, c
     return plan_fa(s).scratch;
 }
 
-kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
-                            const kb_fa_params* prm, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
-                            void* stream) {
+}  // extern "C"
+
+namespace {
+
+kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                  const kb_fa_params* prm, const kb_tensor* dst, float* dst_ml, void* scratch, size_t scratch_bytes,
+                  void* stream) {
     if (!prm || !dst) return KB_ERR_ARG;
     FaShape s;
     kb_status st = check_fa(q, k, v, mask, &s);
@@ -163,12 +167,14 @@ kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_ten
     if (prm->causal && prm->ring < 0) return KB_ERR_ARG;
 
     if (s.n_kv == 0) {
-        // no cells: every row's softmax sum is 0, so the output is 0 (ops.cpp:9066)
+        // no cells: every row's softmax sum is 0, so the output is 0 (ops.cpp:9066); partials get l = 0
         const size_t row = (size_t) s.D * 4;
         if (dst->nb[1] != row || dst->nb[2] != row * s.H || dst->nb[3] != row * s.H * s.n_q) return KB_ERR_UNSUPPORTED;
-        return cudaMemsetAsync(dst->data, 0, row * s.H * s.n_q * s.ne3, static_cast<cudaStream_t>(stream)) == cudaSuccess
-                   ? KB_OK
-                   : KB_ERR_CUDA;
+        cudaStream_t cs = static_cast<cudaStream_t>(stream);
+        if (cudaMemsetAsync(dst->data, 0, row * s.H * s.n_q * s.ne3, cs) != cudaSuccess) return KB_ERR_CUDA;
+        if (dst_ml && cudaMemsetAsync(dst_ml, 0, (size_t) 2 * 4 * s.H * s.n_q * s.ne3, cs) != cudaSuccess)
+            return KB_ERR_CUDA;
+        return KB_OK;
     }
     const FaPlan pl = plan_fa(s);
     if (pl.scratch > 0 && (!scratch || scratch_bytes < pl.scratch)) return KB_ERR_SCRATCH;
@@ -222,6 +228,8 @@ kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_ten
     p.d_nb1 = (int64_t) dst->nb[1];
     p.d_nb2 = (int64_t) dst->nb[2];
     p.d_nb3 = (int64_t) dst->nb[3];
+    p.partial_out = dst_ml != nullptr;
+    p.dst_ml = dst_ml;
     p.err = kb::device_error_word();
     p.wait_ns = g_wait_ns;
 
@@ -230,6 +238,38 @@ kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_ten
     if ((st = encode_kv_map(v, &tmV)) != KB_OK) return st;
     cudaError_t e = kb::launch_fa_stream(p, pl.nrg, k->type, tmK, tmV, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                            const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                            void* stream) {
+    return fa_impl(q, k, v, mask, params, dst, nullptr, scratch, scratch_bytes, stream);
+}
+
+kb_status kb_flash_attn_ext_partial(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                    const kb_fa_params* params, const kb_tensor* o_part, float* ml_part, void* scratch,
+                                    size_t scratch_bytes, void* stream) {
+    if (!ml_part) return KB_ERR_ARG;
+    return fa_impl(q, k, v, mask, params, o_part, ml_part, scratch, scratch_bytes, stream);
+}
+
+kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t part_stride, int32_t n_parts, int64_t rows,
+                         int32_t head_dim, float* dst, void* stream) {
+    if (!o_parts || !ml_parts || !dst || n_parts <= 0 || n_parts > 1024 || rows < 0 || head_dim <= 0) return KB_ERR_ARG;
+    if (n_parts > 1 && part_stride < rows * head_dim) return KB_ERR_ARG;
+    // vector loads: 16-byte aligned parts, head_dim a multiple of 8
+    if (head_dim % 8 != 0 || part_stride % 4 != 0 || !aligned16(reinterpret_cast<uintptr_t>(o_parts)) ||
+        (reinterpret_cast<uintptr_t>(ml_parts) & 7) != 0)
+        return KB_ERR_ARG;
+    return kb::launch_lse_combine(o_parts, ml_parts, part_stride, n_parts, rows, head_dim, dst,
+                                  static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? KB_OK
+               : KB_ERR_CUDA;
 }
 
 kb_status kb_device_error(int32_t* code, int clear) {

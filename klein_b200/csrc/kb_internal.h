@@ -38,8 +38,10 @@ struct FaStreamParams {
     // outputs
     float* o_part;                   // scratch: [ne3][H_kv][chunk][split][RPC][D]
     float* ml_part;                  // scratch: [ne3][H_kv][chunk][split][RPC][2] (max in log2 units, sum)
-    char* dst;                       // f32 [D, H, n_q, ne3]
+    char* dst;                       // f32 [D, H, n_q, ne3]; with partial_out: unnormalised o, same layout
     int64_t d_nb1, d_nb2, d_nb3;
+    int partial_out;                 // write (o, m, l) partials instead of the normalised output
+    float* dst_ml;                   // partial_out: f32 [ne3][n_q][H][2] = (max in log2 units, sum)
     int* err;                        // device error word
     uint64_t wait_ns;                // budget of every bounded wait
 };
@@ -52,6 +54,10 @@ size_t fa_stream_smem_bytes(int nrg, int kv_type);
 // launches the split-KV streaming kernel (+ the LSE combine when n_splits > 1)
 cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream);
+
+// merges n_parts partial results: o_p [rows][D] at o_parts + p*stride, ml_p [rows][2] at ml_parts + p*stride
+cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int D,
+                               float* dst, cudaStream_t stream);
 
 int* device_error_word();  // address of the current device's error word (null on failure)
 

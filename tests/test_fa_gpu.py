@@ -174,3 +174,43 @@ def test_scratch_too_small_is_rejected(kb, cuda):
     assert rc == kb.KB_ERR_SCRATCH
     torch.cuda.synchronize()
     assert float(out.abs().max()) == 0.0
+
+
+def test_partials_and_lse_combine(kb, cuda):
+    """Two parts of the KV sequence computed with kb_flash_attn_ext_partial and merged with kb_lse_combine
+    give the full attention (the per-GPU step of the sequence split, run on one GPU)."""
+    import ctypes
+    import torch
+
+    from klein_b200.kv_split import kv_range, local_bounds, packed_part_floats
+
+    n_q, n_kv, world, D, H = 4, 5000, 3, 256, 24
+    q, kc, vc, kd, vd = O.make_fa_inputs(99, n_q, n_kv)
+    qt = torch.from_numpy(q).to(cuda).unsqueeze(0)
+    rows = n_q * H
+    pf = packed_part_floats(rows, D)
+    parts = torch.zeros(world, pf, device=cuda)
+    L = kb.lib()
+    qv = kb.kb_tensor(qt.data_ptr(), kb.F32, [D, n_q, H, 1], [4, H * D * 4, D * 4, n_q * H * D * 4])
+    for r in range(world):
+        lo, hi = kv_range(n_kv, world, r)
+        kt = torch.from_numpy(kc[lo:hi].copy()).to(cuda)
+        vt = torch.from_numpy(vc[lo:hi].copy()).to(cuda)
+        kv, vv = kb.kv_cache_view(kt, kb.F16, 4, D), kb.kv_cache_view(vt, kb.F16, 4, D)
+        pos0, kv_lo = local_bounds(lo, n_kv - n_q, 0)
+        prm = kb.fa_params(1 / 16, causal=True, pos0=pos0, kv_lo=kv_lo)
+        ov = kb.kb_tensor(parts[r].data_ptr(), kb.F32, [D, H, n_q, 1], [4, D * 4, H * D * 4, rows * D * 4])
+        need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(prm))
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=cuda)
+        rc = L.kb_flash_attn_ext_partial(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), None, ctypes.byref(prm),
+                                         ctypes.byref(ov), ctypes.c_void_p(parts[r].data_ptr() + rows * D * 4),
+                                         ctypes.c_void_p(scratch.data_ptr()), need, None)
+        assert rc == 0
+        torch.cuda.synchronize()
+    out = torch.empty(rows, D, device=cuda)
+    rc = L.kb_lse_combine(ctypes.c_void_p(parts.data_ptr()), ctypes.c_void_p(parts.data_ptr() + rows * D * 4),
+                          pf, world, rows, D, ctypes.c_void_p(out.data_ptr()), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
+    check_attention(out.cpu().numpy().reshape(n_q, H, D), exact_np(O.q_round_f16(q), kd, vd, mask))
