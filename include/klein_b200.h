@@ -117,6 +117,29 @@ kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t pa
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                        const kb_fa_params* params);
 
+/*
+ * Size of the device buffer built into the library for kb_flash_attn_ext_noalloc (per GPU, held from the
+ * library's load until the process exits).
+ */
+#define KB_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/*
+ * kb_flash_attn_ext for callers that cannot allocate device memory: code running while a CUDA graph is
+ * being captured (no cudaMalloc there), hosts that give the whole GPU to their own memory pools up front,
+ * and foreign-language bindings that pass raw pointers but have no device allocator. Same operands,
+ * semantics and errors as kb_flash_attn_ext, but the split-KV partials live in a fixed buffer of
+ * KB_NOALLOC_SCRATCH_BYTES compiled into the library, so the call itself allocates nothing.
+ *   - A call that would need more partials than the buffer holds returns KB_ERR_SCRATCH
+ *     (kb_flash_attn_ext_scratch_bytes gives the need; 262,144 cells x 4 tokens x 24/4 heads needs ~3.7 MB).
+ *   - The first call on each device looks up the buffer's device address (cudaGetSymbolAddress); make
+ *     that first call before any stream capture on that device.
+ *   - All calls on a device share the buffer: calls that overlap on the GPU (other streams, other host
+ *     threads) race on it and must be serialised by the caller. Nothing in it needs clearing between calls.
+ * This entry point has no counterpart in the reference (ggml-cuda always draws scratch from its pool).
+ */
+kb_status kb_flash_attn_ext_noalloc(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                    const kb_fa_params* params, const kb_tensor* dst, void* stream);
+
 /* Device-side error word of the current device: the code of the last bounded wait that ran out
  * (0 = none). clear != 0 resets it. Synchronous (reads device memory). */
 kb_status kb_device_error(int32_t* code, int clear);

@@ -21,6 +21,8 @@ F32, F16, Q8_0, I32, I64, BF16 = 0, 1, 8, 26, 27, 30
 TYPE_SIZE = {F32: 4, F16: 2, I32: 4, I64: 8, BF16: 2}
 Q8_0_BLOCK_BYTES = 34
 
+NOALLOC_SCRATCH_BYTES = 8 << 20  # KB_NOALLOC_SCRATCH_BYTES
+
 KB_OK, KB_ERR_ARG, KB_ERR_BAD_SHAPE, KB_ERR_UNSUPPORTED, KB_ERR_SCRATCH, KB_ERR_CUDA, KB_ERR_TIMEOUT = range(7)
 STATUS_NAMES = ["OK", "ERR_ARG", "ERR_BAD_SHAPE", "ERR_UNSUPPORTED", "ERR_SCRATCH", "ERR_CUDA", "ERR_TIMEOUT"]
 
@@ -30,6 +32,7 @@ EXPORTED = [
     "kb_flash_attn_ext_partial",
     "kb_lse_combine",
     "kb_flash_attn_ext_scratch_bytes",
+    "kb_flash_attn_ext_noalloc",
     "kb_device_error",
     "kb_version",
 ]
@@ -71,6 +74,9 @@ def lib():
         L.kb_lse_combine.argtypes = [c_void_p, c_void_p, c_int64, c_int32, c_int64, c_int32, c_void_p, c_void_p]
         L.kb_flash_attn_ext_scratch_bytes.restype = c_size_t
         L.kb_flash_attn_ext_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
+        L.kb_flash_attn_ext_noalloc.restype = c_int32
+        L.kb_flash_attn_ext_noalloc.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
+                                                P(KbTensor), c_void_p]
         L.kb_device_error.restype = c_int32
         L.kb_device_error.argtypes = [P(c_int32), c_int32]
         L.kb_version.restype = ctypes.c_char_p

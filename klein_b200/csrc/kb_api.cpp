@@ -242,6 +242,20 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
 
 }  // namespace
 
+namespace kb {
+
+kb_status flash_attn_with_scratch(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                  const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                                  void* stream) {
+    return fa_impl(q, k, v, mask, params, dst, nullptr, scratch, scratch_bytes, stream);
+}
+
+size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_fa_params* params) {
+    return kb_flash_attn_ext_scratch_bytes(q, k, v, params);
+}
+
+}  // namespace kb
+
 extern "C" {
 
 kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/klein_b200.h"
+
 namespace kb {
 
 constexpr int FA_D = 256;            // head dimension of qwen35 full attention (K and V)
@@ -59,6 +61,12 @@ cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, cons
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int D,
                                float* dst, cudaStream_t stream);
 
-int* device_error_word();  // address of the current device's error word (null on failure)
+int* device_error_word();
+
+// kb_flash_attn_ext with caller-chosen scratch, and its scratch size (shared by the C-ABI entry points)
+kb_status flash_attn_with_scratch(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                  const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                                  void* stream);
+size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_fa_params* params);  // address of the current device's error word (null on failure)
 
 }  // namespace kb
