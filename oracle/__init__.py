@@ -30,6 +30,10 @@ def _ptr(a):
     return None if a is None else c_void_p(a.ctypes.data)
 
 
+def ctypes_float(x) -> c_float:
+    return c_float(float(x))
+
+
 def _cpu_has_avx512() -> bool:
     try:
         with open("/proc/cpuinfo") as f:
@@ -52,8 +56,10 @@ def restate():
             raise RuntimeError(f"{path} is missing: run `make -C oracle restate`")
         lib = ctypes.CDLL(path)
         lib.rs_fp32_to_fp16.restype = c_uint16
+        lib.rs_fp32_to_fp16.argtypes = [c_float]
         lib.rs_fp16_to_fp32.restype = c_float
         lib.rs_visible.restype = c_int
+        lib.rs_visible.argtypes = [c_int64] * 6
         lib.rs_set_rows.restype = c_int
         _restate = lib
     return _restate
