@@ -190,6 +190,34 @@ def run_reference(args, rank: int):
 
 # ------------------------------------------------------------------------------------------------ GPU arm
 
+def quantize_q8_0_rows(torch, x):
+    """Device-side q8_0 quantisation of f32 rows [n, k] (k % 32 == 0) with quantize_row_q8_0_ref's rule
+    (d = amax/127 stored as f16, q = round(x / d)); builds the synthetic q8_0 caches of the benchmark."""
+    n, k = x.shape
+    blk = x.view(n, k // 32, 32)
+    d = blk.abs().amax(-1) / 127.0
+    inv = torch.where(d > 0, 1.0 / d, torch.zeros_like(d))
+    qv = torch.round(blk * inv.unsqueeze(-1)).clamp(-127, 127).to(torch.int8)
+    out = torch.empty(n, k // 32, 34, dtype=torch.uint8, device=x.device)
+    out[:, :, :2] = d.to(torch.float16).view(torch.uint8).view(n, k // 32, 2)
+    out[:, :, 2:] = qv.view(torch.uint8)
+    return out.view(n, k // 32 * 34)
+
+
+def make_layers(kb, torch, dev, gen, n_kv, kv_type):
+    layers = []
+    for _ in range(LAYERS):
+        kf = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        vf = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        if kv_type == "f16":
+            kc, vc, t = kf.half(), vf.half(), kb.F16
+        else:
+            kc, vc, t = quantize_q8_0_rows(torch, kf), quantize_q8_0_rows(torch, vf), kb.Q8_0
+        del kf, vf
+        layers.append((kc, vc, kb.kv_cache_view(kc, t, H_KV, D), kb.kv_cache_view(vc, t, H_KV, D)))
+    return layers
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int):
     import ctypes
 
@@ -210,11 +238,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     n_kv = hi - lo
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000 + rank)
-    layers = []
-    for _ in range(LAYERS):
-        kc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
-        vc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
-        layers.append((kc, vc, kb.kv_cache_view(kc, kb.F16, H_KV, D), kb.kv_cache_view(vc, kb.F16, H_KV, D)))
+    layers = make_layers(kb, torch, dev, gen, n_kv, "f16")
     q = torch.randn(1, N_Q, H, D, device=dev, generator=gen)
     out = torch.empty(1, N_Q, H, D, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -315,6 +339,36 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     e2e_ms = max(f0.elapsed_time(f1), t_wall * 1e3)
     qt.data = q.data_ptr()
 
+    # secondary: the same verify step over a q8_0 cache (config[3]'s other variant)
+    secondary = {}
+    if not args.no_secondary:
+        del layers[:]
+        torch.cuda.empty_cache()
+        layers.extend(make_layers(kb, torch, dev, gen, n_kv, "q8_0"))
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            step()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        qms = g0.elapsed_time(g1)
+        if world > 1:
+            t = torch.tensor([qms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            qms = float(t.item())
+        q_us = qms * 1e3 / (args.steps * LAYERS)
+        qbytes = kv_bytes_per_layer(n_kv, "q8_0")
+        pk, _ = measured_peaks()
+        secondary["verify_q8_0"] = {
+            "value": round(q_us, 2), "unit": UNIT, "kv_type": "q8_0",
+            "roofline": {"bound": "hbm", "achieved": round(qbytes / (q_us * 1e-6) / 1e9, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(qbytes / (q_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
+                         "algorithmic_bytes_per_launch": qbytes,
+                         "traffic": ncu_traffic("fa_stream_q8_0_verify262k")}}
+
     peaks, peak_kind = measured_peaks()
     bytes_layer = kv_bytes_per_layer(n_kv, "f16")
     achieved = bytes_layer / (us_per_layer * 1e-6) / 1e9
@@ -336,6 +390,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 "h2d_bytes_per_step": LAYERS * N_Q * H * D * 4, "d2h_bytes_per_step": LAYERS * N_Q * H * D * 4},
         "clocks": clk.summary(),
     }
+    if secondary:
+        line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as O
 
@@ -362,6 +418,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 cache)")
     args = ap.parse_args()
     global LAYERS
     LAYERS = args.layers

@@ -76,7 +76,8 @@ typedef struct kb_fa_params {
  * GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext, ggml.h:2476-2495; CPU semantics ops.cpp:8842-9574;
  * replaces ggml_cuda_flash_attn_ext, ggml-cuda/fattn.cu:758-772).
  *   q    f32  [D, n_q, H, ne3]       any byte strides (klein passes a permuted view, graph.cpp:118)
- *   k, v f16/q8_0/bf16 [D, n_kv, H_kv, ne3k]  nb[0] = element size; H % H_kv == 0, ne3 % ne3k == 0
+ *   k, v f16/q8_0 [D, n_kv, H_kv, ne3k]  nb[0] = element size (34 = block size for q8_0); H % H_kv == 0,
+ *                                    ne3 % ne3k == 0; base and nb[1..3] multiples of 16 bytes
  *   mask f16  [n_kv, >= n_q, ne32, ne33] contiguous, or NULL; broadcast over heads as in ggml
  *   dst  f32  [D, H, n_q, ne3]       ("permuted" result); nb[0] = 4
  * Head h reads KV head h / (H / H_kv). A row whose every cell is masked produces zeros.
@@ -116,6 +117,57 @@ kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t pa
  * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                        const kb_fa_params* params);
+
+/*
+ * GGML_OP_GATED_DELTA_NET (ggml_gated_delta_net, ggml.h:2639-2660; CPU semantics ops.cpp:11123-11275;
+ * replaces ggml_cuda_op_gated_delta_net, ggml-cuda/gated_delta_net.cu:320-327), recurrent form.
+ *   q, k  f32 [S, H_k, T, n_seqs_q/k]   rows contiguous (klein's L2-normalised views of the conv output)
+ *   v     f32 [S, H_v, T, n_seqs]       value head h reads q/k head h % H_k
+ *   g     f32 [1, H_v, T, n_seqs] (scalar log-decay) or [S, H_v, T, n_seqs] (per-channel, "KDA"), contiguous
+ *   beta  f32 [1, H_v, T, n_seqs] contiguous
+ *   state f32 [S, S, H_v, n_seqs] contiguous: s0, stored transposed (element (i, j) = S[j][i])
+ *   dst   f32 [S*H_v, T*n_seqs + K*S*n_seqs] contiguous: attention output [S, H_v, T, n_seqs], then K state slots
+ *         [S, S, H_v, n_seqs] most recent first (slot s = state s tokens before the end); only slots < min(T, K)
+ *         are written.
+ * Supported here: S = 128; every pointer and row stride 16-byte aligned.
+ */
+kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
+                             const kb_tensor* beta, const kb_tensor* state, int32_t K, const kb_tensor* dst,
+                             void* stream);
+
+/*
+ * The same recurrence writing straight into klein's recurrent-state cache, i.e. ggml_gated_delta_net followed
+ * by klein's two copies (graph.cpp:169-184) in one kernel:
+ *   state  f32 [S, S, H_v, n_seqs]: read as s0, then overwritten with slot 0 (the state after the last token)
+ *   snap   [S*S*H_v*n_seqs, >= min(T,K)-1] rows of f16, bf16 or f32 (klein's ssm_snap, state.cpp:74-78):
+ *          slot s (1 <= s < min(T, K)) goes to row s-1, converted with round-to-nearest-even; may be NULL when
+ *          min(T, K) == 1
+ *   attn   f32 [S, H_v, T, n_seqs] attention output (any row strides)
+ */
+kb_status kb_gated_delta_net_cache(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
+                                   const kb_tensor* beta, const kb_tensor* state, const kb_tensor* snap, int32_t K,
+                                   const kb_tensor* attn, void* stream);
+
+/*
+ * State::rollback_recurrent (state.cpp:162-183): after s rejected draft tokens, for each of n_layers DeltaNet
+ * layers, conv slot s -> conv slot 0 (f32, conv [n_snapshots][conv_row]) and snapshot row s-1 (snap_type f16,
+ * bf16 or f32, snap [n_snapshots-1][ssm_row]) -> the f32 state ssm [ssm_row]; the restored state equals the
+ * snapshot exactly. s == 0 is a no-op; 1 <= s < n_snapshots. The pointer arrays are host arrays of device
+ * pointers (n_layers <= 64), replacing the per-layer ggml_cpy graph with one launch.
+ */
+kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t conv_row, const void* const* snap,
+                                int32_t snap_type, float* const* ssm, int64_t ssm_row, int32_t s, int32_t n_snapshots,
+                                void* stream);
+
+/*
+ * ggml_set_rows (ops.cpp:5446-5500; replaces ggml-cuda/set-rows.cu:8-110), klein's KV-cache write
+ * (graph.cpp:111-112): dst row idx[r] <- src row r for every (i2, i3), converted to dst's type.
+ *   dst f32 / f16 / bf16 / q8_0 [ne0, n_rows, ne2, ne3]; src f32 [ne0, n_src, ne2, ne3] (rows contiguous);
+ *   idx i64 or i32 [n_src, ne11, ne12] broadcast over ne2 % ne11, ne3 % ne12. ne0 % 32 == 0.
+ *   q8_0 rounding is quantize_row_q8_0_ref's (ggml-quants.c:276-299), bit for bit.
+ * An out-of-range index (ggml asserts) skips that row and sets the device error word (kb_device_error).
+ */
+kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream);
 
 /*
  * Size of the device buffer built into the library for kb_flash_attn_ext_noalloc (per GPU, held from the

@@ -31,6 +31,10 @@ EXPORTED = [
     "kb_flash_attn_ext",
     "kb_flash_attn_ext_partial",
     "kb_lse_combine",
+    "kb_gated_delta_net",
+    "kb_gated_delta_net_cache",
+    "kb_rollback_recurrent",
+    "kb_set_rows",
     "kb_flash_attn_ext_scratch_bytes",
     "kb_flash_attn_ext_noalloc",
     "kb_device_error",
@@ -77,6 +81,16 @@ def lib():
         L.kb_flash_attn_ext_noalloc.restype = c_int32
         L.kb_flash_attn_ext_noalloc.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
                                                 P(KbTensor), c_void_p]
+        T4 = [P(KbTensor)] * 6
+        L.kb_gated_delta_net.restype = c_int32
+        L.kb_gated_delta_net.argtypes = T4 + [c_int32, P(KbTensor), c_void_p]
+        L.kb_gated_delta_net_cache.restype = c_int32
+        L.kb_gated_delta_net_cache.argtypes = T4 + [P(KbTensor), c_int32, P(KbTensor), c_void_p]
+        L.kb_rollback_recurrent.restype = c_int32
+        L.kb_rollback_recurrent.argtypes = [c_int32, c_void_p, c_int64, c_void_p, c_int32, c_void_p, c_int64, c_int32,
+                                            c_int32, c_void_p]
+        L.kb_set_rows.restype = c_int32
+        L.kb_set_rows.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), c_void_p]
         L.kb_device_error.restype = c_int32
         L.kb_device_error.argtypes = [P(c_int32), c_int32]
         L.kb_version.restype = ctypes.c_char_p
@@ -117,6 +131,10 @@ def from_torch(x, type_: int | None = None) -> KbTensor:
     nb = [s * es for s in reversed(x.stride())]
     while len(nb) < 4:
         nb.append(nb[-1] * ne[len(nb) - 1] if nb else es)
+    # a size-1 dimension gets ggml's packed stride (its stride is arbitrary in torch/numpy, e.g. 0 for None axes)
+    for i in range(4):
+        if ne[i] == 1:
+            nb[i] = es if i == 0 else nb[i - 1] * ne[i - 1]
     return kb_tensor(x.data_ptr(), type_, ne, nb)
 
 
@@ -184,3 +202,64 @@ def device_error(clear: bool = True) -> int:
     code = c_int32(0)
     check("kb_device_error", lib().kb_device_error(ctypes.byref(code), int(clear)))
     return code.value
+
+
+def _stream(x, stream):
+    import torch
+
+    return torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+
+
+def gated_delta_net(q, k, v, g, beta, state, K: int, stream=None):
+    """GGML_OP_GATED_DELTA_NET through kb_gated_delta_net. Torch f32 tensors in ggml order reversed:
+    q, k [n_seqs][T][H_k][S]; v [n_seqs][T][H_v][S]; g [n_seqs][T][H_v][1 or S]; beta [n_seqs][T][H_v][1];
+    state [n_seqs][H_v][S][S]. Returns ggml's packed f32 result as a flat tensor."""
+    import torch
+
+    n_seqs, T, H_v, S = v.shape
+    n = S * H_v * T * n_seqs + K * S * S * H_v * n_seqs
+    out = torch.empty(n, dtype=torch.float32, device=v.device)
+    dt = kb_tensor(out.data_ptr(), F32, [S * H_v, T * n_seqs + K * S * n_seqs, 1, 1], [4, S * H_v * 4])
+    args = [from_torch(x) for x in (q, k, v, g, beta.reshape(n_seqs, T, H_v, 1), state)]
+    rc = lib().kb_gated_delta_net(*[ctypes.byref(a) for a in args], K, ctypes.byref(dt), c_void_p(_stream(v, stream)))
+    check("kb_gated_delta_net", rc)
+    return out
+
+
+def gated_delta_net_cache(q, k, v, g, beta, state, snap, K: int, attn=None, stream=None):
+    """klein's fused form through kb_gated_delta_net_cache: state (f32 [n_seqs][H_v][S][S]) is updated in place
+    to slot 0; snap (f16/bf16/f32 [K-1][S*S*H_v*n_seqs] or None) receives slots 1..min(T,K)-1.
+    Returns the attention output f32 [n_seqs][T][H_v][S]."""
+    import torch
+
+    n_seqs, T, H_v, S = v.shape
+    if attn is None:
+        attn = torch.empty(n_seqs, T, H_v, S, dtype=torch.float32, device=v.device)
+    args = [from_torch(x) for x in (q, k, v, g, beta.reshape(n_seqs, T, H_v, 1), state)]
+    st = from_torch(snap) if snap is not None else None
+    at = from_torch(attn)
+    rc = lib().kb_gated_delta_net_cache(*[ctypes.byref(a) for a in args], ctypes.byref(st) if st is not None else None, K,
+                                        ctypes.byref(at), c_void_p(_stream(v, stream)))
+    check("kb_gated_delta_net_cache", rc)
+    return attn
+
+
+def set_rows(dst: KbTensor, src, idx, stream=None):
+    """ggml_set_rows through kb_set_rows: src torch f32 [n_src][ne0] (or 4-d), idx torch i64/i32 [n_src]."""
+    s4 = src if src.dim() == 4 else src.reshape((1,) * (4 - src.dim()) + tuple(src.shape))
+    st = from_torch(s4)
+    it = from_torch(idx)
+    rc = lib().kb_set_rows(ctypes.byref(dst), ctypes.byref(st), ctypes.byref(it), c_void_p(_stream(src, stream)))
+    check("kb_set_rows", rc)
+
+
+def rollback_recurrent(convs, snaps, ssms, snap_type: int, s: int, n_snapshots: int, stream=None):
+    """State::rollback_recurrent through kb_rollback_recurrent; lists of torch tensors, one entry per layer."""
+    n = len(convs)
+    P = c_void_p * max(n, 1)
+    conv_p = P(*[c.data_ptr() for c in convs])
+    snap_p = P(*[x.data_ptr() for x in snaps])
+    ssm_p = P(*[x.data_ptr() for x in ssms])
+    rc = lib().kb_rollback_recurrent(n, conv_p, convs[0].shape[-1], snap_p, snap_type, ssm_p, ssms[0].numel(), s,
+                                     n_snapshots, c_void_p(_stream(convs[0], stream)))
+    check("kb_rollback_recurrent", rc)

@@ -1,20 +1,26 @@
 // Split-KV streaming attention for decode (1 query token) and the MTP verify step (a few tokens):
 // GGML_OP_FLASH_ATTN_EXT with few query rows over a long KV cache. HBM-bound: every K/V byte is read
-// once, staged by TMA into a 3-deep shared-memory ring, and consumed by warp-level tensor-core MMA.
+// once, staged by TMA into a shared-memory ring, and consumed by warp-level tensor-core MMA.
 //
 // Work split. One CTA per (KV split, KV head, row chunk). The rows of a KV head are its n_q * gqa query
-// rows (query i, head-in-group g -> row i*gqa + g); a CTA takes up to 32 of them as NRG groups of 8.
-// Consumer warp (rg, kg) owns row group rg and keys 16kg..16kg+15 of every 64-key tile, and keeps its own
-// online-softmax state (max, sum, O^T 256x8 in registers) over its keys, so the main loop needs no
-// cross-warp synchronisation: S^T = K Q^T (16 keys x 8 rows) is an m16n8k16 chain over D, P^T goes from
-// the accumulator into the B fragment of O^T += V^T P^T with two movmatrix transposes, and V^T comes from
-// ldmatrix.trans. At the end the 4 key groups merge through shared memory (log-sum-exp), and when the KV
-// range is split over several CTAs a second kernel merges the per-split partials the same way
-// (the combine of ggml's ops.cpp:9370-9438 / fattn-common.cuh:924-978).
+// rows (query i, head-in-group g -> row i*gqa + g); a CTA takes up to 24 of them as NRG groups of 8.
+// Consumer warp (rg, kg) owns row group rg and cells 16kg..16kg+15 of every 64-cell tile, and keeps its
+// own online-softmax state (max, sum, O^T 256x8 in registers) over its cells: S^T = K Q^T (16 cells x 8
+// rows) is an m16n8k16 chain over D, P^T goes from the accumulator into the B fragment of O^T += V^T P^T
+// with two movmatrix transposes, and V^T comes from ldmatrix.trans. At the end the 4 key groups merge
+// through shared memory (log-sum-exp), and when the KV range is split over several CTAs a second kernel
+// merges the per-split partials the same way (the combine of ggml's ops.cpp:9370-9438 /
+// fattn-common.cuh:924-978).
+//
+// f16 cache: TMA writes the K/V tiles straight into the swizzled f16 layout the MMA fragments read.
+// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0) of 64 cells into a 4-deep ring;
+// all warps then dequantise the tile into the same swizzled f16 layout (v = f16(q * d), one rounding) and
+// the f16 code path runs unchanged. Q is first rounded as ggml rounds it for a q8_0 K
+// (quantize_row_q8_0_ref, ggml-quants.c:276-299), so the scores use Q's q8_0 values like ggml's dot.
 //
 // Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
-// the K dot type (f16 for f16 K, :8960), scores are scaled, soft-capped, masked (-inf cells skipped), and
-// a row with no visible cell yields zeros (:9066). Accumulation is f32 throughout.
+// the K dot type (f16 for f16 K, q8_0 for q8_0 K, :8960), scores are scaled, soft-capped, masked (-inf
+// cells skipped), and a row with no visible cell yields zeros (:9066). Accumulation is f32 throughout.
 #include "kb_common.cuh"
 #include "kb_internal.h"
 
@@ -25,16 +31,25 @@ namespace {
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int D = FA_D;
 constexpr int TILE = FA_TILE;
-constexpr int ST = FA_STAGES;
 constexpr int NKG = FA_NKG;
-constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 keys][64 dims] f16, 128B-swizzled
+constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 cells][64 dims] f16, 128B-swizzled
 constexpr int STAGE_F16 = 2 * KTILE_F16;       // K + V
+constexpr int ST = FA_STAGES;                  // f16 ring depth
+constexpr int QROW = D / 32 * 34;              // bytes of one head's row in a q8_0 cache (272)
+constexpr int QTILE_RAW = TILE * QROW;         // 17,408 B of raw blocks per tile
+constexpr int QSTAGE = 2 * QTILE_RAW;          // K + V raw
+constexpr int QST = 4;                         // q8_0 raw ring depth
 constexpr int QSTRIDE = D + 8;                 // f16 elements per staged Q row (padded)
 
 __host__ __device__ constexpr int q_bytes(int nrg) { return nrg * 8 * QSTRIDE * 2; }
 
 __host__ __device__ constexpr size_t smem_f16(int nrg) {
     return 1024 /* alignment slack */ + (size_t) ST * STAGE_F16 + q_bytes(nrg) + 2 * ST * sizeof(uint64_t);
+}
+
+__host__ __device__ constexpr size_t smem_q8(int nrg) {
+    return 1024 + (size_t) STAGE_F16 /* dequantised tile */ + (size_t) QST * QSTAGE + q_bytes(nrg) +
+           2 * QST * sizeof(uint64_t);
 }
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
@@ -82,227 +97,182 @@ __device__ __forceinline__ void store_row(const FaStreamParams& p, int qi, int h
     }
 }
 
+// Per-thread constants of a consumer warp.
+struct WarpCtx {
+    int qi0, qi1, h0, h1;   // the thread's two rows: query index and head
+    float slope0, slope1;   // ALiBi slopes of those heads
+    int64_t min_pos;        // position of the CTA's first query: cells up to it are visible to every row
+    int kg;                 // key group: cells 16kg..16kg+15 of each tile
+    int kkey, kdo;          // K tile row / dim offset addressed by this lane (A fragment)
+    int vkey, vdo;          // V tile row / dim offset addressed by this lane (A^T fragment)
+};
+
+__device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int dim) {
+    // [4 chunks of 64 dims][64 rows][128 B], 16-byte units XOR-swizzled with row % 8 (TMA SWIZZLE_128B)
+    return base + (dim >> 6) * (TILE * 128) + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4);
+}
+
+// One 64-cell tile for one warp: S^T = K Q^T, online softmax, O^T += V^T P^T.
+// kb / vb: shared addresses of the f16 K and V tiles in the swizzled layout.
+__device__ __forceinline__ void tile_compute(const FaStreamParams& p, uint32_t kb, uint32_t vb, int64_t tkey0, int b,
+                                             int lane, const WarpCtx& w, const uint32_t (&qf)[16][2], float (&o)[16][4],
+                                             float& m0, float& m1, float& l0, float& l1) {
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+        uint32_t a[4];
+        ldsm_x4(a, swz_addr(kb, w.kkey, 16 * kk + w.kdo));
+        if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
+        else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
+    }
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
+
+    const int64_t key0 = tkey0 + 16 * w.kg + (lane >> 2), key1 = key0 + 8;
+    const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && tkey0 + TILE <= p.n_kv &&
+                       (!p.causal || (tkey0 >= p.kv_lo && tkey0 + TILE - 1 <= w.min_pos));
+    float sc[4];
+    if (plain) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] = x[e] * p.scale_log2;
+    } else {
+        sc[0] = masked_score(p, x[0], key0, w.qi0, w.h0, b, w.slope0);
+        sc[1] = masked_score(p, x[1], key0, w.qi1, w.h1, b, w.slope1);
+        sc[2] = masked_score(p, x[2], key1, w.qi0, w.h0, b, w.slope0);
+        sc[3] = masked_score(p, x[3], key1, w.qi1, w.h1, b, w.slope1);
+    }
+    // online softmax over this warp's 16 cells, per row (lanes sharing lane%4 share rows)
+    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float ref0 = mn0 == -INFINITY ? 0.0f : mn0, ref1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
+    const float p0 = exp2f(sc[0] - ref0), p1 = exp2f(sc[1] - ref1);
+    const float p2 = exp2f(sc[2] - ref0), p3 = exp2f(sc[3] - ref1);
+    l0 = l0 * al0 + (p0 + p2);
+    l1 = l1 * al1 + (p1 + p3);
+    m0 = mn0;
+    m1 = mn1;
+    if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+        for (int mm = 0; mm < 16; ++mm) {
+            o[mm][0] *= al0;
+            o[mm][1] *= al1;
+            o[mm][2] *= al0;
+            o[mm][3] *= al1;
+        }
+    }
+    // P^T as the B fragment of O^T += V^T P^T
+    const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
+    const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) {
+        uint32_t a[4];
+        ldsm_x4_trans(a, swz_addr(vb, w.vkey, 16 * mm + w.vdo));
+        mma_f16_16816(o[mm], a, pb0, pb1);
+    }
+}
+
+__device__ __forceinline__ WarpCtx make_ctx(const FaStreamParams& p, int warp, int lane, int row0, int hk) {
+    WarpCtx w;
+    const int rg = warp / NKG;
+    w.kg = warp % NKG;
+    const int mi = lane >> 3, rr = lane & 7;
+    const int gr0 = row0 + 8 * rg + 2 * (lane & 3), gr1 = gr0 + 1;
+    w.qi0 = gr0 / p.gqa;
+    w.qi1 = gr1 / p.gqa;
+    w.h0 = hk * p.gqa + gr0 % p.gqa;
+    w.h1 = hk * p.gqa + gr1 % p.gqa;
+    w.slope0 = slope_of(p, w.h0);
+    w.slope1 = slope_of(p, w.h1);
+    w.min_pos = p.pos0 + row0 / p.gqa;
+    w.kkey = 16 * w.kg + (mi & 1) * 8 + rr;
+    w.kdo = (mi >> 1) * 8;
+    w.vkey = 16 * w.kg + (mi >> 1) * 8 + rr;
+    w.vdo = (mi & 1) * 8;
+    return w;
+}
+
+// Q fragments (B operand of S^T = K Q^T) of row group rg from the staged f16 Q rows
+__device__ __forceinline__ void load_q_frags(const __half* Qs, int rg, int lane, uint32_t (&qf)[16][2]) {
+    const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint32_t r4[4];
+        ldsm_x4(r4, smem_u32(Qs + (8 * rg + rr) * QSTRIDE + 32 * j + 8 * mi));
+        qf[2 * j][0] = r4[0];
+        qf[2 * j][1] = r4[1];
+        qf[2 * j + 1][0] = r4[2];
+        qf[2 * j + 1][1] = r4[3];
+    }
+}
+
+// Stages the CTA's Q rows as f16. f16 K: plain rounding. q8_0 K: each 32-element block is first quantised
+// like quantize_row_q8_0_ref (d = amax/127, q = roundf(x / d), d kept as f16), then stored as f16(q * d).
+template <bool Q8>
+__device__ __forceinline__ void stage_q(const FaStreamParams& p, __half* Qs, int rpc, int rows, int row0, int hk, int b) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    if (Q8) {
+        for (int task = warp; task < rpc * (D / 32); task += nwarps) {
+            const int r = task / (D / 32), blk = task % (D / 32);
+            float x = 0.0f;
+            if (r < rows) {
+                const int gr = row0 + r;
+                const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+                x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
+                                                    b * p.q_nb3);
+            }
+            float amax = fabsf(x);
+#pragma unroll
+            for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const float qv = roundf(x * id);
+            const float dh = __half2float(__float2half_rn(d));
+            Qs[r * QSTRIDE + 32 * blk + lane] = __float2half_rn(qv * dh);
+        }
+    } else if (p.q_vec4) {
+        for (int idx = threadIdx.x; idx < rpc * (D / 4); idx += blockDim.x) {
+            const int r = idx / (D / 4), c4 = idx % (D / 4);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < rows) {
+                const int gr = row0 + r;
+                const int qi = gr / p.gqa, h = hk * p.gqa + (gr - qi * p.gqa);
+                x = *reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3 + c4 * 16);
+            }
+            __half2* dst = reinterpret_cast<__half2*>(Qs + r * QSTRIDE + 4 * c4);
+            dst[0] = __floats2half2_rn(x.x, x.y);
+            dst[1] = __floats2half2_rn(x.z, x.w);
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < rpc * D; idx += blockDim.x) {
+            const int r = idx / D, d = idx % D;
+            float x = 0.0f;
+            if (r < rows) {
+                const int gr = row0 + r;
+                const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+                x = *reinterpret_cast<const float*>(p.q + (int64_t) d * 4 + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3);
+            }
+            Qs[r * QSTRIDE + d] = __float2half_rn(x);
+        }
+    }
+}
+
+// Merges the 4 key groups of every row group (through shared memory) and writes the CTA's result: the
+// final output when the KV range is not split, else the split's (o, m, l) partial.
 template <int NRG>
-__global__ void __launch_bounds__(NRG * NKG * 32)
-    fa_stream_f16_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                         const FaStreamParams p) {
-    constexpr int NC = NRG * NKG;  // consumer warps; lane 0 of warp 0 also issues the TMA loads
-    constexpr int RPC = NRG * 8;   // rows per CTA
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = smem;
-    __half* Qs = reinterpret_cast<__half*>(smem + ST * STAGE_F16);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * STAGE_F16 + q_bytes(NRG));
-    uint64_t* empty = full + ST;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, hk = blockIdx.y;
-    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
-    const int64_t key_begin = (int64_t) split * p.keys_per_split;
-    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
-    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
-    const int row0 = chunk * RPC;
-    const int rows = min(RPC, p.R - row0);
-    const bool issuer = threadIdx.x == 0;
-    __shared__ int s_failed;
-
-    if (issuer) {
-        s_failed = 0;
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NC);
-        }
-        fence_barrier_init();
-    }
-    // stage Q rows of this CTA as f16 (rounding to the f16 K dot type); padded rows are zero
-    for (int idx = threadIdx.x; idx < RPC * D; idx += blockDim.x) {
-        const int r = idx / D, d = idx % D;
-        float x = 0.0f;
-        if (r < rows) {
-            const int gr = row0 + r;
-            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-            x = *reinterpret_cast<const float*>(p.q + (int64_t) d * 4 + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3);
-        }
-        Qs[r * QSTRIDE + d] = __float2half_rn(x);
-    }
-    __syncthreads();
-
-    // TMA issue state (meaningful in the issuing thread only)
-    int next_issue = 0;
-    uint64_t pol = 0;
-    const int kb3 = b / p.rk3;
-    auto issue = [&](int t) {
-        const int s = t % ST;
-        mbar_arrive_expect_tx(&full[s], STAGE_F16);
-        const int key = (int) (key_begin + (int64_t) t * TILE);
-        uint8_t* kdst = stages + s * STAGE_F16;
-        uint8_t* vdst = kdst + KTILE_F16;
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(kdst + c * (TILE * 128), &tmK, &full[s], c * 64, hk, key, kb3, pol);
-            tma_load_4d(vdst + c * (TILE * 128), &tmV, &full[s], c * 64, hk, key, kb3, pol);
-        }
-    };
-    if (issuer && n_tiles > 0) {
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-        pol = l2_policy_evict_first();
-        for (; next_issue < min(ST, n_tiles); ++next_issue) issue(next_issue);
-    }
-
-    bool failed = false;
-    float o[16][4];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-#pragma unroll
-    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
-
+__device__ __forceinline__ void merge_key_groups(const FaStreamParams& p, float* Ow, int warp, int lane, int rows, int row0,
+                                                 int hk, int b, int split, int chunk, const float (&o)[16][4], float m0,
+                                                 float m1, float l0, float l1) {
+    constexpr int NC = NRG * NKG, RPC = NRG * 8;
+    float* Mw = Ow + NC * 8 * D;  // [NC][8]
+    float* Lw = Mw + NC * 8;      // [NC][8]
     {
-        const int rg = warp / NKG, kg = warp % NKG;
-        const bool active = rg * 8 < rows;
-        const int mi = lane >> 3, rr = lane & 7;
-
-        uint32_t qf[16][2];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            uint32_t r4[4];
-            ldsm_x4(r4, smem_u32(Qs + (8 * rg + rr) * QSTRIDE + 32 * j + 8 * mi));
-            qf[2 * j][0] = r4[0];
-            qf[2 * j][1] = r4[1];
-            qf[2 * j + 1][0] = r4[2];
-            qf[2 * j + 1][1] = r4[3];
-        }
-
-        // this thread's two rows (columns of S^T / O^T): rl0 = 8rg + 2(lane%4), rl1 = rl0 + 1
-        const int gr0 = row0 + 8 * rg + 2 * (lane & 3), gr1 = gr0 + 1;
-        const int qi0 = gr0 / p.gqa, qi1 = gr1 / p.gqa;
-        const int h0 = hk * p.gqa + gr0 % p.gqa, h1 = hk * p.gqa + gr1 % p.gqa;
-        const float slope0 = slope_of(p, h0), slope1 = slope_of(p, h1);
-        // first query row of this CTA: keys up to its position are visible to every row (causal, no ring)
-        const int64_t min_pos = p.pos0 + row0 / p.gqa;
-
-        const int kkey = 16 * kg + (mi & 1) * 8 + rr;  // K tile row addressed by this lane (A fragment)
-        const int kdo = (mi >> 1) * 8;
-        const int vkey = 16 * kg + (mi >> 1) * 8 + rr;  // V tile row addressed by this lane (A^T fragment)
-        const int vdo = (mi & 1) * 8;
-
-        for (int t = 0; t < n_tiles; ++t) {
-            const int s = t % ST;
-            if (issuer) {
-                // tile t must have been issued: wait for its stage to be released by every warp
-                while (next_issue <= t) {
-                    const int si = next_issue % ST;
-                    if (!mbar_wait(&empty[si], ((next_issue / ST) - 1) & 1, p.wait_ns)) {
-                        record_error(p.err, DEV_ERR_WAIT_EMPTY);
-                        failed = true;
-                        break;
-                    }
-                    issue(next_issue++);
-                }
-            }
-            __syncwarp();
-            if (!failed && !mbar_wait(&full[s], (t / ST) & 1, p.wait_ns)) {
-                record_error(p.err, DEV_ERR_WAIT_FULL);
-                failed = true;
-            }
-            if (__any_sync(0xffffffffu, failed)) {
-                failed = true;
-                break;
-            }
-            if (active) {
-                const uint32_t kb = smem_u32(stages + s * STAGE_F16);
-                const uint32_t vb = kb + KTILE_F16;
-                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int kk = 0; kk < 16; ++kk) {
-                    const int dim = 16 * kk + kdo;
-                    const uint32_t addr = kb + (dim >> 6) * (TILE * 128) + kkey * 128 + ((((dim & 63) >> 3) ^ (kkey & 7)) << 4);
-                    uint32_t a[4];
-                    ldsm_x4(a, addr);
-                    if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
-                    else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
-                }
-                float x[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
-
-                const int64_t tkey0 = key_begin + (int64_t) t * TILE;
-                const int64_t key0 = tkey0 + 16 * kg + (lane >> 2), key1 = key0 + 8;
-                const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && tkey0 + TILE <= p.n_kv &&
-                                   (!p.causal || (tkey0 >= p.kv_lo && tkey0 + TILE - 1 <= min_pos));
-                float sc[4];
-                if (plain) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) sc[e] = x[e] * p.scale_log2;
-                } else {
-                    sc[0] = masked_score(p, x[0], key0, qi0, h0, b, slope0);
-                    sc[1] = masked_score(p, x[1], key0, qi1, h1, b, slope1);
-                    sc[2] = masked_score(p, x[2], key1, qi0, h0, b, slope0);
-                    sc[3] = masked_score(p, x[3], key1, qi1, h1, b, slope1);
-                }
-                // online softmax over this warp's 16 keys, per row (lanes sharing lane%4 share rows)
-                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-                }
-                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-                const float ref0 = mn0 == -INFINITY ? 0.0f : mn0, ref1 = mn1 == -INFINITY ? 0.0f : mn1;
-                const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
-                const float p0 = exp2f(sc[0] - ref0), p1 = exp2f(sc[1] - ref1);
-                const float p2 = exp2f(sc[2] - ref0), p3 = exp2f(sc[3] - ref1);
-                l0 = l0 * al0 + (p0 + p2);
-                l1 = l1 * al1 + (p1 + p3);
-                m0 = mn0;
-                m1 = mn1;
-                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
-#pragma unroll
-                    for (int mm = 0; mm < 16; ++mm) {
-                        o[mm][0] *= al0;
-                        o[mm][1] *= al1;
-                        o[mm][2] *= al0;
-                        o[mm][3] *= al1;
-                    }
-                }
-                // P^T as the B fragment of O^T += V^T P^T
-                const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
-                const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
-#pragma unroll
-                for (int mm = 0; mm < 16; ++mm) {
-                    const int dim = 16 * mm + vdo;
-                    const uint32_t addr = vb + (dim >> 6) * (TILE * 128) + vkey * 128 + ((((dim & 63) >> 3) ^ (vkey & 7)) << 4);
-                    uint32_t a[4];
-                    ldsm_x4_trans(a, addr);
-                    mma_f16_16816(o[mm], a, pb0, pb1);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (issuer) {
-                // refill without blocking: issue every further tile whose stage all warps have released
-                while (next_issue < n_tiles && next_issue < t + 1 + ST) {
-                    const int si = next_issue % ST;
-                    if (!mbar_try_wait(&empty[si], ((next_issue / ST) - 1) & 1)) break;
-                    issue(next_issue++);
-                }
-            }
-        }
-        // row sums over the warp's lanes
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-        }
-    }
-
-    // ---------------------------------------------------------------------- merge the key groups
-    if (failed && lane == 0) atomicExch(&s_failed, 1);
-    __syncthreads();  // every issued stage consumed: the ring is free for the merge buffers
-    if (s_failed) return;  // a bounded wait ran out (error word set): leave the outputs alone
-    float* Ow = reinterpret_cast<float*>(stages);  // [NC][8 rows][D]
-    float* Mw = Ow + NC * 8 * D;                   // [NC][8]
-    float* Lw = Mw + NC * 8;                       // [NC][8]
-    if (warp < NC) {
         const int ra = 2 * (lane & 3), dl = lane >> 2;
         float* ow = Ow + warp * 8 * D;
 #pragma unroll
@@ -320,7 +290,6 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
         }
     }
     __syncthreads();
-
     const int64_t part_row0 = ((((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits + split) * RPC;
     for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
         const int r = idx / D, d = idx % D;
@@ -332,10 +301,10 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
         if (M != -INFINITY) {
 #pragma unroll
             for (int kg = 0; kg < NKG; ++kg) {
-                const int w = rg * NKG + kg;
-                const float f = exp2f(Mw[w * 8 + ri] - M);
-                O += f * Ow[(w * 8 + ri) * D + d];
-                L += f * Lw[w * 8 + ri];
+                const int wi = rg * NKG + kg;
+                const float f = exp2f(Mw[wi * 8 + ri] - M);
+                O += f * Ow[(wi * 8 + ri) * D + d];
+                L += f * Lw[wi * 8 + ri];
             }
         }
         if (p.n_splits == 1) {
@@ -352,6 +321,303 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ f16 cache
+
+template <int NRG>
+__global__ void __launch_bounds__(NRG * NKG * 32)
+    fa_stream_f16_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const FaStreamParams p) {
+    constexpr int NC = NRG * NKG;  // consumer warps; lane 0 of warp 0 also issues the TMA loads
+    constexpr int RPC = NRG * 8;   // rows per CTA
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = smem;
+    __half* Qs = reinterpret_cast<__half*>(smem + ST * STAGE_F16);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * STAGE_F16 + q_bytes(NRG));
+    uint64_t* empty = full + ST;
+    __shared__ int s_failed;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, hk = blockIdx.y;
+    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
+    const int64_t key_begin = (int64_t) split * p.keys_per_split;
+    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
+    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
+    const int row0 = chunk * RPC;
+    const int rows = min(RPC, p.R - row0);
+    const bool issuer = threadIdx.x == 0;
+
+    // TMA issue state (meaningful in the issuing thread only)
+    int next_issue = 0;
+    uint64_t pol = 0;
+    const int kb3 = b / p.rk3;
+    auto issue = [&](int t) {
+        const int s = t % ST;
+        mbar_arrive_expect_tx(&full[s], STAGE_F16);
+        const int key = (int) (key_begin + (int64_t) t * TILE);
+        uint8_t* kdst = stages + s * STAGE_F16;
+        uint8_t* vdst = kdst + KTILE_F16;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(kdst + c * (TILE * 128), &tmK, &full[s], c * 64, hk, key, kb3, pol);
+            tma_load_4d(vdst + c * (TILE * 128), &tmV, &full[s], c * 64, hk, key, kb3, pol);
+        }
+    };
+    if (issuer) {
+        s_failed = 0;
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NC);
+        }
+        fence_barrier_init();
+        // start streaming before anything else: the first stages land while Q is staged
+        if (n_tiles > 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            pol = l2_policy_evict_first();
+            for (; next_issue < min(ST, n_tiles); ++next_issue) issue(next_issue);
+        }
+    }
+    stage_q<false>(p, Qs, RPC, rows, row0, hk, b);
+    __syncthreads();
+
+    bool failed = false;
+    float o[16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
+    const bool active = (warp / NKG) * 8 < rows;
+    uint32_t qf[16][2];
+    load_q_frags(Qs, warp / NKG, lane, qf);
+    const WarpCtx w = make_ctx(p, warp, lane, row0, hk);
+
+    for (int t = 0; t < n_tiles; ++t) {
+        const int s = t % ST;
+        if (issuer) {
+            // tile t must have been issued: wait for its stage to be released by every warp
+            while (next_issue <= t) {
+                const int si = next_issue % ST;
+                if (!mbar_wait(&empty[si], ((next_issue / ST) - 1) & 1, p.wait_ns)) {
+                    record_error(p.err, DEV_ERR_WAIT_EMPTY);
+                    failed = true;
+                    break;
+                }
+                issue(next_issue++);
+            }
+        }
+        __syncwarp();
+        if (!failed && !mbar_wait(&full[s], (t / ST) & 1, p.wait_ns)) {
+            record_error(p.err, DEV_ERR_WAIT_FULL);
+            failed = true;
+        }
+        if (__any_sync(0xffffffffu, failed)) {
+            failed = true;
+            break;
+        }
+        if (active) {
+            const uint32_t kb = smem_u32(stages + s * STAGE_F16);
+            tile_compute(p, kb, kb + KTILE_F16, key_begin + (int64_t) t * TILE, b, lane, w, qf, o, m0, m1, l0, l1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (issuer) {
+            // refill without blocking: issue every further tile whose stage all warps have released
+            while (next_issue < n_tiles && next_issue < t + 1 + ST) {
+                const int si = next_issue % ST;
+                if (!mbar_try_wait(&empty[si], ((next_issue / ST) - 1) & 1)) break;
+                issue(next_issue++);
+            }
+        }
+    }
+    // row sums over the warp's lanes
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    if (failed && lane == 0) atomicExch(&s_failed, 1);
+    __syncthreads();  // every issued stage consumed: the ring is free for the merge buffers
+    if (s_failed) return;  // a bounded wait ran out (error word set): leave the outputs alone
+    merge_key_groups<NRG>(p, reinterpret_cast<float*>(stages), warp, lane, rows, row0, hk, b, split, chunk, o, m0, m1, l0,
+                          l1);
+}
+
+// ------------------------------------------------------------------------------------------------ q8_0 cache
+
+// Dequantises one raw q8_0 tile pair (K then V, 64 cells x 272 bytes each, as TMA left them) into the f16
+// swizzled layout. Work unit = 16 elements (half a block) of one cell of K or V; each thread takes UPT units,
+// all of whose raw words are loaded before any is converted (the loop is unrolled for that).
+template <int NT>
+__device__ __forceinline__ void dequant_tile(const uint8_t* raw, uint8_t* f16tile, int tid) {
+    constexpr int UNITS = 2 * TILE * (D / 16);
+    constexpr int UPT = (UNITS + NT - 1) / NT;
+    uint32_t wq[UPT][4];
+    __half dh[UPT];
+#pragma unroll
+    for (int k = 0; k < UPT; ++k) {
+        const int u = tid + k * NT;
+        if (u < UNITS) {
+            const int tensor = u / (TILE * (D / 16)), rem = u % (TILE * (D / 16));
+            const int r = rem / (D / 16), bh = rem % (D / 16), blk = bh >> 1, hf = bh & 1;
+            const uint8_t* src = raw + tensor * QTILE_RAW + r * QROW + blk * 34;
+            dh[k] = *reinterpret_cast<const __half*>(src);
+            if (blk & 1) {
+                // quants at src + 2 + 16hf are 4-byte aligned for odd blocks (34 * blk + 2 = 0 mod 4)
+                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + 2 + 16 * hf);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) wq[k][i] = s32[i];
+            } else {
+                // even blocks: 2 bytes off; read the aligned words around them and shift
+                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + 16 * hf);
+                uint32_t W[5];
+#pragma unroll
+                for (int i = 0; i < 5; ++i) W[i] = s32[i];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) wq[k][i] = __funnelshift_r(W[i], W[i + 1], 16);
+            }
+        }
+    }
+    const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
+#pragma unroll
+    for (int k = 0; k < UPT; ++k) {
+        const int u = tid + k * NT;
+        if (u < UNITS) {
+            const int tensor = u / (TILE * (D / 16)), rem = u % (TILE * (D / 16));
+            const int r = rem / (D / 16), bh = rem % (D / 16), blk = bh >> 1, hf = bh & 1;
+            const __half2 d2 = __halves2half2(dh[k], dh[k]);
+            uint32_t outw[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                // int8 q -> f16: (q ^ 0x80) in the low mantissa byte of 1024.0 gives 1152 + q exactly
+                const uint32_t xw = wq[k][i] ^ 0x80808080u;
+                uint32_t lo = __byte_perm(xw, 0x64646464u, 0x4140), hi = __byte_perm(xw, 0x64646464u, 0x4342);
+                __half2 l2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), d2);
+                __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), d2);
+                outw[2 * i] = *reinterpret_cast<uint32_t*>(&l2);
+                outw[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            const int dim0 = 32 * blk + 16 * hf;
+            uint8_t* dst = f16tile + tensor * KTILE_F16 + (dim0 >> 6) * (TILE * 128) + r * 128;
+            const int u0 = (dim0 & 63) >> 3;
+            *reinterpret_cast<uint4*>(dst + ((u0 ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+            *reinterpret_cast<uint4*>(dst + (((u0 + 1) ^ (r & 7)) << 4)) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
+        }
+    }
+}
+
+template <int NRG>
+__global__ void __launch_bounds__(NRG * NKG * 32)
+    fa_stream_q8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        const FaStreamParams p) {
+    constexpr int NC = NRG * NKG;
+    constexpr int RPC = NRG * 8;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* f16tile = smem;                       // dequantised K | V tile (64 KiB)
+    uint8_t* raw = smem + STAGE_F16;               // QST raw stages of K | V blocks
+    __half* Qs = reinterpret_cast<__half*>(raw + QST * QSTAGE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(raw + QST * QSTAGE + q_bytes(NRG));
+    uint64_t* empty = full + QST;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, hk = blockIdx.y;
+    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
+    const int64_t key_begin = (int64_t) split * p.keys_per_split;
+    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
+    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
+    const int row0 = chunk * RPC;
+    const int rows = min(RPC, p.R - row0);
+    const bool issuer = threadIdx.x == 0;
+
+    int next_issue = 0;
+    uint64_t pol = 0;
+    const int kb3 = b / p.rk3;
+    auto issue = [&](int t) {
+        const int s = t % QST;
+        mbar_arrive_expect_tx(&full[s], QSTAGE);
+        const int key = (int) (key_begin + (int64_t) t * TILE);
+        uint8_t* dst = raw + s * QSTAGE;
+        tma_load_4d(dst, &tmK, &full[s], 0, hk, key, kb3, pol);
+        tma_load_4d(dst + QTILE_RAW, &tmV, &full[s], 0, hk, key, kb3, pol);
+    };
+    if (issuer) {
+        for (int s = 0; s < QST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NC);
+        }
+        fence_barrier_init();
+        if (n_tiles > 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            pol = l2_policy_evict_first();
+            for (; next_issue < min(QST, n_tiles); ++next_issue) issue(next_issue);
+        }
+    }
+    stage_q<true>(p, Qs, RPC, rows, row0, hk, b);
+    __syncthreads();
+
+    bool failed = false;
+    float o[16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
+    const bool active = (warp / NKG) * 8 < rows;
+    uint32_t qf[16][2];
+    load_q_frags(Qs, warp / NKG, lane, qf);
+    const WarpCtx w = make_ctx(p, warp, lane, row0, hk);
+    const uint32_t kb = smem_u32(f16tile);
+
+    for (int t = 0; t < n_tiles; ++t) {
+        const int s = t % QST;
+        if (issuer) {
+            while (next_issue <= t) {
+                const int si = next_issue % QST;
+                if (!mbar_wait(&empty[si], ((next_issue / QST) - 1) & 1, p.wait_ns)) {
+                    record_error(p.err, DEV_ERR_WAIT_EMPTY);
+                    failed = true;
+                    break;
+                }
+                issue(next_issue++);
+            }
+        }
+        __syncwarp();
+        if (!failed && !mbar_wait(&full[s], (t / QST) & 1, p.wait_ns)) {
+            record_error(p.err, DEV_ERR_WAIT_FULL);
+            failed = true;
+        }
+        // every warp dequantises, so the whole CTA agrees on leaving before anyone waits at a barrier
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        dequant_tile<NC * 32>(raw + s * QSTAGE, f16tile, threadIdx.x);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (issuer) {
+            while (next_issue < n_tiles && next_issue < t + 1 + QST) {
+                const int si = next_issue % QST;
+                if (!mbar_try_wait(&empty[si], ((next_issue / QST) - 1) & 1)) break;
+                issue(next_issue++);
+            }
+        }
+        __syncthreads();  // the f16 tile is complete
+        if (active)
+            tile_compute(p, kb, kb + KTILE_F16, key_begin + (int64_t) t * TILE, b, lane, w, qf, o, m0, m1, l0, l1);
+        __syncthreads();  // the f16 tile is consumed
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    if (failed) return;  // every thread took the same exit; the error word is set
+    // every issued tile was consumed: the f16 tile and the raw ring are free for the merge buffers
+    merge_key_groups<NRG>(p, reinterpret_cast<float*>(smem), warp, lane, rows, row0, hk, b, split, chunk, o, m0, m1, l0,
+                          l1);
+}
+
+// ------------------------------------------------------------------------------------------------ merges
+
 // Merge of n partial results (o_s, m_s, l_s) of one row by one 256-thread block:
 // out = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s with M = max over parts with l_s > 0 (0 if none).
 // The (m, l) pairs are reduced across the block, then warp w accumulates parts w, w+8, ... with every lane
@@ -360,7 +626,7 @@ constexpr int MERGE_THREADS = 256;
 constexpr int MERGE_MAX_PARTS = 1024;
 
 __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const float* __restrict__ ml, int64_t ml_stride,
-                          int n, int Dd, float* __restrict__ out_row, int64_t out_stride_elems, float* __restrict__ ml_out) {
+                          int n, int Dd, float* __restrict__ out_row, float* __restrict__ ml_out) {
     __shared__ float f[MERGE_MAX_PARTS];
     __shared__ float red[MERGE_THREADS / 32];
     __shared__ float acc_s[MERGE_THREADS / 32][256 + 4];
@@ -375,21 +641,21 @@ __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const f
     if (lane == 0) red[warp] = mx;
     __syncthreads();
     float M = red[0];
-    for (int w = 1; w < MERGE_THREADS / 32; ++w) M = fmaxf(M, red[w]);
+    for (int wi = 1; wi < MERGE_THREADS / 32; ++wi) M = fmaxf(M, red[wi]);
     __syncthreads();
     // weights and the weighted sum of l
     float lsum = 0.0f;
     for (int s = tid; s < n; s += MERGE_THREADS) {
         const float l = ml[s * ml_stride + 1];
-        const float w = (l > 0.0f && M != -INFINITY) ? exp2f(ml[s * ml_stride] - M) : 0.0f;
-        f[s] = w;
-        lsum += w * l;
+        const float wt = (l > 0.0f && M != -INFINITY) ? exp2f(ml[s * ml_stride] - M) : 0.0f;
+        f[s] = wt;
+        lsum += wt * l;
     }
     for (int off = 16; off; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
     if (lane == 0) red[warp] = lsum;
     __syncthreads();
     float L = 0.0f;
-    for (int w = 0; w < MERGE_THREADS / 32; ++w) L += red[w];
+    for (int wi = 0; wi < MERGE_THREADS / 32; ++wi) L += red[wi];
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     for (int d0 = 0; d0 < Dd; d0 += 256) {
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -397,11 +663,11 @@ __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const f
         if (d < Dd) {
 #pragma unroll 4
             for (int s = warp; s < n; s += MERGE_THREADS / 32) {
-                const float w = f[s];
+                const float wt = f[s];
                 const float4* src = reinterpret_cast<const float4*>(o + s * o_stride + d);
                 const float4 x = src[0], y = src[1];
-                a[0] += w * x.x; a[1] += w * x.y; a[2] += w * x.z; a[3] += w * x.w;
-                a[4] += w * y.x; a[5] += w * y.y; a[6] += w * y.z; a[7] += w * y.w;
+                a[0] += wt * x.x; a[1] += wt * x.y; a[2] += wt * x.z; a[3] += wt * x.w;
+                a[4] += wt * y.x; a[5] += wt * y.y; a[6] += wt * y.z; a[7] += wt * y.w;
             }
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc_s[warp][lane * 8 + e] = a[e];
@@ -410,12 +676,8 @@ __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const f
         if (d0 + tid < Dd) {
             float t = 0.0f;
 #pragma unroll
-            for (int w = 0; w < MERGE_THREADS / 32; ++w) t += acc_s[w][tid];
-            if (ml_out) {
-                out_row[(int64_t) (d0 + tid) * out_stride_elems] = t;  // partial output: unnormalised
-            } else {
-                out_row[(int64_t) (d0 + tid) * out_stride_elems] = t * inv;
-            }
+            for (int wi = 0; wi < MERGE_THREADS / 32; ++wi) t += acc_s[wi][tid];
+            out_row[d0 + tid] = ml_out ? t : t * inv;  // partial output stays unnormalised
         }
         __syncthreads();
     }
@@ -435,7 +697,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) fa_combine_kernel(const FaStrea
     float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
     float* ml_out = p.partial_out ? p.dst_ml + (((int64_t) b * p.n_q + qi) * p.n_head + h) * 2 : nullptr;
     merge_row(p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + (base * RPC + r) * 2, (int64_t) RPC * 2,
-              p.n_splits, D, out, 1, ml_out);
+              p.n_splits, D, out, ml_out);
 }
 
 // Merges partial results computed over disjoint KV ranges (e.g. one per GPU), one row per block.
@@ -444,22 +706,29 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
                                                                     int n_parts, int64_t rows, int Dd,
                                                                     float* __restrict__ dst) {
     const int64_t r = blockIdx.x;
-    merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, 1, nullptr);
+    merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
 }
 
-template <int NRG>
-cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
-    auto kern = fa_stream_f16_kernel<NRG>;
-    const size_t smem = smem_f16(NRG);
-    static bool attr_set[64] = {};  // the attribute is per device: set it once on each
+// ------------------------------------------------------------------------------------------------ launch
+
+template <typename Kern>
+cudaError_t set_smem_once(Kern kern, size_t smem, bool (&done)[64]) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+    return e;
+}
+
+template <int NRG, bool Q8>
+cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
+    static bool attr_done[64] = {};  // the smem attribute is per device: set it once on each
+    auto kern = Q8 ? fa_stream_q8_kernel<NRG> : fa_stream_f16_kernel<NRG>;
+    const size_t smem = Q8 ? smem_q8(NRG) : smem_f16(NRG);
+    cudaError_t e = set_smem_once(kern, smem, attr_done);
+    if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
     kern<<<grid, NRG * NKG * 32, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
@@ -478,18 +747,15 @@ cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int6
     return cudaGetLastError();
 }
 
-size_t fa_stream_smem_bytes(int nrg, int kv_type) {
-    (void) kv_type;
-    return smem_f16(nrg);
-}
+size_t fa_stream_smem_bytes(int nrg, int kv_type) { return kv_type == 8 ? smem_q8(nrg) : smem_f16(nrg); }
 
 cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream) {
-    (void) kv_type;
+    const bool q8 = kv_type == 8;
     switch (nrg) {
-        case 1: return launch_nrg<1>(p, tmK, tmV, stream);
-        case 2: return launch_nrg<2>(p, tmK, tmV, stream);
-        default: return launch_nrg<3>(p, tmK, tmV, stream);
+        case 1: return q8 ? launch_nrg<1, true>(p, tmK, tmV, stream) : launch_nrg<1, false>(p, tmK, tmV, stream);
+        case 2: return q8 ? launch_nrg<2, true>(p, tmK, tmV, stream) : launch_nrg<2, false>(p, tmK, tmV, stream);
+        default: return q8 ? launch_nrg<3, true>(p, tmK, tmV, stream) : launch_nrg<3, false>(p, tmK, tmV, stream);
     }
 }
 

@@ -9,6 +9,7 @@
 #include <mutex>
 
 #include "../../include/klein_b200.h"
+#include "kb_gdn.h"
 #include "kb_internal.h"
 
 namespace {
@@ -66,7 +67,7 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     if (!q || !k || !v) return KB_ERR_ARG;
     if (q->type != KB_TYPE_F32) return KB_ERR_UNSUPPORTED;
     if (k->type != v->type) return KB_ERR_UNSUPPORTED;
-    if (k->type != KB_TYPE_F16) return KB_ERR_UNSUPPORTED;
+    if (k->type != KB_TYPE_F16 && k->type != KB_TYPE_Q8_0) return KB_ERR_UNSUPPORTED;
     s->D = (int) q->ne[0];
     s->n_q = (int) q->ne[1];
     s->H = (int) q->ne[2];
@@ -79,7 +80,8 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     if (v->ne[1] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return KB_ERR_BAD_SHAPE;
     if (s->H_kv <= 0 || s->H % s->H_kv != 0 || s->ne3k <= 0 || s->ne3 % s->ne3k != 0) return KB_ERR_BAD_SHAPE;
     if (s->n_q <= 0 || s->H <= 0 || s->ne3 <= 0 || s->n_kv < 0) return KB_ERR_BAD_SHAPE;
-    if (q->nb[0] != 4 || k->nb[0] != 2 || v->nb[0] != 2) return KB_ERR_BAD_SHAPE;
+    const size_t kv_es = k->type == KB_TYPE_Q8_0 ? 34 : 2;  // nb[0]: element size, or block size for q8_0
+    if (q->nb[0] != 4 || k->nb[0] != kv_es || v->nb[0] != kv_es) return KB_ERR_BAD_SHAPE;
     if (s->D != kb::FA_D) return KB_ERR_UNSUPPORTED;
     if (mask) {
         if (mask->type != KB_TYPE_F16 || mask->nb[0] != 2) return KB_ERR_UNSUPPORTED;
@@ -125,6 +127,19 @@ FaPlan plan_fa(const FaShape& s) {
 kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return KB_ERR_CUDA;
+    if (t->type == KB_TYPE_Q8_0) {
+        // raw blocks: one head's row is ne0/32 blocks of 34 bytes, read as 32-bit words without swizzle;
+        // dims: words of a head row, KV head, cell, batch; box = a whole head row x 64 cells
+        const cuuint64_t words = (cuuint64_t) t->ne[0] / 32 * 34 / 4;
+        const cuuint64_t dims[4] = {words, (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[3]};
+        const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
+        const cuuint32_t box[4] = {(cuuint32_t) words, 1, (cuuint32_t) kb::FA_TILE, 1};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, t->data, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        return r == CUDA_SUCCESS ? KB_OK : KB_ERR_CUDA;
+    }
     // dims (innermost first): head dim, KV head, cell, batch; box = 64 dims x 1 head x 64 cells
     const cuuint64_t dims[4] = {(cuuint64_t) t->ne[0], (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[3]};
     const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
@@ -184,6 +199,8 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     p.q_nb1 = (int64_t) q->nb[1];
     p.q_nb2 = (int64_t) q->nb[2];
     p.q_nb3 = (int64_t) q->nb[3];
+    p.q_vec4 = aligned16(reinterpret_cast<uintptr_t>(q->data)) && aligned16(q->nb[1]) && aligned16(q->nb[2]) &&
+               aligned16(q->nb[3]);
     p.n_q = s.n_q;
     p.n_head = s.H;
     p.n_head_kv = s.H_kv;
@@ -284,6 +301,168 @@ kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t pa
                    cudaSuccess
                ? KB_OK
                : KB_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------------------------- DeltaNet
+
+}  // extern "C"
+
+namespace {
+
+bool rows_f32(const kb_tensor* t) { return t && t->type == KB_TYPE_F32 && t->nb[0] == 4; }
+
+bool contiguous_f32(const kb_tensor* t) {
+    return rows_f32(t) && t->nb[1] == (size_t) t->ne[0] * 4 && t->nb[2] == t->nb[1] * t->ne[1] &&
+           t->nb[3] == t->nb[2] * t->ne[2];
+}
+
+int snap_code(int32_t type) { return type == KB_TYPE_F32 ? 0 : type == KB_TYPE_F16 ? 1 : type == KB_TYPE_BF16 ? 2 : -1; }
+
+// checks the operands of GGML_OP_GATED_DELTA_NET (ggml.c:6375-6428) and fills the input half of the params
+kb_status gdn_inputs(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
+                     const kb_tensor* beta, const kb_tensor* state, int32_t K, kb::GdnParams* p) {
+    if (!q || !k || !v || !g || !beta || !state) return KB_ERR_ARG;
+    if (!rows_f32(q) || !rows_f32(k) || !rows_f32(v) || !contiguous_f32(g) || !contiguous_f32(beta) ||
+        !contiguous_f32(state))
+        return KB_ERR_UNSUPPORTED;
+    const int64_t S = v->ne[0], H = v->ne[1], T = v->ne[2], n_seqs = v->ne[3];
+    if (K < 1 || T < 1 || n_seqs < 1) return KB_ERR_BAD_SHAPE;
+    if (q->ne[0] != S || k->ne[0] != S || q->ne[1] != k->ne[1] || q->ne[2] != T || k->ne[2] != T) return KB_ERR_BAD_SHAPE;
+    if (k->ne[1] <= 0 || H % k->ne[1] != 0 || n_seqs % q->ne[3] != 0 || n_seqs % k->ne[3] != 0) return KB_ERR_BAD_SHAPE;
+    if (!(g->ne[0] == 1 || g->ne[0] == S) || g->ne[1] != H || g->ne[2] != T || g->ne[3] != n_seqs) return KB_ERR_BAD_SHAPE;
+    if (beta->ne[0] != 1 || beta->ne[1] != H || beta->ne[2] != T || beta->ne[3] != n_seqs) return KB_ERR_BAD_SHAPE;
+    if (state->ne[0] != S || state->ne[1] != S || state->ne[2] != H || state->ne[3] != n_seqs) return KB_ERR_BAD_SHAPE;
+    if (S != 128) return KB_ERR_UNSUPPORTED;
+    // float4 loads: q, k, state (and a per-channel gate) need 16-byte aligned rows
+    for (const kb_tensor* t : {q, k, state, g}) {
+        if (t == g && g->ne[0] != S) continue;
+        if (!aligned16(reinterpret_cast<uintptr_t>(t->data)) || !aligned16(t->nb[1]) || !aligned16(t->nb[2]) ||
+            !aligned16(t->nb[3]))
+            return KB_ERR_UNSUPPORTED;
+    }
+    p->q = static_cast<const char*>(q->data);
+    p->q_nb1 = q->nb[1], p->q_nb2 = q->nb[2], p->q_nb3 = q->nb[3];
+    p->k = static_cast<const char*>(k->data);
+    p->k_nb1 = k->nb[1], p->k_nb2 = k->nb[2], p->k_nb3 = k->nb[3];
+    p->v = static_cast<const char*>(v->data);
+    p->v_nb1 = v->nb[1], p->v_nb2 = v->nb[2], p->v_nb3 = v->nb[3];
+    p->g = static_cast<const char*>(g->data);
+    p->g_nb1 = g->nb[1], p->g_nb2 = g->nb[2], p->g_nb3 = g->nb[3];
+    p->kda = g->ne[0] == S;
+    p->beta = static_cast<const char*>(beta->data);
+    p->b_nb1 = beta->nb[1], p->b_nb2 = beta->nb[2], p->b_nb3 = beta->nb[3];
+    p->s0 = static_cast<const float*>(state->data);
+    p->s0_seq_stride = (int64_t) (state->nb[3] / 4);
+    p->S = (int) S, p->H_k = (int) k->ne[1], p->H_v = (int) H, p->T = (int) T, p->n_seqs = (int) n_seqs, p->K = K;
+    p->rq3 = (int) (n_seqs / q->ne[3]);
+    p->rk3 = (int) (n_seqs / k->ne[3]);
+    return KB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
+                             const kb_tensor* beta, const kb_tensor* state, int32_t K, const kb_tensor* dst,
+                             void* stream) {
+    kb::GdnParams p{};
+    kb_status st = gdn_inputs(q, k, v, g, beta, state, K, &p);
+    if (st != KB_OK) return st;
+    if (!dst) return KB_ERR_ARG;
+    const int64_t S = p.S, H = p.H_v, T = p.T, n_seqs = p.n_seqs;
+    // ggml's packed result: [S*H, T*n_seqs + K*S*n_seqs] f32, contiguous
+    if (!contiguous_f32(dst) || dst->ne[0] != S * H || dst->ne[1] != T * n_seqs + (int64_t) K * S * n_seqs ||
+        dst->ne[2] != 1 || dst->ne[3] != 1)
+        return KB_ERR_BAD_SHAPE;
+    if (!aligned16(reinterpret_cast<uintptr_t>(dst->data))) return KB_ERR_UNSUPPORTED;
+    char* base = static_cast<char*>(dst->data);
+    p.attn = base;
+    p.a_nb1 = S * 4, p.a_nb2 = S * H * 4, p.a_nb3 = S * H * T * 4;
+    const int64_t attn_bytes = S * H * T * n_seqs * 4, slot_bytes = S * S * H * n_seqs * 4;
+    p.slot0 = base + attn_bytes;
+    p.slots = base + attn_bytes + slot_bytes;
+    p.slots_stride = slot_bytes;
+    p.slots_type = 0;
+    return kb::launch_gdn_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_gated_delta_net_cache(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
+                                   const kb_tensor* beta, const kb_tensor* state, const kb_tensor* snap, int32_t K,
+                                   const kb_tensor* attn, void* stream) {
+    kb::GdnParams p{};
+    kb_status st = gdn_inputs(q, k, v, g, beta, state, K, &p);
+    if (st != KB_OK) return st;
+    if (!attn || !rows_f32(attn)) return KB_ERR_ARG;
+    if (attn->ne[0] != p.S || attn->ne[1] != p.H_v || attn->ne[2] != p.T || attn->ne[3] != p.n_seqs) return KB_ERR_BAD_SHAPE;
+    const int n_written = p.T < K ? p.T : K;
+    if (n_written > 1) {
+        // snapshot rows: [S*S*H*n_seqs, >= n_written - 1], contiguous rows of f16 / bf16 / f32
+        if (!snap) return KB_ERR_ARG;
+        const int code = snap_code(snap->type);
+        if (code < 0) return KB_ERR_UNSUPPORTED;
+        const int64_t es = code == 0 ? 4 : 2;
+        if (snap->ne[0] != (int64_t) p.S * p.S * p.H_v * p.n_seqs || snap->ne[1] < n_written - 1 ||
+            snap->nb[0] != (size_t) es || !aligned16(reinterpret_cast<uintptr_t>(snap->data)) || !aligned16(snap->nb[1]))
+            return KB_ERR_BAD_SHAPE;
+        p.slots = static_cast<char*>(snap->data);
+        p.slots_stride = (int64_t) snap->nb[1];
+        p.slots_type = code;
+    }
+    p.attn = static_cast<char*>(attn->data);
+    p.a_nb1 = attn->nb[1], p.a_nb2 = attn->nb[2], p.a_nb3 = attn->nb[3];
+    p.slot0 = static_cast<char*>(state->data);  // slot 0 overwrites the state it was computed from
+    return kb::launch_gdn_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream) {
+    if (!dst || !src || !idx) return KB_ERR_ARG;
+    if (!rows_f32(src)) return KB_ERR_UNSUPPORTED;
+    if (idx->type != KB_TYPE_I64 && idx->type != KB_TYPE_I32) return KB_ERR_UNSUPPORTED;
+    const int t = dst->type;
+    if (t != KB_TYPE_F32 && t != KB_TYPE_F16 && t != KB_TYPE_BF16 && t != KB_TYPE_Q8_0) return KB_ERR_UNSUPPORTED;
+    const int64_t ne0 = src->ne[0];
+    if (dst->ne[0] != ne0 || ne0 % 32 != 0) return t == KB_TYPE_Q8_0 || dst->ne[0] != ne0 ? KB_ERR_BAD_SHAPE : KB_ERR_UNSUPPORTED;
+    if (dst->ne[2] != src->ne[2] || dst->ne[3] != src->ne[3] || idx->ne[0] != src->ne[1]) return KB_ERR_BAD_SHAPE;
+    if (idx->ne[1] <= 0 || idx->ne[2] <= 0 || src->ne[2] % idx->ne[1] != 0 || src->ne[3] % idx->ne[2] != 0)
+        return KB_ERR_BAD_SHAPE;
+    const size_t es = t == KB_TYPE_F32 ? 4 : t == KB_TYPE_Q8_0 ? 34 : 2;
+    if (dst->nb[0] != es) return KB_ERR_BAD_SHAPE;
+    kb::SetRowsParams p{};
+    p.src = static_cast<const char*>(src->data);
+    p.s_nb1 = src->nb[1], p.s_nb2 = src->nb[2], p.s_nb3 = src->nb[3];
+    p.idx = static_cast<const char*>(idx->data);
+    p.i_nb0 = idx->nb[0], p.i_nb1 = idx->nb[1], p.i_nb2 = idx->nb[2];
+    p.idx_i32 = idx->type == KB_TYPE_I32;
+    p.ne11 = idx->ne[1], p.ne12 = idx->ne[2];
+    p.dst = static_cast<char*>(dst->data);
+    p.d_nb1 = dst->nb[1], p.d_nb2 = dst->nb[2], p.d_nb3 = dst->nb[3];
+    p.dst_type = t;
+    p.ne0 = ne0, p.n_src = src->ne[1], p.ne2 = src->ne[2], p.ne3 = src->ne[3], p.n_rows = dst->ne[1];
+    p.err = kb::device_error_word();
+    return kb::launch_set_rows(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t conv_row, const void* const* snap,
+                                int32_t snap_type, float* const* ssm, int64_t ssm_row, int32_t s, int32_t n_snapshots,
+                                void* stream) {
+    if (s <= 0) return KB_OK;  // nothing rejected (state.cpp:163)
+    if (s >= n_snapshots) return KB_ERR_ARG;
+    if (n_layers < 0 || n_layers > kb::MAX_ROLLBACK_LAYERS || !conv || !snap || !ssm) return KB_ERR_ARG;
+    const int code = snap_code(snap_type);
+    if (code < 0) return KB_ERR_UNSUPPORTED;
+    if (conv_row % 4 != 0 || ssm_row % 4 != 0 || conv_row <= 0 || ssm_row <= 0) return KB_ERR_UNSUPPORTED;
+    kb::RollbackParams p{};
+    for (int l = 0; l < n_layers; ++l) {
+        if (!conv[l] || !snap[l] || !ssm[l] || !aligned16(reinterpret_cast<uintptr_t>(conv[l])) ||
+            !aligned16(reinterpret_cast<uintptr_t>(ssm[l])) || (reinterpret_cast<uintptr_t>(snap[l]) & 7) != 0)
+            return KB_ERR_ARG;
+        p.conv[l] = conv[l];
+        p.snap[l] = static_cast<const char*>(snap[l]);
+        p.ssm[l] = ssm[l];
+    }
+    p.n_layers = n_layers, p.conv_row = conv_row, p.ssm_row = ssm_row, p.snap_type = code, p.s = s;
+    return kb::launch_rollback(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 
 kb_status kb_device_error(int32_t* code, int clear) {

@@ -18,6 +18,7 @@ constexpr int FA_NKG = 4;            // key groups (consumer warps per 8-row gro
 struct FaStreamParams {
     const char* q;                   // f32 [D, n_q, H, ne3]
     int64_t q_nb1, q_nb2, q_nb3;
+    int q_vec4;                      // q rows 16-byte aligned: stage them with float4 loads
     int n_q, n_head, n_head_kv, gqa, ne3, rk3;
     int R;                           // rows per KV head = n_q * gqa
     int64_t n_kv;

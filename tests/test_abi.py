@@ -68,3 +68,55 @@ def test_fa_rejects_bad_descriptors(kb):
     a["k"].nb[1] = 2040  # TMA needs 16-byte strides
     assert _call(kb, a) == kb.KB_ERR_UNSUPPORTED
     assert kb.lib().kb_flash_attn_ext(None, None, None, None, None, None, None, 0, None) == kb.KB_ERR_ARG
+
+
+no_gpu = pytest.mark.skipif(__import__("torch").cuda.is_available(),
+                            reason="passing validation would launch on host pointers")
+
+
+@no_gpu
+def test_gdn_descriptors_validate(kb):
+    """Operands shaped like klein's DeltaNet node pass validation (the call then fails only for lack of a GPU),
+    malformed ones are rejected."""
+    import numpy as np
+    import torch
+
+    import oracle as O
+
+    q, k, v, g, beta, s0 = O.make_gdn_inputs(1, 4)
+    ts = [torch.from_numpy(np.ascontiguousarray(a)) for a in (q, k, v, g, beta[..., None], s0)]
+    args = [kb.from_torch(t) for t in ts]
+    S, H, T, K = 128, 48, 4, 4
+    out = torch.zeros(S * H * T + K * S * S * H)
+    dt = kb.kb_tensor(out.data_ptr(), kb.F32, [S * H, T + K * S, 1, 1], [4, S * H * 4])
+    call = lambda a, d=dt, K_=K: kb.lib().kb_gated_delta_net(*[ctypes.byref(x) for x in a], K_, ctypes.byref(d), None)
+    assert call(args) == kb.KB_ERR_CUDA  # validation passed; no device here
+    bad = list(args)
+    bad[3] = kb.from_torch(torch.zeros(1, T, H, 7))  # gate neither scalar nor per-channel
+    assert call(bad) == kb.KB_ERR_BAD_SHAPE
+    assert call(args, K_=0) == kb.KB_ERR_BAD_SHAPE
+    small = kb.kb_tensor(out.data_ptr(), kb.F32, [S * H, T + K * S - 1, 1, 1], [4, S * H * 4])
+    assert call(args, d=small) == kb.KB_ERR_BAD_SHAPE
+    snap = torch.zeros(K - 1, S * S * H, dtype=torch.float16)
+    attn = torch.zeros(1, T, H, S)
+    rc = kb.lib().kb_gated_delta_net_cache(*[ctypes.byref(x) for x in args], ctypes.byref(kb.from_torch(snap)), K,
+                                           ctypes.byref(kb.from_torch(attn)), None)
+    assert rc == kb.KB_ERR_CUDA
+
+
+@no_gpu
+def test_set_rows_and_rollback_validate(kb):
+    import torch
+
+    cache = torch.zeros(16, 1024, dtype=torch.float16)
+    src = torch.zeros(1, 1, 3, 1024)
+    idx = torch.zeros(3, dtype=torch.int64)
+    L = kb.lib()
+    d, s_, i_ = kb.from_torch(cache), kb.from_torch(src), kb.from_torch(idx)
+    assert L.kb_set_rows(ctypes.byref(d), ctypes.byref(s_), ctypes.byref(i_), None) == kb.KB_ERR_CUDA
+    odd = kb.from_torch(torch.zeros(1, 1, 3, 1000))
+    assert L.kb_set_rows(ctypes.byref(d), ctypes.byref(odd), ctypes.byref(i_), None) == kb.KB_ERR_BAD_SHAPE
+    f = ctypes.c_void_p * 1
+    assert L.kb_rollback_recurrent(1, f(64), 64, f(64), kb.F16, f(64), 64, 0, 4, None) == kb.KB_OK  # s = 0: no-op
+    assert L.kb_rollback_recurrent(1, f(64), 64, f(64), kb.F16, f(64), 64, 4, 4, None) == kb.KB_ERR_ARG
+    assert L.kb_rollback_recurrent(1, f(64), 64, f(64), 99, f(64), 64, 1, 4, None) == kb.KB_ERR_UNSUPPORTED

@@ -214,3 +214,35 @@ def test_partials_and_lse_combine(kb, cuda):
     torch.cuda.synchronize()
     mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
     check_attention(out.cpu().numpy().reshape(n_q, H, D), exact_np(O.q_round_f16(q), kd, vd, mask))
+
+
+# ---------------------------------------------------------------------------------------------- q8_0 cache
+
+@pytest.mark.parametrize("n_q,n_kv", [(1, 4096), (4, 4096), (4, 65), (1, 1000), (3, 777), (8, 300)])
+def test_q8_0_causal_analytic(kb, cuda, n_q, n_kv):
+    q, kc, vc, kd, vd = O.make_fa_inputs(2000 + n_q * 7 + n_kv, n_q, n_kv, kv_type=O.GGML_Q8_0)
+    pos0 = n_kv - n_q
+    mask = O.rs_visible_mask(n_q, n_kv, pos0)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0)
+    exact = exact_np(O.q_round_q8_0(q), kd, vd, mask)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_Q8_0, 4, mask=mask.astype(np.float16), n_threads=4, use_ref=False) \
+        if O.ref_available() else None
+    check_attention(gpu, exact, ggml)
+
+
+def test_q8_0_dense_mask_and_ring(kb, cuda):
+    ring, n_q, pos0 = 2048, 4, 9000
+    q, kc, vc, kd, vd = O.make_fa_inputs(31, n_q, ring, kv_type=O.GGML_Q8_0)
+    mask = O.rs_visible_mask(n_q, ring, pos0, ring=ring)
+    exact = exact_np(O.q_round_q8_0(q), kd, vd, mask)
+    check_attention(run_gpu(kb, cuda, q, kc, vc, 4, mask=mask), exact)
+    check_attention(run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0, ring=ring), exact)
+
+
+def test_q8_0_long_verify_262144(kb, cuda):
+    """config[3] shape (q8_0): 4 tokens, causal among the last 4, 262,144 cells."""
+    n_q, n_kv = 4, 262144
+    q, kc, vc, kd, vd = O.make_fa_inputs(4711, n_q, n_kv, kv_type=O.GGML_Q8_0)
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q)
+    check_attention(gpu, exact_np(O.q_round_q8_0(q), kd, vd, mask))
