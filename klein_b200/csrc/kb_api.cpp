@@ -59,15 +59,22 @@ struct FaPlan {
 };
 
 struct FaShape {
-    int D, n_q, H, ne3, H_kv, ne3k, gqa, R;
+    int D, n_q, H, ne3, H_kv, ne3k, gqa, R, kv_type;
     int64_t n_kv;
 };
+
+// Prefill (tcgen05) kernel: 128-query tiles of one head; f16 or bf16 K/V; whole-output calls only.
+constexpr int PREFILL_MIN_Q = 128;
+bool use_prefill(const FaShape& s, const kb_fa_params* prm, bool partial) {
+    return !partial && s.n_q >= PREFILL_MIN_Q && (s.kv_type == KB_TYPE_F16 || s.kv_type == KB_TYPE_BF16) &&
+           !(prm && prm->causal && prm->ring > 0);
+}
 
 kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask, FaShape* s) {
     if (!q || !k || !v) return KB_ERR_ARG;
     if (q->type != KB_TYPE_F32) return KB_ERR_UNSUPPORTED;
     if (k->type != v->type) return KB_ERR_UNSUPPORTED;
-    if (k->type != KB_TYPE_F16 && k->type != KB_TYPE_Q8_0) return KB_ERR_UNSUPPORTED;
+    if (k->type != KB_TYPE_F16 && k->type != KB_TYPE_Q8_0 && k->type != KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;
     s->D = (int) q->ne[0];
     s->n_q = (int) q->ne[1];
     s->H = (int) q->ne[2];
@@ -81,6 +88,7 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     if (s->H_kv <= 0 || s->H % s->H_kv != 0 || s->ne3k <= 0 || s->ne3 % s->ne3k != 0) return KB_ERR_BAD_SHAPE;
     if (s->n_q <= 0 || s->H <= 0 || s->ne3 <= 0 || s->n_kv < 0) return KB_ERR_BAD_SHAPE;
     const size_t kv_es = k->type == KB_TYPE_Q8_0 ? 34 : 2;  // nb[0]: element size, or block size for q8_0
+    s->kv_type = k->type;
     if (q->nb[0] != 4 || k->nb[0] != kv_es || v->nb[0] != kv_es) return KB_ERR_BAD_SHAPE;
     if (s->D != kb::FA_D) return KB_ERR_UNSUPPORTED;
     if (mask) {
@@ -145,7 +153,8 @@ kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
     const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
     const cuuint32_t box[4] = {64, 1, (cuuint32_t) kb::FA_TILE, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    const CUtensorMapDataType dt = t->type == KB_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = enc(map, dt, 4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? KB_OK : KB_ERR_CUDA;
 }
@@ -161,6 +170,7 @@ size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, c
     (void) params;
     FaShape s;
     if (check_fa(q, k, v, nullptr, &s) != KB_OK) return 0;
+    if (use_prefill(s, params, false)) return 0;
     return plan_fa(s).scratch;
 }
 
@@ -191,6 +201,46 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
             return KB_ERR_CUDA;
         return KB_OK;
     }
+    const float log2e_ = 1.4426950408889634f;
+    if (use_prefill(s, prm, dst_ml != nullptr)) {
+        const bool qv4 = aligned16(reinterpret_cast<uintptr_t>(q->data)) && aligned16(q->nb[1]) && aligned16(q->nb[2]) &&
+                         aligned16(q->nb[3]);
+        if (!qv4 || !aligned16(dst->nb[1]) || !aligned16(dst->nb[2]) || !aligned16(dst->nb[3]) ||
+            !aligned16(reinterpret_cast<uintptr_t>(dst->data)))
+            return KB_ERR_UNSUPPORTED;
+        kb::FaPrefillParams pp{};
+        pp.q = static_cast<const char*>(q->data);
+        pp.q_nb1 = (int64_t) q->nb[1], pp.q_nb2 = (int64_t) q->nb[2], pp.q_nb3 = (int64_t) q->nb[3];
+        pp.n_q = s.n_q, pp.n_head = s.H, pp.n_head_kv = s.H_kv, pp.gqa = s.gqa, pp.ne3 = s.ne3, pp.rk3 = s.ne3 / s.ne3k;
+        pp.n_qtiles = (s.n_q + 127) / 128;
+        pp.n_kv = s.n_kv;
+        if (mask) {
+            pp.mask = static_cast<const char*>(mask->data);
+            pp.m_nb1 = (int64_t) mask->nb[1], pp.m_nb2 = (int64_t) mask->nb[2], pp.m_nb3 = (int64_t) mask->nb[3];
+            pp.m_ne2 = (int) mask->ne[2], pp.m_ne3 = (int) mask->ne[3];
+        }
+        pp.scale_log2 = prm->scale * log2e_;
+        pp.has_softcap = prm->logit_softcap != 0.0f;
+        if (pp.has_softcap) {
+            pp.scale_sc = prm->scale / prm->logit_softcap;
+            pp.softcap_log2 = prm->logit_softcap * log2e_;
+        }
+        pp.max_bias = prm->max_bias;
+        pp.n_head_log2 = 1 << (int) std::floor(std::log2((double) s.H));
+        pp.m0 = std::pow(2.0f, -(prm->max_bias) / pp.n_head_log2);
+        pp.m1 = std::pow(2.0f, -(prm->max_bias / 2.0f) / pp.n_head_log2);
+        pp.causal = prm->causal, pp.pos0 = prm->pos0, pp.kv_lo = prm->kv_lo;
+        pp.dst = static_cast<char*>(dst->data);
+        pp.d_nb1 = (int64_t) dst->nb[1], pp.d_nb2 = (int64_t) dst->nb[2], pp.d_nb3 = (int64_t) dst->nb[3];
+        pp.err = kb::device_error_word();
+        pp.wait_ns = g_wait_ns;
+        CUtensorMap tK, tV;
+        if ((st = encode_kv_map(k, &tK)) != KB_OK) return st;
+        if ((st = encode_kv_map(v, &tV)) != KB_OK) return st;
+        cudaError_t e = kb::launch_fa_prefill(pp, s.kv_type == KB_TYPE_BF16 ? 1 : 0, tK, tV, static_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+    }
+    if (s.kv_type == KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;  // bf16 caches: prefill shapes only
     const FaPlan pl = plan_fa(s);
     if (pl.scratch > 0 && (!scratch || scratch_bytes < pl.scratch)) return KB_ERR_SCRATCH;
 

@@ -58,6 +58,32 @@ size_t fa_stream_smem_bytes(int nrg, int kv_type);
 cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream);
 
+// Parameters of one causal-prefill launch (tcgen05 kernel): one CTA per 128-query tile of one head.
+struct FaPrefillParams {
+    const char* q;                   // f32 [D, n_q, H, ne3], rows 16-byte aligned
+    int64_t q_nb1, q_nb2, q_nb3;
+    int n_q, n_head, n_head_kv, gqa, ne3, rk3, n_qtiles;
+    int64_t n_kv;
+    const char* mask;                // f16 [n_kv, n_q', ne32, ne33] or null
+    int64_t m_nb1, m_nb2, m_nb3;
+    int m_ne2, m_ne3;
+    float scale_log2, scale_sc, softcap_log2;
+    int has_softcap;
+    float max_bias, m0, m1;
+    int n_head_log2;
+    int causal;
+    int64_t pos0, kv_lo;
+    char* dst;                       // f32 [D, H, n_q, ne3]
+    int64_t d_nb1, d_nb2, d_nb3;
+    int* err;
+    uint64_t wait_ns;
+};
+
+size_t fa_prefill_smem_bytes();
+// fmt: 0 = f16 K/V, 1 = bf16 K/V
+cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                              cudaStream_t stream);
+
 // merges n_parts partial results: o_p [rows][D] at o_parts + p*stride, ml_p [rows][2] at ml_parts + p*stride
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int D,
                                float* dst, cudaStream_t stream);

@@ -248,6 +248,21 @@ def ref_cpy(src: np.ndarray, src_type: int, dst: np.ndarray, dst_type: int) -> i
 # ----------------------------------------------------------------------------------------------------------
 # seeded synthetic inputs (the BASELINE configurations' distributions)
 
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """IEEE f32 -> bf16 bit patterns, round to nearest even (ggml's GGML_FP32_TO_BF16 for finite values)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def q_round_bf16(q: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(q)).reshape(q.shape)
+
+
 def make_fa_inputs(seed: int, n_q: int, n_kv: int, H=24, H_kv=4, D=256, kv_type=GGML_F16):
     """Q f32 [n_q][H][D] ~N(0,1); K, V cache rows ~N(0,1) stored as kv_type. Returns (q, k_cache, v_cache,
     k_deq, v_deq) where *_deq are the exact f32 values the cache holds."""
@@ -261,6 +276,9 @@ def make_fa_inputs(seed: int, n_q: int, n_kv: int, H=24, H_kv=4, D=256, kv_type=
     elif kv_type == GGML_Q8_0:
         kc, vc = rs_quantize_q8_0(kf), rs_quantize_q8_0(vf)
         kd, vd = rs_dequantize_q8_0(kc), rs_dequantize_q8_0(vc)
+    elif kv_type == GGML_BF16:
+        kc, vc = f32_to_bf16_bits(kf), f32_to_bf16_bits(vf)
+        kd, vd = bf16_bits_to_f32(kc).reshape(kf.shape), bf16_bits_to_f32(vc).reshape(vf.shape)
     else:
         raise ValueError(kv_type)
     return q, kc, vc, kd.reshape(n_kv, H_kv, D), vd.reshape(n_kv, H_kv, D)
