@@ -204,6 +204,99 @@ def quantize_q8_0_rows(torch, x):
     return out.view(n, k // 32 * 34)
 
 
+def bench_prefill(kb, torch, dev, steps, warmup):
+    """config[2] attention half: causal prefill of 4,096 tokens, 24 Q / 4 KV heads, D 256, bf16 Q/K/V, through
+    kb_flash_attn_ext (tcgen05 kernel). Two independent Q/K/V sets alternate so inputs exceed L2."""
+    T = 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    sets = []
+    for _ in range(2):
+        q = torch.randn(1, T, H, D, device=dev, generator=gen).bfloat16().float()
+        k = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
+        v = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
+        sets.append((q, k, v, kb.kv_cache_view(k, kb.BF16, H_KV, D), kb.kv_cache_view(v, kb.BF16, H_KV, D)))
+    out = torch.empty(1, T, H, D, device=dev)
+    for i in range(warmup):
+        q, _, _, kv, vv = sets[i % 2]
+        kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        q, _, _, kv, vv = sets[i % 2]
+        kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    flops = 2.0 * D * H * T * (T + 1)  # causal pairs only, QK^T and PV
+    tf = flops / (us * 1e-6) / 1e12
+    pk, kind = measured_peaks()
+    return {"value": round(tf, 1), "unit": "TFLOP/s", "us_per_layer": round(us, 2), "kv_type": "bf16",
+            "workload": "config[2] causal prefill, 4096 tokens, 24 Q / 4 KV heads, D 256, bf16",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(tf / pk["bf16_tflops"], 4), "peak_kind": kind + " burst",
+                         "frac_of_sustained": round(tf / pk.get("bf16_tflops_sustained", pk["bf16_tflops"]), 4),
+                         "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic("fa_prefill_bf16_4096")}}
+
+
+def bench_gdn(kb, torch, dev, steps, warmup):
+    """config[1]: gated DeltaNet 4-token verify step with K = 4 snapshots (48 value / 16 key heads, d 128), in
+    klein's cache form (state updated in place, f16 snapshots), over 48 layers so the states exceed L2."""
+    L_, T, K, S, Hv, Hk = 48, 4, 4, 128, 48, 16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    q = torch.nn.functional.normalize(torch.randn(1, T, Hk, S, device=dev, generator=gen), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(1, T, Hk, S, device=dev, generator=gen), dim=-1)
+    v = torch.randn(1, T, Hv, S, device=dev, generator=gen)
+    g = -torch.nn.functional.softplus(torch.randn(1, T, Hv, 1, device=dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(1, T, Hv, 1, device=dev, generator=gen))
+    states = [torch.randn(1, Hv, S, S, device=dev, generator=gen) * 0.02 for _ in range(L_)]
+    snaps = [torch.zeros(K - 1, S * S * Hv, dtype=torch.float16, device=dev) for _ in range(L_)]
+    attn = torch.empty(1, T, Hv, S, device=dev)
+    import ctypes
+
+    L = kb.lib()
+    ins = [kb.from_torch(x) for x in (q, k, v, g, beta)]
+    outs = [(kb.from_torch(states[l]), kb.from_torch(snaps[l])) for l in range(L_)]
+    at = kb.from_torch(attn)
+
+    def step(stream):
+        for l in range(L_):
+            rc = L.kb_gated_delta_net_cache(*[ctypes.byref(x) for x in ins], ctypes.byref(outs[l][0]),
+                                            ctypes.byref(outs[l][1]), K, ctypes.byref(at), ctypes.c_void_p(stream))
+            if rc != 0:
+                raise kb.KbError("kb_gated_delta_net_cache", rc)
+
+    # the 48-layer step as one CUDA graph (klein's ggml-cuda backend replays its step graphs the same way)
+    side = torch.cuda.Stream(dev)
+    with torch.cuda.stream(side):
+        step(side.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(torch.cuda.current_stream(dev).cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    us = e0.elapsed_time(e1) * 1e3 / (steps * L_)
+    nbytes = S * S * Hv * 4 * 2 + (K - 1) * S * S * Hv * 2 + (2 * T * Hk * S + 2 * T * Hv * S + 2 * T * Hv) * 4
+    gbs = nbytes / (us * 1e-6) / 1e9
+    pk, _ = measured_peaks()
+    return {"value": round(us, 2), "unit": "us/layer",
+            "workload": "config[1] DeltaNet verify step: 4 tokens, K = 4 f16 snapshots, 48/16 heads, d 128",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes_per_launch": nbytes,
+                         "traffic": ncu_traffic("gdn_recurrent_verify")}}
+
+
 def make_layers(kb, torch, dev, gen, n_kv, kv_type):
     layers = []
     for _ in range(LAYERS):
@@ -390,6 +483,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 "h2d_bytes_per_step": LAYERS * N_Q * H * D * 4, "d2h_bytes_per_step": LAYERS * N_Q * H * D * 4},
         "clocks": clk.summary(),
     }
+    if not args.no_secondary and world == 1:
+        del layers[:]
+        torch.cuda.empty_cache()
+        secondary["prefill_bf16_4096"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
+        secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

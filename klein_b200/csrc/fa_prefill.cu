@@ -31,7 +31,8 @@ constexpr int BN = 64;                        // cells per K/V block
 constexpr int QTILE = BM * D * 2;             // 64 KiB: 4 chunks of [128 rows][128 B]
 constexpr int KVTILE = BN * D * 2;            // 32 KiB: 4 chunks of [64 cells][128 B]
 constexpr int NSTAGE = 2;
-constexpr int THREADS = 6 * 32;
+constexpr int SOFTMAX_WARPS = 8;               // two warpgroups: each owns half of a row's 64 cells
+constexpr int THREADS = (SOFTMAX_WARPS + 2) * 32;
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 units: rescale O only when the max grows by > 2^8
 
@@ -41,6 +42,8 @@ struct Smem {
     uint8_t v[NSTAGE][KVTILE];
     uint64_t k_full[NSTAGE], k_empty[NSTAGE], v_full[NSTAGE], v_empty[NSTAGE];
     uint64_t s_full[NSTAGE], s_free[NSTAGE], p_full[NSTAGE], o_done;
+    float xmax[2][2][BM];                      // [block parity][half][row]: half-row maxima exchanged per block
+    float xl[2][BM];                           // [half][row]: half-row softmax sums for the epilogue
     uint32_t tmem_base;
     int failed;
 };
@@ -96,8 +99,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.v_full[s], 1);
             mbar_init(&sm.v_empty[s], 1);
             mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.s_free[s], 4);
-            mbar_init(&sm.p_full[s], 4);
+            mbar_init(&sm.s_free[s], SOFTMAX_WARPS);
+            mbar_init(&sm.p_full[s], SOFTMAX_WARPS);
         }
         mbar_init(&sm.o_done, 1);
         sm.failed = 0;
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
 
-    if (warp == 4) {
+    if (warp == SOFTMAX_WARPS) {
         // -------------------------------------------------------------------------------- TMA producer
         if (lane == 0 && nb > 0) {
             tma_prefetch_desc(&tmK);
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tma_load_4d(sm.v[s] + c * (BN * 128), &tmV, &sm.v_full[s], c * 64, hk, cell, kb3);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == SOFTMAX_WARPS + 1) {
         // -------------------------------------------------------------------------------- MMA issuer
         if (lane == 0 && nb > 0) {
             constexpr uint32_t idS = umma_idesc_f16(FMT, BM, BN, false, false);
@@ -198,10 +201,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!*failed) issue_pv(nb - 1);
         }
     } else {
-        // -------------------------------------------------------------------------------- softmax (warps 0-3)
-        const int r = warp * 32 + lane;           // query row of this thread = TMEM lane
+        // -------------------------------------------------------------------------------- softmax (warps 0-7)
+        // row r = TMEM lane (warp % 4) * 32 + lane; half = warp / 4 owns cells [32 half, 32 half + 32) of each
+        // 64-cell block and dims [128 half, 128 half + 128) of O. The two halves of a row agree on its max
+        // through shared memory once per block. Every thread reaches every named barrier, failed or not.
+        const int half = warp >> 2;
+        const int r = (warp & 3) * 32 + lane;
         const int qi = q0 + r;
-        const uint32_t lane_addr = tmem + ((uint32_t) (warp * 32) << 16);
+        const uint32_t lane_addr = tmem + ((uint32_t) ((warp & 3) * 32) << 16);
         const __half* mrow = nullptr;
         float slope = 1.0f;
         if (p.mask && qi < p.n_q)
@@ -209,90 +216,125 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (p.max_bias > 0.0f)
             slope = h < p.n_head_log2 ? powf(p.m0, (float) (h + 1)) : powf(p.m1, (float) (2 * (h - p.n_head_log2) + 1));
         const int64_t row_pos = p.pos0 + q0;  // position of the tile's first query
+        const float scl = p.scale_log2;
         float m = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nb && ok; ++j) {
+        for (int j = 0; j < nb; ++j) {
             const int s = j % NSTAGE;
-            if (!wait_or_fail(&sm.s_full[s], (j / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sv[2][32];
-            tmem_ld32(lane_addr + TM_S + s * BN, sv[0]);
-            tmem_ld32(lane_addr + TM_S + s * BN + 32, sv[1]);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.s_free[s]);
-
-            const int64_t cell0 = c_lo + (int64_t) j * BN;
-            // every row of the tile sees every cell of the block: no per-element checks
-            const bool plain = !mrow && !p.has_softcap && cell0 + BN <= p.n_kv &&
-                               (!p.causal || (cell0 >= p.kv_lo && cell0 + BN - 1 <= row_pos)) && q0 + BM <= p.n_q;
-            float sc[BN];
-            float bmax = -INFINITY;
+            ok = ok && wait_or_fail(&sm.s_full[s], (j / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            ok = __all_sync(0xffffffffu, ok);
+            uint32_t sv[32];
+            float bm = -INFINITY;
+            const int64_t blk0 = c_lo + (int64_t) j * BN;
+            const bool plain = !mrow && !p.has_softcap && blk0 + BN <= p.n_kv &&
+                               (!p.causal || (blk0 >= p.kv_lo && blk0 + BN - 1 <= row_pos)) && q0 + BM <= p.n_q;
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(lane_addr + TM_S + s * BN + half * 32, sv);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.s_free[s]);
+                if (plain) {
+                    // scale > 0: the max of the scaled scores is the scaled max of the raw ones
+                    float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < BN; ++e) {
-                const float x = __uint_as_float(sv[e >> 5][e & 31]);
-                sc[e] = plain ? x * p.scale_log2 : prefill_score(p, x, cell0 + e, qi, mrow, slope);
-                bmax = fmaxf(bmax, sc[e]);
+                    for (int e = 0; e < 32; e += 4) {
+                        a0 = fmaxf(a0, __uint_as_float(sv[e]));
+                        a1 = fmaxf(a1, __uint_as_float(sv[e + 1]));
+                        a2 = fmaxf(a2, __uint_as_float(sv[e + 2]));
+                        a3 = fmaxf(a3, __uint_as_float(sv[e + 3]));
+                    }
+                    bm = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * scl;
+                } else {
+                    const int64_t cell0 = blk0 + half * 32;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const float sc = prefill_score(p, __uint_as_float(sv[e]), cell0 + e, qi, mrow, slope);
+                        sv[e] = __float_as_uint(sc);
+                        bm = fmaxf(bm, sc);
+                    }
+                }
+                sm.xmax[j & 1][half][r] = bm;
             }
+            named_bar_sync(1, SOFTMAX_WARPS * 32);
+            if (!ok) continue;
+            const float bmax = fmaxf(bm, sm.xmax[j & 1][half ^ 1][r]);
             // lazy rescale
             float m_use = m;
             bool rescale = false;
-            if (bmax > m + RESCALE_THRESHOLD || m == -INFINITY) {
-                if (bmax != -INFINITY) {
-                    m_use = bmax;
-                    rescale = m != -INFINITY;
-                }
+            if ((bmax > m + RESCALE_THRESHOLD || m == -INFINITY) && bmax != -INFINITY) {
+                m_use = bmax;
+                rescale = m != -INFINITY;
             }
             // PV_{j-1} must be complete before O is rescaled or P_j overwrites P_{j-2}'s buffer
-            if (j >= 1 && !wait_or_fail(&sm.o_done, (j - 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) {
-                ok = false;
-                break;
-            }
+            if (j >= 1) ok = wait_or_fail(&sm.o_done, (j - 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) continue;
             tc_fence_after();
             if (__any_sync(0xffffffffu, rescale)) {
                 const float alpha = rescale ? exp2f(m - m_use) : 1.0f;
                 l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c = 0; c < D / 64; ++c) {
                     uint32_t ov[32];
-                    tmem_ld32(lane_addr + TM_O + c * 32, ov);
+                    const uint32_t ta = lane_addr + TM_O + half * (D / 2) + c * 32;
+                    tmem_ld32(ta, ov);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                    tmem_st32(lane_addr + TM_O + c * 32, ov);
+                    tmem_st32(ta, ov);
                 }
                 tmem_wait_st();
             }
             m = m_use;
             const float mref = m == -INFINITY ? 0.0f : m;
-            uint32_t pk[32];
-            float lsum = 0.0f;
+            uint32_t pk[16];
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            if (plain) {
 #pragma unroll
-            for (int e = 0; e < BN; e += 2) {
-                const float p0 = exp2f(sc[e] - mref), p1 = exp2f(sc[e + 1] - mref);
-                lsum += p0 + p1;
-                pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
+                for (int e = 0; e < 32; e += 4) {
+                    const float p0 = exp2f(fmaf(__uint_as_float(sv[e]), scl, -mref));
+                    const float p1 = exp2f(fmaf(__uint_as_float(sv[e + 1]), scl, -mref));
+                    const float p2 = exp2f(fmaf(__uint_as_float(sv[e + 2]), scl, -mref));
+                    const float p3 = exp2f(fmaf(__uint_as_float(sv[e + 3]), scl, -mref));
+                    s0 += p0, s1 += p1, s2 += p2, s3 += p3;
+                    pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
+                    pk[(e >> 1) + 1] = FMT == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float p0 = exp2f(__uint_as_float(sv[e]) - mref), p1 = exp2f(__uint_as_float(sv[e + 1]) - mref);
+                    const float p2 = exp2f(__uint_as_float(sv[e + 2]) - mref), p3 = exp2f(__uint_as_float(sv[e + 3]) - mref);
+                    s0 += p0, s1 += p1, s2 += p2, s3 += p3;
+                    pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
+                    pk[(e >> 1) + 1] = FMT == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
+                }
             }
-            l += lsum;
-            tmem_st32(lane_addr + TM_P + s * 32, pk);
+            l += (s0 + s1) + (s2 + s3);
+            tmem_st16(lane_addr + TM_P + s * 32 + half * 16, pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.p_full[s]);
         }
-        // epilogue: O / l for this row
-        if (ok && nb > 0 && wait_or_fail(&sm.o_done, (nb - 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) {
+        // epilogue: O / (l_half0 + l_half1) for this row, each half writing its 128 dims
+        sm.xl[half][r] = l;
+        named_bar_sync(1, SOFTMAX_WARPS * 32);
+        const float lt = sm.xl[0][r] + sm.xl[1][r];
+        if (nb > 0) {
+            ok = ok && wait_or_fail(&sm.o_done, (nb - 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            ok = __all_sync(0xffffffffu, ok);
+        }
+        float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + (int64_t) qi * p.d_nb2 + b * p.d_nb3) + half * (D / 2);
+        if (ok && nb > 0) {
             tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + (int64_t) qi * p.d_nb2 + b * p.d_nb3);
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < D / 64; ++c) {
                 uint32_t ov[32];
-                tmem_ld32(lane_addr + TM_O + c * 32, ov);
+                tmem_ld32(lane_addr + TM_O + half * (D / 2) + c * 32, ov);
                 tmem_wait_ld();
                 if (qi < p.n_q) {
 #pragma unroll
@@ -303,8 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
         } else if (nb == 0 && qi < p.n_q) {
-            float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + (int64_t) qi * p.d_nb2 + b * p.d_nb3);
-            for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(out + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int d = 0; d < D / 2; d += 4) *reinterpret_cast<float4*>(out + d) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     tc_fence_before();

@@ -63,23 +63,39 @@ __global__ void __launch_bounds__(WARPS * 32) gdn_recurrent_kernel(const GdnPara
 #pragma unroll
     for (int c = 0; c < CPW; ++c) M[c] = *reinterpret_cast<const float4*>(s0 + (int64_t) (j0 + c) * S + 4 * lane);
 
-    for (int t = 0; t < p.T; ++t) {
-        const float4 k4 = *reinterpret_cast<const float4*>(p.k + sq_k * p.k_nb3 + t * p.k_nb2 + hk * p.k_nb1 + lane * 16);
-        const float4 q4 = *reinterpret_cast<const float4*>(p.q + sq_q * p.q_nb3 + t * p.q_nb2 + hk * p.q_nb1 + lane * 16);
+    // token inputs, loaded one token ahead of the math that uses them
+    struct TokIn {
+        float4 k4, q4, g4;
+        float v[CPW];
+        float beta;
+    };
+    auto load_tok = [&](int t, TokIn& in) {
+        in.k4 = *reinterpret_cast<const float4*>(p.k + sq_k * p.k_nb3 + t * p.k_nb2 + hk * p.k_nb1 + lane * 16);
+        in.q4 = *reinterpret_cast<const float4*>(p.q + sq_q * p.q_nb3 + t * p.q_nb2 + hk * p.q_nb1 + lane * 16);
         const char* vrow = p.v + seq * p.v_nb3 + t * p.v_nb2 + h * p.v_nb1;
-        const float beta = *reinterpret_cast<const float*>(p.beta + seq * p.b_nb3 + t * p.b_nb2 + h * p.b_nb1);
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) in.v[c] = *reinterpret_cast<const float*>(vrow + (int64_t) (j0 + c) * 4);
+        in.beta = *reinterpret_cast<const float*>(p.beta + seq * p.b_nb3 + t * p.b_nb2 + h * p.b_nb1);
         const char* grow = p.g + seq * p.g_nb3 + t * p.g_nb2 + h * p.g_nb1;
+        if (KDA) in.g4 = *reinterpret_cast<const float4*>(grow + lane * 16);
+        else in.g4.x = *reinterpret_cast<const float*>(grow);
+    };
+    TokIn cur, nxt;
+    load_tok(0, cur);
+    for (int t = 0; t < p.T; ++t) {
+        if (t + 1 < p.T) load_tok(t + 1, nxt);
+        const float4 k4 = cur.k4, q4 = cur.q4;
+        const float beta = cur.beta;
         float4 e;
         if (KDA) {
-            const float4 g4 = *reinterpret_cast<const float4*>(grow + lane * 16);
-            e = make_float4(expf(g4.x), expf(g4.y), expf(g4.z), expf(g4.w));
+            e = make_float4(expf(cur.g4.x), expf(cur.g4.y), expf(cur.g4.z), expf(cur.g4.w));
         } else {
-            const float eg = expf(*reinterpret_cast<const float*>(grow));
+            const float eg = expf(cur.g4.x);
             e = make_float4(eg, eg, eg, eg);
         }
         float vj[CPW];
 #pragma unroll
-        for (int c = 0; c < CPW; ++c) vj[c] = *reinterpret_cast<const float*>(vrow + (int64_t) (j0 + c) * 4);
+        for (int c = 0; c < CPW; ++c) vj[c] = cur.v[c];
         float sk[CPW];
 #pragma unroll
         for (int c = 0; c < CPW; ++c) {
@@ -126,6 +142,7 @@ __global__ void __launch_bounds__(WARPS * 32) gdn_recurrent_kernel(const GdnPara
 #pragma unroll
             for (int c = 0; c < CPW; ++c) store4(base, type, e0 + (int64_t) (j0 + c) * S + 4 * lane, M[c]);
         }
+        cur = nxt;
     }
 }
 
