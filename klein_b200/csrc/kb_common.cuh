@@ -10,7 +10,7 @@
 namespace kb {
 
 // error codes written to the device error word (kb_device_error)
-enum : int { DEV_ERR_NONE = 0, DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_WAIT_PEER = 3 };
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_WAIT_PEER = 3, DEV_ERR_ALIGN = 5 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
