@@ -264,7 +264,8 @@ def bench_gdn(kb, torch, dev, steps, warmup):
     def step(stream):
         for l in range(L_):
             rc = L.kb_gated_delta_net_cache(*[ctypes.byref(x) for x in ins], ctypes.byref(outs[l][0]),
-                                            ctypes.byref(outs[l][1]), K, ctypes.byref(at), ctypes.c_void_p(stream))
+                                            ctypes.byref(outs[l][1]), K, ctypes.byref(at), None, 0,
+                                            ctypes.c_void_p(stream))
             if rc != 0:
                 raise kb.KbError("kb_gated_delta_net_cache", rc)
 

@@ -129,11 +129,16 @@ size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, c
  *   dst   f32 [S*H_v, T*n_seqs + K*S*n_seqs] contiguous: attention output [S, H_v, T, n_seqs], then K state slots
  *         [S, S, H_v, n_seqs] most recent first (slot s = state s tokens before the end); only slots < min(T, K)
  *         are written.
+ *   scratch  optional device memory (16-byte aligned). Calls with T - min(T, K) + 1 >= 64 tokens and the scalar
+ *         gate run the chunked tensor-core form (64-token chunks) when scratch holds at least one chunk's records
+ *         for every head (n_seqs * H_v * 65,792 bytes); kb_gated_delta_net_scratch_bytes gives the size for one
+ *         pass, less runs several passes. Without scratch, or for the per-channel gate, the recurrent kernel
+ *         processes every token (same results within the stated tolerance, slower for long prompts).
  * Supported here: S = 128; every pointer and row stride 16-byte aligned.
  */
 kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
                              const kb_tensor* beta, const kb_tensor* state, int32_t K, const kb_tensor* dst,
-                             void* stream);
+                             void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * The same recurrence writing straight into klein's recurrent-state cache, i.e. ggml_gated_delta_net followed
@@ -143,10 +148,16 @@ kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_te
  *          slot s (1 <= s < min(T, K)) goes to row s-1, converted with round-to-nearest-even; may be NULL when
  *          min(T, K) == 1
  *   attn   f32 [S, H_v, T, n_seqs] attention output (any row strides)
+ *   scratch as for kb_gated_delta_net
  */
 kb_status kb_gated_delta_net_cache(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
                                    const kb_tensor* beta, const kb_tensor* state, const kb_tensor* snap, int32_t K,
-                                   const kb_tensor* attn, void* stream);
+                                   const kb_tensor* attn, void* scratch, size_t scratch_bytes, void* stream);
+
+/* Scratch for one pass of the chunked DeltaNet form over these operands (v: [S, H_v, T, n_seqs], g: the gate);
+ * 0 when the call would not use it (short T, per-channel gate). A ggml-cuda shim takes it from the backend's
+ * pool (ggml_cuda_pool_alloc), as launch_fattn does for its partials (fattn-common.cuh:1019-1021). */
+size_t kb_gated_delta_net_scratch_bytes(const kb_tensor* v, const kb_tensor* g, int32_t K);
 
 /*
  * State::rollback_recurrent (state.cpp:162-183): after s rejected draft tokens, for each of n_layers DeltaNet

@@ -33,6 +33,7 @@ EXPORTED = [
     "kb_lse_combine",
     "kb_gated_delta_net",
     "kb_gated_delta_net_cache",
+    "kb_gated_delta_net_scratch_bytes",
     "kb_rollback_recurrent",
     "kb_set_rows",
     "kb_flash_attn_ext_scratch_bytes",
@@ -83,9 +84,11 @@ def lib():
                                                 P(KbTensor), c_void_p]
         T4 = [P(KbTensor)] * 6
         L.kb_gated_delta_net.restype = c_int32
-        L.kb_gated_delta_net.argtypes = T4 + [c_int32, P(KbTensor), c_void_p]
+        L.kb_gated_delta_net.argtypes = T4 + [c_int32, P(KbTensor), c_void_p, c_size_t, c_void_p]
         L.kb_gated_delta_net_cache.restype = c_int32
-        L.kb_gated_delta_net_cache.argtypes = T4 + [P(KbTensor), c_int32, P(KbTensor), c_void_p]
+        L.kb_gated_delta_net_cache.argtypes = T4 + [P(KbTensor), c_int32, P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_gated_delta_net_scratch_bytes.restype = c_size_t
+        L.kb_gated_delta_net_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), c_int32]
         L.kb_rollback_recurrent.restype = c_int32
         L.kb_rollback_recurrent.argtypes = [c_int32, c_void_p, c_int64, c_void_p, c_int32, c_void_p, c_int64, c_int32,
                                             c_int32, c_void_p]
@@ -210,10 +213,26 @@ def _stream(x, stream):
     return torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
 
 
-def gated_delta_net(q, k, v, g, beta, state, K: int, stream=None):
+def gdn_scratch(v, g, K: int, scratch=None):
+    """(pointer, bytes) of DeltaNet scratch: `scratch` if given (a torch uint8 tensor, or False for none), else a
+    new buffer of kb_gated_delta_net_scratch_bytes (none when the call does not use it)."""
+    import torch
+
+    if scratch is False:
+        return None, 0
+    if scratch is None:
+        n = lib().kb_gated_delta_net_scratch_bytes(ctypes.byref(from_torch(v)), ctypes.byref(from_torch(g)), K)
+        if n == 0:
+            return None, 0
+        scratch = torch.empty(n, dtype=torch.uint8, device=v.device)
+    return scratch, scratch.numel()
+
+
+def gated_delta_net(q, k, v, g, beta, state, K: int, scratch=None, stream=None):
     """GGML_OP_GATED_DELTA_NET through kb_gated_delta_net. Torch f32 tensors in ggml order reversed:
     q, k [n_seqs][T][H_k][S]; v [n_seqs][T][H_v][S]; g [n_seqs][T][H_v][1 or S]; beta [n_seqs][T][H_v][1];
-    state [n_seqs][H_v][S][S]. Returns ggml's packed f32 result as a flat tensor."""
+    state [n_seqs][H_v][S][S]. Returns ggml's packed f32 result as a flat tensor. scratch: see gdn_scratch
+    (False forces the recurrent kernel for every token)."""
     import torch
 
     n_seqs, T, H_v, S = v.shape
@@ -221,12 +240,15 @@ def gated_delta_net(q, k, v, g, beta, state, K: int, stream=None):
     out = torch.empty(n, dtype=torch.float32, device=v.device)
     dt = kb_tensor(out.data_ptr(), F32, [S * H_v, T * n_seqs + K * S * n_seqs, 1, 1], [4, S * H_v * 4])
     args = [from_torch(x) for x in (q, k, v, g, beta.reshape(n_seqs, T, H_v, 1), state)]
-    rc = lib().kb_gated_delta_net(*[ctypes.byref(a) for a in args], K, ctypes.byref(dt), c_void_p(_stream(v, stream)))
+    buf, nbytes = gdn_scratch(v, g, K, scratch)
+    rc = lib().kb_gated_delta_net(*[ctypes.byref(a) for a in args], K, ctypes.byref(dt),
+                                  c_void_p(buf.data_ptr() if buf is not None else None), nbytes,
+                                  c_void_p(_stream(v, stream)))
     check("kb_gated_delta_net", rc)
     return out
 
 
-def gated_delta_net_cache(q, k, v, g, beta, state, snap, K: int, attn=None, stream=None):
+def gated_delta_net_cache(q, k, v, g, beta, state, snap, K: int, attn=None, scratch=None, stream=None):
     """klein's fused form through kb_gated_delta_net_cache: state (f32 [n_seqs][H_v][S][S]) is updated in place
     to slot 0; snap (f16/bf16/f32 [K-1][S*S*H_v*n_seqs] or None) receives slots 1..min(T,K)-1.
     Returns the attention output f32 [n_seqs][T][H_v][S]."""
@@ -238,8 +260,10 @@ def gated_delta_net_cache(q, k, v, g, beta, state, snap, K: int, attn=None, stre
     args = [from_torch(x) for x in (q, k, v, g, beta.reshape(n_seqs, T, H_v, 1), state)]
     st = from_torch(snap) if snap is not None else None
     at = from_torch(attn)
+    buf, nbytes = gdn_scratch(v, g, K, scratch)
     rc = lib().kb_gated_delta_net_cache(*[ctypes.byref(a) for a in args], ctypes.byref(st) if st is not None else None, K,
-                                        ctypes.byref(at), c_void_p(_stream(v, stream)))
+                                        ctypes.byref(at), c_void_p(buf.data_ptr() if buf is not None else None), nbytes,
+                                        c_void_p(_stream(v, stream)))
     check("kb_gated_delta_net_cache", rc)
     return attn
 

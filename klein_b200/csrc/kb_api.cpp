@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -409,13 +410,93 @@ kb_status gdn_inputs(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
     return KB_OK;
 }
 
+// Prompt-length calls run the chunked tensor-core form over tokens [0, Tc), Tc = T - min(T, K) + 1: its final
+// state is slot min(T, K) - 1. The remaining min(T, K) - 1 tokens, whose per-token states are the other slots,
+// run through the recurrent kernel from there.
+constexpr int64_t GDN_CHUNKED_MIN_TOKENS = 64;
+
+int64_t gdn_chunked_tokens(int64_t T, int32_t K) { return T - std::min<int64_t>(T, K) + 1; }
+
+size_t gdn_chunked_bytes(int64_t T, int32_t K, int64_t H_v, int64_t n_seqs, bool kda) {
+    const int64_t Tc = gdn_chunked_tokens(T, K);
+    if (kda || Tc < GDN_CHUNKED_MIN_TOKENS) return 0;
+    return (size_t) (n_seqs * H_v * ((Tc + kb::GDN_CHUNK - 1) / kb::GDN_CHUNK) * kb::GDN_REC_BYTES);
+}
+
+// the chunked kernel writes its outputs by TMA: f32 (value dim, head, token, sequence), box 128 x 1 x 64 x 1,
+// tokens clipped at tok_end
+bool encode_attn_map(const kb::GdnParams& p, int64_t tok_end, CUtensorMap* map) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t) p.S, (cuuint64_t) p.H_v, (cuuint64_t) tok_end, (cuuint64_t) p.n_seqs};
+    const cuuint64_t strides[3] = {(cuuint64_t) p.a_nb1, (cuuint64_t) p.a_nb2, (cuuint64_t) p.a_nb3};
+    const cuuint32_t box[4] = {(cuuint32_t) p.S, 1, (cuuint32_t) kb::GDN_CHUNK, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.attn, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+kb_status gdn_run(const kb::GdnParams& p, bool packed, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+    const int64_t S = p.S, T = p.T, n_w = std::min<int64_t>(T, p.K), Tc = gdn_chunked_tokens(T, p.K);
+    const int64_t per_chunk = (int64_t) p.n_seqs * p.H_v * kb::GDN_REC_BYTES;
+    const bool out_ok = aligned16(reinterpret_cast<uintptr_t>(p.attn)) && aligned16(p.a_nb1) && aligned16(p.a_nb2) &&
+                        aligned16(p.a_nb3);
+    const bool chunked = gdn_chunked_bytes(T, p.K, p.H_v, p.n_seqs, p.kda) > 0 && scratch && out_ok &&
+                         (int64_t) scratch_bytes >= per_chunk && aligned16(reinterpret_cast<uintptr_t>(scratch));
+    if (!chunked) return kb::launch_gdn_recurrent(p, stream) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+    // the chunked part leaves slot n_w - 1: in the packed result, or in the f32 state (+ its snapshot row)
+    float* s_out;
+    char* snap = nullptr;
+    if (packed) {
+        s_out = reinterpret_cast<float*>(n_w == 1 ? p.slot0 : p.slots + (n_w - 2) * p.slots_stride);
+    } else {
+        s_out = reinterpret_cast<float*>(p.slot0);
+        if (n_w >= 2) snap = p.slots + (n_w - 2) * p.slots_stride;
+    }
+    const int64_t state_stride = S * S * p.H_v;  // floats per sequence
+    kb::GdnChunkParams c{};
+    c.in = p;
+    c.rec = static_cast<char*>(scratch);
+    c.s_out = s_out;
+    c.s_out_seq_stride = state_stride;
+    c.snap_type = p.slots_type;
+    c.err = kb::device_error_word();
+    c.wait_ns = g_wait_ns;
+    const int64_t n_chunks = (Tc + kb::GDN_CHUNK - 1) / kb::GDN_CHUNK;
+    const int64_t per_pass = std::min<int64_t>(n_chunks, (int64_t) scratch_bytes / per_chunk);
+    for (int64_t c0 = 0; c0 < n_chunks; c0 += per_pass) {
+        const int64_t nc = std::min(per_pass, n_chunks - c0);
+        c.tok0 = c0 * kb::GDN_CHUNK;
+        c.n_tok = std::min(nc * kb::GDN_CHUNK, Tc - c.tok0);
+        c.n_chunks = (int) nc;
+        c.s0 = c0 == 0 ? p.s0 : s_out;
+        c.s0_seq_stride = c0 == 0 ? p.s0_seq_stride : state_stride;
+        c.snap = c0 + nc >= n_chunks ? snap : nullptr;
+        CUtensorMap tmO;
+        if (!encode_attn_map(p, c.tok0 + c.n_tok, &tmO)) return KB_ERR_CUDA;
+        if (kb::launch_gdn_chunked(c, tmO, stream) != cudaSuccess) return KB_ERR_CUDA;
+    }
+    if (n_w == 1) return KB_OK;
+    kb::GdnParams t = p;
+    t.q += Tc * p.q_nb2;
+    t.k += Tc * p.k_nb2;
+    t.v += Tc * p.v_nb2;
+    t.g += Tc * p.g_nb2;
+    t.beta += Tc * p.b_nb2;
+    t.attn += Tc * p.a_nb2;
+    t.T = (int) (n_w - 1);
+    t.s0 = s_out;
+    t.s0_seq_stride = state_stride;
+    return kb::launch_gdn_recurrent(t, stream) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
 }  // namespace
 
 extern "C" {
 
 kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
                              const kb_tensor* beta, const kb_tensor* state, int32_t K, const kb_tensor* dst,
-                             void* stream) {
+                             void* scratch, size_t scratch_bytes, void* stream) {
     kb::GdnParams p{};
     kb_status st = gdn_inputs(q, k, v, g, beta, state, K, &p);
     if (st != KB_OK) return st;
@@ -434,12 +515,12 @@ kb_status kb_gated_delta_net(const kb_tensor* q, const kb_tensor* k, const kb_te
     p.slots = base + attn_bytes + slot_bytes;
     p.slots_stride = slot_bytes;
     p.slots_type = 0;
-    return kb::launch_gdn_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+    return gdn_run(p, true, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
 kb_status kb_gated_delta_net_cache(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* g,
                                    const kb_tensor* beta, const kb_tensor* state, const kb_tensor* snap, int32_t K,
-                                   const kb_tensor* attn, void* stream) {
+                                   const kb_tensor* attn, void* scratch, size_t scratch_bytes, void* stream) {
     kb::GdnParams p{};
     kb_status st = gdn_inputs(q, k, v, g, beta, state, K, &p);
     if (st != KB_OK) return st;
@@ -462,7 +543,12 @@ kb_status kb_gated_delta_net_cache(const kb_tensor* q, const kb_tensor* k, const
     p.attn = static_cast<char*>(attn->data);
     p.a_nb1 = attn->nb[1], p.a_nb2 = attn->nb[2], p.a_nb3 = attn->nb[3];
     p.slot0 = static_cast<char*>(state->data);  // slot 0 overwrites the state it was computed from
-    return kb::launch_gdn_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+    return gdn_run(p, false, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t kb_gated_delta_net_scratch_bytes(const kb_tensor* v, const kb_tensor* g, int32_t K) {
+    if (!v || !g || K < 1 || v->ne[0] != 128) return 0;
+    return gdn_chunked_bytes(v->ne[2], K, v->ne[1], v->ne[3], g->ne[0] != 1);
 }
 
 kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream) {

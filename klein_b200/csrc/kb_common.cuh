@@ -92,6 +92,15 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// untiled bulk copy global -> shared (both addresses 16-byte aligned, bytes a multiple of 16), completion counted
+// on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // L2 policy for data read exactly once (streamed KV): evict first
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;

@@ -1,6 +1,7 @@
 // Internal parameter blocks of the DeltaNet, KV-write and rollback kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -31,6 +32,35 @@ struct GdnParams {
 };
 
 cudaError_t launch_gdn_recurrent(const GdnParams& p, cudaStream_t stream);
+
+// Chunked form (scalar gate, S = 128): tokens [tok0, tok0 + n_tok) in chunks of GDN_CHUNK. The prep kernel writes
+// one record per (sequence, value head, chunk) into caller scratch; the state kernel consumes them in order.
+constexpr int GDN_CHUNK = 64;
+constexpr int GDN_REC_W = 0;          // W = T^-1 diag(beta Gamma) K, f16 image [2][64 s][64 i], 128B-swizzled
+constexpr int GDN_REC_AQ_HI = 16384;  // A_qk hi, f16 image [64 t][64 s]
+constexpr int GDN_REC_AQ_LO = 24576;  // A_qk lo
+constexpr int GDN_REC_U = 32768;      // U~ = T^-1 diag(beta) V, f32 [64 s][128 j]
+constexpr int GDN_REC_G = 65536;      // G, f32 [64]: running sums of the log-gates within the chunk
+constexpr int64_t GDN_REC_BYTES = 65536 + 256;
+
+struct GdnChunkParams {
+    GdnParams in;                     // inputs and the attention output (its slot fields are unused)
+    int64_t tok0, n_tok;              // token range of this pass
+    int n_chunks;                     // ceil(n_tok / GDN_CHUNK)
+    char* rec;                        // [n_seqs][H_v][n_chunks] records of GDN_REC_BYTES, 16-byte aligned
+    const float* s0;                  // state before tok0 (f32, transposed), per-sequence stride in floats
+    int64_t s0_seq_stride;
+    float* s_out;                     // state after the pass (may alias s0)
+    int64_t s_out_seq_stride;
+    char* snap;                       // optional copy of s_out in snap_type (0 f32, 1 f16, 2 bf16), element
+    int snap_type;                    //   ((seq * H_v + h) * S + j) * S + i
+    int* err;
+    uint64_t wait_ns;
+};
+
+// tmO: 4-d f32 map over the attention output (value dim, head, token, sequence) with box {128, 1, 64, 1}, its
+// token extent ending at tok0 + n_tok
+cudaError_t launch_gdn_chunked(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream);
 
 // Cache row write (ggml_set_rows): dst row idx[r] of every (i2, i3) <- src row r converted to dst_type.
 struct SetRowsParams {

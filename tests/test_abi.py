@@ -89,7 +89,8 @@ def test_gdn_descriptors_validate(kb):
     S, H, T, K = 128, 48, 4, 4
     out = torch.zeros(S * H * T + K * S * S * H)
     dt = kb.kb_tensor(out.data_ptr(), kb.F32, [S * H, T + K * S, 1, 1], [4, S * H * 4])
-    call = lambda a, d=dt, K_=K: kb.lib().kb_gated_delta_net(*[ctypes.byref(x) for x in a], K_, ctypes.byref(d), None)
+    call = lambda a, d=dt, K_=K: kb.lib().kb_gated_delta_net(*[ctypes.byref(x) for x in a], K_, ctypes.byref(d), None, 0,
+                                                             None)
     assert call(args) == kb.KB_ERR_CUDA  # validation passed; no device here
     bad = list(args)
     bad[3] = kb.from_torch(torch.zeros(1, T, H, 7))  # gate neither scalar nor per-channel
@@ -100,7 +101,7 @@ def test_gdn_descriptors_validate(kb):
     snap = torch.zeros(K - 1, S * S * H, dtype=torch.float16)
     attn = torch.zeros(1, T, H, S)
     rc = kb.lib().kb_gated_delta_net_cache(*[ctypes.byref(x) for x in args], ctypes.byref(kb.from_torch(snap)), K,
-                                           ctypes.byref(kb.from_torch(attn)), None)
+                                           ctypes.byref(kb.from_torch(attn)), None, 0, None)
     assert rc == kb.KB_ERR_CUDA
 
 

@@ -51,7 +51,7 @@ def test_slot_rules(kb, cuda, T, K):
     args = [kb.from_torch(x) for x in to_dev(cuda, q, k, v, g, beta[..., None], s0)]
     import ctypes
 
-    assert kb.lib().kb_gated_delta_net(*[ctypes.byref(a) for a in args], K, ctypes.byref(dt), None) == 0
+    assert kb.lib().kb_gated_delta_net(*[ctypes.byref(a) for a in args], K, ctypes.byref(dt), None, 0, None) == 0
     torch.cuda.synchronize()
     attn, slots = split_packed(out.cpu().numpy(), S, H, T, 1, K)
     ex_attn, ex_slots = split_packed(O.rs_gated_delta_net_f64(q, k, v, g, beta, s0, K), S, H, T, 1, K)
