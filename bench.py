@@ -298,6 +298,51 @@ def bench_gdn(kb, torch, dev, steps, warmup):
                          "traffic": ncu_traffic("gdn_recurrent_verify")}}
 
 
+def bench_gdn_prefill(kb, torch, dev, steps, warmup):
+    """config[2] DeltaNet half: 4,096 tokens in 64-token chunks from a zero state (48 value / 16 key heads, d 128,
+    K = 4 slots) through kb_gated_delta_net with scratch (tcgen05 prep + state kernels, the last 3 tokens
+    recurrent). Two input sets alternate; the records (202 MB) exceed L2 as well."""
+    import ctypes
+
+    import numpy as np
+
+    T, K = 4096, 4
+    rng = np.random.default_rng(4096)
+    sets = []
+    for _ in range(2):
+        q = rng.standard_normal((1, T, 16, 128), dtype=np.float32)
+        k = rng.standard_normal((1, T, 16, 128), dtype=np.float32)
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = rng.standard_normal((1, T, 48, 128), dtype=np.float32)
+        beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((1, T, 48, 1))))).astype(np.float32)
+        g = (-np.logaddexp(0.0, rng.standard_normal((1, T, 48, 1)))).astype(np.float32)
+        s0 = np.zeros((1, 48, 128, 128), dtype=np.float32)
+        sets.append([torch.from_numpy(a).to(dev) for a in (q, k, v, g, beta, s0)])
+    nbytes = kb.lib().kb_gated_delta_net_scratch_bytes(ctypes.byref(kb.from_torch(sets[0][2])),
+                                                      ctypes.byref(kb.from_torch(sets[0][3])), K)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    for i in range(warmup):
+        kb.gated_delta_net(*sets[i % 2], K, scratch=scratch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        kb.gated_delta_net(*sets[i % 2], K, scratch=scratch)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    C, d, H = 64, 128, 48
+    flops = T * H * (10 * C * d + 6 * d * d)  # chunked-form algorithmic count (35.4 GFLOP)
+    tf = flops / (us * 1e-6) / 1e12
+    pk, kind = measured_peaks()
+    return {"value": round(us, 1), "unit": "us/layer", "tflops_algorithmic": round(tf, 2),
+            "workload": "config[2] gated DeltaNet prefill, 4096 tokens, chunk 64, 48 value / 16 key heads, d 128",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(tf / pk["bf16_tflops"], 4), "peak_kind": kind + " burst (f16 operands)",
+                         "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic("gdn_chunk_prefill_4096")}}
+
+
 def make_layers(kb, torch, dev, gen, n_kv, kv_type):
     layers = []
     for _ in range(LAYERS):
@@ -489,6 +534,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         torch.cuda.empty_cache()
         secondary["prefill_bf16_4096"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
+        secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -508,6 +554,52 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         dist.destroy_process_group()
 
 
+def run_case(case: str):
+    """One small, untimed invocation of a workload for profiler captures: three calls of the same operation
+    (capture the third with ncu -s <2 x kernels per call> -c <kernels per call>)."""
+    import numpy as np
+    import torch
+
+    import klein_b200 as kb
+
+    dev = torch.device("cuda:0")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1)
+    if case == "prefill_bf16_4096":
+        T = 4096
+        q = torch.randn(1, T, H, D, device=dev, generator=gen).bfloat16().float()
+        k = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
+        v = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
+        kv, vv = kb.kv_cache_view(k, kb.BF16, H_KV, D), kb.kv_cache_view(v, kb.BF16, H_KV, D)
+        run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0)
+    elif case in ("gdn_prefill_4096", "gdn_verify"):
+        T = 4096 if case == "gdn_prefill_4096" else 4
+        rng = np.random.default_rng(3)
+        q = rng.standard_normal((1, T, 16, 128), dtype=np.float32)
+        k = rng.standard_normal((1, T, 16, 128), dtype=np.float32)
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = rng.standard_normal((1, T, 48, 128), dtype=np.float32)
+        beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((1, T, 48, 1))))).astype(np.float32)
+        g = (-np.logaddexp(0.0, rng.standard_normal((1, T, 48, 1)))).astype(np.float32)
+        s0 = (rng.standard_normal((1, 48, 128, 128)) * (0.0 if T > 4 else 0.02)).astype(np.float32)
+        args = [torch.from_numpy(a).to(dev) for a in (q, k, v, g, beta, s0)]
+        run = lambda: kb.gated_delta_net(*args, 4)
+    elif case in ("verify_f16", "verify_q8_0"):
+        n_kv = 262144
+        global LAYERS
+        LAYERS = 1
+        _, _, kv, vv = make_layers(kb, torch, dev, gen, n_kv, "f16" if case == "verify_f16" else "q8_0")[0]
+        q = torch.randn(1, 4, H, D, device=dev, generator=gen)
+        run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    for _ in range(3):
+        out = run()
+    torch.cuda.synchronize()
+    print(case, "ok", float(out.float().abs().sum()))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,7 +610,13 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 cache)")
+    ap.add_argument("--case", default=None,
+                    choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0"],
+                    help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     global LAYERS
     LAYERS = args.layers
     args.warmup = max(args.warmup, 3)

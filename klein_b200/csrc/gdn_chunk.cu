@@ -13,7 +13,7 @@
 // approximation of it.
 //
 // Two kernels:
-//   prep  (one CTA per chunk, value head and sequence; all in parallel): [K;Q] K^T, the unit-triangular inverse
+//   prep  (one CTA per value head, chunk and sequence; all in parallel): [K;Q] K^T, the unit-triangular inverse
 //         T^-1 (CUDA cores, 16x16 blocks), then W and U~, written with A_qk and G as one record per chunk.
 //   state (one CTA per value head and sequence; sequential over chunks): the f32 state lives in TMEM; per chunk
 //         X = W S, U = U~ - X, dS = K~^T U, O = Q~ S + A_qk U, S <- Gamma_C S + dS. Warps: 8 epilogue (TMEM
@@ -44,9 +44,14 @@ __device__ __forceinline__ uint32_t sw_unit(int row, int u) { return (uint32_t) 
 // byte offset of the 16-bit element (row, col) of such a tile
 __device__ __forceinline__ uint32_t sw_off(int row, int col) { return sw_unit(row, col >> 3) + ((col & 7) << 1); }
 
-// f32 [64][64] in shared memory with the float4 units of a row XOR-swizzled by row (rows and columns both
-// walk without bank conflicts)
-__device__ __forceinline__ int fm(int r, int c) { return r * 64 + ((((c >> 2) ^ (r & 15)) << 2) | (c & 3)); }
+// f32 [64][64] row-major in shared memory with the float4 units of row r XOR-swizzled by r % 16: rows and
+// columns both walk without bank conflicts
+__device__ __forceinline__ float4& fm4(float* m, int r, int u4) {
+    return reinterpret_cast<float4*>(m)[r * 16 + (u4 ^ (r & 15))];
+}
+__device__ __forceinline__ float& fm1(float* m, int r, int c) {
+    return m[r * 64 + (((c >> 2) ^ (r & 15)) << 2) + (c & 3)];
+}
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
@@ -94,21 +99,33 @@ __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, con
 
 constexpr int PREP_THREADS = 160;                 // warps 0-3 compute (TMEM lanes 0-127), warp 4 issues the MMAs
 constexpr uint32_t PT_KQ = 0, PT_W = 64, PT_U = 128;  // TMEM columns: [K;Q]K^T, W^T, U~^T (128 x 64 f32 each)
+constexpr float LOG2E = 1.4426950408889634f;
 
 // 96 KiB in three regions whose contents change between phases (two CTAs fit on an SM):
-//   r0: [K;Q] hi, [2 key-dim chunks][128 rows: K 0-63, Q 64-127][64]; later T^-1 diag(beta Gamma) in chunk 0's
-//       Q rows
-//   r1: [K;Q] lo; later T^-1 f32 [0, 16K) and A f32 [16K, 32K); later T^-1 diag(beta) hi [16K, 24K), lo [24K, 32K)
-//   r2: V hi [2 value-dim chunks][64 rows][64] at 0, lo at 16K; later the W image for the record
+//   r0: [K;Q] hi, [2 key-dim chunks][128 rows: K 0-63, Q 64-127][64]. After [K;Q]K^T the Q rows (r0 + 8K and
+//       r0 + 24K) hold the A_qk hi / lo images until they are stored; then r0 + 8K holds the inverse's block
+//       products and after them T^-1 diag(beta) lo.
+//   r1: [K;Q] lo. Then A f32 [64][64] at r1 and T^-1 f32 at r1 + 16K; once A is consumed, T^-1 diag(beta Gamma)
+//       at r1 and T^-1 diag(beta) hi at r1 + 8K. Finally U~ [64 s][128 j] f32 for the record.
+//   r2: V hi [2 value-dim chunks][64 rows][64] at r2, lo at r2 + 16K; then the W image for the record.
 struct PrepSmem {
     uint8_t r0[32768];
     uint8_t r1[32768];
     uint8_t r2[32768];
-    float G[C], gam[C], beta[C];
+    float G[C], beta[C];
     uint64_t bar;
     uint32_t tmem_base;
     int failed;
 };
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const GdnChunkParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -119,8 +136,11 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
     PrepSmem& sm = *reinterpret_cast<PrepSmem*>(smem_raw);
     const GdnParams& in = p.in;
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int cc = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
-    const int hk = h % in.H_k;
+    // value heads vary fastest, the heads that share a key head next to each other: their K / Q rows come
+    // from L2 after the first read
+    const int R = in.H_v / in.H_k;
+    const int cc = blockIdx.y, seq = blockIdx.z;
+    const int hk = (int) blockIdx.x / R, h = hk + ((int) blockIdx.x % R) * in.H_k;
     const int64_t t_base = p.tok0 + (int64_t) cc * C;
     const int n_valid = (int) min((int64_t) C, p.tok0 + p.n_tok - t_base);
     char* rec = p.rec + (((int64_t) seq * in.H_v + h) * p.n_chunks + cc) * GDN_REC_BYTES;
@@ -132,11 +152,15 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
     uint8_t* kq_lo = sm.r1;
     uint8_t* v_hi = sm.r2;
     uint8_t* v_lo = sm.r2 + 16384;
-    float* tinv = reinterpret_cast<float*>(sm.r1);
-    float* amat = reinterpret_cast<float*>(sm.r1 + 16384);
-    uint8_t* tb_hi = sm.r1 + 16384;
-    uint8_t* tb_lo = sm.r1 + 24576;
-    uint8_t* tbg = sm.r0 + 8192;
+    uint8_t* aq_hi = sm.r0 + 8192;
+    uint8_t* aq_lo = sm.r0 + 24576;
+    float* amat = reinterpret_cast<float*>(sm.r1);          // A, row-major (fm4 layout)
+    float* tinv = reinterpret_cast<float*>(sm.r1 + 16384);  // T^-1, row-major (fm4 layout)
+    float* ytmp = reinterpret_cast<float*>(sm.r0 + 8192);   // block products of the inverse
+    uint8_t* tbg = sm.r1;
+    uint8_t* tb_hi = sm.r1 + 8192;
+    uint8_t* tb_lo = sm.r0 + 8192;
+    float* ust = reinterpret_cast<float*>(sm.r1);
     uint8_t* wst = sm.r2;
     volatile int* failed = &sm.failed;
 
@@ -148,6 +172,16 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
     if (warp == 4) {
         tmem_alloc(&sm.tmem_base, 256);
         tmem_relinquish();
+    }
+    if (tid < C) {
+        float gv = 0.f, bv = 0.f;  // padding tokens: no decay, no write
+        if (tid < n_valid) {
+            const int64_t tok = t_base + tid;
+            gv = *reinterpret_cast<const float*>(in.g + seq * in.g_nb3 + tok * in.g_nb2 + h * in.g_nb1);
+            bv = *reinterpret_cast<const float*>(in.beta + seq * in.b_nb3 + tok * in.b_nb2 + h * in.b_nb1);
+        }
+        sm.G[tid] = gv;
+        sm.beta[tid] = bv;
     }
     // K, Q and V rows as f16 hi/lo, 128B-swizzled; rows past the last token are zero. Each thread converts
     // the 16-byte unit u of rows tid/16 + 8m, with all eight rows' loads in flight at once.
@@ -183,16 +217,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
                 }
             }
         }
-        if (tid < C) {
-            float gv = 0.f, bv = 0.f;  // padding tokens: no decay, no write
-            if (tid < n_valid) {
-                const int64_t tok = t_base + tid;
-                gv = *reinterpret_cast<const float*>(in.g + seq * in.g_nb3 + tok * in.g_nb2 + h * in.g_nb1);
-                bv = *reinterpret_cast<const float*>(in.beta + seq * in.b_nb3 + tok * in.b_nb2 + h * in.b_nb1);
-            }
-            sm.G[tid] = gv;
-            sm.beta[tid] = bv;
-        }
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -216,123 +240,144 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
         }
         umma_commit(&sm.bar);
     }
-    // running log-decay within the chunk, in token order as the recurrence applies it
-    if (tid == 0) {
-        float acc = 0.f;
-        for (int t = 0; t < C; ++t) {
-            acc += sm.G[t];
-            sm.G[t] = acc;
+    // running log-decay within the chunk (inclusive prefix sums; warp 0, two tokens per lane)
+    if (warp == 0) {
+        const int lane = tid & 31;
+        const float g0 = sm.G[2 * lane], g1 = sm.G[2 * lane + 1];
+        float incl = g0 + g1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += y;
         }
+        sm.G[2 * lane + 1] = incl;
+        sm.G[2 * lane] = incl - g1;
     }
     __syncthreads();
-    if (tid < C) {
-        sm.gam[tid] = expf(sm.G[tid]);
-        *reinterpret_cast<float*>(rec + GDN_REC_G + tid * 4) = sm.G[tid];
-    }
+    if (tid < C) *reinterpret_cast<float*>(rec + GDN_REC_G + tid * 4) = sm.G[tid];
+    // Loops below stay rolled over 8-column pieces: this code runs once per CTA.
     if (tid < 128) {
-        if (!wait_or_fail(&sm.bar, 0, p, failed, DEV_ERR_WAIT_FULL)) {
-            // keep going: every thread must reach every barrier; the recorded error marks the result invalid
-        }
+        wait_or_fail(&sm.bar, 0, p, failed, DEV_ERR_WAIT_FULL);  // on failure every thread still meets every barrier
         tc_fence_after();
         const uint32_t lane_addr = tmem + ((uint32_t) (warp * 32) << 16);
-        uint32_t a0[32], a1[32];
-        tmem_ld32(lane_addr + PT_KQ, a0);
-        tmem_ld32(lane_addr + PT_KQ + 32, a1);
-        tmem_wait_ld();
-        if (tid < C) {
-            // A[s][r] = beta_s e^{G_s - G_r} k_s.k_r for r < s, else 0
-            const int s = tid;
-            const float bs = sm.beta[s], Gs = sm.G[s];
+        const int row = tid & (C - 1);  // s for the K K^T rows (warps 0-1), t for the Q K^T rows (warps 2-3)
+        const float Grow = sm.G[row], brow = sm.beta[row];
+#pragma unroll 1
+        for (int pc = 0; pc < C / 8; ++pc) {
+            uint32_t v8[8];
+            tmem_ld8(lane_addr + PT_KQ + pc * 8, v8);
+            tmem_wait_ld();
+            float x[8];
 #pragma unroll
-            for (int r = 0; r < C; ++r) {
-                const float kk = __uint_as_float(r < 32 ? a0[r] : a1[r - 32]);
-                amat[fm(s, r)] = r < s ? bs * expf(Gs - sm.G[r]) * kk : 0.f;
+            for (int e = 0; e < 8; ++e) {
+                const int c = pc * 8 + e;
+                const float d = exp2f((Grow - sm.G[c]) * LOG2E) * __uint_as_float(v8[e]);
+                x[e] = tid < C ? (c < row ? brow * d : 0.f) : (c <= row ? d : 0.f);
             }
-        } else {
-            // A_qk[t][s] = e^{G_t - G_s} q_t.k_s for s <= t, else 0; hi/lo images [64 t][64 s] into the record
-            const int t = tid - C;
-            const float Gt = sm.G[t];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                float x[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int s = u * 8 + e;
-                    const float qk = __uint_as_float(s < 32 ? a0[s] : a1[s - 32]);
-                    x[e] = s <= t ? expf(Gt - sm.G[s]) * qk : 0.f;
-                }
+            if (tid < C) {
+                // A[s][r] = beta_s e^{G_s - G_r} k_s.k_r (r < s), row-major f32
+                fm4(amat, row, 2 * pc) = make_float4(x[0], x[1], x[2], x[3]);
+                fm4(amat, row, 2 * pc + 1) = make_float4(x[4], x[5], x[6], x[7]);
+            } else {
+                // A_qk[t][s] = e^{G_t - G_s} q_t.k_s (s <= t) as hi/lo images [64 t][64 s]
                 uint4 hi, lo;
                 split8(x, hi, lo);
-                *reinterpret_cast<uint4*>(rec + GDN_REC_AQ_HI + sw_unit(t, u)) = hi;
-                *reinterpret_cast<uint4*>(rec + GDN_REC_AQ_LO + sw_unit(t, u)) = lo;
+                *reinterpret_cast<uint4*>(aq_hi + sw_unit(row, pc)) = hi;
+                *reinterpret_cast<uint4*>(aq_lo + sw_unit(row, pc)) = lo;
             }
         }
-        for (int e = tid; e < C * C / 4; e += 128) reinterpret_cast<float4*>(tinv)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    fence_proxy_async_smem();
     __syncthreads();
+    if (tid == 0) {
+        bulk_store(rec + GDN_REC_AQ_HI, aq_hi, 8192);
+        bulk_store(rec + GDN_REC_AQ_LO, aq_lo, 8192);
+        bulk_commit();
+    }
 
-    // T^-1 = (I + A)^-1 by 16 x 16 blocks. Diagonal blocks by forward substitution (one column per thread) ...
-    if (tid < 64) {
+    // T^-1 = (I + A)^-1 in 16 x 16 blocks. Diagonal blocks D_b = (I + A_bb)^-1 by forward substitution, one
+    // column per thread ...
+    if (tid < C) {
         const int o = (tid >> 4) * 16, c = tid & 15;
         float x[16];
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
             float acc = rr == c ? 1.f : 0.f;
 #pragma unroll
-            for (int q = 0; q < rr; ++q) acc -= amat[fm(o + rr, o + q)] * x[q];
+            for (int q = 0; q < rr; ++q) acc = fmaf(-fm1(amat, o + rr, o + q), x[q], acc);
             x[rr] = acc;
         }
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) tinv[fm(o + rr, o + c)] = x[rr];
+        for (int rr = 0; rr < 16; ++rr) fm1(tinv, o + rr, o + c) = x[rr];
     }
+    if (tid == 0) bulk_wait_read();  // the A_qk images have been read out: their space holds Y below
     __syncthreads();
-    // ... then block row bi: T_{bi,j} = -T_{bi,bi} sum_{k=j}^{bi-1} A_{bi,k} T_{k,j}
-    for (int bi = 1; bi < 4; ++bi) {
-        if (tid < 128) {
-            for (int e = tid; e < bi * 256; e += 128) {
-                const int j = e >> 8, rr = (e >> 4) & 15, cc2 = e & 15;
-                float acc = 0.f;
-                for (int k = j; k < bi; ++k) {
+    // ... then the blocks below the diagonal by distance l: T_{bi,bj} = -D_bi Y, Y = sum_{k=bj}^{bi-1} A_{bi,k} T_{k,bj}.
+    // A task is one row segment (row rr, columns 4 c4 .. 4 c4 + 3) of one block.
+#pragma unroll 1
+    for (int l = 1; l < 4; ++l) {
+        const int n_tasks = (4 - l) * 64;
+#pragma unroll 1
+        for (int task = tid; task < n_tasks && tid < 128; task += 128) {
+            const int bj = task >> 6, bi = bj + l, rr = (task >> 2) & 15, c4 = task & 3;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int k = bj; k < bi; ++k) {
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) acc += amat[fm(bi * 16 + rr, k * 16 + q)] * tinv[fm(k * 16 + q, j * 16 + cc2)];
+                for (int q = 0; q < 16; ++q) {
+                    const float a = fm1(amat, bi * 16 + rr, k * 16 + q);
+                    const float4 t = fm4(tinv, k * 16 + q, bj * 4 + c4);
+                    acc.x = fmaf(a, t.x, acc.x);
+                    acc.y = fmaf(a, t.y, acc.y);
+                    acc.z = fmaf(a, t.z, acc.z);
+                    acc.w = fmaf(a, t.w, acc.w);
                 }
-                tinv[fm(bi * 16 + rr, j * 16 + cc2)] = acc;
             }
+            reinterpret_cast<float4*>(ytmp)[task] = acc;  // Y of block bj, row rr, unit c4
         }
         __syncthreads();
-        if (tid < bi * 16) {
-            const int j = tid >> 4, cc2 = tid & 15;
-            float y[16];
+#pragma unroll 1
+        for (int task = tid; task < n_tasks && tid < 128; task += 128) {
+            const int bj = task >> 6, bi = bj + l, rr = (task >> 2) & 15, c4 = task & 3;
+            const float4* y = reinterpret_cast<const float4*>(ytmp) + bj * 64 + c4;  // row q at y[4 q]
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int q = 0; q < 16; ++q) y[q] = tinv[fm(bi * 16 + q, j * 16 + cc2)];
-#pragma unroll
-            for (int rr = 0; rr < 16; ++rr) {
-                float acc = 0.f;
-#pragma unroll
-                for (int q = 0; q <= rr; ++q) acc += tinv[fm(bi * 16 + rr, bi * 16 + q)] * y[q];
-                tinv[fm(bi * 16 + rr, j * 16 + cc2)] = -acc;
+            for (int q = 0; q < 16; ++q) {
+                if (q <= rr) {
+                    const float d = fm1(tinv, bi * 16 + rr, bi * 16 + q);
+                    const float4 yq = y[4 * q];
+                    acc.x = fmaf(d, yq.x, acc.x);
+                    acc.y = fmaf(d, yq.y, acc.y);
+                    acc.z = fmaf(d, yq.z, acc.z);
+                    acc.w = fmaf(d, yq.w, acc.w);
+                }
             }
+            fm4(tinv, bi * 16 + rr, bj * 4 + c4) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
         }
         __syncthreads();
     }
-    // B operands [s][64 r]: T^-1 diag(beta) as hi/lo (A is dead now), T^-1 diag(beta Gamma) in f16
+    // B operands [s][64 r]: T^-1 diag(beta) as hi/lo and T^-1 diag(beta Gamma) in f16 (A is consumed: its space
+    // takes them). Thread (s, half) writes row s, columns [32 half, 32 half + 32); T^-1 is zero above the diagonal.
     if (tid < 128) {
-        for (int e = tid; e < C * 8; e += 128) {
-            const int s = e >> 3, u = e & 7;
+        const int sr = tid & (C - 1), half = tid >> 6;
+#pragma unroll 1
+        for (int u = half * 4; u < half * 4 + 4; ++u) {
+            const float4 t0 = fm4(tinv, sr, 2 * u), t1 = fm4(tinv, sr, 2 * u + 1);
+            const float tt[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
             float x[8], y[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int r = u * 8 + k;
-                x[k] = tinv[fm(s, r)] * sm.beta[r];
-                y[k] = x[k] * sm.gam[r];
+            for (int e = 0; e < 8; ++e) {
+                const int r = u * 8 + e;
+                const float tv = r <= sr ? tt[e] : 0.f;
+                x[e] = tv * sm.beta[r];
+                y[e] = x[e] * exp2f(sm.G[r] * LOG2E);
             }
             uint4 hi, lo;
             split8(x, hi, lo);
-            *reinterpret_cast<uint4*>(tb_hi + sw_unit(s, u)) = hi;
-            *reinterpret_cast<uint4*>(tb_lo + sw_unit(s, u)) = lo;
-            const uint4 g16 = make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]),
-                                         pack_half2(y[6], y[7]));
-            *reinterpret_cast<uint4*>(tbg + sw_unit(s, u)) = g16;
+            *reinterpret_cast<uint4*>(tb_hi + sw_unit(sr, u)) = hi;
+            *reinterpret_cast<uint4*>(tb_lo + sw_unit(sr, u)) = lo;
+            *reinterpret_cast<uint4*>(tbg + sw_unit(sr, u)) = make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]),
+                                                                         pack_half2(y[4], y[5]), pack_half2(y[6], y[7]));
         }
     }
     fence_proxy_async_smem();
@@ -350,7 +395,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
                     smem_desc_sw128(smem_u32(tbg) + ks * 32, 16, 1024), idw, ks > 0);
         // U~^T = V^T (T^-1 diag(beta))^T in three passes; V chunks 8 KiB apart
         int n = 0;
-#pragma unroll
+#pragma unroll 1
         for (int pass = 0; pass < 3; ++pass) {
             const uint32_t a = smem_u32(pass == 2 ? v_lo : v_hi), b = smem_u32(pass == 1 ? tb_lo : tb_hi);
 #pragma unroll
@@ -364,31 +409,33 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
         const bool ok = wait_or_fail(&sm.bar, 1, p, failed, DEV_ERR_WAIT_FULL);
         tc_fence_after();
         const uint32_t lane_addr = tmem + ((uint32_t) (warp * 32) << 16);
-        uint32_t w0[32], w1[32], u0[32], u1[32];
-        tmem_ld32(lane_addr + PT_W, w0);
-        tmem_ld32(lane_addr + PT_W + 32, w1);
-        tmem_ld32(lane_addr + PT_U, u0);
-        tmem_ld32(lane_addr + PT_U + 32, u1);
-        tmem_wait_ld();
-        if (ok) {
-            // lane = key dim i for W^T: W image [i chunk][64 s][64 i] (B operand of the state kernel, K-major)
-            const int i = tid;
-            uint8_t* wdst = wst + (i >> 6) * 8192;
+        // lane = key dim i for W^T: W image [i chunk][64 s][64 i] (B operand of the state kernel, K-major);
+        // lane = value dim j for U~^T: U~[s][j] f32
+        uint8_t* wdst = wst + (tid >> 6) * 8192;
+#pragma unroll 1
+        for (int pc = 0; pc < C / 8; ++pc) {
+            uint32_t w8[8], u8[8];
+            tmem_ld8(lane_addr + PT_W + pc * 8, w8);
+            tmem_ld8(lane_addr + PT_U + pc * 8, u8);
+            tmem_wait_ld();
+            if (ok) {
 #pragma unroll
-            for (int s = 0; s < C; ++s)
-                *reinterpret_cast<__half*>(wdst + sw_off(s, i & 63)) = __float2half_rn(__uint_as_float(s < 32 ? w0[s] : w1[s - 32]));
-            // lane = value dim j for U~^T: U~[s][j] f32
-            float* udst = reinterpret_cast<float*>(rec + GDN_REC_U) + tid;
-#pragma unroll
-            for (int s = 0; s < C; ++s) udst[s * S] = __uint_as_float(s < 32 ? u0[s] : u1[s - 32]);
+                for (int e = 0; e < 8; ++e) {
+                    const int sr = pc * 8 + e;
+                    *reinterpret_cast<__half*>(wdst + sw_off(sr, tid & 63)) = __float2half_rn(__uint_as_float(w8[e]));
+                    ust[sr * S + tid] = __uint_as_float(u8[e]);
+                }
+            }
         }
     }
+    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid < 128) {
-        const uint4* src = reinterpret_cast<const uint4*>(wst);
-        uint4* dst = reinterpret_cast<uint4*>(rec + GDN_REC_W);
-        for (int e = tid; e < 16384 / 16; e += 128) dst[e] = src[e];
+    if (tid == 0) {
+        bulk_store(rec + GDN_REC_W, wst, 16384);
+        bulk_store(rec + GDN_REC_U, ust, C * S * 4);
+        bulk_commit();
+        bulk_wait_all();  // shared memory must outlive the stores that read it
     }
     if (warp == 4) {
         tc_fence_after();
@@ -401,7 +448,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_chunk_prep_kernel(const G
 constexpr int EPI_WARPS = 8;  // two per TMEM lane quadrant: warp w owns lanes 32 (w % 4) .. + 31 and column half w / 4
 constexpr int W_MMA = EPI_WARPS, W_LOAD = EPI_WARPS + 1, W_CONV = EPI_WARPS + 2;  // + 4 converter warps
 constexpr int ST_THREADS = (EPI_WARPS + 6) * 32;
-constexpr uint32_t TS_S = 0, TS_DS = 128, TS_X = 256, TS_O = 320, TS_UH = 384, TS_UL = 416;  // TMEM columns
+constexpr uint32_t TS_S = 0, TS_DS = 128, TS_X = 256, TS_O = 320, TS_UH = 384, TS_UL = 416, TS_X2 = 448;  // TMEM columns
 
 struct StateSmem {
     uint8_t st_hi[2 * 128 * 128];    // S^T hi (A operand, K-major): [key-dim chunk][128 j][64 i]
@@ -453,9 +500,6 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
                  "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                  : "memory");
 }
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(ST_THREADS, 1)
     gdn_chunk_state_kernel(const __grid_constant__ CUtensorMap tmO, const GdnChunkParams p) {
@@ -544,11 +588,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (!wait_or_fail(&sm.s_ready, par, p, failed, DEV_ERR_WAIT_FULL)) break;
                 if (!wait_or_fail(&sm.w_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
                 tc_fence_after();
-                // X = S^T W^T  (X[j][s] = (W S)[s][j])
+                // X = S^T W^T  (X[j][s] = (W S)[s][j]), the two key-dim halves in separate accumulators: two
+                // chains of 4 MMAs complete sooner than one of 8
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_ss(tmem + TS_X, smem_desc_sw128(st_hi + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                            smem_desc_sw128(w + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), id64, kk > 0);
+                    umma_ss(tmem + ((kk >> 2) ? TS_X2 : TS_X),
+                            smem_desc_sw128(st_hi + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                            smem_desc_sw128(w + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), id64, (kk & 3) > 0);
                 umma_commit(&sm.x_full);
                 umma_commit(&sm.w_empty);
                 // O = S^T Q~^T, three passes (O of the previous chunk must have been read out)
@@ -557,7 +603,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (!wait_or_fail(&sm.qt_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
                 tc_fence_after();
                 int n = 0;
-#pragma unroll
+#pragma unroll 1
                 for (int pass = 0; pass < 3; ++pass) {
                     const uint32_t a = pass == 2 ? st_lo : st_hi, b = pass == 1 ? qt_lo : qt_hi;
 #pragma unroll
@@ -571,7 +617,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (!wait_or_fail(&sm.kt_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
                 tc_fence_after();
                 n = 0;
-#pragma unroll
+#pragma unroll 1
                 for (int pass = 0; pass < 3; ++pass) {
                     const uint32_t ua = pass == 2 ? TS_UL : TS_UH, b = pass == 1 ? kt_lo : kt_hi;
 #pragma unroll
@@ -583,7 +629,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 // O += U^T A_qk^T, three passes
                 if (!wait_or_fail(&sm.aq_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
                 tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                 for (int pass = 0; pass < 3; ++pass) {
                     const uint32_t ua = pass == 2 ? TS_UL : TS_UH, b = aq + (pass == 1 ? 8192 : 0);
 #pragma unroll
@@ -609,6 +655,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             const int64_t t_base = p.tok0 + (int64_t) c * C;
             const int n_valid = (int) min((int64_t) C, p.tok0 + p.n_tok - t_base);
             const uint32_t par = (c - 1) & 1;
+#pragma unroll 1
             for (int which = 0; which < 2; ++which) {  // 0: Q~, 1: K~
                 float x[8][8];
 #pragma unroll
@@ -656,7 +703,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         const bool leader = tid == 0;                         // issues the output stores
         {
             const float* s0 = p.s0 + seq * p.s0_seq_stride + row_elem;
-#pragma unroll
+#pragma unroll 1
             for (int qq = 0; qq < 2; ++qq) {
                 const int q = 2 * hf + qq;
                 float x[32];
@@ -690,16 +737,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             // U = U~ - W S for tokens [32 hf, 32 hf + 32) as hi/lo f16 in TMEM (A operand of the next products)
             if (!wait_or_fail(&sm.x_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
             tc_fence_after();
-            uint32_t xs[32];
+            uint32_t xs[32], xs2[32];
             tmem_ld32(lane_addr + TS_X + hf * 32, xs);
+            tmem_ld32(lane_addr + TS_X2 + hf * 32, xs2);
             tmem_wait_ld();
             if (!wait_or_fail(&sm.u_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
             uint32_t uh[16], ul[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const int s0i = hf * 32 + 2 * e;
-                const float a = sm.u[s0i * S + j] - __uint_as_float(xs[2 * e]);
-                const float b = sm.u[(s0i + 1) * S + j] - __uint_as_float(xs[2 * e + 1]);
+                const float a = sm.u[s0i * S + j] - (__uint_as_float(xs[2 * e]) + __uint_as_float(xs2[2 * e]));
+                const float b = sm.u[(s0i + 1) * S + j] - (__uint_as_float(xs[2 * e + 1]) + __uint_as_float(xs2[2 * e + 1]));
                 split2(a, b, uh[e], ul[e]);
             }
             __syncwarp();
@@ -714,7 +762,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             if (!wait_or_fail(&sm.ds_full, par, p, failed, DEV_ERR_WAIT_FULL)) break;
             tc_fence_after();
             const bool last = c == n_chunks - 1;
-#pragma unroll
+#pragma unroll 1
             for (int qq = 0; qq < 2; ++qq) {
                 const int q = 2 * hf + qq;
                 uint32_t ms[32], ds[32];
@@ -742,7 +790,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.s_ready);
             if (!last) {
-#pragma unroll
+#pragma unroll 1
                 for (int qq = 0; qq < 2; ++qq) {
                     const int q = 2 * hf + qq;
                     uint32_t ms[32];
@@ -813,7 +861,7 @@ cudaError_t launch_gdn_chunked(const GdnChunkParams& p, const CUtensorMap& tmO, 
     if (e != cudaSuccess) return e;
     e = set_smem(gdn_chunk_state_kernel, sizeof(StateSmem), state_done);
     if (e != cudaSuccess) return e;
-    gdn_chunk_prep_kernel<<<dim3(p.n_chunks, p.in.H_v, p.in.n_seqs), PREP_THREADS, sizeof(PrepSmem), stream>>>(p);
+    gdn_chunk_prep_kernel<<<dim3(p.in.H_v, p.n_chunks, p.in.n_seqs), PREP_THREADS, sizeof(PrepSmem), stream>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     gdn_chunk_state_kernel<<<dim3(p.in.H_v, p.in.n_seqs), ST_THREADS, sizeof(StateSmem), stream>>>(tmO, p);
