@@ -72,7 +72,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 4-d tiled bulk tensor load into shared memory, completion counted on an mbarrier (no multicast)
+// 4-d tiled bulk tensor load into this CTA's shared memory, completion counted on an mbarrier
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
                                             int c3, uint64_t l2_policy) {
     asm volatile(
@@ -93,7 +93,7 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
 }
 
 // untiled bulk copy global -> shared (both addresses 16-byte aligned, bytes a multiple of 16), completion counted
-// on an mbarrier (no multicast)
+// on an mbarrier; this CTA only
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(smem_dst)),
