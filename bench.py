@@ -16,6 +16,7 @@ from the reference sources) on the host cores, one layer per step, and prints th
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -368,7 +369,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's version banner off stdout (one JSON line)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
+        if args.exchange == "nccl":
+            args.eager = True  # NCCL collectives stay out of the step graphs
     kb.lib()
 
     from klein_b200.kv_split import kv_range, local_bounds, packed_part_floats
@@ -396,17 +400,25 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     st = ctypes.c_void_p(stream.cuda_stream)
 
     rows = N_Q * H
+    xchg = None
     if world > 1:
-        # per-rank packed partial [o rows x D | (m, l) rows x 2], all-gathered over NCCL, merged by kb_lse_combine
+        # per-rank packed partial [o rows x D | (m, l) rows x 2], exchanged over NVLink (kb_partials_push into every
+        # rank's gather buffer + kb_lse_combine_wait), or all-gathered over NCCL and merged by kb_lse_combine
         pf = packed_part_floats(rows, D)
         part = torch.empty(pf, device=dev)
         gathered = torch.empty(world * pf, device=dev)
+        if args.exchange == "p2p":
+            def all_gather_obj(obj):
+                objs = [None] * world
+                dist.all_gather_object(objs, obj)
+                return objs
+            xchg = kb.PeerExchange(rank, world, pf, all_gather_obj)
         pt = kb.kb_tensor(part.data_ptr(), kb.F32, [D, H, N_Q, 1], [4, D * 4, H * D * 4, N_Q * H * D * 4])
         ml_ptr = ctypes.c_void_p(part.data_ptr() + rows * D * 4)
         g_o = ctypes.c_void_p(gathered.data_ptr())
         g_ml = ctypes.c_void_p(gathered.data_ptr() + rows * D * 4)
 
-    def layer_call(l):
+    def layer_call(l, st):
         if world == 1:
             rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(layers[l][2]), ctypes.byref(layers[l][3]), None,
                                      ctypes.byref(prm), ctypes.byref(dt), sp, ctypes.c_size_t(need), st)
@@ -417,18 +429,39 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                          ctypes.byref(prm), ctypes.byref(pt), ml_ptr, sp, ctypes.c_size_t(need), st)
         if rc != 0:
             raise kb.KbError("kb_flash_attn_ext_partial", rc)
+        if xchg is not None:
+            xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), st.value)
+            return
         dist.all_gather_into_tensor(gathered, part)
         rc = L.kb_lse_combine(g_o, g_ml, ctypes.c_int64(pf), world, ctypes.c_int64(rows), D,
                               ctypes.c_void_p(out.data_ptr()), st)
         if rc != 0:
             raise kb.KbError("kb_lse_combine", rc)
 
-    def step():
+    def step(st):
         for l in range(LAYERS):
-            layer_call(l)
+            layer_call(l, st)
 
+    def graphed(fn):
+        # one step captured as a CUDA graph (as ggml-cuda runs klein's forward); replays on the current stream
+        if args.eager:
+            return lambda: fn(st)
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            fn(ctypes.c_void_p(cap.cuda_stream))
+        stream.wait_stream(cap)
+        graphs.append(g)
+        return g.replay
+
+    graphs = []
     for _ in range(args.warmup):
-        step()
+        step(st)
+    torch.cuda.synchronize()
+    run_step = graphed(step)
+    for _ in range(2):
+        run_step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
@@ -437,7 +470,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
-            step()
+            run_step()
         e1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -457,21 +490,26 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     o_host = torch.empty(LAYERS, N_Q, H, D).pin_memory()
     q_dev = torch.empty(LAYERS, N_Q, H, D, device=dev)
 
-    def e2e_step():
-        for l in range(LAYERS):
-            q_dev[l].copy_(q_host[l], non_blocking=True)
-            qt.data = q_dev[l].data_ptr()
-            layer_call(l)
-            o_host[l].copy_(out[0], non_blocking=True)
+    def e2e_step(st):
+        cs = torch.cuda.ExternalStream(st.value, device=dev) if st.value else torch.cuda.current_stream(dev)
+        with torch.cuda.stream(cs):
+            for l in range(LAYERS):
+                q_dev[l].copy_(q_host[l], non_blocking=True)
+                qt.data = q_dev[l].data_ptr()
+                layer_call(l, st)
+                o_host[l].copy_(out[0], non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
-        e2e_step()
+        e2e_step(st)
+    torch.cuda.synchronize()
+    run_e2e = graphed(e2e_step)
+    run_e2e()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall = time.perf_counter()
     f0.record(stream)
     for _ in range(args.steps):
-        e2e_step()
+        run_e2e()
     f1.record(stream)
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
@@ -481,16 +519,20 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     # secondary: the same verify step over a q8_0 cache (config[3]'s other variant)
     secondary = {}
     if not args.no_secondary:
+        graphs.clear()  # the f16 graphs refer to the cache about to be freed
         del layers[:]
         torch.cuda.empty_cache()
         layers.extend(make_layers(kb, torch, dev, gen, n_kv, "q8_0"))
         for _ in range(args.warmup):
-            step()
+            step(st)
+        torch.cuda.synchronize()
+        run_q8 = graphed(step)  # a new capture: the f16 step's graph refers to the freed f16 cache
+        run_q8()
         torch.cuda.synchronize()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         for _ in range(args.steps):
-            step()
+            run_q8()
         g1.record(stream)
         torch.cuda.synchronize()
         qms = g0.elapsed_time(g1)
@@ -518,11 +560,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "config": {"workload": "config[3] long verify: 4 query tokens per layer, causal among the last 4, "
                                "262144-cell f16 KV cache (4 KV heads x 256), 24 Q heads, 16 layers per step",
                    "n_kv": N_KV, "kv_type": "f16", "layers_per_step": LAYERS,
-                   "parallelism": f"kv-split{world}" if world > 1 else "single",
+                   "parallelism": f"kv-split{world}-{args.exchange}" if world > 1 else "single",
                    "l2": "inputs larger than L2: each layer streams 1.07 GB of KV"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": peak_kind,
-                     "traffic": ncu_traffic("fa_stream_f16_verify262k"),
+                     # ncu DRAM bytes of one full-cache launch; a rank of an N-way split streams 1/N of the cells
+                     "traffic": (lambda t: None if t is None else int(t / world))(ncu_traffic("fa_stream_f16_verify262k")),
                      "algorithmic_bytes_per_launch": bytes_layer},
         "gpu_launches": launches,
         "e2e": {"value": round(e2e_ms * 1e3 / (args.steps * LAYERS), 2), "unit": UNIT,
@@ -530,6 +573,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "clocks": clk.summary(),
     }
     if not args.no_secondary and world == 1:
+        graphs.clear()  # the f16 graphs refer to the cache about to be freed
         del layers[:]
         torch.cuda.empty_cache()
         secondary["prefill_bf16_4096"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
@@ -550,7 +594,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             line["cpu_baseline"] = None
     if rank == 0:
         print(json.dumps(line), flush=True)
+    graphs.clear()  # graphs that hold collective calls go before the process group
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's last exchange has landed before peer buffers go away
+        if xchg is not None:
+            xchg.close()
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -610,6 +660,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 cache)")
+    ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph per step")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: partials exchange over NVLink peer stores (default) or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")

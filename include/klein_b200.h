@@ -113,6 +113,37 @@ kb_status kb_flash_attn_ext_partial(const kb_tensor* q, const kb_tensor* k, cons
 kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t part_stride, int32_t n_parts, int64_t rows,
                          int32_t head_dim, float* dst, void* stream);
 
+/*
+ * Exchange of the split partials between GPUs over NVLink without a collective library (the all-gather step of
+ * the KV-sequence split; ggml's split-KV exchanges them between CPU threads, ops.cpp:9489-9520, and has no
+ * multi-GPU counterpart). One process per GPU; every rank holds
+ *   a gather buffer  two slot sets of n_ranks packed partials (slot_set_floats >= n_ranks * part_floats each)
+ *   a flag array     int32 [n_ranks + 2], zero at start: one epoch per source rank, then this rank's epoch
+ *                    counter and a completion counter used by the merge
+ * both from kb_peer_alloc (zeroed device memory with a 64-byte CUDA IPC handle); kb_peer_open maps another
+ * process's buffer from its handle (peer access over NVLink), kb_peer_close unmaps, kb_peer_free releases.
+ *   kb_partials_push     writes `part` (this rank's packed partial, part_floats floats, 16-byte aligned) into slot
+ *                        `rank` of slot set (e & 1) of every rank's gather buffer, e = this rank's counter + 1, then
+ *                        stores e into flags[r][rank] of every rank r with system-scope release. gather / flags: host
+ *                        arrays of n_ranks (<= KB_MAX_PEERS) device pointers, this rank's own buffers included.
+ *   kb_lse_combine_wait  waits until every source's epoch in this rank's flag array reaches counter + 1 (gives up
+ *                        after 1 s and sets the device error word), merges that slot set of this rank's gather
+ *                        buffer like kb_lse_combine (parts at gather + p * part_stride, (m, l) after the rows * D
+ *                        output floats), and advances the counter.
+ * The epochs live in device memory, so both calls can be captured in a CUDA graph and replayed. A rank runs at most
+ * one exchange ahead of the slowest rank, so the two slot sets never hold data still being merged.
+ */
+#define KB_IPC_HANDLE_BYTES 64
+#define KB_MAX_PEERS 16
+kb_status kb_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+kb_status kb_peer_open(const void* ipc_handle, void** dev_ptr);
+kb_status kb_peer_close(void* dev_ptr);
+kb_status kb_peer_free(void* dev_ptr);
+kb_status kb_partials_push(const float* part, int64_t part_floats, float* const* gather, int64_t slot_set_floats,
+                           int32_t* const* flags, int32_t rank, int32_t n_ranks, void* stream);
+kb_status kb_lse_combine_wait(const float* gather, int64_t part_stride, int64_t slot_set_floats, int32_t n_parts,
+                              int64_t rows, int32_t head_dim, int32_t* flags, float* dst, void* stream);
+
 /* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
  * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,

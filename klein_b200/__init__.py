@@ -40,6 +40,12 @@ EXPORTED = [
     "kb_flash_attn_ext_noalloc",
     "kb_device_error",
     "kb_version",
+    "kb_peer_alloc",
+    "kb_peer_open",
+    "kb_peer_close",
+    "kb_peer_free",
+    "kb_partials_push",
+    "kb_lse_combine_wait",
 ]
 
 
@@ -97,6 +103,19 @@ def lib():
         L.kb_device_error.restype = c_int32
         L.kb_device_error.argtypes = [P(c_int32), c_int32]
         L.kb_version.restype = ctypes.c_char_p
+        L.kb_peer_alloc.restype = c_int32
+        L.kb_peer_alloc.argtypes = [c_size_t, P(c_void_p), c_void_p]
+        L.kb_peer_open.restype = c_int32
+        L.kb_peer_open.argtypes = [c_void_p, P(c_void_p)]
+        L.kb_peer_close.restype = c_int32
+        L.kb_peer_close.argtypes = [c_void_p]
+        L.kb_peer_free.restype = c_int32
+        L.kb_peer_free.argtypes = [c_void_p]
+        L.kb_partials_push.restype = c_int32
+        L.kb_partials_push.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p]
+        L.kb_lse_combine_wait.restype = c_int32
+        L.kb_lse_combine_wait.argtypes = [c_void_p, c_int64, c_int64, c_int32, c_int64, c_int32, c_void_p, c_void_p,
+                                          c_void_p]
         _lib = L
     return _lib
 
@@ -201,6 +220,30 @@ def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bia
     return out
 
 
+def flash_attn_ext_partial(q, k: KbTensor, v: KbTensor, scale: float, part, causal=False, pos0=0, kv_lo=0, ring=0,
+                           stream=None):
+    """kb_flash_attn_ext_partial into `part`, a flat f32 torch tensor of kv_split.packed_part_floats(n_q*H, D):
+    the unnormalised output rows [n_q*H][D] followed by (m, l) per row. q as for flash_attn_ext (ne3 = 1)."""
+    import torch
+
+    if q.dim() == 3:
+        q = q.unsqueeze(0)
+    _, n_q, H, D = q.shape
+    qt = kb_tensor(q.data_ptr(), F32, [D, n_q, H, 1], [4, q.stride(1) * 4, q.stride(2) * 4, q.stride(0) * 4])
+    pt = kb_tensor(part.data_ptr(), F32, [D, H, n_q, 1], [4, D * 4, H * D * 4, n_q * H * D * 4])
+    prm = fa_params(scale, causal=causal, pos0=pos0, kv_lo=kv_lo, ring=ring)
+    L = lib()
+    nbytes = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(prm))
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
+    rc = L.kb_flash_attn_ext_partial(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), None, ctypes.byref(prm),
+                                     ctypes.byref(pt), c_void_p(part.data_ptr() + n_q * H * D * 4),
+                                     c_void_p(scratch.data_ptr()), c_size_t(nbytes), c_void_p(st))
+    check("kb_flash_attn_ext_partial", rc)
+    part._kb_scratch = scratch
+    return part
+
+
 def device_error(clear: bool = True) -> int:
     code = c_int32(0)
     check("kb_device_error", lib().kb_device_error(ctypes.byref(code), int(clear)))
@@ -287,3 +330,59 @@ def rollback_recurrent(convs, snaps, ssms, snap_type: int, s: int, n_snapshots: 
     rc = lib().kb_rollback_recurrent(n, conv_p, convs[0].shape[-1], snap_p, snap_type, ssm_p, ssms[0].numel(), s,
                                      n_snapshots, c_void_p(_stream(convs[0], stream)))
     check("kb_rollback_recurrent", rc)
+
+
+# ------------------------------------------------------------------------------------------------ peers
+
+IPC_HANDLE_BYTES = 64
+
+
+def peer_alloc(nbytes: int):
+    """(device pointer, 64-byte IPC handle) of a zeroed buffer other processes can map (kb_peer_alloc)."""
+    ptr = c_void_p()
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check("kb_peer_alloc", lib().kb_peer_alloc(nbytes, ctypes.byref(ptr), h))
+    return ptr.value, h.raw
+
+
+def peer_open(handle: bytes) -> int:
+    ptr = c_void_p()
+    check("kb_peer_open", lib().kb_peer_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr)))
+    return ptr.value
+
+
+class PeerExchange:
+    """The all-gather of split partials over NVLink (kb_partials_push + kb_lse_combine_wait) for one process per
+    GPU. `exchange_handles(obj) -> list` gathers a picklable object from every rank (e.g. a gloo / NCCL process
+    group's all_gather_object). part_floats: packed partial size (kv_split.packed_part_floats). The epochs live on
+    the device, so exchange_and_combine can be captured in a CUDA graph."""
+
+    def __init__(self, rank: int, n_ranks: int, part_floats: int, exchange_handles):
+        self.rank, self.n, self.pf = rank, n_ranks, part_floats
+        self.set_floats = n_ranks * part_floats
+        self.gbuf, gh = peer_alloc(2 * self.set_floats * 4)  # two slot sets
+        self.fbuf, fh = peer_alloc(max(256, (n_ranks + 2) * 4))
+        handles = exchange_handles((gh, fh))
+        self.gather = [self.gbuf if r == rank else peer_open(handles[r][0]) for r in range(n_ranks)]
+        self.flags = [self.fbuf if r == rank else peer_open(handles[r][1]) for r in range(n_ranks)]
+        self._g = (c_void_p * n_ranks)(*self.gather)
+        self._f = (c_void_p * n_ranks)(*self.flags)
+
+    def exchange_and_combine(self, part_ptr: int, rows: int, head_dim: int, dst_ptr: int, stream: int) -> None:
+        """Push this rank's packed partial to every rank, wait for all of them, merge into dst (rows x head_dim)."""
+        L = lib()
+        check("kb_partials_push", L.kb_partials_push(c_void_p(part_ptr), self.pf, self._g, self.set_floats, self._f,
+                                                     self.rank, self.n, c_void_p(stream)))
+        check("kb_lse_combine_wait", L.kb_lse_combine_wait(c_void_p(self.gbuf), self.pf, self.set_floats, self.n, rows,
+                                                           head_dim, c_void_p(self.fbuf), c_void_p(dst_ptr),
+                                                           c_void_p(stream)))
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank has finished its last exchange)."""
+        L = lib()
+        for r in range(self.n):
+            if r != self.rank:
+                L.kb_peer_close(c_void_p(self.gather[r]))
+                L.kb_peer_close(c_void_p(self.flags[r]))
+        L.kb_peer_free(c_void_p(self.gbuf))
+        L.kb_peer_free(c_void_p(self.fbuf))

@@ -701,11 +701,51 @@ __global__ void __launch_bounds__(MERGE_THREADS) fa_combine_kernel(const FaStrea
 }
 
 // Merges partial results computed over disjoint KV ranges (e.g. one per GPU), one row per block.
+// Optionally the merge of an exchange between GPUs (see peer.cu): flags = [n_parts flags | epoch counter | done
+// counter] of this rank. One thread per CTA polls with system-scope acquire loads, bounded by wait_ns.
 __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float* __restrict__ o_parts,
                                                                     const float* __restrict__ ml_parts, int64_t stride,
                                                                     int n_parts, int64_t rows, int Dd,
-                                                                    float* __restrict__ dst) {
+                                                                    float* __restrict__ dst, int* flags,
+                                                                    int64_t slot_set_floats, int* err, uint64_t wait_ns) {
     const int64_t r = blockIdx.x;
+    if (flags) {
+        __shared__ int ready, epoch;
+        if (threadIdx.x == 0) {
+            ready = 1;
+            epoch = *reinterpret_cast<volatile int*>(flags + n_parts) + 1;
+            const uint64_t t0 = globaltimer_ns();
+            for (int p = 0; p < n_parts && ready; ++p) {
+                for (;;) {
+                    int v;
+                    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
+                    if (v - epoch >= 0) break;
+                    if (globaltimer_ns() - t0 > wait_ns) {
+                        record_error(err, DEV_ERR_WAIT_PEER);
+                        ready = 0;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        __syncthreads();
+        if (ready) {
+            const int64_t set = (int64_t) (epoch & 1) * slot_set_floats;
+            merge_row(o_parts + set + r * Dd, stride, ml_parts + set + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
+        }
+        // the last CTA to finish advances the epoch counter (every CTA has read it before counting itself done)
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(flags + n_parts + 1, 1) == (int) rows - 1) {
+                flags[n_parts + 1] = 0;
+                __threadfence();
+                atomicAdd(flags + n_parts, 1);
+            }
+        }
+        return;
+    }
     merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
 }
 
@@ -741,9 +781,11 @@ cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CU
 }  // namespace
 
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int Dd,
-                               float* dst, cudaStream_t stream) {
+                               float* dst, cudaStream_t stream, int* flags, int64_t slot_set_floats, int* err,
+                               uint64_t wait_ns) {
     if (rows <= 0) return cudaSuccess;
-    lse_combine_kernel<<<(unsigned) rows, MERGE_THREADS, 0, stream>>>(o_parts, ml_parts, stride, n_parts, rows, Dd, dst);
+    lse_combine_kernel<<<(unsigned) rows, MERGE_THREADS, 0, stream>>>(o_parts, ml_parts, stride, n_parts, rows, Dd, dst,
+                                                                        flags, slot_set_floats, err, wait_ns);
     return cudaGetLastError();
 }
 

@@ -354,6 +354,75 @@ kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t pa
                : KB_ERR_CUDA;
 }
 
+kb_status kb_lse_combine_wait(const float* gather, int64_t part_stride, int64_t slot_set_floats, int32_t n_parts,
+                              int64_t rows, int32_t head_dim, int32_t* flags, float* dst, void* stream) {
+    if (!gather || !flags || !dst || n_parts <= 0 || n_parts > KB_MAX_PEERS || rows <= 0 || head_dim <= 0) return KB_ERR_ARG;
+    if (part_stride < rows * head_dim + rows * 2 || slot_set_floats < part_stride * n_parts) return KB_ERR_ARG;
+    if (head_dim % 8 != 0 || part_stride % 4 != 0 || slot_set_floats % 4 != 0 ||
+        !aligned16(reinterpret_cast<uintptr_t>(gather)) || (reinterpret_cast<uintptr_t>(flags) & 3) != 0)
+        return KB_ERR_ARG;
+    return kb::launch_lse_combine(gather, gather + rows * head_dim, part_stride, n_parts, rows, head_dim, dst,
+                                  static_cast<cudaStream_t>(stream), flags, slot_set_floats, kb::device_error_word(),
+                                  g_wait_ns) == cudaSuccess
+               ? KB_OK
+               : KB_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------------------------- peer exchange
+
+kb_status kb_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+    if (!dev_ptr || !ipc_handle || bytes == 0) return KB_ERR_ARG;
+    *dev_ptr = nullptr;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return KB_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return KB_ERR_CUDA;
+    }
+    static_assert(sizeof(h) == KB_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(ipc_handle, &h, sizeof(h));
+    *dev_ptr = p;
+    return KB_OK;
+}
+
+kb_status kb_peer_open(const void* ipc_handle, void** dev_ptr) {
+    if (!ipc_handle || !dev_ptr) return KB_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_peer_close(void* dev_ptr) {
+    if (!dev_ptr) return KB_ERR_ARG;
+    return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_peer_free(void* dev_ptr) {
+    if (!dev_ptr) return KB_ERR_ARG;
+    return cudaFree(dev_ptr) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_partials_push(const float* part, int64_t part_floats, float* const* gather, int64_t slot_set_floats,
+                           int32_t* const* flags, int32_t rank, int32_t n_ranks, void* stream) {
+    if (!part || !gather || !flags || n_ranks < 1 || n_ranks > KB_MAX_PEERS || rank < 0 || rank >= n_ranks ||
+        part_floats <= 0 || part_floats % 4 != 0 || slot_set_floats < part_floats * n_ranks || slot_set_floats % 4 != 0)
+        return KB_ERR_ARG;
+    if (!aligned16(reinterpret_cast<uintptr_t>(part))) return KB_ERR_ARG;
+    kb::PeerPushParams pp{};
+    pp.part = part;
+    pp.part_floats = part_floats;
+    pp.slot_set_floats = slot_set_floats;
+    for (int r = 0; r < n_ranks; ++r) {
+        if (!gather[r] || !flags[r] || !aligned16(reinterpret_cast<uintptr_t>(gather[r]))) return KB_ERR_ARG;
+        pp.gather[r] = gather[r];
+        pp.flags[r] = flags[r];
+    }
+    pp.rank = rank;
+    pp.n_ranks = n_ranks;
+    return kb::launch_partials_push(pp, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------------------------------------- DeltaNet
 
 }  // extern "C"

@@ -85,8 +85,27 @@ cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorM
                               cudaStream_t stream);
 
 // merges n_parts partial results: o_p [rows][D] at o_parts + p*stride, ml_p [rows][2] at ml_parts + p*stride
+// Plain merge: flags == nullptr. Exchange merge: flags = this rank's flag array [n_parts flags | epoch counter |
+// done counter]; every CTA reads the counter, merges slot set (counter + 1) & 1 (parts at
+// o_parts + set * slot_set_floats) after waiting, bounded by wait_ns, until flags[p] >= counter + 1 for all p; the
+// last CTA to finish advances the counter.
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int D,
-                               float* dst, cudaStream_t stream);
+                               float* dst, cudaStream_t stream, int* flags = nullptr, int64_t slot_set_floats = 0,
+                               int* err = nullptr, uint64_t wait_ns = 0);
+
+// Writes this rank's packed partial into slot `rank` of slot set (epoch & 1) of every rank's gather buffer
+// (peer mappings), epoch = this rank's counter + 1, then releases epoch into flags[dst][rank] (system scope).
+// One CTA per destination rank.
+constexpr int MAX_PEERS = 16;
+struct PeerPushParams {
+    const float* part;
+    int64_t part_floats;                 // multiple of 4
+    int64_t slot_set_floats;             // floats between the two slot sets of a gather buffer
+    float* gather[MAX_PEERS];            // each rank's gather buffer
+    int* flags[MAX_PEERS];               // each rank's flag array [n_ranks flags | epoch counter | done counter]
+    int rank, n_ranks;
+};
+cudaError_t launch_partials_push(const PeerPushParams& p, cudaStream_t stream);
 
 int* device_error_word();
 
