@@ -1,17 +1,21 @@
 // Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM): GGML_OP_FLASH_ATTN_EXT with
 // many query tokens over an f16 or bf16 KV cache (klein's prompt chunks; config[2]'s 4,096-token prefill).
 //
-// One CTA computes a 128-query tile of one head. Roles:
-//   warps 0-15 softmax, 4 warpgroups: query row r is TMEM lane r; warpgroup g handles cells [16g, 16g+16)
-//              of each block and O dims [64g, 64g+64); they stage Q, run the online softmax, rescale O when
-//              needed, and write the normalised output
-//   warps 16-17 TMA producers for K and for V (independent chains): 64 cells x 256 dims, 2-deep rings,
-//              128-byte swizzle
-//   warp 18    MMA issuer (one thread): S_j = Q K_j^T (SS form, 16 MMAs of K=16) into a double-buffered TMEM
-//              S, then O += P_{j-1} V_{j-1} (TS form: P from TMEM) — so the QK^T of block j overlaps the
-//              softmax of block j-1
-// TMEM (512 columns): O 128 x 256 f32 at [0, 256), S_0/S_1 128 x 64 f32 at [256, 384), P_0/P_1 128 x 64
-// f16|bf16 (packed two per column) at [384, 448).
+// One CTA computes a 128-query tile of one head. Roles (8 warps):
+//   warps 0-3  softmax, one thread per query row (row r = TMEM lane r, all 64 cells of a block): stage Q, run the
+//              online softmax (unmasked blocks on the packed f32x2 pipe), rescale O when needed, write the
+//              normalised output. One thread per row needs no exchange of row maxima between warps.
+//   warps 4-5  TMA producers for K and for V (independent chains): 64 cells x 256 dims, 128-byte swizzle, rings
+//              of 3 tiles each
+//   warp 6     S issuer (one thread): S_j = Q K_j^T, 16 MMAs of K = 16 into S buffer j % 3, once PV_{j-3} (the
+//              last reader of that buffer) has completed
+//   warp 7     PV issuer (one thread): O += P_j V_j (TS form: P from TMEM) as soon as the softmax has written P_j.
+//              The tensor core accepts only a few MMAs ahead of the one executing, so one thread issuing both
+//              would hold PV back behind the 16 S MMAs.
+// TMEM (512 columns): O 128 x 256 f32 at [0, 256), S_0..S_2 128 x 64 f32 at [256, 448), Q dims 0-127 (f16|bf16
+// packed two per column) at [448, 512); Q dims 128-255 sit in shared memory. P_j (32 columns) overwrites the first
+// half of S_j once the softmax has read S_j. Three S / P buffers let S_{j+3} wait only for PV_j, so the loop
+// S -> softmax -> PV spans three blocks; the split Q leaves shared memory to 3-deep K and V rings.
 //
 // Online softmax with a lazy rescale: a row's running max m is only raised (and O, l rescaled) when a block's
 // max exceeds it by more than 8 (log2 units); otherwise exponents use the stale m, which O and l share, so the
@@ -30,30 +34,62 @@ constexpr float LOG2E = 1.4426950408889634f;
 constexpr int D = 256;
 constexpr int BM = 128;                       // query rows per CTA
 constexpr int BN = 64;                        // cells per K/V block
-constexpr int QTILE = BM * D * 2;             // 64 KiB: 4 chunks of [128 rows][128 B]
 constexpr int KVTILE = BN * D * 2;            // 32 KiB: 4 chunks of [64 cells][128 B]
 constexpr int KSTAGE = 3;                     // K ring depth (the K chain is latency-bound: depth sets the rate)
-constexpr int NSTAGE = 2;                     // V ring depth and the S / P / PV double buffers
-constexpr int SOFTMAX_WGS = 4;                 // softmax warpgroups: each owns 64 / SOFTMAX_WGS cells of a row
+constexpr int VSTAGE = 3;                     // V ring depth
+constexpr int NSTAGE = 3;                     // S / P buffers: S_{j+3} may start once PV_j has read P_j
+constexpr int SOFTMAX_WGS = 1;                 // softmax warpgroups: each owns 64 / SOFTMAX_WGS cells of a row
 constexpr int SOFTMAX_WARPS = 4 * SOFTMAX_WGS;
 constexpr int CPT = BN / SOFTMAX_WGS;           // cells per softmax thread per block
 constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread (rescale / epilogue)
-constexpr int THREADS = (SOFTMAX_WARPS + 3) * 32;  // + K producer, V producer, MMA issuer
-constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
+constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // + K producer, V producer, S issuer, PV issuer
+constexpr int W_KPROD = SOFTMAX_WARPS, W_VPROD = SOFTMAX_WARPS + 1, W_SMMA = SOFTMAX_WARPS + 2, W_PVMMA = SOFTMAX_WARPS + 3;
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_Q = 448;  // Q: dims 0-127 (the other half is in shared memory)
+constexpr int QT_DIMS = 128;                           // Q dims held in TMEM
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 units: rescale O only when the max grows by > 2^8
 
 struct Smem {
-    uint8_t q[QTILE];                          // 1024-aligned (offset 0)
-    uint8_t k[KSTAGE][KVTILE];
-    uint8_t v[NSTAGE][KVTILE];
-    uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[NSTAGE], v_empty[NSTAGE];
-    uint64_t s_full[NSTAGE], s_free[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
+    uint8_t q[(D - QT_DIMS) / 64][BM * 128];   // Q dims 128-255: K-major, 128B-swizzled [chunk][128 rows][128 B]
+    uint8_t k[KSTAGE][KVTILE];                 // (1024-aligned offsets)
+    uint8_t v[VSTAGE][KVTILE];
+    uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[VSTAGE], v_empty[VSTAGE];
+    uint64_t s_full[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
     __half xmax[2][SOFTMAX_WGS][BM];           // [block parity][group][row]: partial row maxima exchanged per block
     uint32_t tmem_base;
     int failed;
 };
 // the epilogue's partial row sums [group][row] reuse the K ring, idle once the last PV has completed
 static_assert(SOFTMAX_WGS * BM * sizeof(float) <= KVTILE, "row sums fit in a K stage");
+
+// packed f32x2 arithmetic (two lanes of a 64-bit register pair per instruction), 3-input max, ex2 with flush
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaPrefillParams& p, volatile int* failed,
                                              int code) {
@@ -113,11 +149,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.k_full[s], 1);
             mbar_init(&sm.k_empty[s], 1);
         }
-        for (int s = 0; s < NSTAGE; ++s) {
+        for (int s = 0; s < VSTAGE; ++s) {
             mbar_init(&sm.v_full[s], 1);
             mbar_init(&sm.v_empty[s], 1);
+        }
+        for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.s_free[s], SOFTMAX_WARPS);
             mbar_init(&sm.p_full[s], SOFTMAX_WARPS);
             mbar_init(&sm.o_done[s], 1);
         }
@@ -128,40 +165,60 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_alloc(&sm.tmem_base, 512);
         tmem_relinquish();
     }
-    // stage Q (rounded to the K type) into the K-major 128B-swizzled layout: 4 chunks of [128 rows][128 B]
-    for (int idx = threadIdx.x; idx < BM * (D / 8); idx += THREADS) {
-        const int r = idx / (D / 8), u = idx % (D / 8);  // row, 16-byte unit of 8 dims
-        const int qi = q0 + r;
-        float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (qi < p.n_q) {
-            const float4* src = reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3 + u * 32);
-            const float4 a = src[0], c = src[1];
-            x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = c.x, x[5] = c.y, x[6] = c.z, x[7] = c.w;
-        }
-        uint4 w;
-        if (FMT == 0) {
-            w = make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
-        } else {
-            w = make_uint4(pack_bf162(x[0], x[1]), pack_bf162(x[2], x[3]), pack_bf162(x[4], x[5]), pack_bf162(x[6], x[7]));
-        }
-        const int chunk = u >> 3, cu = u & 7;
-        *reinterpret_cast<uint4*>(sm.q + chunk * (BM * 128) + r * 128 + ((cu ^ (r & 7)) << 4)) = w;
-    }
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
+    if (warp < SOFTMAX_WARPS) {
+        // Q rounded to the K type into TMEM (the A operand of QK^T): row r = lane, dims [OPT grp, OPT grp + OPT) as
+        // packed pairs, 32 columns (64 dims) at a time
+        const int grp = warp >> 2, r = (warp & 3) * 32 + lane, qi = q0 + r;
+#pragma unroll 1
+        for (int c = 0; c < OPT / 64; ++c) {
+            uint32_t qv[32];
+            if (qi < p.n_q) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3) + (grp * OPT + c * 64) / 4;
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const float4 a = src[u];
+                    qv[2 * u] = FMT == 0 ? pack_half2(a.x, a.y) : pack_bf162(a.x, a.y);
+                    qv[2 * u + 1] = FMT == 0 ? pack_half2(a.z, a.w) : pack_bf162(a.z, a.w);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 32; ++u) qv[u] = 0u;
+            }
+            const int d0 = grp * OPT + c * 64;
+            if (d0 < QT_DIMS) {
+                tmem_st32(tmem + ((uint32_t) ((warp & 3) * 32) << 16) + TM_Q + d0 / 2, qv);
+            } else {
+                uint8_t* img = sm.q[(d0 - QT_DIMS) / 64];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    *reinterpret_cast<uint4*>(img + r * 128 + ((u ^ (r & 7)) << 4)) =
+                        make_uint4(qv[4 * u], qv[4 * u + 1], qv[4 * u + 2], qv[4 * u + 3]);
+            }
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+    }
+    // the S issuer starts once Q is in TMEM; the producers and the PV issuer do not wait for it
+    if (warp < SOFTMAX_WARPS || warp == W_SMMA) {
+        named_bar_sync(2, (SOFTMAX_WARPS + 1) * 32);
+        tc_fence_after();
+    }
 
-    if (warp == SOFTMAX_WARPS || warp == SOFTMAX_WARPS + 1) {
+    if (warp == W_KPROD || warp == W_VPROD) {
         // -------------------------------------------------------------------------------- TMA producers
         // K and V run independent chains: K_j waits only for S_{j-2}, V_j only for PV_{j-2}
-        const bool is_v = warp == SOFTMAX_WARPS + 1;
+        const bool is_v = warp == W_VPROD;
         if (lane == 0 && nb > 0) {
             const CUtensorMap* map = is_v ? &tmV : &tmK;
             tma_prefetch_desc(map);
-            const int depth = is_v ? NSTAGE : KSTAGE;
+            const int depth = is_v ? VSTAGE : KSTAGE;
             for (int j = 0; j < nb; ++j) {
                 const int s = j % depth;
                 const int cell = (int) block_cell(j);
@@ -173,32 +230,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int c = 0; c < D / 64; ++c) tma_load_4d(dst + c * (BN * 128), map, fullb, c * 64, hk, cell, kb3);
             }
         }
-    } else if (warp == SOFTMAX_WARPS + 2) {
-        // -------------------------------------------------------------------------------- MMA issuer
+    } else if (warp == W_SMMA) {
+        // -------------------------------------------------------------------------------- S issuer
+        // S_j = Q K_j^T into buffer j % 2, once PV_{j-2} (the last reader of that buffer, through P_{j-2}) has
+        // completed. A separate PV issuer keeps PV from waiting behind these 16 MMAs: the tensor core accepts only
+        // a few MMAs ahead of the one executing, so issuing them takes about as long as running them.
         if (lane == 0 && nb > 0) {
             constexpr uint32_t idS = umma_idesc_f16(FMT, BM, BN, false, false);
-            constexpr uint32_t idO = umma_idesc_f16(FMT, BM, D, false, true);
-            const uint32_t q_addr = smem_u32(sm.q);
-            auto issue_pv = [&](int i) -> bool {
-                const int s = i % NSTAGE;
-                if (!wait_or_fail(&sm.p_full[s], (i / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
-                if (!wait_or_fail(&sm.v_full[s], (i / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
-                tc_fence_after();
-                const uint32_t v_addr = smem_u32(sm.v[s]);
-#pragma unroll
-                for (int ks = 0; ks < BN / 16; ++ks) {
-                    // B = V block, MN-major: 64-dim chunks 8 KiB apart (LBO), 8-cell groups 1 KiB apart (SBO)
-                    const uint64_t bdesc = smem_desc_sw128(v_addr + ks * 16 * 128, BN * 128, 1024);
-                    umma_ts(tmem + TM_O, tmem + TM_P + s * 32 + ks * 8, bdesc, idO, i > 0 || ks > 0);
-                }
-                umma_commit(&sm.o_done[s]);
-                umma_commit(&sm.v_empty[s]);
-                return true;
-            };
             for (int j = 0; j < nb; ++j) {
                 const int s = j % NSTAGE, ks_ = j % KSTAGE;
                 if (!wait_or_fail(&sm.k_full[ks_], (j / KSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
-                if (j >= NSTAGE && !wait_or_fail(&sm.s_free[s], ((j / NSTAGE) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY))
+                if (j >= NSTAGE && !wait_or_fail(&sm.o_done[s], ((j / NSTAGE) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY))
                     break;
                 tc_fence_after();
                 const uint32_t k_addr = smem_u32(sm.k[ks_]);
@@ -206,16 +248,42 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int c = 0; c < D / 64; ++c) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t adesc = smem_desc_sw128(q_addr + c * (BM * 128) + kk * 32, 16, 1024);
+                        // A = Q (dims 0-127 from TMEM, 8 packed columns per step; dims 128-255 from shared
+                        // memory), B = K block, K-major
                         const uint64_t bdesc = smem_desc_sw128(k_addr + c * (BN * 128) + kk * 32, 16, 1024);
-                        umma_ss(tmem + TM_S + s * BN, adesc, bdesc, idS, (c | kk) != 0);
+                        if (c * 64 < QT_DIMS) {
+                            umma_ts(tmem + TM_S + s * BN, tmem + TM_Q + (c * 4 + kk) * 8, bdesc, idS, (c | kk) != 0);
+                        } else {
+                            const uint64_t adesc =
+                                smem_desc_sw128(smem_u32(sm.q[(c * 64 - QT_DIMS) / 64]) + kk * 32, 16, 1024);
+                            umma_ss(tmem + TM_S + s * BN, adesc, bdesc, idS, true);
+                        }
                     }
                 }
                 umma_commit(&sm.s_full[s]);
                 umma_commit(&sm.k_empty[ks_]);
-                if (j >= 1 && !issue_pv(j - 1)) break;
             }
-            if (!*failed) issue_pv(nb - 1);
+        }
+    } else if (warp == W_PVMMA) {
+        // -------------------------------------------------------------------------------- PV issuer
+        // O += P_i V_i as soon as the softmax has written P_i (into the first half of S_i's columns)
+        if (lane == 0 && nb > 0) {
+            constexpr uint32_t idO = umma_idesc_f16(FMT, BM, D, false, true);
+            for (int i = 0; i < nb; ++i) {
+                const int s = i % NSTAGE, vs = i % VSTAGE;
+                if (!wait_or_fail(&sm.p_full[s], (i / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
+                if (!wait_or_fail(&sm.v_full[vs], (i / VSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(sm.v[vs]);
+#pragma unroll
+                for (int ks = 0; ks < BN / 16; ++ks) {
+                    // B = V block, MN-major: 64-dim chunks 8 KiB apart (LBO), 8-cell groups 1 KiB apart (SBO)
+                    const uint64_t bdesc = smem_desc_sw128(v_addr + ks * 16 * 128, BN * 128, 1024);
+                    umma_ts(tmem + TM_O, tmem + TM_S + s * BN + ks * 8, bdesc, idO, i > 0 || ks > 0);
+                }
+                umma_commit(&sm.o_done[s]);
+                umma_commit(&sm.v_empty[vs]);
+            }
         }
     } else {
         // -------------------------------------------------------------------------------- softmax
@@ -245,24 +313,38 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t blk0 = block_cell(j);
             const bool plain = !mrow && !p.has_softcap && blk0 + BN <= p.n_kv &&
                                (!p.causal || (blk0 >= p.kv_lo && blk0 + BN - 1 <= row_pos)) && q0 + BM <= p.n_q;
+            // without a mask tensor or softcap the visible cells of a row form one range [e_lo, e_hi) of the block
+            const bool analytic = !mrow && !p.has_softcap;
             if (ok) {
                 tc_fence_after();
                 tmem_ld<CPT>(lane_addr + TM_S + s * BN + grp * CPT, sv);
                 tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.s_free[s]);
                 if (plain) {
-                    // scale > 0: the max of the scaled scores is the scaled max of the raw ones
+                    // scale > 0: the max of the scaled scores is the scaled max of the raw ones (3-input max)
                     float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-                    for (int e = 0; e < CPT; e += 4) {
-                        a0 = fmaxf(a0, __uint_as_float(sv[e]));
-                        a1 = fmaxf(a1, __uint_as_float(sv[e + 1]));
-                        a2 = fmaxf(a2, __uint_as_float(sv[e + 2]));
-                        a3 = fmaxf(a3, __uint_as_float(sv[e + 3]));
+                    for (int e = 0; e < CPT; e += 8) {
+                        a0 = max3f(a0, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+                        a1 = max3f(a1, __uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3]));
+                        a2 = max3f(a2, __uint_as_float(sv[e + 4]), __uint_as_float(sv[e + 5]));
+                        a3 = max3f(a3, __uint_as_float(sv[e + 6]), __uint_as_float(sv[e + 7]));
                     }
                     bm = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * scl;
+                } else if (analytic) {
+                    const int64_t cell0 = blk0 + grp * CPT;
+                    int64_t lo = 0, hi = min((int64_t) CPT, p.n_kv - cell0);
+                    if (p.causal) {
+                        lo = max(lo, p.kv_lo - cell0);
+                        hi = min(hi, p.pos0 + qi + 1 - cell0);
+                    }
+                    if (qi >= p.n_q) hi = 0;
+                    const int e_lo = (int) max((int64_t) 0, lo), e_hi = (int) max((int64_t) 0, hi);
+#pragma unroll
+                    for (int e = 0; e < CPT; ++e) {
+                        const float sc = (e >= e_lo && e < e_hi) ? __uint_as_float(sv[e]) * scl : -INFINITY;
+                        sv[e] = __float_as_uint(sc);
+                        bm = fmaxf(bm, sc);
+                    }
                 } else {
                     const int64_t cell0 = blk0 + grp * CPT;
 #pragma unroll
@@ -274,13 +356,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 // exchanged as f16 rounded up (no cell exceeds the shared reference); scores are clamped to f16's
                 // range first, a bound (6e4 in log2 units) no attention score reaches
-                sm.xmax[j & 1][grp][r] = __float2half_ru(fminf(bm, 60000.0f));
+                if (SOFTMAX_WGS > 1) sm.xmax[j & 1][grp][r] = __float2half_ru(fminf(bm, 60000.0f));
             }
-            named_bar_sync(1, SOFTMAX_WARPS * 32);
+            if (SOFTMAX_WGS > 1) named_bar_sync(1, SOFTMAX_WARPS * 32);
             if (!ok) continue;
-            float bmax = -INFINITY;
+            float bmax = bm;
+            if (SOFTMAX_WGS > 1) {
+                bmax = -INFINITY;
 #pragma unroll
-            for (int g2 = 0; g2 < SOFTMAX_WGS; ++g2) bmax = fmaxf(bmax, __half2float(sm.xmax[j & 1][g2][r]));
+                for (int g2 = 0; g2 < SOFTMAX_WGS; ++g2) bmax = fmaxf(bmax, __half2float(sm.xmax[j & 1][g2][r]));
+            }
             // lazy rescale
             float m_use = m;
             bool rescale = false;
@@ -292,8 +377,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // O may only be rescaled once PV_{j-1} is complete
             if (any_rescale && j >= 1)
                 ok = wait_or_fail(&sm.o_done[(j - 1) % NSTAGE], ((j - 1) / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
-            // P_j reuses P_{j-2}'s buffer: PV_{j-2} must be complete
-            if (j >= NSTAGE) ok = ok && wait_or_fail(&sm.o_done[s], ((j / NSTAGE) - 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            // (P_j reuses S_j's columns; PV_{j-2}, the last reader of this buffer, ran before S_j was written)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) continue;
             tc_fence_after();
@@ -317,16 +401,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t pk[CPT / 2];
             float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
             if (plain) {
+                // pairs of cells on the packed f32x2 pipe: x = score * scale - m, then ex2, then the row sums
+                const uint64_t sc2 = f2pack(scl, scl), nm2 = f2pack(-mref, -mref);
+                uint64_t acc0 = 0, acc1 = 0;  // (0.f, 0.f)
 #pragma unroll
                 for (int e = 0; e < CPT; e += 4) {
-                    const float p0 = exp2f(fmaf(__uint_as_float(sv[e]), scl, -mref));
-                    const float p1 = exp2f(fmaf(__uint_as_float(sv[e + 1]), scl, -mref));
-                    const float p2 = exp2f(fmaf(__uint_as_float(sv[e + 2]), scl, -mref));
-                    const float p3 = exp2f(fmaf(__uint_as_float(sv[e + 3]), scl, -mref));
-                    s0 += p0, s1 += p1, s2 += p2, s3 += p3;
+                    float x0, x1, x2, x3;
+                    f2unpack(ffma2(f2pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc2, nm2), x0, x1);
+                    f2unpack(ffma2(f2pack(__uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3])), sc2, nm2), x2, x3);
+                    const float p0 = ex2_ftz(x0), p1 = ex2_ftz(x1), p2 = ex2_ftz(x2), p3 = ex2_ftz(x3);
+                    acc0 = fadd2(acc0, f2pack(p0, p1));
+                    acc1 = fadd2(acc1, f2pack(p2, p3));
                     pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
                     pk[(e >> 1) + 1] = FMT == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
                 }
+                f2unpack(fadd2(acc0, acc1), s0, s1);
             } else {
 #pragma unroll
                 for (int e = 0; e < CPT; e += 4) {
@@ -338,7 +427,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             l += (s0 + s1) + (s2 + s3);
-            tmem_st<CPT / 2>(lane_addr + TM_P + s * 32 + grp * (CPT / 2), pk);
+            // P_j into the first half of S_j's columns (every group has read its S_j: the named barrier above)
+            tmem_st<CPT / 2>(lane_addr + TM_S + s * BN + grp * (CPT / 2), pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();

@@ -83,15 +83,22 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                  : "memory");
 }
 
-// loads / stores of N consecutive columns (N = 32 or 16 / 16 or 8)
+// loads / stores of N consecutive columns (loads: N = 64, 32 or 16; stores: N = 32, 16 or 8)
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
-    if constexpr (N == 32) tmem_ld32(taddr, r);
-    else tmem_ld16(taddr, r);
+    if constexpr (N == 64) {
+        tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    } else if constexpr (N == 32) {
+        tmem_ld32(taddr, r);
+    } else {
+        tmem_ld16(taddr, r);
+    }
 }
 template <int N>
 __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
-    if constexpr (N == 16) tmem_st16(taddr, r);
+    if constexpr (N == 32) tmem_st32(taddr, r);
+    else if constexpr (N == 16) tmem_st16(taddr, r);
     else tmem_st8(taddr, r);
 }
 
