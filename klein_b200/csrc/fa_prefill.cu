@@ -61,25 +61,7 @@ struct Smem {
 // the epilogue's partial row sums [group][row] reuse the K ring, idle once the last PV has completed
 static_assert(SOFTMAX_WGS * BM * sizeof(float) <= KVTILE, "row sums fit in a K stage");
 
-// packed f32x2 arithmetic (two lanes of a 64-bit register pair per instruction), 3-input max, ex2 with flush
-__device__ __forceinline__ uint64_t f2pack(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
+// 3-input max, ex2 with flush to zero
 __device__ __forceinline__ float max3f(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -13,10 +13,10 @@
 // fattn-common.cuh:924-978).
 //
 // f16 cache: TMA writes the K/V tiles straight into the swizzled f16 layout the MMA fragments read.
-// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0) of 64 cells into a 4-deep ring;
-// all warps then dequantise the tile into the same swizzled f16 layout (v = f16(q * d), one rounding) and
-// the f16 code path runs unchanged. Q is first rounded as ggml rounds it for a q8_0 K
-// (quantize_row_q8_0_ref, ggml-quants.c:276-299), so the scores use Q's q8_0 values like ggml's dot.
+// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0) of 64 cells into a 4-deep ring.
+// Q is quantised to q8_0 as ggml quantises it for a q8_0 K (quantize_row_q8_0_ref, ggml-quants.c:276-299) and
+// the scores are int8 MMAs on the raw K blocks scaled per block (ggml's q8_0 x q8_0 dot); only V is
+// dequantised, to f16 (v = f16(q * d), one rounding), for the same P V code as the f16 path.
 //
 // Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
 // the K dot type (f16 for f16 K, q8_0 for q8_0 K, :8960), scores are scaled, soft-capped, masked (-inf
@@ -47,9 +47,10 @@ __host__ __device__ constexpr size_t smem_f16(int nrg) {
     return 1024 /* alignment slack */ + (size_t) ST * STAGE_F16 + q_bytes(nrg) + 2 * ST * sizeof(uint64_t);
 }
 
+// q8_0 kernel: raw ring | V f16 tiles x 2 | Q int8 [rows][D] | Q block scales f32 [rows][D/32] | barriers
+__host__ __device__ constexpr int q8_qbytes(int nrg) { return nrg * 8 * D + nrg * 8 * (D / 32) * 4; }
 __host__ __device__ constexpr size_t smem_q8(int nrg) {
-    return 1024 + (size_t) STAGE_F16 /* dequantised tile */ + (size_t) QST * QSTAGE + q_bytes(nrg) +
-           2 * QST * sizeof(uint64_t);
+    return 1024 + (size_t) QST * QSTAGE + 2 * (size_t) KTILE_F16 + q8_qbytes(nrg) + 2 * QST * sizeof(uint64_t);
 }
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
@@ -114,21 +115,10 @@ __device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int dim) {
 
 // One 64-cell tile for one warp: S^T = K Q^T, online softmax, O^T += V^T P^T.
 // kb / vb: shared addresses of the f16 K and V tiles in the swizzled layout.
-__device__ __forceinline__ void tile_compute(const FaStreamParams& p, uint32_t kb, uint32_t vb, int64_t tkey0, int b,
-                                             int lane, const WarpCtx& w, const uint32_t (&qf)[16][2], float (&o)[16][4],
-                                             float& m0, float& m1, float& l0, float& l1) {
-    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-        uint32_t a[4];
-        ldsm_x4(a, swz_addr(kb, w.kkey, 16 * kk + w.kdo));
-        if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
-        else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
-    }
-    float x[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
-
+// online softmax and O^T += V^T P^T for this warp's 16 cells x 8 rows, from the raw scores x (S^T fragment)
+__device__ __forceinline__ void tile_softmax_pv(const FaStreamParams& p, uint32_t vb, int64_t tkey0, int b, int lane,
+                                                const WarpCtx& w, const float (&x)[4], float (&o)[16][4], float& m0,
+                                                float& m1, float& l0, float& l1) {
     const int64_t key0 = tkey0 + 16 * w.kg + (lane >> 2), key1 = key0 + 8;
     const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && tkey0 + TILE <= p.n_kv &&
                        (!p.causal || (tkey0 >= p.kv_lo && tkey0 + TILE - 1 <= w.min_pos));
@@ -178,6 +168,23 @@ __device__ __forceinline__ void tile_compute(const FaStreamParams& p, uint32_t k
     }
 }
 
+__device__ __forceinline__ void tile_compute(const FaStreamParams& p, uint32_t kb, uint32_t vb, int64_t tkey0, int b,
+                                             int lane, const WarpCtx& w, const uint32_t (&qf)[16][2], float (&o)[16][4],
+                                             float& m0, float& m1, float& l0, float& l1) {
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+        uint32_t a[4];
+        ldsm_x4(a, swz_addr(kb, w.kkey, 16 * kk + w.kdo));
+        if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
+        else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
+    }
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
+    tile_softmax_pv(p, vb, tkey0, b, lane, w, x, o, m0, m1, l0, l1);
+}
+
 __device__ __forceinline__ WarpCtx make_ctx(const FaStreamParams& p, int warp, int lane, int row0, int hk) {
     WarpCtx w;
     const int rg = warp / NKG;
@@ -212,31 +219,9 @@ __device__ __forceinline__ void load_q_frags(const __half* Qs, int rg, int lane,
     }
 }
 
-// Stages the CTA's Q rows as f16. f16 K: plain rounding. q8_0 K: each 32-element block is first quantised
-// like quantize_row_q8_0_ref (d = amax/127, q = roundf(x / d), d kept as f16), then stored as f16(q * d).
-template <bool Q8>
+// Stages the CTA's Q rows as f16 (f16 K: Q is rounded to f16, ggml's vec_dot type for an f16 K).
 __device__ __forceinline__ void stage_q(const FaStreamParams& p, __half* Qs, int rpc, int rows, int row0, int hk, int b) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    if (Q8) {
-        for (int task = warp; task < rpc * (D / 32); task += nwarps) {
-            const int r = task / (D / 32), blk = task % (D / 32);
-            float x = 0.0f;
-            if (r < rows) {
-                const int gr = row0 + r;
-                const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-                x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
-                                                    b * p.q_nb3);
-            }
-            float amax = fabsf(x);
-#pragma unroll
-            for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            const float d = amax / 127.0f;
-            const float id = d != 0.0f ? 1.0f / d : 0.0f;
-            const float qv = roundf(x * id);
-            const float dh = __half2float(__float2half_rn(d));
-            Qs[r * QSTRIDE + 32 * blk + lane] = __float2half_rn(qv * dh);
-        }
-    } else if (p.q_vec4) {
+    if (p.q_vec4) {
         for (int idx = threadIdx.x; idx < rpc * (D / 4); idx += blockDim.x) {
             const int r = idx / (D / 4), c4 = idx % (D / 4);
             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -378,7 +363,7 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
             for (; next_issue < min(ST, n_tiles); ++next_issue) issue(next_issue);
         }
     }
-    stage_q<false>(p, Qs, RPC, rows, row0, hk, b);
+    stage_q(p, Qs, RPC, rows, row0, hk, b);
     __syncthreads();
 
     bool failed = false;
@@ -443,32 +428,130 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
 }
 
 // ------------------------------------------------------------------------------------------------ q8_0 cache
+//
+// S^T = K Q^T straight from the raw q8_0 blocks with the int8 tensor-core MMA (m16n8k32: one k32 step = one
+// block): per block, the int32 dot of the quants times d_K times d_Q, which is ggml's q8_0 x q8_0 dot
+// (ggml_vec_dot_q8_0_q8_0 after Q is quantised to K's vec_dot type, ops.cpp:8960). Only V is dequantised to f16
+// (for the P V product), into a double-buffered tile, so the dequantisation of tile t+1 and the math of tile t
+// share one CTA barrier.
 
-// Dequantises one raw q8_0 tile pair (K then V, 64 cells x 272 bytes each, as TMA left them) into the f16
-// swizzled layout. Work unit = 16 elements (half a block) of one cell of K or V; each thread takes UPT units,
-// all of whose raw words are loaded before any is converted (the loop is unrolled for that).
+// Q rows quantised to q8_0 with quantize_row_q8_0_ref's rounding (d = amax / 127 stored as f16, q = round(x / d)):
+// Qi8 [rows][D] int8, Qd [rows][D/32] f32 (the f16 scale, widened)
+__device__ __forceinline__ void stage_q_int8(const FaStreamParams& p, int8_t* Qi8, float* Qd, int rpc, int rows, int row0,
+                                             int hk, int b) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int task = warp; task < rpc * (D / 32); task += nwarps) {
+        const int r = task / (D / 32), blk = task % (D / 32);
+        float x = 0.0f;
+        if (r < rows) {
+            const int gr = row0 + r;
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
+                                                b * p.q_nb3);
+        }
+        float amax = fabsf(x);
+#pragma unroll
+        for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        Qi8[r * D + 32 * blk + lane] = (int8_t) roundf(x * id);
+        if (lane == 0) Qd[r * (D / 32) + blk] = __half2float(__float2half_rn(d));
+    }
+}
+
+// this warp's Q as int8 B fragments (rows 8 rg + lane/4; dims 32 blk + 4 (lane%4) and +16) and the block scales
+// of the two rows its accumulator columns hold (8 rg + 2 (lane%4) and +1)
+__device__ __forceinline__ void load_q8_frags(const int8_t* Qi8, const float* Qd, int rg, int lane, uint32_t (&qb)[8][2],
+                                              float (&dq)[8][2]) {
+    const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int blk = 0; blk < D / 32; ++blk) {
+        qb[blk][0] = *reinterpret_cast<const uint32_t*>(Qi8 + (8 * rg + g) * D + 32 * blk + 4 * tig);
+        qb[blk][1] = *reinterpret_cast<const uint32_t*>(Qi8 + (8 * rg + g) * D + 32 * blk + 16 + 4 * tig);
+        dq[blk][0] = Qd[(8 * rg + 2 * tig) * (D / 32) + blk];
+        dq[blk][1] = Qd[(8 * rg + 2 * tig + 1) * (D / 32) + blk];
+    }
+}
+
+// 4 quants at a byte offset that is 2 (mod 4): the two aligned words around them, shifted
+__device__ __forceinline__ uint32_t ld_q4(const uint8_t* base, int off, bool aligned) {
+    if (aligned) return *reinterpret_cast<const uint32_t*>(base + off);
+    return __funnelshift_r(*reinterpret_cast<const uint32_t*>(base + off - 2), *reinterpret_cast<const uint32_t*>(base + off + 2),
+                           16);
+}
+
+// raw scores S^T (cells 16 kg + lane/4 and +8, the rows of the accumulator columns) from the raw K tile
+__device__ __forceinline__ void tile_scores_q8(const uint8_t* kraw, int kg, int lane, const uint32_t (&qb)[8][2],
+                                               const float (&dq)[8][2], float (&x)[4]) {
+    const int g = lane >> 2, tig = lane & 3;
+    const uint8_t* r0 = kraw + (16 * kg + g) * QROW;
+    const uint8_t* r1 = r0 + 8 * QROW;
+    x[0] = x[1] = x[2] = x[3] = 0.0f;
+#pragma unroll
+    for (int blk = 0; blk < D / 32; ++blk) {
+        // quants of block blk start at 34 blk + 2: a multiple of 4 for odd blocks
+        const int off = 34 * blk + 2 + 4 * tig;
+        const bool al = blk & 1;
+        uint32_t a[4];
+        a[0] = ld_q4(r0, off, al);
+        a[1] = ld_q4(r1, off, al);
+        a[2] = ld_q4(r0, off + 16, al);
+        a[3] = ld_q4(r1, off + 16, al);
+        int d[4] = {0, 0, 0, 0};
+        mma_s8_16832(d, a, qb[blk][0], qb[blk][1]);
+        const float k0 = __half2float(*reinterpret_cast<const __half*>(r0 + 34 * blk));
+        const float k1 = __half2float(*reinterpret_cast<const __half*>(r1 + 34 * blk));
+        // sumi * (d_K * d_Q), ggml's order
+        x[0] = fmaf((float) d[0], k0 * dq[blk][0], x[0]);
+        x[1] = fmaf((float) d[1], k0 * dq[blk][1], x[1]);
+        x[2] = fmaf((float) d[2], k1 * dq[blk][0], x[2]);
+        x[3] = fmaf((float) d[3], k1 * dq[blk][1], x[3]);
+    }
+}
+
+// V dequantisation plan of one thread: up to UPT work units (16 elements = half a block of one cell), their
+// sources in a raw stage (2 x the block's offset + which half) and destination offsets in the f16 V tile
+// (-1: no unit)
+constexpr int VUNITS = TILE * (D / 16);
 template <int NT>
-__device__ __forceinline__ void dequant_tile(const uint8_t* raw, uint8_t* f16tile, int tid) {
-    constexpr int UNITS = 2 * TILE * (D / 16);
-    constexpr int UPT = (UNITS + NT - 1) / NT;
+struct VPlan {
+    static constexpr int UPT = (VUNITS + NT - 1) / NT;
+    int src[UPT], dst[UPT];
+    __device__ __forceinline__ void init(int tid) {
+#pragma unroll
+        for (int k = 0; k < UPT; ++k) {
+            const int u = tid + k * NT;
+            if (u < VUNITS) {
+                const int r = u / (D / 16), bh = u % (D / 16), blk = bh >> 1, hf = bh & 1;
+                src[k] = 2 * (QTILE_RAW + r * QROW + blk * 34) + hf;
+                const int dim0 = 32 * blk + 16 * hf, u0 = (dim0 & 63) >> 3;
+                dst[k] = (dim0 >> 6) * (TILE * 128) + r * 128 + ((u0 ^ (r & 7)) << 4);
+            } else {
+                src[k] = 0;
+                dst[k] = -1;
+            }
+        }
+    }
+};
+
+// raw V blocks of one stage -> f16 V tile (128B-swizzled [4 dim boxes][64 cells][128 B]); all loads of a
+// thread's units are in flight before any is converted
+template <int NT>
+__device__ __forceinline__ void dequant_v(const uint8_t* raw, uint8_t* vtile, const VPlan<NT>& pl) {
+    constexpr int UPT = VPlan<NT>::UPT;
     uint32_t wq[UPT][4];
     __half dh[UPT];
 #pragma unroll
     for (int k = 0; k < UPT; ++k) {
-        const int u = tid + k * NT;
-        if (u < UNITS) {
-            const int tensor = u / (TILE * (D / 16)), rem = u % (TILE * (D / 16));
-            const int r = rem / (D / 16), bh = rem % (D / 16), blk = bh >> 1, hf = bh & 1;
-            const uint8_t* src = raw + tensor * QTILE_RAW + r * QROW + blk * 34;
-            dh[k] = *reinterpret_cast<const __half*>(src);
-            if (blk & 1) {
-                // quants at src + 2 + 16hf are 4-byte aligned for odd blocks (34 * blk + 2 = 0 mod 4)
-                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + 2 + 16 * hf);
+        if (pl.dst[k] >= 0) {
+            const uint8_t* blkp = raw + (pl.src[k] >> 1);  // start of the block (its f16 scale)
+            dh[k] = *reinterpret_cast<const __half*>(blkp);
+            const uint8_t* qp = blkp + 2 + 16 * (pl.src[k] & 1);
+            if ((reinterpret_cast<uintptr_t>(qp) & 3) == 0) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) wq[k][i] = s32[i];
+                for (int i = 0; i < 4; ++i) wq[k][i] = reinterpret_cast<const uint32_t*>(qp)[i];
             } else {
-                // even blocks: 2 bytes off; read the aligned words around them and shift
-                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + 16 * hf);
+                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(qp - 2);
                 uint32_t W[5];
 #pragma unroll
                 for (int i = 0; i < 5; ++i) W[i] = s32[i];
@@ -480,10 +563,7 @@ __device__ __forceinline__ void dequant_tile(const uint8_t* raw, uint8_t* f16til
     const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
 #pragma unroll
     for (int k = 0; k < UPT; ++k) {
-        const int u = tid + k * NT;
-        if (u < UNITS) {
-            const int tensor = u / (TILE * (D / 16)), rem = u % (TILE * (D / 16));
-            const int r = rem / (D / 16), bh = rem % (D / 16), blk = bh >> 1, hf = bh & 1;
+        if (pl.dst[k] >= 0) {
             const __half2 d2 = __halves2half2(dh[k], dh[k]);
             uint32_t outw[8];
 #pragma unroll
@@ -496,11 +576,10 @@ __device__ __forceinline__ void dequant_tile(const uint8_t* raw, uint8_t* f16til
                 outw[2 * i] = *reinterpret_cast<uint32_t*>(&l2);
                 outw[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
             }
-            const int dim0 = 32 * blk + 16 * hf;
-            uint8_t* dst = f16tile + tensor * KTILE_F16 + (dim0 >> 6) * (TILE * 128) + r * 128;
-            const int u0 = (dim0 & 63) >> 3;
-            *reinterpret_cast<uint4*>(dst + ((u0 ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            *reinterpret_cast<uint4*>(dst + (((u0 + 1) ^ (r & 7)) << 4)) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
+            uint8_t* dst = vtile + pl.dst[k];
+            *reinterpret_cast<uint4*>(dst) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+            // the next 16-byte unit of the row: unit index + 1 = unit ^ 1 (the first is even), swizzle preserved
+            *reinterpret_cast<uint4*>(reinterpret_cast<uintptr_t>(dst) ^ 16) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
         }
     }
 }
@@ -513,10 +592,11 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
     constexpr int RPC = NRG * 8;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* f16tile = smem;                       // dequantised K | V tile (64 KiB)
-    uint8_t* raw = smem + STAGE_F16;               // QST raw stages of K | V blocks
-    __half* Qs = reinterpret_cast<__half*>(raw + QST * QSTAGE);
-    uint64_t* full = reinterpret_cast<uint64_t*>(raw + QST * QSTAGE + q_bytes(NRG));
+    uint8_t* raw = smem;                                 // QST raw stages of K | V blocks
+    uint8_t* vtiles = raw + QST * QSTAGE;                // two dequantised V tiles
+    int8_t* Qi8 = reinterpret_cast<int8_t*>(vtiles + 2 * KTILE_F16);
+    float* Qd = reinterpret_cast<float*>(Qi8 + RPC * D);
+    uint64_t* full = reinterpret_cast<uint64_t*>(Qd + RPC * (D / 32));
     uint64_t* empty = full + QST;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -529,7 +609,6 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
     const int rows = min(RPC, p.R - row0);
     const bool issuer = threadIdx.x == 0;
 
-    int next_issue = 0;
     uint64_t pol = 0;
     const int kb3 = b / p.rk3;
     auto issue = [&](int t) {
@@ -550,10 +629,10 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
             pol = l2_policy_evict_first();
-            for (; next_issue < min(QST, n_tiles); ++next_issue) issue(next_issue);
+            for (int t = 0; t < min(QST, n_tiles); ++t) issue(t);
         }
     }
-    stage_q<true>(p, Qs, RPC, rows, row0, hk, b);
+    stage_q_int8(p, Qi8, Qd, RPC, rows, row0, hk, b);
     __syncthreads();
 
     bool failed = false;
@@ -562,56 +641,61 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
 #pragma unroll
     for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
     const bool active = (warp / NKG) * 8 < rows;
-    uint32_t qf[16][2];
-    load_q_frags(Qs, warp / NKG, lane, qf);
+    uint32_t qb[8][2];
+    float dq[8][2];
+    load_q8_frags(Qi8, Qd, warp / NKG, lane, qb, dq);
     const WarpCtx w = make_ctx(p, warp, lane, row0, hk);
-    const uint32_t kb = smem_u32(f16tile);
+    VPlan<NC * 32> plan;
+    plan.init(threadIdx.x);
 
-    for (int t = 0; t < n_tiles; ++t) {
-        const int s = t % QST;
-        if (issuer) {
-            while (next_issue <= t) {
-                const int si = next_issue % QST;
-                if (!mbar_wait(&empty[si], ((next_issue / QST) - 1) & 1, p.wait_ns)) {
-                    record_error(p.err, DEV_ERR_WAIT_EMPTY);
-                    failed = true;
-                    break;
-                }
-                issue(next_issue++);
-            }
-        }
-        __syncwarp();
-        if (!failed && !mbar_wait(&full[s], (t / QST) & 1, p.wait_ns)) {
+    // V of tile 0 first; then per tile: dequantise V of tile t+1 into the other buffer, compute tile t
+    if (n_tiles > 0) {
+        if (!mbar_wait(&full[0], 0, p.wait_ns)) {
             record_error(p.err, DEV_ERR_WAIT_FULL);
             failed = true;
         }
-        // every warp dequantises, so the whole CTA agrees on leaving before anyone waits at a barrier
-        if (__syncthreads_or(failed)) {
-            failed = true;
-            break;
+        dequant_v(raw, vtiles, plan);
+    }
+    failed = __syncthreads_or(failed);
+    for (int t = 0; t < n_tiles && !failed; ++t) {
+        const int s = t % QST;
+        if (t + 1 < n_tiles) {
+            const int s1 = (t + 1) % QST;
+            if (!mbar_wait(&full[s1], ((t + 1) / QST) & 1, p.wait_ns)) {
+                record_error(p.err, DEV_ERR_WAIT_FULL);
+                failed = true;
+            }
+            dequant_v(raw + s1 * QSTAGE, vtiles + ((t + 1) & 1) * KTILE_F16, plan);
         }
-        dequant_tile<NC * 32>(raw + s * QSTAGE, f16tile, threadIdx.x);
+        if (active) {
+            float x[4];
+            tile_scores_q8(raw + s * QSTAGE, w.kg, lane, qb, dq, x);
+            tile_softmax_pv(p, smem_u32(vtiles + (t & 1) * KTILE_F16), key_begin + (int64_t) t * TILE, b, lane, w, x, o,
+                            m0, m1, l0, l1);
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (issuer) {
-            while (next_issue < n_tiles && next_issue < t + 1 + QST) {
-                const int si = next_issue % QST;
-                if (!mbar_try_wait(&empty[si], ((next_issue / QST) - 1) & 1)) break;
-                issue(next_issue++);
+        if (lane == 0) mbar_arrive(&empty[s]);  // K (scores) and V (dequantised last round) of stage s are consumed
+        // one barrier per tile: V tile t is free for tile t+2, V tile t+1 is complete, and all agree on failures
+        failed = __syncthreads_or(failed);
+        if (issuer && !failed && t + QST < n_tiles) {
+            // every warp has released stage s before the barrier, so this wait returns at once
+            if (!mbar_wait(&empty[s], (t / QST) & 1, p.wait_ns)) {
+                record_error(p.err, DEV_ERR_WAIT_EMPTY);
+                failed = true;
+            } else {
+                issue(t + QST);
             }
         }
-        __syncthreads();  // the f16 tile is complete
-        if (active)
-            tile_compute(p, kb, kb + KTILE_F16, key_begin + (int64_t) t * TILE, b, lane, w, qf, o, m0, m1, l0, l1);
-        __syncthreads();  // the f16 tile is consumed
     }
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, off);
         l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
-    if (failed) return;  // every thread took the same exit; the error word is set
-    // every issued tile was consumed: the f16 tile and the raw ring are free for the merge buffers
+    // an issuer failure after the last barrier is seen by the issuer only: bring everyone to the same exit
+    failed = __syncthreads_or(failed);
+    if (failed) return;  // the error word is set
+    // every issued tile was consumed: the ring and the V tiles are free for the merge buffers
     merge_key_groups<NRG>(p, reinterpret_cast<float*>(smem), warp, lane, rows, row0, hk, b, split, chunk, o, m0, m1, l0,
                           l1);
 }
