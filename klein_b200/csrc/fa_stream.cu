@@ -23,6 +23,7 @@
 // cells skipped), and a row with no visible cell yields zeros (:9066). Accumulation is f32 throughout.
 #include "kb_common.cuh"
 #include "kb_internal.h"
+#include "kb_tcgen05.cuh"
 
 namespace kb {
 
@@ -833,6 +834,528 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
     merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
 }
 
+// ------------------------------------------------------------------------------------------------ q8_0 cache, tcgen05
+//
+// The same (split, KV head, row chunk) CTAs, on the 5th-generation tensor cores. The rows of a chunk are the N
+// columns (16 or 32) of S^T = K Q^T, computed for 128 cells at a time (M = 128): every K and V byte is read by
+// the tensor core once per CTA instead of once per row group, and the softmax needs no per-row exchange within
+// a thread. Roles (15 warps):
+//   warps 0-3   softmax, thread = cell (TMEM lane) of the 128-cell block: scale / mask, a running max per row
+//               shared by all cells and raised lazily (only when a block's max exceeds it by more than 2^8,
+//               agreed by a barrier reduction; O^T and the partial sums are rescaled then), P^T as f16 into
+//               shared memory, partial row sums per thread (summed once at the end)
+//   warps 4-7   K dequantisation, thread = cell: its raw q8_0 row (17 aligned 16-byte loads) -> 256 f16 values
+//               f16(q * d) -> TMEM, the A operand of S^T (TS form)
+//   warps 8-11  V dequantisation: raw tile -> f16 [64 cells][256 dims] swizzled tile, the A operand V^T of O^T
+//               (bank-conflict-free assignment: 8 consecutive cells x 4 blocks per warp instruction)
+//   warps 12/13 TMA producers of the raw K and V tiles (independent rings of 4 and 3 tiles)
+//   warp 14     MMA issuer: S^T_j (16 MMAs of K 16), then O^T += V^T P^T of block j-1 (2 M-halves x 4 K-steps
+//               per 64-cell tile), so S_{j+1} runs under the softmax of block j
+// TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), K f16 2 x 128 at 128.
+// Numerics as the mma.sync kernel's f16 path: Q quantised to q8_0 and widened to f16(q * d), K and V widened
+// to f16(q * d), f32 accumulation, P rounded to f16.
+namespace tc {
+constexpr int BLK = 128;  // cells per S^T block
+constexpr int KRAW = 4, VRAW = 3;
+constexpr int W_KDQ = 4, W_VDQ = 8, W_KTMA = 12, W_VTMA = 13, W_MMA = 14;
+constexpr int THREADS = 15 * 32;
+constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
+constexpr float THRESH = 8.0f;  // log2 units
+
+template <int N>
+struct Smem {
+    uint8_t v[2][KTILE_F16];        // f16 V tiles [4 dim chunks][64 cells][128 B], 128B-swizzled
+    uint8_t q[D / 64][N * 128];     // Q f16, K-major swizzled: the B operand of S^T
+    uint8_t p[2][2][N * 128];       // P^T [buffer][64-cell half][N rows][128 B]: the B operand of O^T
+    uint8_t kraw[KRAW][QTILE_RAW];  // raw q8_0 rows, 272 B per cell
+    uint8_t vraw[VRAW][QTILE_RAW];
+    float red[4][N];                // per-warp row maxima / sums
+    float mrow[N];                  // running row maxima (log2 units), shared by all cells
+    float alpha[N];                 // rescale factors of the last raise
+    int row_qi[N], row_h[N];
+    float row_slope[N];
+    uint64_t kfull[KRAW], kempty[KRAW], vfull[VRAW], vempty[VRAW];
+    uint64_t k_full[2], k_free[2], s_full[2], p_full[2], p_free[2], v_full[2], v_free[2], o_done;
+    uint32_t tmem_base;
+    int failed;
+};
+
+__device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaStreamParams& p, volatile int* failed,
+                                             int code) {
+    if (*failed) return false;
+    if (mbar_wait(bar, parity, p.wait_ns)) return true;
+    record_error(p.err, code);
+    *failed = 1;
+    return false;
+}
+
+// OR of a predicate over the `count` threads that reach named barrier `id`
+__device__ __forceinline__ bool bar_red_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t) pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
+// Reduces N per-row values over the 32 lanes of a warp; lane l ends with row (l % N). Each step halves the
+// values a lane holds: it keeps one half, sends the other to its partner (31 shuffles for N = 32).
+template <int N, bool MAX>
+__device__ __forceinline__ float warp_rows_reduce(float (&v)[N], int lane) {
+    auto op = [](float a, float b) { return MAX ? fmaxf(a, b) : a + b; };
+    if constexpr (N == 16) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = op(v[i], __shfl_xor_sync(0xffffffffu, v[i], 16));
+    }
+#pragma unroll
+    for (int off = N / 2, cnt = N / 2; off >= 1; off >>= 1, cnt >>= 1) {
+        const bool upper = lane & off;
+#pragma unroll
+        for (int i = 0; i < cnt; ++i) {
+            const float send = upper ? v[i] : v[i + cnt];
+            const float keep = upper ? v[i + cnt] : v[i];
+            v[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, off));
+        }
+    }
+    return v[0];
+}
+
+// 4 q8_0 quants -> two f16 pairs q * d ((q ^ 0x80) in the low mantissa byte of 1024 is 1152 + q exactly)
+__device__ __forceinline__ void q4_to_f16(uint32_t qw, __half2 d2, uint32_t& lo, uint32_t& hi) {
+    const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
+    const uint32_t xw = qw ^ 0x80808080u;
+    uint32_t a = __byte_perm(xw, 0x64646464u, 0x4140), c = __byte_perm(xw, 0x64646464u, 0x4342);
+    __half2 l2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&a), bias), d2);
+    __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&c), bias), d2);
+    lo = *reinterpret_cast<uint32_t*>(&l2);
+    hi = *reinterpret_cast<uint32_t*>(&h2);
+}
+
+// V dequantisation slots: slot set ss (0-3) x slot (0-3) -> 2 * block + half, 4 bits each. In every set the
+// first quant words of the 4 slots are 0, 1, 2, 3 (mod 4), so 8 consecutive cells x 4 slots hit 32 distinct banks:
+//   {(0,0) (1,0) (3,0) (5,0)}  {(0,1) (1,1) (3,1) (5,1)}  {(7,0) (2,0) (4,0) (6,0)}  {(7,1) (2,1) (4,1) (6,1)}
+constexpr uint64_t VSLOTS = 0x0ULL | (0ULL << 0) | (2ULL << 4) | (6ULL << 8) | (10ULL << 12) | (1ULL << 16) | (3ULL << 20) |
+                            (7ULL << 24) | (11ULL << 28) | (14ULL << 32) | (4ULL << 36) | (8ULL << 40) | (12ULL << 44) |
+                            (15ULL << 48) | (5ULL << 52) | (9ULL << 56) | (13ULL << 60);
+
+template <int N>
+__global__ void __launch_bounds__(THREADS, 1)
+    fa_stream_q8tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                          const FaStreamParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if (smem_u32(smem_raw) & 1023) {
+        if (threadIdx.x == 0) record_error(p.err, DEV_ERR_ALIGN);
+        return;
+    }
+    Smem<N>& sm = *reinterpret_cast<Smem<N>*>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, hk = blockIdx.y;
+    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
+    const int64_t key_begin = (int64_t) split * p.keys_per_split;
+    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
+    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
+    const int nblk = (n_tiles + 1) / 2;
+    const int row0 = chunk * N;
+    const int rows = min(N, p.R - row0);
+    const int kb3 = b / p.rk3;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KRAW; ++s) {
+            mbar_init(&sm.kfull[s], 1);
+            mbar_init(&sm.kempty[s], 2);
+        }
+        for (int s = 0; s < VRAW; ++s) {
+            mbar_init(&sm.vfull[s], 1);
+            mbar_init(&sm.vempty[s], 4);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sm.k_full[s], 4);
+            mbar_init(&sm.k_free[s], 1);
+            mbar_init(&sm.s_full[s], 1);
+            mbar_init(&sm.p_full[s], 4);
+            mbar_init(&sm.p_free[s], 1);
+            mbar_init(&sm.v_full[s], 4);
+            mbar_init(&sm.v_free[s], 1);
+        }
+        mbar_init(&sm.o_done, 1);
+        sm.failed = 0;
+        fence_barrier_init();
+    }
+    if (warp == W_MMA) {
+        tmem_alloc(&sm.tmem_base, 512);
+        tmem_relinquish();
+    }
+    // Q quantised like quantize_row_q8_0_ref, stored as f16(q * d) in the swizzled K-major image; rows past the
+    // chunk are zero
+    for (int task = warp; task < N * (D / 32); task += THREADS / 32) {
+        const int r = task / (D / 32), blk = task % (D / 32);
+        float x = 0.0f;
+        if (r < rows) {
+            const int gr = row0 + r;
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
+                                                b * p.q_nb3);
+        }
+        float amax = fabsf(x);
+#pragma unroll
+        for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const float qv = roundf(x * id);
+        const float dh = __half2float(__float2half_rn(d));
+        const int dim = 32 * blk + lane, e = dim & 63;
+        *reinterpret_cast<__half*>(sm.q[dim >> 6] + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
+            __float2half_rn(qv * dh);
+    }
+    if (threadIdx.x < N) {
+        const int r = threadIdx.x;
+        const int gr = row0 + min(r, max(rows - 1, 0));
+        const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+        sm.row_qi[r] = qi;
+        sm.row_h[r] = h;
+        sm.row_slope[r] = slope_of(p, h);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+    volatile int* failed = &sm.failed;
+
+    if (warp == W_KTMA || warp == W_VTMA) {
+        // ------------------------------------------------------------------------ TMA producers
+        const bool is_v = warp == W_VTMA;
+        if (lane == 0 && n_tiles > 0) {
+            const CUtensorMap* map = is_v ? &tmV : &tmK;
+            tma_prefetch_desc(map);
+            const uint64_t pol = l2_policy_evict_first();
+            const int depth = is_v ? VRAW : KRAW;
+            for (int t = 0; t < n_tiles; ++t) {
+                const int s = t % depth;
+                uint64_t* empty = is_v ? &sm.vempty[s] : &sm.kempty[s];
+                uint64_t* fullb = is_v ? &sm.vfull[s] : &sm.kfull[s];
+                uint8_t* dst = is_v ? sm.vraw[s] : sm.kraw[s];
+                if (t >= depth && !wait_or_fail(empty, ((t / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                mbar_arrive_expect_tx(fullb, QTILE_RAW);
+                tma_load_4d(dst, map, fullb, 0, hk, (int) (key_begin + (int64_t) t * TILE), kb3, pol);
+            }
+        }
+    } else if (warp == W_MMA) {
+        // ------------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idS = umma_idesc_f16(0, BLK, N, false, false);
+            constexpr uint32_t idO = umma_idesc_f16(0, BLK, N, true, false);
+            const uint32_t q_addr = smem_u32(sm.q);
+            auto pv = [&](int i) -> bool {
+                if (!wait_or_fail(&sm.p_full[i & 1], (i >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
+                for (int tt = 0; tt < 2; ++tt) {
+                    const int t = 2 * i + tt;
+                    if (t >= n_tiles) break;
+                    if (!wait_or_fail(&sm.v_full[t & 1], (t >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(sm.v[t & 1]), p_addr = smem_u32(sm.p[i & 1][tt]);
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+                        for (int ks = 0; ks < TILE / 16; ++ks) {
+                            // A = V^T, MN-major: dims of 64-dim chunks 8 KiB apart (LBO), 8-cell groups 1 KiB
+                            // apart (SBO); B = P^T, K-major
+                            const uint64_t adesc = smem_desc_sw128(v_addr + hh * 2 * (TILE * 128) + ks * 16 * 128,
+                                                                   TILE * 128, 1024);
+                            const uint64_t bdesc = smem_desc_sw128(p_addr + ks * 32, 16, 1024);
+                            umma_ss(tmem + TM_O + hh * N, adesc, bdesc, idO, i > 0 || tt > 0 || ks > 0);
+                        }
+                    }
+                    umma_commit(&sm.v_free[t & 1]);
+                }
+                umma_commit(&sm.p_free[i & 1]);
+                return true;
+            };
+            bool ok = true;
+            for (int j = 0; j < nblk && ok; ++j) {
+                if (!wait_or_fail(&sm.k_full[j & 1], (j >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint64_t bdesc = smem_desc_sw128(q_addr + (k >> 2) * (N * 128) + (k & 3) * 32, 16, 1024);
+                    umma_ts(tmem + TM_S + (j & 1) * N, tmem + TM_K + (j & 1) * 128 + k * 8, bdesc, idS, k > 0);
+                }
+                umma_commit(&sm.s_full[j & 1]);
+                umma_commit(&sm.k_free[j & 1]);
+                if (j >= 1) ok = pv(j - 1);
+            }
+            if (ok && nblk > 0) pv(nblk - 1);
+            umma_commit(&sm.o_done);  // also on failure: the final wait before the dealloc covers every MMA
+        }
+    } else if (warp >= W_KDQ && warp < W_VDQ) {
+        // ------------------------------------------------------------------------ K dequantisation -> TMEM
+        const int i = warp - W_KDQ;
+        const int half = i >> 1, cell = 32 * (i & 1) + lane;
+        const uint32_t lane_base = tmem + ((uint32_t) (32 * i) << 16);
+        for (int j = 0; j < nblk; ++j) {
+            const int t = 2 * j + half;
+            bool ok = j < 2 || wait_or_fail(&sm.k_free[j & 1], ((j >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            if (t < n_tiles) {
+                ok = wait_or_fail(&sm.kfull[t % KRAW], (t / KRAW) & 1, p, failed, DEV_ERR_WAIT_FULL);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                const uint4* row = reinterpret_cast<const uint4*>(sm.kraw[t % KRAW] + cell * QROW);
+                tc_fence_after();
+                uint32_t w[QROW / 4];
+#pragma unroll
+                for (int blk = 0; blk < D / 32; ++blk) {
+                    // the row in two halves of registers: words 0-35 for blocks 0-3 (bytes 0-135), 32-67 for 4-7
+                    if (blk == 0 || blk == 4) {
+#pragma unroll
+                        for (int u = (blk == 0 ? 0 : 8); u < (blk == 0 ? 9 : QROW / 16); ++u) {
+                            const uint4 x = row[u];
+                            w[4 * u] = x.x, w[4 * u + 1] = x.y, w[4 * u + 2] = x.z, w[4 * u + 3] = x.w;
+                        }
+                    }
+                    const uint32_t sw = w[(34 * blk) / 4];
+                    const uint16_t dbits = (34 * blk) % 4 == 0 ? (uint16_t) (sw & 0xffffu) : (uint16_t) (sw >> 16);
+                    const __half dh = __ushort_as_half(dbits);
+                    const __half2 d2 = __halves2half2(dh, dh);
+                    uint32_t out[16];
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const int byte = 34 * blk + 2 + 4 * g;
+                        const uint32_t qw = byte % 4 == 0 ? w[byte / 4] : __funnelshift_r(w[byte / 4], w[byte / 4 + 1], 16);
+                        q4_to_f16(qw, d2, out[2 * g], out[2 * g + 1]);
+                    }
+                    tmem_st16(lane_base + TM_K + (j & 1) * 128 + 16 * blk, out);
+                }
+                tmem_wait_st();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.kempty[t % KRAW]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.k_full[j & 1]);
+        }
+    } else if (warp >= W_VDQ && warp < W_KTMA) {
+        // ------------------------------------------------------------------------ V dequantisation -> smem
+        const int i = warp - W_VDQ;
+        const int ci = lane & 7, slot = lane >> 3;
+        int bh_of[4];  // 2 * block + half of this lane's slot in each slot set
+#pragma unroll
+        for (int ss = 0; ss < 4; ++ss) bh_of[ss] = (int) ((VSLOTS >> (4 * (4 * ss + slot))) & 15);
+        for (int t = 0; t < n_tiles; ++t) {
+            bool ok = wait_or_fail(&sm.vfull[t % VRAW], (t / VRAW) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            ok = ok && (t < 2 || wait_or_fail(&sm.v_free[t & 1], ((t >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY));
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            const uint8_t* raw = sm.vraw[t % VRAW];
+            uint8_t* dst = sm.v[t & 1];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                // round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, slot set m / 2
+                const int r = 8 * (i + 4 * (m & 1)) + ci;
+                const int bh = bh_of[m >> 1], blk = bh >> 1, hf = bh & 1;
+                const uint8_t* rowp = raw + r * QROW;
+                const int qb = 34 * blk + 2 + 16 * hf;  // first quant byte
+                const uint32_t* w32 = reinterpret_cast<const uint32_t*>(rowp + (qb & ~3));
+                const int sh = (qb & 3) * 8;
+                uint32_t W[5];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) W[k] = w32[k];
+                W[4] = sh ? w32[4] : 0u;
+                const __half dh = *reinterpret_cast<const __half*>(rowp + 34 * blk);
+                const __half2 d2 = __halves2half2(dh, dh);
+                uint32_t o8[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) q4_to_f16(__funnelshift_r(W[k], W[k + 1], sh), d2, o8[2 * k], o8[2 * k + 1]);
+                const int dim0 = 32 * blk + 16 * hf, u0 = (dim0 & 63) >> 3;
+                uint8_t* d0 = dst + (dim0 >> 6) * (TILE * 128) + r * 128 + ((u0 ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(d0) = make_uint4(o8[0], o8[1], o8[2], o8[3]);
+                // unit u0 + 1 (u0 even): the swizzled address XOR 16
+                *reinterpret_cast<uint4*>(reinterpret_cast<uintptr_t>(d0) ^ 16) = make_uint4(o8[4], o8[5], o8[6], o8[7]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&sm.v_full[t & 1]);
+                mbar_arrive(&sm.vempty[t % VRAW]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------------ softmax (warps 0-3)
+        const int c = 32 * warp + lane;  // cell of the block = TMEM lane
+        const uint32_t lane_addr = tmem + ((uint32_t) (32 * warp) << 16);
+        const float scl = p.scale_log2;
+        const int64_t min_pos = p.pos0 + sm.row_qi[0];
+        float l[N];
+#pragma unroll
+        for (int r = 0; r < N; ++r) l[r] = 0.0f;
+        if (threadIdx.x < N) sm.mrow[threadIdx.x] = -INFINITY;
+        named_bar_sync(1, 128);
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j) {
+            ok = ok && wait_or_fail(&sm.s_full[j & 1], (j >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            float s[N];
+            const int64_t key0 = key_begin + (int64_t) j * BLK, key = key0 + c;
+            if (ok) {
+                tc_fence_after();
+                uint32_t sv[N];
+                tmem_ld<N>(lane_addr + TM_S + (j & 1) * N, sv);
+                tmem_wait_ld();
+                const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && key0 + BLK <= key_end &&
+                                   (!p.causal || (key0 >= p.kv_lo && key0 + BLK - 1 <= min_pos));
+                if (plain) {
+#pragma unroll
+                    for (int r = 0; r < N; ++r) s[r] = r < rows ? __uint_as_float(sv[r]) * scl : -INFINITY;
+                } else {
+                    const bool in = key < key_end;
+#pragma unroll
+                    for (int r = 0; r < N; ++r)
+                        s[r] = (r < rows && in) ? masked_score(p, __uint_as_float(sv[r]), key, sm.row_qi[r], sm.row_h[r], b,
+                                                               sm.row_slope[r])
+                                                : -INFINITY;
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < N; ++r) s[r] = -INFINITY;
+            }
+            // every softmax thread agrees on leaving, and on raising the row maxima
+            if (bar_red_or(1, 128, !ok)) {
+                ok = false;
+                break;
+            }
+            bool bump = false;
+#pragma unroll
+            for (int r = 0; r < N; ++r) bump |= s[r] > sm.mrow[r] + THRESH;
+            if (bar_red_or(1, 128, bump)) {
+                // block maxima per row, 16 rows at a time (registers)
+#pragma unroll
+                for (int h16 = 0; h16 < N / 16; ++h16) {
+                    float v[16];
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) v[r] = s[16 * h16 + r];
+                    const float wm = warp_rows_reduce<16, true>(v, lane);
+                    if (lane < 16) sm.red[warp][16 * h16 + lane] = wm;
+                }
+                named_bar_sync(1, 128);
+                if (threadIdx.x < N) {
+                    const int r = threadIdx.x;
+                    const float bm = fmaxf(fmaxf(sm.red[0][r], sm.red[1][r]), fmaxf(sm.red[2][r], sm.red[3][r]));
+                    const float mo = sm.mrow[r], mn = fmaxf(mo, bm);
+                    sm.alpha[r] = mn == mo ? 1.0f : exp2f(mo - mn);
+                    sm.mrow[r] = mn;
+                }
+                named_bar_sync(1, 128);  // new maxima and factors visible; sm.red read before it is written again
+                bool any_alpha = false;
+#pragma unroll
+                for (int r = 0; r < N; ++r) {
+                    const float a = sm.alpha[r];
+                    any_alpha |= a != 1.0f;
+                    l[r] *= a;
+                }
+                if (j > 0 && any_alpha) {
+                    // O^T holds PV of blocks 0..j-1: rescale its columns once PV_{j-1} has completed
+                    ok = wait_or_fail(&sm.p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+                    if (ok) {
+                        tc_fence_after();
+                        // 16 columns at a time: the scores and sums stay in registers meanwhile
+#pragma unroll 1
+                        for (int c16 = 0; c16 < 2 * N; c16 += 16) {
+                            uint32_t ov[16];
+                            tmem_ld16(lane_addr + TM_O + c16, ov);
+                            tmem_wait_ld();
+                            const float* al = sm.alpha + (c16 % N);
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * al[e]);
+                            tmem_st16(lane_addr + TM_O + c16, ov);
+                        }
+                        tmem_wait_st();
+                    }
+                }
+            }
+            // P^T into buffer j % 2 once PV_{j-2} has read it
+            ok = ok && (j < 2 || wait_or_fail(&sm.p_free[j & 1], ((j >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY));
+            uint8_t* pb = sm.p[j & 1][c >> 6];
+            const int cc = c & 63;
+            if (ok) {
+#pragma unroll
+                for (int r = 0; r < N; ++r) {
+                    const float mr = sm.mrow[r];
+                    const float ref = mr == -INFINITY ? 0.0f : mr;
+                    const float pr = ex2_ftz(s[r] - ref);
+                    l[r] += pr;
+                    if (r < rows)
+                        *reinterpret_cast<__half*>(pb + r * 128 + (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) =
+                            __float2half_rn(pr);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.p_full[j & 1]);
+        }
+        // row sums over the block's cells, then over the 4 warps
+        named_bar_sync(1, 128);
+#pragma unroll
+        for (int h16 = 0; h16 < N / 16; ++h16) {
+            float v[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) v[r] = l[16 * h16 + r];
+            const float wl = warp_rows_reduce<16, false>(v, lane);
+            if (lane < 16) sm.red[warp][16 * h16 + lane] = wl;
+        }
+        named_bar_sync(1, 128);
+        if (ok && nblk > 0) ok = wait_or_fail(&sm.o_done, 0, p, failed, DEV_ERR_WAIT_FULL);
+        if (!*failed) {
+            const int64_t part_row0 =
+                ((((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits + split) * N;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                // dims [128 hh, 128 hh + 128) of O^T are on the lanes: this thread holds dim 128 hh + c
+                uint32_t ov[N];
+#pragma unroll
+                for (int r = 0; r < N; ++r) ov[r] = 0u;
+                if (ok && nblk > 0) {
+                    tc_fence_after();
+                    tmem_ld<N>(lane_addr + TM_O + hh * N, ov);
+                    tmem_wait_ld();
+                }
+                const int d = 128 * hh + c;
+#pragma unroll 4
+                for (int r = 0; r < rows; ++r) {
+                    const float L = (sm.red[0][r] + sm.red[1][r]) + (sm.red[2][r] + sm.red[3][r]);
+                    const float M = nblk > 0 ? sm.mrow[r] : -INFINITY;
+                    float O = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < N; ++e)
+                        if (e == r) O = __uint_as_float(ov[e]);
+                    if (p.n_splits == 1) {
+                        store_row(p, sm.row_qi[r], sm.row_h[r], b, d, O, M, L);
+                    } else {
+                        p.o_part[(part_row0 + r) * D + d] = O;
+                        if (d == 0) {
+                            p.ml_part[(part_row0 + r) * 2 + 0] = M;
+                            p.ml_part[(part_row0 + r) * 2 + 1] = L;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // every MMA has completed before the columns are released (o_done is committed on every path)
+    if (warp == W_MMA) mbar_wait(&sm.o_done, 0, p.wait_ns);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == W_MMA) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace tc
+
 // ------------------------------------------------------------------------------------------------ launch
 
 template <typename Kern>
@@ -862,7 +1385,30 @@ cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CU
     return cudaGetLastError();
 }
 
+template <int N>
+cudaError_t launch_q8tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
+    static bool attr_done[64] = {};
+    auto kern = tc::fa_stream_q8tc_kernel<N>;
+    const size_t smem = sizeof(tc::Smem<N>);
+    cudaError_t e = set_smem_once(kern, smem, attr_done);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
+    kern<<<grid, tc::THREADS, smem, stream>>>(tmK, tmV, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || p.n_splits == 1) return e;
+    dim3 cgrid(p.R, p.n_head_kv, p.ne3);
+    fa_combine_kernel<N><<<cgrid, MERGE_THREADS, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_fa_stream_q8tc(const FaStreamParams& p, int rpc, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                                  cudaStream_t stream) {
+    return rpc <= 16 ? launch_q8tc<16>(p, tmK, tmV, stream) : launch_q8tc<32>(p, tmK, tmV, stream);
+}
+
+size_t fa_stream_q8tc_smem_bytes(int rpc) { return rpc <= 16 ? sizeof(tc::Smem<16>) : sizeof(tc::Smem<32>); }
 
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int Dd,
                                float* dst, cudaStream_t stream, int* flags, int64_t slot_set_floats, int* err,

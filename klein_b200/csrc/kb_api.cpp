@@ -54,7 +54,8 @@ bool aligned16(size_t x) { return (x & 15) == 0; }
 
 // The split-KV plan of one streaming attention call.
 struct FaPlan {
-    int nrg = 1, n_row_chunks = 1, n_splits = 1;
+    bool q8tc = false;  // q8_0 cache: the tcgen05 kernel
+    int nrg = 1, rpc = 8, n_row_chunks = 1, n_splits = 1;
     int64_t keys_per_split = 0;
     size_t scratch = 0;
 };
@@ -111,23 +112,27 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
 
 FaPlan plan_fa(const FaShape& s) {
     FaPlan pl;
+    pl.q8tc = s.kv_type == KB_TYPE_Q8_0;
     pl.nrg = kb::fa_stream_nrg(s.R);
-    pl.n_row_chunks = (s.R + pl.nrg * 8 - 1) / (pl.nrg * 8);
+    pl.rpc = pl.q8tc ? kb::fa_q8tc_rpc(s.R) : pl.nrg * 8;
+    pl.n_row_chunks = (s.R + pl.rpc - 1) / pl.rpc;
     const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
     const int64_t base = (int64_t) s.H_kv * pl.n_row_chunks * s.ne3;
-    const int64_t tiles = (s.n_kv + kb::FA_TILE - 1) / kb::FA_TILE;
+    // split unit: a 64-cell tile, or a 128-cell block for the tcgen05 kernel
+    const int unit = pl.q8tc ? kb::FA_TC_BLOCK : kb::FA_TILE;
+    const int64_t tiles = (s.n_kv + unit - 1) / unit;
     int64_t target = sms / base;
     if (target < 1) target = 1;
     if (tiles == 0) {
         pl.n_splits = 1;
-        pl.keys_per_split = kb::FA_TILE;
+        pl.keys_per_split = unit;
     } else {
         const int64_t tps = (tiles + target - 1) / target;
-        pl.keys_per_split = tps * kb::FA_TILE;
+        pl.keys_per_split = tps * unit;
         pl.n_splits = (int) ((tiles + tps - 1) / tps);
     }
     if (pl.n_splits > 1) {
-        const size_t rows = (size_t) base * pl.n_splits * pl.nrg * 8;
+        const size_t rows = (size_t) base * pl.n_splits * pl.rpc;
         pl.scratch = rows * kb::FA_D * 4 + 256 + rows * 2 * 4;
     }
     return pl;
@@ -287,7 +292,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     p.keys_per_split = pl.keys_per_split;
     p.n_row_chunks = pl.n_row_chunks;
     if (pl.scratch > 0) {
-        const size_t rows = (size_t) s.H_kv * pl.n_row_chunks * s.ne3 * pl.n_splits * pl.nrg * 8;
+        const size_t rows = (size_t) s.H_kv * pl.n_row_chunks * s.ne3 * pl.n_splits * pl.rpc;
         p.o_part = static_cast<float*>(scratch);
         const uintptr_t ml = (reinterpret_cast<uintptr_t>(scratch) + rows * kb::FA_D * 4 + 255) & ~uintptr_t(255);
         p.ml_part = reinterpret_cast<float*>(ml);
@@ -304,7 +309,8 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     CUtensorMap tmK, tmV;
     if ((st = encode_kv_map(k, &tmK)) != KB_OK) return st;
     if ((st = encode_kv_map(v, &tmV)) != KB_OK) return st;
-    cudaError_t e = kb::launch_fa_stream(p, pl.nrg, k->type, tmK, tmV, static_cast<cudaStream_t>(stream));
+    cudaError_t e = pl.q8tc ? kb::launch_fa_stream_q8tc(p, pl.rpc, tmK, tmV, static_cast<cudaStream_t>(stream))
+                            : kb::launch_fa_stream(p, pl.nrg, k->type, tmK, tmV, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 

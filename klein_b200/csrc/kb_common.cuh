@@ -164,6 +164,18 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
     return d;
 }
 
+// 3-input max; ex2 with flush to zero
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // D(16x8 s32) += A(16x32 s8, row) * B(32x8 s8, col)
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(

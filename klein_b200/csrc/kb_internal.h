@@ -58,6 +58,13 @@ size_t fa_stream_smem_bytes(int nrg, int kv_type);
 cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream);
 
+// q8_0 caches on tcgen05: chunks of rpc = 16 or 32 rows, KV splits of whole 128-cell blocks (FA_TC_BLOCK)
+constexpr int FA_TC_BLOCK = 128;
+inline int fa_q8tc_rpc(int R) { return R <= 16 ? 16 : 32; }
+size_t fa_stream_q8tc_smem_bytes(int rpc);
+cudaError_t launch_fa_stream_q8tc(const FaStreamParams& p, int rpc, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                                  cudaStream_t stream);
+
 // Parameters of one causal-prefill launch (tcgen05 kernel): one CTA per 128-query tile of one head.
 struct FaPrefillParams {
     const char* q;                   // f32 [D, n_q, H, ne3], rows 16-byte aligned
