@@ -1154,29 +1154,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!ok) break;
             const uint8_t* raw = sm.vraw[t % VRAW];
             uint8_t* dst = sm.v[t & 1];
+            // all 8 rounds' loads first, then the conversions and stores (shared loads are not moved past
+            // shared stores). Round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, slot set m / 2.
+#pragma unroll 1
+            for (int m0 = 0; m0 < 8; m0 += 4) {
+            uint32_t W[4][5];
+            __half dh[4];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                // round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, slot set m / 2
-                const int r = 8 * (i + 4 * (m & 1)) + ci;
-                const int bh = bh_of[m >> 1], blk = bh >> 1, hf = bh & 1;
+            for (int mm = 0; mm < 4; ++mm) {
+                const int r = 8 * (i + 4 * (mm & 1)) + ci;
+                const int bh = m0 ? bh_of[2 + (mm >> 1)] : bh_of[mm >> 1], blk = bh >> 1, hf = bh & 1;
                 const uint8_t* rowp = raw + r * QROW;
                 const int qb = 34 * blk + 2 + 16 * hf;  // first quant byte
                 const uint32_t* w32 = reinterpret_cast<const uint32_t*>(rowp + (qb & ~3));
-                const int sh = (qb & 3) * 8;
-                uint32_t W[5];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) W[k] = w32[k];
-                W[4] = sh ? w32[4] : 0u;
-                const __half dh = *reinterpret_cast<const __half*>(rowp + 34 * blk);
-                const __half2 d2 = __halves2half2(dh, dh);
+                for (int k = 0; k < 4; ++k) W[mm][k] = w32[k];
+                W[mm][4] = (qb & 3) ? w32[4] : 0u;
+                dh[mm] = *reinterpret_cast<const __half*>(rowp + 34 * blk);
+            }
+#pragma unroll
+            for (int mm = 0; mm < 4; ++mm) {
+                const int r = 8 * (i + 4 * (mm & 1)) + ci;
+                const int bh = m0 ? bh_of[2 + (mm >> 1)] : bh_of[mm >> 1], blk = bh >> 1, hf = bh & 1;
+                const int sh = ((34 * blk + 2 + 16 * hf) & 3) * 8;
+                const __half2 d2 = __halves2half2(dh[mm], dh[mm]);
                 uint32_t o8[8];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) q4_to_f16(__funnelshift_r(W[k], W[k + 1], sh), d2, o8[2 * k], o8[2 * k + 1]);
+                for (int k = 0; k < 4; ++k)
+                    q4_to_f16(__funnelshift_r(W[mm][k], W[mm][k + 1], sh), d2, o8[2 * k], o8[2 * k + 1]);
                 const int dim0 = 32 * blk + 16 * hf, u0 = (dim0 & 63) >> 3;
                 uint8_t* d0 = dst + (dim0 >> 6) * (TILE * 128) + r * 128 + ((u0 ^ (r & 7)) << 4);
                 *reinterpret_cast<uint4*>(d0) = make_uint4(o8[0], o8[1], o8[2], o8[3]);
                 // unit u0 + 1 (u0 even): the swizzled address XOR 16
                 *reinterpret_cast<uint4*>(reinterpret_cast<uintptr_t>(d0) ^ 16) = make_uint4(o8[4], o8[5], o8[6], o8[7]);
+            }
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -1211,6 +1222,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (plain) {
 #pragma unroll
                     for (int r = 0; r < N; ++r) s[r] = r < rows ? __uint_as_float(sv[r]) * scl : -INFINITY;
+                } else if (!p.mask && !p.has_softcap && p.ring == 0) {
+                    // causal bounds only: row r sees cells [kv_lo, pos0 + qi_r] below the split's end
+                    const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
+#pragma unroll
+                    for (int r = 0; r < N; ++r) {
+                        const bool vis = r < rows && in && (!p.causal || key <= p.pos0 + sm.row_qi[r]);
+                        s[r] = vis ? __uint_as_float(sv[r]) * scl : -INFINITY;
+                    }
                 } else {
                     const bool in = key < key_end;
 #pragma unroll
@@ -1282,16 +1301,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint8_t* pb = sm.p[j & 1][c >> 6];
             const int cc = c & 63;
             if (ok) {
+                // all loads of the row maxima before the first store (the compiler keeps shared loads behind
+                // shared stores), then the stores
 #pragma unroll
                 for (int r = 0; r < N; ++r) {
                     const float mr = sm.mrow[r];
                     const float ref = mr == -INFINITY ? 0.0f : mr;
-                    const float pr = ex2_ftz(s[r] - ref);
-                    l[r] += pr;
+                    s[r] = ex2_ftz(s[r] - ref);
+                    l[r] += s[r];
+                }
+#pragma unroll
+                for (int r = 0; r < N; ++r)
                     if (r < rows)
                         *reinterpret_cast<__half*>(pb + r * 128 + (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) =
-                            __float2half_rn(pr);
-                }
+                            __float2half_rn(s[r]);
             }
             fence_proxy_async_smem();
             tc_fence_before();
