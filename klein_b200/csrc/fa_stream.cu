@@ -839,7 +839,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
 // The same (split, KV head, row chunk) CTAs, on the 5th-generation tensor cores. The rows of a chunk are the N
 // columns (16 or 32) of S^T = K Q^T, computed for 128 cells at a time (M = 128): every K and V byte is read by
 // the tensor core once per CTA instead of once per row group, and the softmax needs no per-row exchange within
-// a thread. Roles (15 warps):
+// a thread. Roles (16 warps):
 //   warps 0-3   softmax, thread = cell (TMEM lane) of the 128-cell block: scale / mask, a running max per row
 //               shared by all cells and raised lazily (only when a block's max exceeds it by more than 2^8,
 //               agreed by a barrier reduction; O^T and the partial sums are rescaled then), P^T as f16 into
@@ -849,16 +849,18 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
 //   warps 8-11  V dequantisation: raw tile -> f16 [64 cells][256 dims] swizzled tile, the A operand V^T of O^T
 //               (bank-conflict-free assignment: 8 consecutive cells x 4 blocks per warp instruction)
 //   warps 12/13 TMA producers of the raw K and V tiles (independent rings of 4 and 3 tiles)
-//   warp 14     MMA issuer: S^T_j (16 MMAs of K 16), then O^T += V^T P^T of block j-1 (2 M-halves x 4 K-steps
-//               per 64-cell tile), so S_{j+1} runs under the softmax of block j
+//   warp 14     S issuer: S^T_j = K_j Q^T (16 MMAs of K 16) into buffer j % 2 once the softmax has read S_{j-2}
+//   warp 15     PV issuer: O^T += V^T P^T of block j (2 M-halves x 4 K-steps per 64-cell tile) once P_j is written.
+//               Two issuers: the tensor core accepts only a few MMAs ahead, so one thread would hold S_{j+2} back
+//               behind the 16 PV MMAs of block j.
 // TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), K f16 2 x 128 at 128.
 // Numerics as the mma.sync kernel's f16 path: Q quantised to q8_0 and widened to f16(q * d), K and V widened
 // to f16(q * d), f32 accumulation, P rounded to f16.
 namespace tc {
 constexpr int BLK = 128;  // cells per S^T block
 constexpr int KRAW = 4, VRAW = 3;
-constexpr int W_KDQ = 4, W_VDQ = 8, W_KTMA = 12, W_VTMA = 13, W_MMA = 14;
-constexpr int THREADS = 15 * 32;
+constexpr int W_KDQ = 4, W_VDQ = 8, W_KTMA = 12, W_VTMA = 13, W_SMMA = 14, W_PVMMA = 15;
+constexpr int THREADS = 16 * 32;
 constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
 constexpr float THRESH = 8.0f;  // log2 units
 
@@ -871,11 +873,12 @@ struct Smem {
     uint8_t vraw[VRAW][QTILE_RAW];
     float red[4][N];                // per-warp row maxima / sums
     float mrow[N];                  // running row maxima (log2 units), shared by all cells
+    float nref[N];                  // -(row max) per row: +inf while the row has seen nothing, -inf past the rows
     float alpha[N];                 // rescale factors of the last raise
     int row_qi[N], row_h[N];
     float row_slope[N];
     uint64_t kfull[KRAW], kempty[KRAW], vfull[VRAW], vempty[VRAW];
-    uint64_t k_full[2], k_free[2], s_full[2], p_full[2], p_free[2], v_full[2], v_free[2], o_done;
+    uint64_t k_full[2], k_free[2], s_full[2], p_full[2], p_free[2], v_full[2], v_free[2], o_done, s_done;
     uint32_t tmem_base;
     int failed;
 };
@@ -983,10 +986,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.v_free[s], 1);
         }
         mbar_init(&sm.o_done, 1);
+        mbar_init(&sm.s_done, 1);
         sm.failed = 0;
         fence_barrier_init();
     }
-    if (warp == W_MMA) {
+    if (warp == W_SMMA) {
         tmem_alloc(&sm.tmem_base, 512);
         tmem_relinquish();
     }
@@ -1045,18 +1049,38 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_4d(dst, map, fullb, 0, hk, (int) (key_begin + (int64_t) t * TILE), kb3, pol);
             }
         }
-    } else if (warp == W_MMA) {
-        // ------------------------------------------------------------------------ MMA issuer
+    } else if (warp == W_SMMA) {
+        // ------------------------------------------------------------------------ S issuer
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(0, BLK, N, false, false);
-            constexpr uint32_t idO = umma_idesc_f16(0, BLK, N, true, false);
             const uint32_t q_addr = smem_u32(sm.q);
-            auto pv = [&](int i) -> bool {
-                if (!wait_or_fail(&sm.p_full[i & 1], (i >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
-                for (int tt = 0; tt < 2; ++tt) {
+            for (int j = 0; j < nblk; ++j) {
+                if (!wait_or_fail(&sm.k_full[j & 1], (j >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
+                // the softmax has read S_{j-2} (it wrote P_{j-2} after its TMEM loads completed)
+                if (j >= 2 && !wait_or_fail(&sm.p_full[j & 1], ((j >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint64_t bdesc = smem_desc_sw128(q_addr + (k >> 2) * (N * 128) + (k & 3) * 32, 16, 1024);
+                    umma_ts(tmem + TM_S + (j & 1) * N, tmem + TM_K + (j & 1) * 128 + k * 8, bdesc, idS, k > 0);
+                }
+                umma_commit(&sm.s_full[j & 1]);
+                umma_commit(&sm.k_free[j & 1]);
+            }
+            umma_commit(&sm.s_done);  // on every path: the wait before the dealloc covers these MMAs
+        }
+    } else if (warp == W_PVMMA) {
+        // ------------------------------------------------------------------------ PV issuer
+        if (lane == 0) {
+            constexpr uint32_t idO = umma_idesc_f16(0, BLK, N, true, false);
+            for (int i = 0; i < nblk; ++i) {
+                if (!wait_or_fail(&sm.p_full[i & 1], (i >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
+                bool ok = true;
+                for (int tt = 0; tt < 2 && ok; ++tt) {
                     const int t = 2 * i + tt;
                     if (t >= n_tiles) break;
-                    if (!wait_or_fail(&sm.v_full[t & 1], (t >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) return false;
+                    ok = wait_or_fail(&sm.v_full[t & 1], (t >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
+                    if (!ok) break;
                     tc_fence_after();
                     const uint32_t v_addr = smem_u32(sm.v[t & 1]), p_addr = smem_u32(sm.p[i & 1][tt]);
 #pragma unroll
@@ -1073,24 +1097,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     umma_commit(&sm.v_free[t & 1]);
                 }
+                if (!ok) break;
                 umma_commit(&sm.p_free[i & 1]);
-                return true;
-            };
-            bool ok = true;
-            for (int j = 0; j < nblk && ok; ++j) {
-                if (!wait_or_fail(&sm.k_full[j & 1], (j >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
-                tc_fence_after();
-#pragma unroll
-                for (int k = 0; k < D / 16; ++k) {
-                    const uint64_t bdesc = smem_desc_sw128(q_addr + (k >> 2) * (N * 128) + (k & 3) * 32, 16, 1024);
-                    umma_ts(tmem + TM_S + (j & 1) * N, tmem + TM_K + (j & 1) * 128 + k * 8, bdesc, idS, k > 0);
-                }
-                umma_commit(&sm.s_full[j & 1]);
-                umma_commit(&sm.k_free[j & 1]);
-                if (j >= 1) ok = pv(j - 1);
             }
-            if (ok && nblk > 0) pv(nblk - 1);
-            umma_commit(&sm.o_done);  // also on failure: the final wait before the dealloc covers every MMA
+            umma_commit(&sm.o_done);  // on every path
         }
     } else if (warp >= W_KDQ && warp < W_VDQ) {
         // ------------------------------------------------------------------------ K dequantisation -> TMEM
@@ -1108,29 +1118,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!ok) break;
                 const uint4* row = reinterpret_cast<const uint4*>(sm.kraw[t % KRAW] + cell * QROW);
                 tc_fence_after();
-                uint32_t w[QROW / 4];
+                // two halves of the row, one loop body: bytes [128 hb, 128 hb + 144) by 9 aligned 16-byte loads;
+                // the half's 4 blocks start at byte 8 hb of that window, so the second half is shifted 2 words
+#pragma unroll 1
+                for (int hb = 0; hb < 2; ++hb) {
+                    uint32_t w[36];
 #pragma unroll
-                for (int blk = 0; blk < D / 32; ++blk) {
-                    // the row in two halves of registers: words 0-35 for blocks 0-3 (bytes 0-135), 32-67 for 4-7
-                    if (blk == 0 || blk == 4) {
+                    for (int u = 0; u < 9; ++u) {
+                        const uint4 x = row[8 * hb + u];
+                        w[4 * u] = x.x, w[4 * u + 1] = x.y, w[4 * u + 2] = x.z, w[4 * u + 3] = x.w;
+                    }
 #pragma unroll
-                        for (int u = (blk == 0 ? 0 : 8); u < (blk == 0 ? 9 : QROW / 16); ++u) {
-                            const uint4 x = row[u];
-                            w[4 * u] = x.x, w[4 * u + 1] = x.y, w[4 * u + 2] = x.z, w[4 * u + 3] = x.w;
+                    for (int k = 0; k < 34; ++k) w[k] = hb ? w[k + 2] : w[k];
+#pragma unroll
+                    for (int bl = 0; bl < 4; ++bl) {
+                        const uint32_t sw = w[(34 * bl) / 4];
+                        const uint16_t dbits = (34 * bl) % 4 == 0 ? (uint16_t) (sw & 0xffffu) : (uint16_t) (sw >> 16);
+                        const __half dh = __ushort_as_half(dbits);
+                        const __half2 d2 = __halves2half2(dh, dh);
+                        uint32_t out[16];
+#pragma unroll
+                        for (int g = 0; g < 8; ++g) {
+                            const int byte = 34 * bl + 2 + 4 * g;
+                            const uint32_t qw =
+                                byte % 4 == 0 ? w[byte / 4] : __funnelshift_r(w[byte / 4], w[byte / 4 + 1], 16);
+                            q4_to_f16(qw, d2, out[2 * g], out[2 * g + 1]);
                         }
+                        tmem_st16(lane_base + TM_K + (j & 1) * 128 + 16 * (4 * hb + bl), out);
                     }
-                    const uint32_t sw = w[(34 * blk) / 4];
-                    const uint16_t dbits = (34 * blk) % 4 == 0 ? (uint16_t) (sw & 0xffffu) : (uint16_t) (sw >> 16);
-                    const __half dh = __ushort_as_half(dbits);
-                    const __half2 d2 = __halves2half2(dh, dh);
-                    uint32_t out[16];
-#pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        const int byte = 34 * blk + 2 + 4 * g;
-                        const uint32_t qw = byte % 4 == 0 ? w[byte / 4] : __funnelshift_r(w[byte / 4], w[byte / 4 + 1], 16);
-                        q4_to_f16(qw, d2, out[2 * g], out[2 * g + 1]);
-                    }
-                    tmem_st16(lane_base + TM_K + (j & 1) * 128 + 16 * blk, out);
                 }
                 tmem_wait_st();
                 __syncwarp();
@@ -1205,58 +1220,79 @@ __global__ void __launch_bounds__(THREADS, 1)
         float l[N];
 #pragma unroll
         for (int r = 0; r < N; ++r) l[r] = 0.0f;
-        if (threadIdx.x < N) sm.mrow[threadIdx.x] = -INFINITY;
+        if (threadIdx.x < N) {
+            sm.mrow[threadIdx.x] = -INFINITY;
+            sm.nref[threadIdx.x] = threadIdx.x < rows ? INFINITY : -INFINITY;
+        }
         named_bar_sync(1, 128);
         bool ok = true;
         for (int j = 0; j < nblk; ++j) {
             ok = ok && wait_or_fail(&sm.s_full[j & 1], (j >> 1) & 1, p, failed, DEV_ERR_WAIT_FULL);
-            float s[N];
+            // x = score (log2 units) - the row's max (+inf for a visible cell of a row that has seen nothing yet);
+            // -inf where not visible and past the rows. With_ref false: the scores themselves.
             const int64_t key0 = key_begin + (int64_t) j * BLK, key = key0 + c;
-            if (ok) {
-                tc_fence_after();
+            auto scores = [&](float (&x)[N], bool with_ref) {
                 uint32_t sv[N];
                 tmem_ld<N>(lane_addr + TM_S + (j & 1) * N, sv);
                 tmem_wait_ld();
                 const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && key0 + BLK <= key_end &&
                                    (!p.causal || (key0 >= p.kv_lo && key0 + BLK - 1 <= min_pos));
-                if (plain) {
+                if (plain && with_ref) {
+                    // pairs of rows on the packed f32x2 pipe: x = s * scale + nref
+                    const uint64_t sc2 = f2pack(scl, scl);
 #pragma unroll
-                    for (int r = 0; r < N; ++r) s[r] = r < rows ? __uint_as_float(sv[r]) * scl : -INFINITY;
+                    for (int r = 0; r < N; r += 4) {
+                        const float4 nr = *reinterpret_cast<const float4*>(sm.nref + r);
+                        f2unpack(ffma2(f2pack(__uint_as_float(sv[r]), __uint_as_float(sv[r + 1])), sc2, f2pack(nr.x, nr.y)),
+                                 x[r], x[r + 1]);
+                        f2unpack(ffma2(f2pack(__uint_as_float(sv[r + 2]), __uint_as_float(sv[r + 3])), sc2,
+                                       f2pack(nr.z, nr.w)),
+                                 x[r + 2], x[r + 3]);
+                    }
                 } else if (!p.mask && !p.has_softcap && p.ring == 0) {
                     // causal bounds only: row r sees cells [kv_lo, pos0 + qi_r] below the split's end
                     const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
 #pragma unroll
                     for (int r = 0; r < N; ++r) {
                         const bool vis = r < rows && in && (!p.causal || key <= p.pos0 + sm.row_qi[r]);
-                        s[r] = vis ? __uint_as_float(sv[r]) * scl : -INFINITY;
+                        x[r] = vis ? fmaf(__uint_as_float(sv[r]), scl, with_ref ? sm.nref[r] : 0.0f) : -INFINITY;
                     }
                 } else {
                     const bool in = key < key_end;
 #pragma unroll
-                    for (int r = 0; r < N; ++r)
-                        s[r] = (r < rows && in) ? masked_score(p, __uint_as_float(sv[r]), key, sm.row_qi[r], sm.row_h[r], b,
-                                                               sm.row_slope[r])
-                                                : -INFINITY;
+                    for (int r = 0; r < N; ++r) {
+                        const float ms = (r < rows && in) ? masked_score(p, __uint_as_float(sv[r]), key, sm.row_qi[r],
+                                                                         sm.row_h[r], b, sm.row_slope[r])
+                                                          : -INFINITY;
+                        x[r] = (ms == -INFINITY || !with_ref) ? ms : ms + sm.nref[r];
+                    }
                 }
+            };
+            float x[N];
+            if (ok) {
+                tc_fence_after();
+                scores(x, true);
             } else {
 #pragma unroll
-                for (int r = 0; r < N; ++r) s[r] = -INFINITY;
+                for (int r = 0; r < N; ++r) x[r] = -INFINITY;
             }
-            // every softmax thread agrees on leaving, and on raising the row maxima
-            if (bar_red_or(1, 128, !ok)) {
-                ok = false;
-                break;
-            }
-            bool bump = false;
+            float xm = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < N; ++r) bump |= s[r] > sm.mrow[r] + THRESH;
-            if (bar_red_or(1, 128, bump)) {
-                // block maxima per row, 16 rows at a time (registers)
+            for (int r = 0; r < N; r += 2) xm = max3f(xm, x[r], x[r + 1]);
+            // one barrier reduction in the common case: does anyone leave, or see a cell more than 2^8 above its
+            // row's reference? (P is computed against the reference, so values up to 2^8 are fine in f16)
+            if (bar_red_or(1, 128, !ok || xm > THRESH)) {
+                if (bar_red_or(1, 128, !ok)) {
+                    ok = false;
+                    break;
+                }
+                // raise: the block's scores again (S_j is still in TMEM), their maxima per row, 16 rows at a time
+                scores(x, false);
 #pragma unroll
                 for (int h16 = 0; h16 < N / 16; ++h16) {
                     float v[16];
 #pragma unroll
-                    for (int r = 0; r < 16; ++r) v[r] = s[16 * h16 + r];
+                    for (int r = 0; r < 16; ++r) v[r] = x[16 * h16 + r];
                     const float wm = warp_rows_reduce<16, true>(v, lane);
                     if (lane < 16) sm.red[warp][16 * h16 + lane] = wm;
                 }
@@ -1267,14 +1303,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const float mo = sm.mrow[r], mn = fmaxf(mo, bm);
                     sm.alpha[r] = mn == mo ? 1.0f : exp2f(mo - mn);
                     sm.mrow[r] = mn;
+                    if (r < rows) sm.nref[r] = mn == -INFINITY ? INFINITY : -mn;
                 }
-                named_bar_sync(1, 128);  // new maxima and factors visible; sm.red read before it is written again
+                named_bar_sync(1, 128);  // new maxima visible; sm.red read before it is written again
                 bool any_alpha = false;
 #pragma unroll
                 for (int r = 0; r < N; ++r) {
                     const float a = sm.alpha[r];
                     any_alpha |= a != 1.0f;
                     l[r] *= a;
+                    x[r] = x[r] == -INFINITY ? -INFINITY : x[r] + sm.nref[r];
                 }
                 if (j > 0 && any_alpha) {
                     // O^T holds PV of blocks 0..j-1: rescale its columns once PV_{j-1} has completed
@@ -1301,20 +1339,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint8_t* pb = sm.p[j & 1][c >> 6];
             const int cc = c & 63;
             if (ok) {
-                // all loads of the row maxima before the first store (the compiler keeps shared loads behind
-                // shared stores), then the stores
 #pragma unroll
                 for (int r = 0; r < N; ++r) {
-                    const float mr = sm.mrow[r];
-                    const float ref = mr == -INFINITY ? 0.0f : mr;
-                    s[r] = ex2_ftz(s[r] - ref);
-                    l[r] += s[r];
+                    x[r] = ex2_ftz(x[r]);
+                    l[r] += x[r];
                 }
 #pragma unroll
                 for (int r = 0; r < N; ++r)
                     if (r < rows)
                         *reinterpret_cast<__half*>(pb + r * 128 + (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) =
-                            __float2half_rn(s[r]);
+                            __float2half_rn(x[r]);
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -1370,11 +1404,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     }
     // every MMA has completed before the columns are released (o_done is committed on every path)
-    if (warp == W_MMA) mbar_wait(&sm.o_done, 0, p.wait_ns);
+    if (warp == W_SMMA) {
+        mbar_wait(&sm.o_done, 0, p.wait_ns);
+        mbar_wait(&sm.s_done, 0, p.wait_ns);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == W_MMA) tmem_dealloc(tmem, 512);
+    if (warp == W_SMMA) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace tc
