@@ -523,6 +523,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         del layers[:]
         torch.cuda.empty_cache()
         layers.extend(make_layers(kb, torch, dev, gen, n_kv, "q8_0"))
+        # the q8_0 kernel plans its own row chunks and splits: size the scratch for it
+        need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]), ctypes.byref(layers[0][3]),
+                                                 ctypes.byref(prm))
+        del scratch
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+        sp = ctypes.c_void_p(scratch.data_ptr())
         for _ in range(args.warmup):
             step(st)
         torch.cuda.synchronize()

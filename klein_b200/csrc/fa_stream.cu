@@ -13,10 +13,10 @@
 // fattn-common.cuh:924-978).
 //
 // f16 cache: TMA writes the K/V tiles straight into the swizzled f16 layout the MMA fragments read.
-// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0) of 64 cells into a 4-deep ring.
-// Q is quantised to q8_0 as ggml quantises it for a q8_0 K (quantize_row_q8_0_ref, ggml-quants.c:276-299) and
-// the scores are int8 MMAs on the raw K blocks scaled per block (ggml's q8_0 x q8_0 dot); only V is
-// dequantised, to f16 (v = f16(q * d), one rounding), for the same P V code as the f16 path.
+// q8_0 cache: a tcgen05 kernel (below, namespace tc): TMA brings the raw 34-byte blocks (ggml-common.h
+// block_q8_0), dequantisation warps widen K into TMEM and V into shared memory, and S^T / O^T are 128-cell
+// tcgen05 MMAs. Q is quantised to q8_0 as ggml quantises it for a q8_0 K (quantize_row_q8_0_ref,
+// ggml-quants.c:276-299) and widened to f16(q * d).
 //
 // Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
 // the K dot type (f16 for f16 K, q8_0 for q8_0 K, :8960), scores are scaled, soft-capped, masked (-inf
@@ -38,8 +38,6 @@ constexpr int STAGE_F16 = 2 * KTILE_F16;       // K + V
 constexpr int ST = FA_STAGES;                  // f16 ring depth
 constexpr int QROW = D / 32 * 34;              // bytes of one head's row in a q8_0 cache (272)
 constexpr int QTILE_RAW = TILE * QROW;         // 17,408 B of raw blocks per tile
-constexpr int QSTAGE = 2 * QTILE_RAW;          // K + V raw
-constexpr int QST = 4;                         // q8_0 raw ring depth
 constexpr int QSTRIDE = D + 8;                 // f16 elements per staged Q row (padded)
 
 __host__ __device__ constexpr int q_bytes(int nrg) { return nrg * 8 * QSTRIDE * 2; }
@@ -48,11 +46,6 @@ __host__ __device__ constexpr size_t smem_f16(int nrg) {
     return 1024 /* alignment slack */ + (size_t) ST * STAGE_F16 + q_bytes(nrg) + 2 * ST * sizeof(uint64_t);
 }
 
-// q8_0 kernel: raw ring | V f16 tiles x 2 | Q int8 [rows][D] | Q block scales f32 [rows][D/32] | barriers
-__host__ __device__ constexpr int q8_qbytes(int nrg) { return nrg * 8 * D + nrg * 8 * (D / 32) * 4; }
-__host__ __device__ constexpr size_t smem_q8(int nrg) {
-    return 1024 + (size_t) QST * QSTAGE + 2 * (size_t) KTILE_F16 + q8_qbytes(nrg) + 2 * QST * sizeof(uint64_t);
-}
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
     if (p.max_bias <= 0.0f) return 1.0f;
@@ -428,279 +421,6 @@ __global__ void __launch_bounds__(NRG * NKG * 32)
                           l1);
 }
 
-// ------------------------------------------------------------------------------------------------ q8_0 cache
-//
-// S^T = K Q^T straight from the raw q8_0 blocks with the int8 tensor-core MMA (m16n8k32: one k32 step = one
-// block): per block, the int32 dot of the quants times d_K times d_Q, which is ggml's q8_0 x q8_0 dot
-// (ggml_vec_dot_q8_0_q8_0 after Q is quantised to K's vec_dot type, ops.cpp:8960). Only V is dequantised to f16
-// (for the P V product), into a double-buffered tile, so the dequantisation of tile t+1 and the math of tile t
-// share one CTA barrier.
-
-// Q rows quantised to q8_0 with quantize_row_q8_0_ref's rounding (d = amax / 127 stored as f16, q = round(x / d)):
-// Qi8 [rows][D] int8, Qd [rows][D/32] f32 (the f16 scale, widened)
-__device__ __forceinline__ void stage_q_int8(const FaStreamParams& p, int8_t* Qi8, float* Qd, int rpc, int rows, int row0,
-                                             int hk, int b) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    for (int task = warp; task < rpc * (D / 32); task += nwarps) {
-        const int r = task / (D / 32), blk = task % (D / 32);
-        float x = 0.0f;
-        if (r < rows) {
-            const int gr = row0 + r;
-            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-            x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
-                                                b * p.q_nb3);
-        }
-        float amax = fabsf(x);
-#pragma unroll
-        for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float d = amax / 127.0f;
-        const float id = d != 0.0f ? 1.0f / d : 0.0f;
-        Qi8[r * D + 32 * blk + lane] = (int8_t) roundf(x * id);
-        if (lane == 0) Qd[r * (D / 32) + blk] = __half2float(__float2half_rn(d));
-    }
-}
-
-// this warp's Q as int8 B fragments (rows 8 rg + lane/4; dims 32 blk + 4 (lane%4) and +16) and the block scales
-// of the two rows its accumulator columns hold (8 rg + 2 (lane%4) and +1)
-__device__ __forceinline__ void load_q8_frags(const int8_t* Qi8, const float* Qd, int rg, int lane, uint32_t (&qb)[8][2],
-                                              float (&dq)[8][2]) {
-    const int g = lane >> 2, tig = lane & 3;
-#pragma unroll
-    for (int blk = 0; blk < D / 32; ++blk) {
-        qb[blk][0] = *reinterpret_cast<const uint32_t*>(Qi8 + (8 * rg + g) * D + 32 * blk + 4 * tig);
-        qb[blk][1] = *reinterpret_cast<const uint32_t*>(Qi8 + (8 * rg + g) * D + 32 * blk + 16 + 4 * tig);
-        dq[blk][0] = Qd[(8 * rg + 2 * tig) * (D / 32) + blk];
-        dq[blk][1] = Qd[(8 * rg + 2 * tig + 1) * (D / 32) + blk];
-    }
-}
-
-// 4 quants at a byte offset that is 2 (mod 4): the two aligned words around them, shifted
-__device__ __forceinline__ uint32_t ld_q4(const uint8_t* base, int off, bool aligned) {
-    if (aligned) return *reinterpret_cast<const uint32_t*>(base + off);
-    return __funnelshift_r(*reinterpret_cast<const uint32_t*>(base + off - 2), *reinterpret_cast<const uint32_t*>(base + off + 2),
-                           16);
-}
-
-// raw scores S^T (cells 16 kg + lane/4 and +8, the rows of the accumulator columns) from the raw K tile
-__device__ __forceinline__ void tile_scores_q8(const uint8_t* kraw, int kg, int lane, const uint32_t (&qb)[8][2],
-                                               const float (&dq)[8][2], float (&x)[4]) {
-    const int g = lane >> 2, tig = lane & 3;
-    const uint8_t* r0 = kraw + (16 * kg + g) * QROW;
-    const uint8_t* r1 = r0 + 8 * QROW;
-    x[0] = x[1] = x[2] = x[3] = 0.0f;
-#pragma unroll
-    for (int blk = 0; blk < D / 32; ++blk) {
-        // quants of block blk start at 34 blk + 2: a multiple of 4 for odd blocks
-        const int off = 34 * blk + 2 + 4 * tig;
-        const bool al = blk & 1;
-        uint32_t a[4];
-        a[0] = ld_q4(r0, off, al);
-        a[1] = ld_q4(r1, off, al);
-        a[2] = ld_q4(r0, off + 16, al);
-        a[3] = ld_q4(r1, off + 16, al);
-        int d[4] = {0, 0, 0, 0};
-        mma_s8_16832(d, a, qb[blk][0], qb[blk][1]);
-        const float k0 = __half2float(*reinterpret_cast<const __half*>(r0 + 34 * blk));
-        const float k1 = __half2float(*reinterpret_cast<const __half*>(r1 + 34 * blk));
-        // sumi * (d_K * d_Q), ggml's order
-        x[0] = fmaf((float) d[0], k0 * dq[blk][0], x[0]);
-        x[1] = fmaf((float) d[1], k0 * dq[blk][1], x[1]);
-        x[2] = fmaf((float) d[2], k1 * dq[blk][0], x[2]);
-        x[3] = fmaf((float) d[3], k1 * dq[blk][1], x[3]);
-    }
-}
-
-// V dequantisation plan of one thread: up to UPT work units (16 elements = half a block of one cell), their
-// sources in a raw stage (2 x the block's offset + which half) and destination offsets in the f16 V tile
-// (-1: no unit)
-constexpr int VUNITS = TILE * (D / 16);
-template <int NT>
-struct VPlan {
-    static constexpr int UPT = (VUNITS + NT - 1) / NT;
-    int src[UPT], dst[UPT];
-    __device__ __forceinline__ void init(int tid) {
-#pragma unroll
-        for (int k = 0; k < UPT; ++k) {
-            const int u = tid + k * NT;
-            if (u < VUNITS) {
-                const int r = u / (D / 16), bh = u % (D / 16), blk = bh >> 1, hf = bh & 1;
-                src[k] = 2 * (QTILE_RAW + r * QROW + blk * 34) + hf;
-                const int dim0 = 32 * blk + 16 * hf, u0 = (dim0 & 63) >> 3;
-                dst[k] = (dim0 >> 6) * (TILE * 128) + r * 128 + ((u0 ^ (r & 7)) << 4);
-            } else {
-                src[k] = 0;
-                dst[k] = -1;
-            }
-        }
-    }
-};
-
-// raw V blocks of one stage -> f16 V tile (128B-swizzled [4 dim boxes][64 cells][128 B]); all loads of a
-// thread's units are in flight before any is converted
-template <int NT>
-__device__ __forceinline__ void dequant_v(const uint8_t* raw, uint8_t* vtile, const VPlan<NT>& pl) {
-    constexpr int UPT = VPlan<NT>::UPT;
-    uint32_t wq[UPT][4];
-    __half dh[UPT];
-#pragma unroll
-    for (int k = 0; k < UPT; ++k) {
-        if (pl.dst[k] >= 0) {
-            const uint8_t* blkp = raw + (pl.src[k] >> 1);  // start of the block (its f16 scale)
-            dh[k] = *reinterpret_cast<const __half*>(blkp);
-            const uint8_t* qp = blkp + 2 + 16 * (pl.src[k] & 1);
-            if ((reinterpret_cast<uintptr_t>(qp) & 3) == 0) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) wq[k][i] = reinterpret_cast<const uint32_t*>(qp)[i];
-            } else {
-                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(qp - 2);
-                uint32_t W[5];
-#pragma unroll
-                for (int i = 0; i < 5; ++i) W[i] = s32[i];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) wq[k][i] = __funnelshift_r(W[i], W[i + 1], 16);
-            }
-        }
-    }
-    const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
-#pragma unroll
-    for (int k = 0; k < UPT; ++k) {
-        if (pl.dst[k] >= 0) {
-            const __half2 d2 = __halves2half2(dh[k], dh[k]);
-            uint32_t outw[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                // int8 q -> f16: (q ^ 0x80) in the low mantissa byte of 1024.0 gives 1152 + q exactly
-                const uint32_t xw = wq[k][i] ^ 0x80808080u;
-                uint32_t lo = __byte_perm(xw, 0x64646464u, 0x4140), hi = __byte_perm(xw, 0x64646464u, 0x4342);
-                __half2 l2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), d2);
-                __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), d2);
-                outw[2 * i] = *reinterpret_cast<uint32_t*>(&l2);
-                outw[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            uint8_t* dst = vtile + pl.dst[k];
-            *reinterpret_cast<uint4*>(dst) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            // the next 16-byte unit of the row: unit index + 1 = unit ^ 1 (the first is even), swizzle preserved
-            *reinterpret_cast<uint4*>(reinterpret_cast<uintptr_t>(dst) ^ 16) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
-        }
-    }
-}
-
-template <int NRG>
-__global__ void __launch_bounds__(NRG * NKG * 32)
-    fa_stream_q8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                        const FaStreamParams p) {
-    constexpr int NC = NRG * NKG;
-    constexpr int RPC = NRG * 8;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* raw = smem;                                 // QST raw stages of K | V blocks
-    uint8_t* vtiles = raw + QST * QSTAGE;                // two dequantised V tiles
-    int8_t* Qi8 = reinterpret_cast<int8_t*>(vtiles + 2 * KTILE_F16);
-    float* Qd = reinterpret_cast<float*>(Qi8 + RPC * D);
-    uint64_t* full = reinterpret_cast<uint64_t*>(Qd + RPC * (D / 32));
-    uint64_t* empty = full + QST;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, hk = blockIdx.y;
-    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
-    const int64_t key_begin = (int64_t) split * p.keys_per_split;
-    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
-    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
-    const int row0 = chunk * RPC;
-    const int rows = min(RPC, p.R - row0);
-    const bool issuer = threadIdx.x == 0;
-
-    uint64_t pol = 0;
-    const int kb3 = b / p.rk3;
-    auto issue = [&](int t) {
-        const int s = t % QST;
-        mbar_arrive_expect_tx(&full[s], QSTAGE);
-        const int key = (int) (key_begin + (int64_t) t * TILE);
-        uint8_t* dst = raw + s * QSTAGE;
-        tma_load_4d(dst, &tmK, &full[s], 0, hk, key, kb3, pol);
-        tma_load_4d(dst + QTILE_RAW, &tmV, &full[s], 0, hk, key, kb3, pol);
-    };
-    if (issuer) {
-        for (int s = 0; s < QST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NC);
-        }
-        fence_barrier_init();
-        if (n_tiles > 0) {
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-            pol = l2_policy_evict_first();
-            for (int t = 0; t < min(QST, n_tiles); ++t) issue(t);
-        }
-    }
-    stage_q_int8(p, Qi8, Qd, RPC, rows, row0, hk, b);
-    __syncthreads();
-
-    bool failed = false;
-    float o[16][4];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-#pragma unroll
-    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
-    const bool active = (warp / NKG) * 8 < rows;
-    uint32_t qb[8][2];
-    float dq[8][2];
-    load_q8_frags(Qi8, Qd, warp / NKG, lane, qb, dq);
-    const WarpCtx w = make_ctx(p, warp, lane, row0, hk);
-    VPlan<NC * 32> plan;
-    plan.init(threadIdx.x);
-
-    // V of tile 0 first; then per tile: dequantise V of tile t+1 into the other buffer, compute tile t
-    if (n_tiles > 0) {
-        if (!mbar_wait(&full[0], 0, p.wait_ns)) {
-            record_error(p.err, DEV_ERR_WAIT_FULL);
-            failed = true;
-        }
-        dequant_v(raw, vtiles, plan);
-    }
-    failed = __syncthreads_or(failed);
-    for (int t = 0; t < n_tiles && !failed; ++t) {
-        const int s = t % QST;
-        if (t + 1 < n_tiles) {
-            const int s1 = (t + 1) % QST;
-            if (!mbar_wait(&full[s1], ((t + 1) / QST) & 1, p.wait_ns)) {
-                record_error(p.err, DEV_ERR_WAIT_FULL);
-                failed = true;
-            }
-            dequant_v(raw + s1 * QSTAGE, vtiles + ((t + 1) & 1) * KTILE_F16, plan);
-        }
-        if (active) {
-            float x[4];
-            tile_scores_q8(raw + s * QSTAGE, w.kg, lane, qb, dq, x);
-            tile_softmax_pv(p, smem_u32(vtiles + (t & 1) * KTILE_F16), key_begin + (int64_t) t * TILE, b, lane, w, x, o,
-                            m0, m1, l0, l1);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // K (scores) and V (dequantised last round) of stage s are consumed
-        // one barrier per tile: V tile t is free for tile t+2, V tile t+1 is complete, and all agree on failures
-        failed = __syncthreads_or(failed);
-        if (issuer && !failed && t + QST < n_tiles) {
-            // every warp has released stage s before the barrier, so this wait returns at once
-            if (!mbar_wait(&empty[s], (t / QST) & 1, p.wait_ns)) {
-                record_error(p.err, DEV_ERR_WAIT_EMPTY);
-                failed = true;
-            } else {
-                issue(t + QST);
-            }
-        }
-    }
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    // an issuer failure after the last barrier is seen by the issuer only: bring everyone to the same exit
-    failed = __syncthreads_or(failed);
-    if (failed) return;  // the error word is set
-    // every issued tile was consumed: the ring and the V tiles are free for the merge buffers
-    merge_key_groups<NRG>(p, reinterpret_cast<float*>(smem), warp, lane, rows, row0, hk, b, split, chunk, o, m0, m1, l0,
-                          l1);
-}
-
 // ------------------------------------------------------------------------------------------------ merges
 
 // Merge of n partial results (o_s, m_s, l_s) of one row by one 256-thread block:
@@ -859,6 +579,10 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
 namespace tc {
 constexpr int BLK = 128;  // cells per S^T block
 constexpr int KRAW = 4, VRAW = 3;
+// Each K-dequantisation warp pair waits on the slots of its own tiles (even or odd) only, so a slot must always
+// carry tiles of one parity: with an odd depth a pair could wait for a phase two ahead of the slot's current one
+// and pass it at once (a parity wait sees only the last two phases).
+static_assert(KRAW % 2 == 0, "K ring slots carry tiles of one parity");
 constexpr int W_KDQ = 4, W_VDQ = 8, W_KTMA = 12, W_VTMA = 13, W_SMMA = 14, W_PVMMA = 15;
 constexpr int THREADS = 16 * 32;
 constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
@@ -1429,11 +1153,11 @@ cudaError_t set_smem_once(Kern kern, size_t smem, bool (&done)[64]) {
     return e;
 }
 
-template <int NRG, bool Q8>
+template <int NRG>
 cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
     static bool attr_done[64] = {};  // the smem attribute is per device: set it once on each
-    auto kern = Q8 ? fa_stream_q8_kernel<NRG> : fa_stream_f16_kernel<NRG>;
-    const size_t smem = Q8 ? smem_q8(NRG) : smem_f16(NRG);
+    auto kern = fa_stream_f16_kernel<NRG>;
+    const size_t smem = smem_f16(NRG);
     cudaError_t e = set_smem_once(kern, smem, attr_done);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
@@ -1479,15 +1203,14 @@ cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int6
     return cudaGetLastError();
 }
 
-size_t fa_stream_smem_bytes(int nrg, int kv_type) { return kv_type == 8 ? smem_q8(nrg) : smem_f16(nrg); }
+size_t fa_stream_smem_bytes(int nrg) { return smem_f16(nrg); }
 
-cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
+cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream) {
-    const bool q8 = kv_type == 8;
     switch (nrg) {
-        case 1: return q8 ? launch_nrg<1, true>(p, tmK, tmV, stream) : launch_nrg<1, false>(p, tmK, tmV, stream);
-        case 2: return q8 ? launch_nrg<2, true>(p, tmK, tmV, stream) : launch_nrg<2, false>(p, tmK, tmV, stream);
-        default: return q8 ? launch_nrg<3, true>(p, tmK, tmV, stream) : launch_nrg<3, false>(p, tmK, tmV, stream);
+        case 1: return launch_nrg<1>(p, tmK, tmV, stream);
+        case 2: return launch_nrg<2>(p, tmK, tmV, stream);
+        default: return launch_nrg<3>(p, tmK, tmV, stream);
     }
 }
 

@@ -310,7 +310,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     if ((st = encode_kv_map(k, &tmK)) != KB_OK) return st;
     if ((st = encode_kv_map(v, &tmV)) != KB_OK) return st;
     cudaError_t e = pl.q8tc ? kb::launch_fa_stream_q8tc(p, pl.rpc, tmK, tmV, static_cast<cudaStream_t>(stream))
-                            : kb::launch_fa_stream(p, pl.nrg, k->type, tmK, tmV, static_cast<cudaStream_t>(stream));
+                            : kb::launch_fa_stream(p, pl.nrg, tmK, tmV, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 

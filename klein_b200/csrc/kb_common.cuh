@@ -176,15 +176,6 @@ __device__ __forceinline__ float ex2_ftz(float x) {
     return y;
 }
 
-// D(16x8 s32) += A(16x32 s8, row) * B(32x8 s8, col)
-__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // transpose of an 8x8 b16 matrix held in the standard fragment layout (thread t: row t/4, cols 2(t%4)..+1)
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
     uint32_t d;

@@ -52,10 +52,10 @@ struct FaStreamParams {
 // rows handled by one CTA for a given row count: 8 * NRG with NRG in 1..3 (more rows -> more CTAs)
 inline int fa_stream_nrg(int R) { return R <= 8 ? 1 : R <= 16 ? 2 : 3; }
 
-size_t fa_stream_smem_bytes(int nrg, int kv_type);
+size_t fa_stream_smem_bytes(int nrg);
 
-// launches the split-KV streaming kernel (+ the LSE combine when n_splits > 1)
-cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, int kv_type, const CUtensorMap& tmK, const CUtensorMap& tmV,
+// launches the split-KV streaming kernel for f16 caches (+ the LSE combine when n_splits > 1)
+cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream);
 
 // q8_0 caches on tcgen05: chunks of rpc = 16 or 32 rows, KV splits of whole 128-cell blocks (FA_TC_BLOCK)
