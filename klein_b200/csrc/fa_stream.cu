@@ -583,18 +583,25 @@ constexpr int KRAW = 4, VRAW = 3;
 // carry tiles of one parity: with an odd depth a pair could wait for a phase two ahead of the slot's current one
 // and pass it at once (a parity wait sees only the last two phases).
 static_assert(KRAW % 2 == 0, "K ring slots carry tiles of one parity");
-constexpr int W_KDQ = 4, W_VDQ = 8, W_KTMA = 12, W_VTMA = 13, W_SMMA = 14, W_PVMMA = 15;
-constexpr int THREADS = 16 * 32;
+// warp roles: q8_0 adds the 8 dequantisation warps (4-11)
+template <bool Q8>
+struct Roles {
+    static constexpr int KDQ = 4, VDQ = 8;
+    static constexpr int KTMA = Q8 ? 12 : 4, VTMA = Q8 ? 13 : 5, SMMA = Q8 ? 14 : 6, PVMMA = Q8 ? 15 : 7;
+    static constexpr int THREADS = (Q8 ? 16 : 8) * 32;
+    static constexpr uint32_t TMEM_COLS = Q8 ? 512 : 128;
+};
 constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
 constexpr float THRESH = 8.0f;  // log2 units
 
-template <int N>
+template <int N, bool Q8>
 struct Smem {
     uint8_t v[2][KTILE_F16];        // f16 V tiles [4 dim chunks][64 cells][128 B], 128B-swizzled
     uint8_t q[D / 64][N * 128];     // Q f16, K-major swizzled: the B operand of S^T
     uint8_t p[2][2][N * 128];       // P^T [buffer][64-cell half][N rows][128 B]: the B operand of O^T
-    uint8_t kraw[KRAW][QTILE_RAW];  // raw q8_0 rows, 272 B per cell
-    uint8_t vraw[VRAW][QTILE_RAW];
+    // q8_0: the raw K ring (272 B per cell); f16: two K blocks [4 dim chunks][128 cells][128 B], the A operand of S^T
+    uint8_t kbuf[Q8 ? KRAW * QTILE_RAW : 2 * 2 * KTILE_F16];
+    uint8_t vraw[Q8 ? VRAW * QTILE_RAW : 16];  // q8_0: the raw V ring
     float red[4][N];                // per-warp row maxima / sums
     float mrow[N];                  // running row maxima (log2 units), shared by all cells
     float nref[N];                  // -(row max) per row: +inf while the row has seen nothing, -inf past the rows
@@ -606,6 +613,8 @@ struct Smem {
     uint32_t tmem_base;
     int failed;
 };
+
+static_assert(sizeof(Smem<32, true>) <= 232448 && sizeof(Smem<32, false>) <= 232448, "fits one SM's shared memory");
 
 __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaStreamParams& p, volatile int* failed,
                                              int code) {
@@ -670,16 +679,20 @@ constexpr uint64_t VSLOTS = 0x0ULL | (0ULL << 0) | (2ULL << 4) | (6ULL << 8) | (
                             (7ULL << 24) | (11ULL << 28) | (14ULL << 32) | (4ULL << 36) | (8ULL << 40) | (12ULL << 44) |
                             (15ULL << 48) | (5ULL << 52) | (9ULL << 56) | (13ULL << 60);
 
-template <int N>
-__global__ void __launch_bounds__(THREADS, 1)
-    fa_stream_q8tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                          const FaStreamParams p) {
+template <int N, bool Q8>
+__global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
+    fa_stream_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        const FaStreamParams p) {
+    using R_ = Roles<Q8>;
+    constexpr int THREADS = R_::THREADS;
+    constexpr int W_KDQ = R_::KDQ, W_VDQ = R_::VDQ, W_KTMA = R_::KTMA, W_VTMA = R_::VTMA, W_SMMA = R_::SMMA,
+                  W_PVMMA = R_::PVMMA;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     if (smem_u32(smem_raw) & 1023) {
         if (threadIdx.x == 0) record_error(p.err, DEV_ERR_ALIGN);
         return;
     }
-    Smem<N>& sm = *reinterpret_cast<Smem<N>*>(smem_raw);
+    Smem<N, Q8>& sm = *reinterpret_cast<Smem<N, Q8>*>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, hk = blockIdx.y;
     const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
@@ -701,12 +714,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.vempty[s], 4);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&sm.k_full[s], 4);
+            // q8_0: the 4 dequantisation warps of each kind arrive; f16: the TMA transaction counts
+            mbar_init(&sm.k_full[s], Q8 ? 4 : 1);
             mbar_init(&sm.k_free[s], 1);
             mbar_init(&sm.s_full[s], 1);
             mbar_init(&sm.p_full[s], 4);
             mbar_init(&sm.p_free[s], 1);
-            mbar_init(&sm.v_full[s], 4);
+            mbar_init(&sm.v_full[s], Q8 ? 4 : 1);
             mbar_init(&sm.v_free[s], 1);
         }
         mbar_init(&sm.o_done, 1);
@@ -715,7 +729,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_barrier_init();
     }
     if (warp == W_SMMA) {
-        tmem_alloc(&sm.tmem_base, 512);
+        tmem_alloc(&sm.tmem_base, R_::TMEM_COLS);
         tmem_relinquish();
     }
     // Q quantised like quantize_row_q8_0_ref, stored as f16(q * d) in the swizzled K-major image; rows past the
@@ -737,8 +751,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float qv = roundf(x * id);
         const float dh = __half2float(__float2half_rn(d));
         const int dim = 32 * blk + lane, e = dim & 63;
+        // q8_0 K: Q rounded to q8_0 (ggml's vec_dot type for q8_0), then f16(q * d); f16 K: Q rounded to f16
         *reinterpret_cast<__half*>(sm.q[dim >> 6] + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
-            __float2half_rn(qv * dh);
+            __float2half_rn(Q8 ? qv * dh : x);
     }
     if (threadIdx.x < N) {
         const int r = threadIdx.x;
@@ -762,15 +777,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             const CUtensorMap* map = is_v ? &tmV : &tmK;
             tma_prefetch_desc(map);
             const uint64_t pol = l2_policy_evict_first();
-            const int depth = is_v ? VRAW : KRAW;
-            for (int t = 0; t < n_tiles; ++t) {
-                const int s = t % depth;
-                uint64_t* empty = is_v ? &sm.vempty[s] : &sm.kempty[s];
-                uint64_t* fullb = is_v ? &sm.vfull[s] : &sm.kfull[s];
-                uint8_t* dst = is_v ? sm.vraw[s] : sm.kraw[s];
-                if (t >= depth && !wait_or_fail(empty, ((t / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
-                mbar_arrive_expect_tx(fullb, QTILE_RAW);
-                tma_load_4d(dst, map, fullb, 0, hk, (int) (key_begin + (int64_t) t * TILE), kb3, pol);
+            if constexpr (Q8) {
+                // raw tiles into rings of KRAW / VRAW tiles
+                const int depth = is_v ? VRAW : KRAW;
+                for (int t = 0; t < n_tiles; ++t) {
+                    const int s = t % depth;
+                    uint64_t* empty = is_v ? &sm.vempty[s] : &sm.kempty[s];
+                    uint64_t* fullb = is_v ? &sm.vfull[s] : &sm.kfull[s];
+                    uint8_t* dst = (is_v ? sm.vraw : sm.kbuf) + s * QTILE_RAW;
+                    if (t >= depth && !wait_or_fail(empty, ((t / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                    mbar_arrive_expect_tx(fullb, QTILE_RAW);
+                    tma_load_4d(dst, map, fullb, 0, hk, (int) (key_begin + (int64_t) t * TILE), kb3, pol);
+                }
+            } else if (!is_v) {
+                // f16 K: 128-cell blocks as [4 dim chunks][128 cells][128 B] (two 64-cell boxes per chunk); a
+                // block's second tile past the split is loaded too (finite cells of the next split, or zeros past
+                // the cache) and masked by the softmax
+                for (int j = 0; j < nblk; ++j) {
+                    if (j >= 2 && !wait_or_fail(&sm.k_free[j & 1], ((j >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                    mbar_arrive_expect_tx(&sm.k_full[j & 1], 2 * KTILE_F16);
+                    uint8_t* dst = sm.kbuf + (j & 1) * 2 * KTILE_F16;
+                    for (int c = 0; c < D / 64; ++c)
+                        for (int h = 0; h < 2; ++h)
+                            tma_load_4d(dst + c * (BLK * 128) + h * (TILE * 128), map, &sm.k_full[j & 1], 64 * c, hk,
+                                        (int) (key_begin + (int64_t) j * BLK + h * TILE), kb3, pol);
+                }
+            } else {
+                // f16 V: 64-cell tiles [4 dim chunks][64 cells][128 B], the A operand V^T as loaded
+                for (int t = 0; t < n_tiles; ++t) {
+                    if (t >= 2 && !wait_or_fail(&sm.v_free[t & 1], ((t >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                    mbar_arrive_expect_tx(&sm.v_full[t & 1], KTILE_F16);
+                    for (int c = 0; c < D / 64; ++c)
+                        tma_load_4d(sm.v[t & 1] + c * (TILE * 128), map, &sm.v_full[t & 1], 64 * c, hk,
+                                    (int) (key_begin + (int64_t) t * TILE), kb3, pol);
+                }
             }
         }
     } else if (warp == W_SMMA) {
@@ -783,10 +823,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // the softmax has read S_{j-2} (it wrote P_{j-2} after its TMEM loads completed)
                 if (j >= 2 && !wait_or_fail(&sm.p_full[j & 1], ((j >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
                 tc_fence_after();
+                const uint32_t k_addr = smem_u32(sm.kbuf + (j & 1) * 2 * KTILE_F16);
 #pragma unroll
                 for (int k = 0; k < D / 16; ++k) {
                     const uint64_t bdesc = smem_desc_sw128(q_addr + (k >> 2) * (N * 128) + (k & 3) * 32, 16, 1024);
-                    umma_ts(tmem + TM_S + (j & 1) * N, tmem + TM_K + (j & 1) * 128 + k * 8, bdesc, idS, k > 0);
+                    if constexpr (Q8) {
+                        // A = K f16 in TMEM (8 packed columns per K-step)
+                        umma_ts(tmem + TM_S + (j & 1) * N, tmem + TM_K + (j & 1) * 128 + k * 8, bdesc, idS, k > 0);
+                    } else {
+                        // A = K block in shared memory, K-major
+                        const uint64_t adesc = smem_desc_sw128(k_addr + (k >> 2) * (BLK * 128) + (k & 3) * 32, 16, 1024);
+                        umma_ss(tmem + TM_S + (j & 1) * N, adesc, bdesc, idS, k > 0);
+                    }
                 }
                 umma_commit(&sm.s_full[j & 1]);
                 umma_commit(&sm.k_free[j & 1]);
@@ -826,7 +874,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             umma_commit(&sm.o_done);  // on every path
         }
-    } else if (warp >= W_KDQ && warp < W_VDQ) {
+    } else if (Q8 && warp >= W_KDQ && warp < W_VDQ) {
         // ------------------------------------------------------------------------ K dequantisation -> TMEM
         const int i = warp - W_KDQ;
         const int half = i >> 1, cell = 32 * (i & 1) + lane;
@@ -840,7 +888,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ok = wait_or_fail(&sm.kfull[t % KRAW], (t / KRAW) & 1, p, failed, DEV_ERR_WAIT_FULL);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
-                const uint4* row = reinterpret_cast<const uint4*>(sm.kraw[t % KRAW] + cell * QROW);
+                const uint4* row = reinterpret_cast<const uint4*>(sm.kbuf + (t % KRAW) * QTILE_RAW + cell * QROW);
                 tc_fence_after();
                 // two halves of the row, one loop body: bytes [128 hb, 128 hb + 144) by 9 aligned 16-byte loads;
                 // the half's 4 blocks start at byte 8 hb of that window, so the second half is shifted 2 words
@@ -879,7 +927,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.k_full[j & 1]);
         }
-    } else if (warp >= W_VDQ && warp < W_KTMA) {
+    } else if (Q8 && warp >= W_VDQ && warp < W_KTMA) {
         // ------------------------------------------------------------------------ V dequantisation -> smem
         const int i = warp - W_VDQ;
         const int ci = lane & 7, slot = lane >> 3;
@@ -891,7 +939,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = ok && (t < 2 || wait_or_fail(&sm.v_free[t & 1], ((t >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY));
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            const uint8_t* raw = sm.vraw[t % VRAW];
+            const uint8_t* raw = sm.vraw + (t % VRAW) * QTILE_RAW;
             uint8_t* dst = sm.v[t & 1];
             // all 8 rounds' loads first, then the conversions and stores (shared loads are not moved past
             // shared stores). Round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, slot set m / 2.
@@ -1135,7 +1183,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == W_SMMA) tmem_dealloc(tmem, 512);
+    if (warp == W_SMMA) tmem_dealloc(tmem, R_::TMEM_COLS);
 }
 
 }  // namespace tc
@@ -1169,15 +1217,15 @@ cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CU
     return cudaGetLastError();
 }
 
-template <int N>
-cudaError_t launch_q8tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
+template <int N, bool Q8>
+cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
     static bool attr_done[64] = {};
-    auto kern = tc::fa_stream_q8tc_kernel<N>;
-    const size_t smem = sizeof(tc::Smem<N>);
+    auto kern = tc::fa_stream_tc_kernel<N, Q8>;
+    const size_t smem = sizeof(tc::Smem<N, Q8>);
     cudaError_t e = set_smem_once(kern, smem, attr_done);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
-    kern<<<grid, tc::THREADS, smem, stream>>>(tmK, tmV, p);
+    kern<<<grid, tc::Roles<Q8>::THREADS, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || p.n_splits == 1) return e;
     dim3 cgrid(p.R, p.n_head_kv, p.ne3);
@@ -1187,12 +1235,18 @@ cudaError_t launch_q8tc(const FaStreamParams& p, const CUtensorMap& tmK, const C
 
 }  // namespace
 
-cudaError_t launch_fa_stream_q8tc(const FaStreamParams& p, int rpc, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                                  cudaStream_t stream) {
-    return rpc <= 16 ? launch_q8tc<16>(p, tmK, tmV, stream) : launch_q8tc<32>(p, tmK, tmV, stream);
+bool fa_stream_use_tc(int kv_type) { return kv_type == 8 || kv_type == 1; }
+
+cudaError_t launch_fa_stream_tc(const FaStreamParams& p, int rpc, int kv_type, const CUtensorMap& tmK,
+                                const CUtensorMap& tmV, cudaStream_t stream) {
+    if (kv_type == 8) return rpc <= 16 ? launch_tc<16, true>(p, tmK, tmV, stream) : launch_tc<32, true>(p, tmK, tmV, stream);
+    return rpc <= 16 ? launch_tc<16, false>(p, tmK, tmV, stream) : launch_tc<32, false>(p, tmK, tmV, stream);
 }
 
-size_t fa_stream_q8tc_smem_bytes(int rpc) { return rpc <= 16 ? sizeof(tc::Smem<16>) : sizeof(tc::Smem<32>); }
+size_t fa_stream_tc_smem_bytes(int rpc, int kv_type) {
+    if (kv_type == 8) return rpc <= 16 ? sizeof(tc::Smem<16, true>) : sizeof(tc::Smem<32, true>);
+    return rpc <= 16 ? sizeof(tc::Smem<16, false>) : sizeof(tc::Smem<32, false>);
+}
 
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int Dd,
                                float* dst, cudaStream_t stream, int* flags, int64_t slot_set_floats, int* err,

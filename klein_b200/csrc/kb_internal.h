@@ -58,12 +58,14 @@ size_t fa_stream_smem_bytes(int nrg);
 cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, const CUtensorMap& tmK, const CUtensorMap& tmV,
                              cudaStream_t stream);
 
-// q8_0 caches on tcgen05: chunks of rpc = 16 or 32 rows, KV splits of whole 128-cell blocks (FA_TC_BLOCK)
+// the tcgen05 streaming kernel (kv_type: KB_TYPE_F16 = 1 or KB_TYPE_Q8_0 = 8): chunks of rpc = 16 or 32 rows, KV
+// splits of whole 128-cell blocks (FA_TC_BLOCK); fa_stream_use_tc says which cache types take it
 constexpr int FA_TC_BLOCK = 128;
-inline int fa_q8tc_rpc(int R) { return R <= 16 ? 16 : 32; }
-size_t fa_stream_q8tc_smem_bytes(int rpc);
-cudaError_t launch_fa_stream_q8tc(const FaStreamParams& p, int rpc, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                                  cudaStream_t stream);
+inline int fa_tc_rpc(int R) { return R <= 16 ? 16 : 32; }
+bool fa_stream_use_tc(int kv_type);
+size_t fa_stream_tc_smem_bytes(int rpc, int kv_type);
+cudaError_t launch_fa_stream_tc(const FaStreamParams& p, int rpc, int kv_type, const CUtensorMap& tmK,
+                                const CUtensorMap& tmV, cudaStream_t stream);
 
 // Parameters of one causal-prefill launch (tcgen05 kernel): one CTA per 128-query tile of one head.
 struct FaPrefillParams {
