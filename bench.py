@@ -645,7 +645,8 @@ def run_case(case: str):
         n_kv = 262144
         global LAYERS
         LAYERS = 1
-        _, _, kv, vv = make_layers(kb, torch, dev, gen, n_kv, "f16" if case == "verify_f16" else "q8_0")[0]
+        # keep the cache tensors (the first two entries) alive: the views only hold their pointers
+        kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, "f16" if case == "verify_f16" else "q8_0")[0]
         q = torch.randn(1, 4, H, D, device=dev, generator=gen)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
     else:

@@ -1,22 +1,17 @@
 // Split-KV streaming attention for decode (1 query token) and the MTP verify step (a few tokens):
-// GGML_OP_FLASH_ATTN_EXT with few query rows over a long KV cache. HBM-bound: every K/V byte is read
-// once, staged by TMA into a shared-memory ring, and consumed by warp-level tensor-core MMA.
+// GGML_OP_FLASH_ATTN_EXT with few query rows over a long KV cache, on the 5th-generation tensor cores.
+// HBM-bound: every K/V byte is read once, by TMA, and consumed by tcgen05 MMAs.
 //
 // Work split. One CTA per (KV split, KV head, row chunk). The rows of a KV head are its n_q * gqa query
-// rows (query i, head-in-group g -> row i*gqa + g); a CTA takes up to 24 of them as NRG groups of 8.
-// Consumer warp (rg, kg) owns row group rg and cells 16kg..16kg+15 of every 64-cell tile, and keeps its
-// own online-softmax state (max, sum, O^T 256x8 in registers) over its cells: S^T = K Q^T (16 cells x 8
-// rows) is an m16n8k16 chain over D, P^T goes from the accumulator into the B fragment of O^T += V^T P^T
-// with two movmatrix transposes, and V^T comes from ldmatrix.trans. At the end the 4 key groups merge
-// through shared memory (log-sum-exp), and when the KV range is split over several CTAs a second kernel
-// merges the per-split partials the same way (the combine of ggml's ops.cpp:9370-9438 /
-// fattn-common.cuh:924-978).
+// rows (query i, head-in-group g -> row i*gqa + g); a chunk of up to 16 or 32 of them forms the N columns of
+// S^T = K Q^T over 128-cell blocks (M = 128), so each K/V byte reaches the tensor core once per CTA. Per-split
+// partials (o, m, l) merge in a second kernel (the combine of ggml's ops.cpp:9370-9438 /
+// fattn-common.cuh:924-978). The kernel, its roles and the softmax scheme are described at namespace tc.
 //
-// f16 cache: TMA writes the K/V tiles straight into the swizzled f16 layout the MMA fragments read.
-// q8_0 cache: a tcgen05 kernel (below, namespace tc): TMA brings the raw 34-byte blocks (ggml-common.h
-// block_q8_0), dequantisation warps widen K into TMEM and V into shared memory, and S^T / O^T are 128-cell
-// tcgen05 MMAs. Q is quantised to q8_0 as ggml quantises it for a q8_0 K (quantize_row_q8_0_ref,
-// ggml-quants.c:276-299) and widened to f16(q * d).
+// f16 cache: TMA writes K blocks and V tiles straight into the swizzled layouts the MMAs read.
+// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0), dequantisation warps widen K into
+// TMEM and V into shared memory. Q is quantised to q8_0 as ggml quantises it for a q8_0 K
+// (quantize_row_q8_0_ref, ggml-quants.c:276-299) and widened to f16(q * d).
 //
 // Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
 // the K dot type (f16 for f16 K, q8_0 for q8_0 K, :8960), scores are scaled, soft-capped, masked (-inf
@@ -32,20 +27,9 @@ namespace {
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int D = FA_D;
 constexpr int TILE = FA_TILE;
-constexpr int NKG = FA_NKG;
 constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 cells][64 dims] f16, 128B-swizzled
-constexpr int STAGE_F16 = 2 * KTILE_F16;       // K + V
-constexpr int ST = FA_STAGES;                  // f16 ring depth
 constexpr int QROW = D / 32 * 34;              // bytes of one head's row in a q8_0 cache (272)
 constexpr int QTILE_RAW = TILE * QROW;         // 17,408 B of raw blocks per tile
-constexpr int QSTRIDE = D + 8;                 // f16 elements per staged Q row (padded)
-
-__host__ __device__ constexpr int q_bytes(int nrg) { return nrg * 8 * QSTRIDE * 2; }
-
-__host__ __device__ constexpr size_t smem_f16(int nrg) {
-    return 1024 /* alignment slack */ + (size_t) ST * STAGE_F16 + q_bytes(nrg) + 2 * ST * sizeof(uint64_t);
-}
-
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
     if (p.max_bias <= 0.0f) return 1.0f;
@@ -90,335 +74,6 @@ __device__ __forceinline__ void store_row(const FaStreamParams& p, int qi, int h
     } else {
         *dst = L > 0.0f ? O / L : 0.0f;
     }
-}
-
-// Per-thread constants of a consumer warp.
-struct WarpCtx {
-    int qi0, qi1, h0, h1;   // the thread's two rows: query index and head
-    float slope0, slope1;   // ALiBi slopes of those heads
-    int64_t min_pos;        // position of the CTA's first query: cells up to it are visible to every row
-    int kg;                 // key group: cells 16kg..16kg+15 of each tile
-    int kkey, kdo;          // K tile row / dim offset addressed by this lane (A fragment)
-    int vkey, vdo;          // V tile row / dim offset addressed by this lane (A^T fragment)
-};
-
-__device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int dim) {
-    // [4 chunks of 64 dims][64 rows][128 B], 16-byte units XOR-swizzled with row % 8 (TMA SWIZZLE_128B)
-    return base + (dim >> 6) * (TILE * 128) + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4);
-}
-
-// One 64-cell tile for one warp: S^T = K Q^T, online softmax, O^T += V^T P^T.
-// kb / vb: shared addresses of the f16 K and V tiles in the swizzled layout.
-// online softmax and O^T += V^T P^T for this warp's 16 cells x 8 rows, from the raw scores x (S^T fragment)
-__device__ __forceinline__ void tile_softmax_pv(const FaStreamParams& p, uint32_t vb, int64_t tkey0, int b, int lane,
-                                                const WarpCtx& w, const float (&x)[4], float (&o)[16][4], float& m0,
-                                                float& m1, float& l0, float& l1) {
-    const int64_t key0 = tkey0 + 16 * w.kg + (lane >> 2), key1 = key0 + 8;
-    const bool plain = !p.mask && !p.has_softcap && p.ring == 0 && tkey0 + TILE <= p.n_kv &&
-                       (!p.causal || (tkey0 >= p.kv_lo && tkey0 + TILE - 1 <= w.min_pos));
-    float sc[4];
-    if (plain) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sc[e] = x[e] * p.scale_log2;
-    } else {
-        sc[0] = masked_score(p, x[0], key0, w.qi0, w.h0, b, w.slope0);
-        sc[1] = masked_score(p, x[1], key0, w.qi1, w.h1, b, w.slope1);
-        sc[2] = masked_score(p, x[2], key1, w.qi0, w.h0, b, w.slope0);
-        sc[3] = masked_score(p, x[3], key1, w.qi1, w.h1, b, w.slope1);
-    }
-    // online softmax over this warp's 16 cells, per row (lanes sharing lane%4 share rows)
-    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float ref0 = mn0 == -INFINITY ? 0.0f : mn0, ref1 = mn1 == -INFINITY ? 0.0f : mn1;
-    const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
-    const float p0 = exp2f(sc[0] - ref0), p1 = exp2f(sc[1] - ref1);
-    const float p2 = exp2f(sc[2] - ref0), p3 = exp2f(sc[3] - ref1);
-    l0 = l0 * al0 + (p0 + p2);
-    l1 = l1 * al1 + (p1 + p3);
-    m0 = mn0;
-    m1 = mn1;
-    if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
-#pragma unroll
-        for (int mm = 0; mm < 16; ++mm) {
-            o[mm][0] *= al0;
-            o[mm][1] *= al1;
-            o[mm][2] *= al0;
-            o[mm][3] *= al1;
-        }
-    }
-    // P^T as the B fragment of O^T += V^T P^T
-    const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
-    const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
-#pragma unroll
-    for (int mm = 0; mm < 16; ++mm) {
-        uint32_t a[4];
-        ldsm_x4_trans(a, swz_addr(vb, w.vkey, 16 * mm + w.vdo));
-        mma_f16_16816(o[mm], a, pb0, pb1);
-    }
-}
-
-__device__ __forceinline__ void tile_compute(const FaStreamParams& p, uint32_t kb, uint32_t vb, int64_t tkey0, int b,
-                                             int lane, const WarpCtx& w, const uint32_t (&qf)[16][2], float (&o)[16][4],
-                                             float& m0, float& m1, float& l0, float& l1) {
-    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-        uint32_t a[4];
-        ldsm_x4(a, swz_addr(kb, w.kkey, 16 * kk + w.kdo));
-        if (kk & 1) mma_f16_16816(acc1, a, qf[kk][0], qf[kk][1]);
-        else mma_f16_16816(acc0, a, qf[kk][0], qf[kk][1]);
-    }
-    float x[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = acc0[e] + acc1[e];
-    tile_softmax_pv(p, vb, tkey0, b, lane, w, x, o, m0, m1, l0, l1);
-}
-
-__device__ __forceinline__ WarpCtx make_ctx(const FaStreamParams& p, int warp, int lane, int row0, int hk) {
-    WarpCtx w;
-    const int rg = warp / NKG;
-    w.kg = warp % NKG;
-    const int mi = lane >> 3, rr = lane & 7;
-    const int gr0 = row0 + 8 * rg + 2 * (lane & 3), gr1 = gr0 + 1;
-    w.qi0 = gr0 / p.gqa;
-    w.qi1 = gr1 / p.gqa;
-    w.h0 = hk * p.gqa + gr0 % p.gqa;
-    w.h1 = hk * p.gqa + gr1 % p.gqa;
-    w.slope0 = slope_of(p, w.h0);
-    w.slope1 = slope_of(p, w.h1);
-    w.min_pos = p.pos0 + row0 / p.gqa;
-    w.kkey = 16 * w.kg + (mi & 1) * 8 + rr;
-    w.kdo = (mi >> 1) * 8;
-    w.vkey = 16 * w.kg + (mi >> 1) * 8 + rr;
-    w.vdo = (mi & 1) * 8;
-    return w;
-}
-
-// Q fragments (B operand of S^T = K Q^T) of row group rg from the staged f16 Q rows
-__device__ __forceinline__ void load_q_frags(const __half* Qs, int rg, int lane, uint32_t (&qf)[16][2]) {
-    const int mi = lane >> 3, rr = lane & 7;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        uint32_t r4[4];
-        ldsm_x4(r4, smem_u32(Qs + (8 * rg + rr) * QSTRIDE + 32 * j + 8 * mi));
-        qf[2 * j][0] = r4[0];
-        qf[2 * j][1] = r4[1];
-        qf[2 * j + 1][0] = r4[2];
-        qf[2 * j + 1][1] = r4[3];
-    }
-}
-
-// Stages the CTA's Q rows as f16 (f16 K: Q is rounded to f16, ggml's vec_dot type for an f16 K).
-__device__ __forceinline__ void stage_q(const FaStreamParams& p, __half* Qs, int rpc, int rows, int row0, int hk, int b) {
-    if (p.q_vec4) {
-        for (int idx = threadIdx.x; idx < rpc * (D / 4); idx += blockDim.x) {
-            const int r = idx / (D / 4), c4 = idx % (D / 4);
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < rows) {
-                const int gr = row0 + r;
-                const int qi = gr / p.gqa, h = hk * p.gqa + (gr - qi * p.gqa);
-                x = *reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3 + c4 * 16);
-            }
-            __half2* dst = reinterpret_cast<__half2*>(Qs + r * QSTRIDE + 4 * c4);
-            dst[0] = __floats2half2_rn(x.x, x.y);
-            dst[1] = __floats2half2_rn(x.z, x.w);
-        }
-    } else {
-        for (int idx = threadIdx.x; idx < rpc * D; idx += blockDim.x) {
-            const int r = idx / D, d = idx % D;
-            float x = 0.0f;
-            if (r < rows) {
-                const int gr = row0 + r;
-                const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-                x = *reinterpret_cast<const float*>(p.q + (int64_t) d * 4 + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3);
-            }
-            Qs[r * QSTRIDE + d] = __float2half_rn(x);
-        }
-    }
-}
-
-// Merges the 4 key groups of every row group (through shared memory) and writes the CTA's result: the
-// final output when the KV range is not split, else the split's (o, m, l) partial.
-template <int NRG>
-__device__ __forceinline__ void merge_key_groups(const FaStreamParams& p, float* Ow, int warp, int lane, int rows, int row0,
-                                                 int hk, int b, int split, int chunk, const float (&o)[16][4], float m0,
-                                                 float m1, float l0, float l1) {
-    constexpr int NC = NRG * NKG, RPC = NRG * 8;
-    float* Mw = Ow + NC * 8 * D;  // [NC][8]
-    float* Lw = Mw + NC * 8;      // [NC][8]
-    {
-        const int ra = 2 * (lane & 3), dl = lane >> 2;
-        float* ow = Ow + warp * 8 * D;
-#pragma unroll
-        for (int mm = 0; mm < 16; ++mm) {
-            ow[ra * D + 16 * mm + dl] = o[mm][0];
-            ow[(ra + 1) * D + 16 * mm + dl] = o[mm][1];
-            ow[ra * D + 16 * mm + 8 + dl] = o[mm][2];
-            ow[(ra + 1) * D + 16 * mm + 8 + dl] = o[mm][3];
-        }
-        if (lane < 4) {
-            Mw[warp * 8 + 2 * lane] = m0;
-            Mw[warp * 8 + 2 * lane + 1] = m1;
-            Lw[warp * 8 + 2 * lane] = l0;
-            Lw[warp * 8 + 2 * lane + 1] = l1;
-        }
-    }
-    __syncthreads();
-    const int64_t part_row0 = ((((int64_t) b * p.n_head_kv + hk) * p.n_row_chunks + chunk) * p.n_splits + split) * RPC;
-    for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
-        const int r = idx / D, d = idx % D;
-        const int rg = r >> 3, ri = r & 7;
-        float M = -INFINITY;
-#pragma unroll
-        for (int kg = 0; kg < NKG; ++kg) M = fmaxf(M, Mw[(rg * NKG + kg) * 8 + ri]);
-        float O = 0.0f, L = 0.0f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int kg = 0; kg < NKG; ++kg) {
-                const int wi = rg * NKG + kg;
-                const float f = exp2f(Mw[wi * 8 + ri] - M);
-                O += f * Ow[(wi * 8 + ri) * D + d];
-                L += f * Lw[wi * 8 + ri];
-            }
-        }
-        if (p.n_splits == 1) {
-            const int gr = row0 + r;
-            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-            store_row(p, qi, h, b, d, O, M, L);
-        } else {
-            p.o_part[(part_row0 + r) * D + d] = O;
-            if (d == 0) {
-                p.ml_part[(part_row0 + r) * 2 + 0] = M;
-                p.ml_part[(part_row0 + r) * 2 + 1] = L;
-            }
-        }
-    }
-}
-
-// ------------------------------------------------------------------------------------------------ f16 cache
-
-template <int NRG>
-__global__ void __launch_bounds__(NRG * NKG * 32)
-    fa_stream_f16_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                         const FaStreamParams p) {
-    constexpr int NC = NRG * NKG;  // consumer warps; lane 0 of warp 0 also issues the TMA loads
-    constexpr int RPC = NRG * 8;   // rows per CTA
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = smem;
-    __half* Qs = reinterpret_cast<__half*>(smem + ST * STAGE_F16);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * STAGE_F16 + q_bytes(NRG));
-    uint64_t* empty = full + ST;
-    __shared__ int s_failed;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, hk = blockIdx.y;
-    const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
-    const int64_t key_begin = (int64_t) split * p.keys_per_split;
-    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
-    const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
-    const int row0 = chunk * RPC;
-    const int rows = min(RPC, p.R - row0);
-    const bool issuer = threadIdx.x == 0;
-
-    // TMA issue state (meaningful in the issuing thread only)
-    int next_issue = 0;
-    uint64_t pol = 0;
-    const int kb3 = b / p.rk3;
-    auto issue = [&](int t) {
-        const int s = t % ST;
-        mbar_arrive_expect_tx(&full[s], STAGE_F16);
-        const int key = (int) (key_begin + (int64_t) t * TILE);
-        uint8_t* kdst = stages + s * STAGE_F16;
-        uint8_t* vdst = kdst + KTILE_F16;
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(kdst + c * (TILE * 128), &tmK, &full[s], c * 64, hk, key, kb3, pol);
-            tma_load_4d(vdst + c * (TILE * 128), &tmV, &full[s], c * 64, hk, key, kb3, pol);
-        }
-    };
-    if (issuer) {
-        s_failed = 0;
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NC);
-        }
-        fence_barrier_init();
-        // start streaming before anything else: the first stages land while Q is staged
-        if (n_tiles > 0) {
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-            pol = l2_policy_evict_first();
-            for (; next_issue < min(ST, n_tiles); ++next_issue) issue(next_issue);
-        }
-    }
-    stage_q(p, Qs, RPC, rows, row0, hk, b);
-    __syncthreads();
-
-    bool failed = false;
-    float o[16][4];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-#pragma unroll
-    for (int mm = 0; mm < 16; ++mm) o[mm][0] = o[mm][1] = o[mm][2] = o[mm][3] = 0.0f;
-    const bool active = (warp / NKG) * 8 < rows;
-    uint32_t qf[16][2];
-    load_q_frags(Qs, warp / NKG, lane, qf);
-    const WarpCtx w = make_ctx(p, warp, lane, row0, hk);
-
-    for (int t = 0; t < n_tiles; ++t) {
-        const int s = t % ST;
-        if (issuer) {
-            // tile t must have been issued: wait for its stage to be released by every warp
-            while (next_issue <= t) {
-                const int si = next_issue % ST;
-                if (!mbar_wait(&empty[si], ((next_issue / ST) - 1) & 1, p.wait_ns)) {
-                    record_error(p.err, DEV_ERR_WAIT_EMPTY);
-                    failed = true;
-                    break;
-                }
-                issue(next_issue++);
-            }
-        }
-        __syncwarp();
-        if (!failed && !mbar_wait(&full[s], (t / ST) & 1, p.wait_ns)) {
-            record_error(p.err, DEV_ERR_WAIT_FULL);
-            failed = true;
-        }
-        if (__any_sync(0xffffffffu, failed)) {
-            failed = true;
-            break;
-        }
-        if (active) {
-            const uint32_t kb = smem_u32(stages + s * STAGE_F16);
-            tile_compute(p, kb, kb + KTILE_F16, key_begin + (int64_t) t * TILE, b, lane, w, qf, o, m0, m1, l0, l1);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (issuer) {
-            // refill without blocking: issue every further tile whose stage all warps have released
-            while (next_issue < n_tiles && next_issue < t + 1 + ST) {
-                const int si = next_issue % ST;
-                if (!mbar_try_wait(&empty[si], ((next_issue / ST) - 1) & 1)) break;
-                issue(next_issue++);
-            }
-        }
-    }
-    // row sums over the warp's lanes
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    if (failed && lane == 0) atomicExch(&s_failed, 1);
-    __syncthreads();  // every issued stage consumed: the ring is free for the merge buffers
-    if (s_failed) return;  // a bounded wait ran out (error word set): leave the outputs alone
-    merge_key_groups<NRG>(p, reinterpret_cast<float*>(stages), warp, lane, rows, row0, hk, b, split, chunk, o, m0, m1, l0,
-                          l1);
 }
 
 // ------------------------------------------------------------------------------------------------ merges
@@ -554,28 +209,31 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
     merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
 }
 
-// ------------------------------------------------------------------------------------------------ q8_0 cache, tcgen05
+// ------------------------------------------------------------------------------------------------ tcgen05 kernel
 //
-// The same (split, KV head, row chunk) CTAs, on the 5th-generation tensor cores. The rows of a chunk are the N
-// columns (16 or 32) of S^T = K Q^T, computed for 128 cells at a time (M = 128): every K and V byte is read by
-// the tensor core once per CTA instead of once per row group, and the softmax needs no per-row exchange within
-// a thread. Roles (16 warps):
-//   warps 0-3   softmax, thread = cell (TMEM lane) of the 128-cell block: scale / mask, a running max per row
-//               shared by all cells and raised lazily (only when a block's max exceeds it by more than 2^8,
-//               agreed by a barrier reduction; O^T and the partial sums are rescaled then), P^T as f16 into
-//               shared memory, partial row sums per thread (summed once at the end)
+// One CTA per (split, KV head, row chunk). The rows of a chunk are the N columns (16 or 32) of S^T = K Q^T,
+// computed for 128 cells at a time (M = 128): every K and V byte is read by the tensor core once per CTA, and the
+// softmax needs no per-row exchange within a thread. Roles (q8_0: 16 warps; f16: 8 warps, no dequantisation):
+//   warps 0-3   softmax, thread = cell (TMEM lane) of the 128-cell block: x = score - row max against row maxima
+//               kept in shared memory (+inf for a row that has seen nothing), one barrier reduction per block to
+//               check max x <= 8 (log2 units, so P <= 2^8 in f16); when a row max rises the scores are re-read
+//               from TMEM, the maxima recomputed, O^T and the partial sums rescaled. P^T as f16 into shared
+//               memory; partial row sums per thread, summed once at the end
+//   q8_0 only:
 //   warps 4-7   K dequantisation, thread = cell: its raw q8_0 row (17 aligned 16-byte loads) -> 256 f16 values
 //               f16(q * d) -> TMEM, the A operand of S^T (TS form)
 //   warps 8-11  V dequantisation: raw tile -> f16 [64 cells][256 dims] swizzled tile, the A operand V^T of O^T
 //               (bank-conflict-free assignment: 8 consecutive cells x 4 blocks per warp instruction)
-//   warps 12/13 TMA producers of the raw K and V tiles (independent rings of 4 and 3 tiles)
-//   warp 14     S issuer: S^T_j = K_j Q^T (16 MMAs of K 16) into buffer j % 2 once the softmax has read S_{j-2}
-//   warp 15     PV issuer: O^T += V^T P^T of block j (2 M-halves x 4 K-steps per 64-cell tile) once P_j is written.
-//               Two issuers: the tensor core accepts only a few MMAs ahead, so one thread would hold S_{j+2} back
-//               behind the 16 PV MMAs of block j.
-// TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), K f16 2 x 128 at 128.
-// Numerics as the mma.sync kernel's f16 path: Q quantised to q8_0 and widened to f16(q * d), K and V widened
-// to f16(q * d), f32 accumulation, P rounded to f16.
+//   then (q8_0 warps 12-15, f16 warps 4-7):
+//               TMA producers of K and V (q8_0: raw tile rings of 4 and 3; f16: two 128-cell K blocks, the SS-form
+//               A operand of S^T, and two 64-cell V tiles)
+//               S issuer: S^T_j = K_j Q^T (16 MMAs of K 16) into buffer j % 2 once the softmax has read S_{j-2}
+//               PV issuer: O^T += V^T P^T of block j (2 M-halves x 4 K-steps per 64-cell tile) once P_j is
+//               written. Two issuers: the tensor core accepts only a few MMAs ahead, so one thread would hold
+//               S_{j+2} back behind the 16 PV MMAs of block j.
+// TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), q8_0: K f16 2 x 128 at 128.
+// Numerics: f16 K: Q rounded to f16; q8_0 K: Q quantised to q8_0 and widened to f16(q * d), K and V widened to
+// f16(q * d). f32 accumulation, P rounded to f16.
 namespace tc {
 constexpr int BLK = 128;  // cells per S^T block
 constexpr int KRAW = 4, VRAW = 3;
@@ -1201,22 +859,6 @@ cudaError_t set_smem_once(Kern kern, size_t smem, bool (&done)[64]) {
     return e;
 }
 
-template <int NRG>
-cudaError_t launch_nrg(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
-    static bool attr_done[64] = {};  // the smem attribute is per device: set it once on each
-    auto kern = fa_stream_f16_kernel<NRG>;
-    const size_t smem = smem_f16(NRG);
-    cudaError_t e = set_smem_once(kern, smem, attr_done);
-    if (e != cudaSuccess) return e;
-    dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
-    kern<<<grid, NRG * NKG * 32, smem, stream>>>(tmK, tmV, p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess || p.n_splits == 1) return e;
-    dim3 cgrid(p.R, p.n_head_kv, p.ne3);
-    fa_combine_kernel<NRG * 8><<<cgrid, MERGE_THREADS, 0, stream>>>(p);
-    return cudaGetLastError();
-}
-
 template <int N, bool Q8>
 cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
     static bool attr_done[64] = {};
@@ -1234,8 +876,6 @@ cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUt
 }
 
 }  // namespace
-
-bool fa_stream_use_tc(int kv_type) { return kv_type == 8 || kv_type == 1; }
 
 cudaError_t launch_fa_stream_tc(const FaStreamParams& p, int rpc, int kv_type, const CUtensorMap& tmK,
                                 const CUtensorMap& tmV, cudaStream_t stream) {
@@ -1255,17 +895,6 @@ cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int6
     lse_combine_kernel<<<(unsigned) rows, MERGE_THREADS, 0, stream>>>(o_parts, ml_parts, stride, n_parts, rows, Dd, dst,
                                                                         flags, slot_set_floats, err, wait_ns);
     return cudaGetLastError();
-}
-
-size_t fa_stream_smem_bytes(int nrg) { return smem_f16(nrg); }
-
-cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                             cudaStream_t stream) {
-    switch (nrg) {
-        case 1: return launch_nrg<1>(p, tmK, tmV, stream);
-        case 2: return launch_nrg<2>(p, tmK, tmV, stream);
-        default: return launch_nrg<3>(p, tmK, tmV, stream);
-    }
 }
 
 }  // namespace kb

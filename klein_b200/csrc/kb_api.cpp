@@ -54,8 +54,7 @@ bool aligned16(size_t x) { return (x & 15) == 0; }
 
 // The split-KV plan of one streaming attention call.
 struct FaPlan {
-    bool tc = false;  // the tcgen05 streaming kernel
-    int nrg = 1, rpc = 8, n_row_chunks = 1, n_splits = 1;
+    int rpc = 32, n_row_chunks = 1, n_splits = 1;
     int64_t keys_per_split = 0;
     size_t scratch = 0;
 };
@@ -112,14 +111,12 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
 
 FaPlan plan_fa(const FaShape& s) {
     FaPlan pl;
-    pl.tc = kb::fa_stream_use_tc(s.kv_type);
-    pl.nrg = kb::fa_stream_nrg(s.R);
-    pl.rpc = pl.tc ? kb::fa_tc_rpc(s.R) : pl.nrg * 8;
+    pl.rpc = kb::fa_tc_rpc(s.R);
     pl.n_row_chunks = (s.R + pl.rpc - 1) / pl.rpc;
     const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
     const int64_t base = (int64_t) s.H_kv * pl.n_row_chunks * s.ne3;
-    // split unit: a 64-cell tile, or a 128-cell block for the tcgen05 kernel
-    const int unit = pl.tc ? kb::FA_TC_BLOCK : kb::FA_TILE;
+    // split unit: a 128-cell block
+    const int unit = kb::FA_TC_BLOCK;
     const int64_t tiles = (s.n_kv + unit - 1) / unit;
     int64_t target = sms / base;
     if (target < 1) target = 1;
@@ -309,8 +306,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     CUtensorMap tmK, tmV;
     if ((st = encode_kv_map(k, &tmK)) != KB_OK) return st;
     if ((st = encode_kv_map(v, &tmV)) != KB_OK) return st;
-    cudaError_t e = pl.tc ? kb::launch_fa_stream_tc(p, pl.rpc, s.kv_type, tmK, tmV, static_cast<cudaStream_t>(stream))
-                          : kb::launch_fa_stream(p, pl.nrg, tmK, tmV, static_cast<cudaStream_t>(stream));
+    cudaError_t e = kb::launch_fa_stream_tc(p, pl.rpc, s.kv_type, tmK, tmV, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 

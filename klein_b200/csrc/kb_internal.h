@@ -11,14 +11,12 @@ namespace kb {
 
 constexpr int FA_D = 256;            // head dimension of qwen35 full attention (K and V)
 constexpr int FA_TILE = 64;          // keys per pipeline stage
-constexpr int FA_STAGES = 3;         // TMA pipeline depth
-constexpr int FA_NKG = 4;            // key groups (consumer warps per 8-row group)
 
 // Parameters of one streaming (decode / verify) attention launch. Byte strides follow ggml.
 struct FaStreamParams {
     const char* q;                   // f32 [D, n_q, H, ne3]
     int64_t q_nb1, q_nb2, q_nb3;
-    int q_vec4;                      // q rows 16-byte aligned: stage them with float4 loads
+    int q_vec4;                      // q rows 16-byte aligned
     int n_q, n_head, n_head_kv, gqa, ne3, rk3;
     int R;                           // rows per KV head = n_q * gqa
     int64_t n_kv;
@@ -36,8 +34,8 @@ struct FaStreamParams {
     int64_t pos0, kv_lo, ring;
     // KV split
     int n_splits;
-    int64_t keys_per_split;          // multiple of FA_TILE
-    int n_row_chunks;                // CTAs along the rows of one KV head (24 rows each at most)
+    int64_t keys_per_split;          // multiple of FA_TC_BLOCK
+    int n_row_chunks;                // CTAs along the rows of one KV head (16 or 32 rows each at most)
     // outputs
     float* o_part;                   // scratch: [ne3][H_kv][chunk][split][RPC][D]
     float* ml_part;                  // scratch: [ne3][H_kv][chunk][split][RPC][2] (max in log2 units, sum)
@@ -49,20 +47,10 @@ struct FaStreamParams {
     uint64_t wait_ns;                // budget of every bounded wait
 };
 
-// rows handled by one CTA for a given row count: 8 * NRG with NRG in 1..3 (more rows -> more CTAs)
-inline int fa_stream_nrg(int R) { return R <= 8 ? 1 : R <= 16 ? 2 : 3; }
-
-size_t fa_stream_smem_bytes(int nrg);
-
-// launches the split-KV streaming kernel for f16 caches (+ the LSE combine when n_splits > 1)
-cudaError_t launch_fa_stream(const FaStreamParams& p, int nrg, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                             cudaStream_t stream);
-
 // the tcgen05 streaming kernel (kv_type: KB_TYPE_F16 = 1 or KB_TYPE_Q8_0 = 8): chunks of rpc = 16 or 32 rows, KV
-// splits of whole 128-cell blocks (FA_TC_BLOCK); fa_stream_use_tc says which cache types take it
+// splits of whole 128-cell blocks (FA_TC_BLOCK)
 constexpr int FA_TC_BLOCK = 128;
 inline int fa_tc_rpc(int R) { return R <= 16 ? 16 : 32; }
-bool fa_stream_use_tc(int kv_type);
 size_t fa_stream_tc_smem_bytes(int rpc, int kv_type);
 cudaError_t launch_fa_stream_tc(const FaStreamParams& p, int rpc, int kv_type, const CUtensorMap& tmK,
                                 const CUtensorMap& tmV, cudaStream_t stream);
