@@ -118,15 +118,17 @@ kb_status kb_lse_combine(const float* o_parts, const float* ml_parts, int64_t pa
  * the KV-sequence split; ggml's split-KV exchanges them between CPU threads, ops.cpp:9489-9520, and has no
  * multi-GPU counterpart). One process per GPU; every rank holds
  *   a gather buffer  two slot sets of n_ranks packed partials (slot_set_floats >= n_ranks * part_floats each)
- *   a flag array     int32 [n_ranks + 2], zero at start: one epoch per source rank, then this rank's epoch
- *                    counter and a completion counter used by the merge
+ *   a flag array     int32 [n_ranks + 2], zero at start: one arrival count per source rank, then this rank's
+ *                    epoch counter and a completion counter used by the merge
  * both from kb_peer_alloc (zeroed device memory with a 64-byte CUDA IPC handle); kb_peer_open maps another
  * process's buffer from its handle (peer access over NVLink), kb_peer_close unmaps, kb_peer_free releases.
  *   kb_partials_push     writes `part` (this rank's packed partial, part_floats floats, 16-byte aligned) into slot
- *                        `rank` of slot set (e & 1) of every rank's gather buffer, e = this rank's counter + 1, then
- *                        stores e into flags[r][rank] of every rank r with system-scope release. gather / flags: host
- *                        arrays of n_ranks (<= KB_MAX_PEERS) device pointers, this rank's own buffers included.
- *   kb_lse_combine_wait  waits until every source's epoch in this rank's flag array reaches counter + 1 (gives up
+ *                        `rank` of slot set (e & 1) of every rank's gather buffer, e = this rank's counter + 1, in
+ *                        32 chunks per destination; each chunk then adds 1 to flags[r][rank] of its destination r
+ *                        with system-scope release, so a complete push of exchange e leaves 32 e there. gather /
+ *                        flags: host arrays of n_ranks (<= KB_MAX_PEERS) device pointers, this rank's own buffers
+ *                        included.
+ *   kb_lse_combine_wait  waits until every source's count in this rank's flag array reaches 32 (counter + 1) (gives up
  *                        after 1 s and sets the device error word), merges that slot set of this rank's gather
  *                        buffer like kb_lse_combine (parts at gather + p * part_stride, (m, l) after the rows * D
  *                        output floats), and advances the counter.
@@ -210,6 +212,31 @@ kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t co
  * An out-of-range index (ggml asserts) skips that row and sets the device error word (kb_device_error).
  */
 kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream);
+
+/*
+ * The attention prologue of klein's Builder::attention (src/graph.cpp:94-112) in one launch: the q / gate split of
+ * the interleaved query projection, ggml_rms_norm(eps) * q_norm / k_norm on every head row, ggml_rope_multi on q and
+ * k, ggml_cont of the gate, and ggml_set_rows of the K and V rows into the caches. Operands (ggml ne / nb):
+ *   qfull  f32 [2 hd nh, n] (per head: hd query values then hd gate values), rows of nb[1] bytes
+ *   kcur, vcur  f32 [hd nkv, n]            pos  i32 [4 n] (section-major: t..., h..., w..., extra...)
+ *   kv_idx i64 [n] (cache cell of each token)              q_norm, k_norm  f32 [hd]
+ *   q_out  f32 [hd, nh, n] contiguous      gate_out  f32 [hd nh, n] contiguous
+ *   k_cache, v_cache  f16 or q8_0 [hd nkv, n_cells] (klein's cache rows)
+ * hd is 64, 128 or 256; rope->n_rot a multiple of 64, at most hd. A kv_idx outside [0, n_cells) skips that row
+ * and sets the device error word.
+ */
+typedef struct kb_rope_params {
+    int32_t n_rot;       /* rotated dims (the first n_rot of each head) */
+    int32_t sections[4]; /* M-RoPE sections: pairs per position component (t, h, w, extra) */
+    int32_t mode;        /* 40 = GGML_ROPE_TYPE_IMROPE (interleaved sections, qwen35) or 8 = GGML_ROPE_TYPE_MROPE */
+    float freq_base;     /* theta base */
+    float freq_scale;    /* 1 for qwen35 */
+    float attn_factor;   /* 1 for qwen35 (YaRN extrapolation is not supported: ext_factor 0) */
+} kb_rope_params;
+kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const kb_tensor* vcur, const kb_tensor* pos,
+                           const kb_tensor* kv_idx, const kb_tensor* q_norm, const kb_tensor* k_norm, float rms_eps,
+                           const kb_rope_params* rope, const kb_tensor* q_out, const kb_tensor* gate_out,
+                           const kb_tensor* k_cache, const kb_tensor* v_cache, void* stream);
 
 /*
  * Size of the device buffer built into the library for kb_flash_attn_ext_noalloc (per GPU, held from the

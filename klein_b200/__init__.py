@@ -46,6 +46,7 @@ EXPORTED = [
     "kb_peer_free",
     "kb_partials_push",
     "kb_lse_combine_wait",
+    "kb_attn_prologue",
 ]
 
 
@@ -57,6 +58,12 @@ class KbError(RuntimeError):
 
 class KbTensor(ctypes.Structure):
     _fields_ = [("type", c_int32), ("ne", c_int64 * 4), ("nb", c_size_t * 4), ("data", c_void_p)]
+
+
+class KbRopeParams(ctypes.Structure):
+    """kb_rope_params: M-RoPE of ggml_rope_multi (mode 40 = IMROPE, 8 = MROPE)."""
+    _fields_ = [("n_rot", c_int32), ("sections", c_int32 * 4), ("mode", c_int32), ("freq_base", ctypes.c_float),
+                ("freq_scale", ctypes.c_float), ("attn_factor", ctypes.c_float)]
 
 
 class KbFaParams(ctypes.Structure):
@@ -100,6 +107,8 @@ def lib():
                                             c_int32, c_void_p]
         L.kb_set_rows.restype = c_int32
         L.kb_set_rows.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), c_void_p]
+        L.kb_attn_prologue.restype = c_int32
+        L.kb_attn_prologue.argtypes = [P(KbTensor)] * 7 + [ctypes.c_float, P(KbRopeParams)] + [P(KbTensor)] * 4 + [c_void_p]
         L.kb_device_error.restype = c_int32
         L.kb_device_error.argtypes = [P(c_int32), c_int32]
         L.kb_version.restype = ctypes.c_char_p
@@ -318,6 +327,39 @@ def set_rows(dst: KbTensor, src, idx, stream=None):
     it = from_torch(idx)
     rc = lib().kb_set_rows(ctypes.byref(dst), ctypes.byref(st), ctypes.byref(it), c_void_p(_stream(src, stream)))
     check("kb_set_rows", rc)
+
+
+def attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, rms_eps: float, n_rot: int, sections, mode: int,
+                  freq_base: float, k_cache: KbTensor, v_cache: KbTensor, freq_scale: float = 1.0,
+                  attn_factor: float = 1.0, stream=None):
+    """klein's attention prologue (graph.cpp:94-112) through kb_attn_prologue. qfull torch f32 [n][nh * 2 hd], kcur /
+    vcur f32 [n][nkv * hd], pos i32 [4 n], kv_idx i64 [n], q_norm / k_norm f32 [hd]; k_cache / v_cache: kb_tensor
+    views [nkv * hd, n_cells] (cache_rows). Returns (q f32 [n][nh][hd], gate f32 [n][nh * hd])."""
+    import torch
+
+    hd = q_norm.shape[-1]
+    n = qfull.shape[0]
+    nh = qfull.shape[1] // (2 * hd)
+    q = torch.empty((n, nh, hd), dtype=torch.float32, device=qfull.device)
+    gate = torch.empty((n, nh * hd), dtype=torch.float32, device=qfull.device)
+    rp = KbRopeParams(n_rot, (c_int32 * 4)(*sections), mode, freq_base, freq_scale, attn_factor)
+    ts = [from_torch(x) for x in (qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm)]
+    rc = lib().kb_attn_prologue(*[ctypes.byref(t) for t in ts], ctypes.c_float(rms_eps), ctypes.byref(rp),
+                                ctypes.byref(from_torch(q)), ctypes.byref(from_torch(gate)), ctypes.byref(k_cache),
+                                ctypes.byref(v_cache), c_void_p(_stream(qfull, stream)))
+    check("kb_attn_prologue", rc)
+    return q, gate
+
+
+def cache_rows(cache, kv_type: int) -> KbTensor:
+    """kb_tensor of a whole cache as ggml's 2-d rows tensor [row elements, n_cells] (the set_rows destination)."""
+    row_bytes = cache.stride(0) * cache.element_size()
+    if kv_type == Q8_0:
+        return kb_tensor(cache.data_ptr(), kv_type, [row_bytes // Q8_0_BLOCK_BYTES * 32, cache.shape[0], 1, 1],
+                         [Q8_0_BLOCK_BYTES, row_bytes, row_bytes * cache.shape[0], row_bytes * cache.shape[0]])
+    es = TYPE_SIZE[kv_type]
+    return kb_tensor(cache.data_ptr(), kv_type, [row_bytes // es, cache.shape[0], 1, 1],
+                     [es, row_bytes, row_bytes * cache.shape[0], row_bytes * cache.shape[0]])
 
 
 def rollback_recurrent(convs, snaps, ssms, snap_type: int, s: int, n_snapshots: int, stream=None):

@@ -1,0 +1,141 @@
+// Attention prologue: the ops between the Q/K/V projections and GGML_OP_FLASH_ATTN_EXT in klein's
+// Builder::attention (graph.cpp:94-112), in one launch instead of a chain of ggml nodes:
+//   q, gate  = the two halves of each head's slice of the interleaved projection [2 hd] (ggml_view_3d)
+//   q, k     = ggml_rms_norm(x, eps) * weight per head row (ops.cpp:4107-4167: the sum of squares in double,
+//              mean rounded to float, scale = 1 / sqrtf(mean + eps), y = x * scale * w)
+//   q, k     = ggml_rope_multi, M-RoPE with interleaved sections for GGML_ROPE_TYPE_IMROPE (ops.cpp:6219-6306,
+//              6376-6450): NeoX pairs (i, i + n_rot / 2) over the first n_rot dims, theta of pair i = the position
+//              component its sector selects times theta_scale^i (the same running f32 product), no YaRN ramp
+//   gate     = ggml_cont of the gate half
+//   caches   = ggml_set_rows of the normed, roped K rows and the V rows at kv_idx, f32 -> f16 (round to
+//              nearest) or q8_0 (per 32 values: d = amax / 127, q = roundf(x / d), as kb_set_rows)
+//
+// Layout: one warp per (token, row), rows = the nh query heads, then the nkv K heads, then the nkv V heads.
+// Lane l holds dims l, l + 32, ..., so a 32-dim q8_0 block is one register across the warp and a rope pair
+// (i, i + n_rot / 2) sits in one lane whenever n_rot / 2 is a multiple of 32.
+#include "kb_common.cuh"
+#include "kb_internal.h"
+
+namespace kb {
+
+namespace {
+
+template <int EPL>  // elements per lane: hd / 32
+__global__ void __launch_bounds__(256) attn_prologue_kernel(const PrologueParams p) {
+    constexpr int HD = 32 * EPL;
+    const int lane = threadIdx.x & 31;
+    const int64_t task = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int rows = p.nh + 2 * p.nkv;
+    if (task >= (int64_t) p.n * rows) return;
+    const int t = (int) (task / rows), r = (int) (task % rows);
+    const bool is_q = r < p.nh, is_v = r >= p.nh + p.nkv;
+    const int kh = is_q ? 0 : (r - p.nh) % p.nkv;
+
+    const float* src = is_q ? reinterpret_cast<const float*>(p.qfull + t * p.q_nb1) + (int64_t) r * 2 * HD
+                            : reinterpret_cast<const float*>(is_v ? p.vcur + t * p.v_nb1 : p.kcur + t * p.k_nb1) + (int64_t) kh * HD;
+    float x[EPL];
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) x[k] = src[lane + 32 * k];
+    if (is_q) {
+        // the gate half, copied as it is
+        const float* gsrc = src + HD;
+        float* gdst = p.gate_out + ((int64_t) t * p.nh + r) * HD;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) gdst[lane + 32 * k] = gsrc[lane + 32 * k];
+    }
+    if (!is_v) {
+        // RMS norm: the sum of squares of float products, accumulated in double as ggml does
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) ss += (double) (x[k] * x[k]);
+#pragma unroll
+        for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float mean = (float) (ss / HD);
+        const float scale = 1.0f / sqrtf(mean + p.eps);
+        const float* w = is_q ? p.q_norm : p.k_norm;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) x[k] = x[k] * scale * w[lane + 32 * k];
+        // M-RoPE over pairs (i, i + n_rot / 2), i = lane + 32 j: element j and its partner j + n_rot / 64
+        const int off = p.n_rot / 64;
+#pragma unroll
+        for (int j = 0; j < EPL; ++j) {
+            if (j >= off) break;
+            const int i = lane + 32 * j;
+            const int sector = i % p.sect_dims;
+            int comp;
+            if (p.imrope) {
+                if (sector % 3 == 1 && sector < 3 * p.sections[1]) comp = 1;
+                else if (sector % 3 == 2 && sector < 3 * p.sections[2]) comp = 2;
+                else if (sector % 3 == 0 && sector < 3 * p.sections[0]) comp = 0;
+                else comp = 3;
+            } else {
+                const int sec_w = p.sections[0] + p.sections[1];
+                if (sector >= p.sections[0] && sector < sec_w) comp = 1;
+                else if (sector >= sec_w && sector < sec_w + p.sections[2]) comp = 2;
+                else if (sector >= sec_w + p.sections[2]) comp = 3;
+                else comp = 0;
+            }
+            float theta = (float) p.pos[(int64_t) comp * p.n + t];
+            for (int s = 0; s < i; ++s) theta *= p.theta_scale;  // ggml's running product, pair by pair
+            theta *= p.freq_scale;
+            const float c = cosf(theta) * p.attn_factor, sn = sinf(theta) * p.attn_factor;
+            float x1 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < EPL; ++k)
+                if (k == j + off) x1 = x[k];
+            const float x0 = x[j];
+            const float y1 = x0 * sn + x1 * c;
+            x[j] = x0 * c - x1 * sn;
+#pragma unroll
+            for (int k = 0; k < EPL; ++k)
+                if (k == j + off) x[k] = y1;
+        }
+    }
+    if (is_q) {
+        float* dst = p.q_out + ((int64_t) t * p.nh + r) * HD;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) dst[lane + 32 * k] = x[k];
+        return;
+    }
+    // K / V row into the cache
+    const int64_t cell = p.kv_idx[t];
+    if (cell < 0 || cell >= p.n_cells) {
+        if (lane == 0) record_error(p.err, 1);
+        return;
+    }
+    char* row = (is_v ? p.v_cache : p.k_cache) + cell * (is_v ? p.vc_nb1 : p.kc_nb1);
+    if (p.cache_type == 1) {
+        __half* d = reinterpret_cast<__half*>(row) + (int64_t) kh * HD;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) d[lane + 32 * k] = __float2half_rn(x[k]);
+    } else {  // q8_0: block k of this head = lanes 0-31 of register k
+        char* hb = row + (int64_t) kh * (HD / 32) * 34;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            float amax = fabsf(x[k]);
+#pragma unroll
+            for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            char* b = hb + k * 34;
+            b[2 + lane] = (char) (int8_t) roundf(x[k] * id);
+            if (lane == 0) *reinterpret_cast<__half*>(b) = __float2half_rn(d);
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_attn_prologue(const PrologueParams& p, int hd, cudaStream_t stream) {
+    const int64_t tasks = (int64_t) p.n * (p.nh + 2 * p.nkv);
+    if (tasks == 0) return cudaSuccess;
+    const unsigned grid = (unsigned) ((tasks + 7) / 8);
+    switch (hd) {
+        case 64: attn_prologue_kernel<2><<<grid, 256, 0, stream>>>(p); break;
+        case 128: attn_prologue_kernel<4><<<grid, 256, 0, stream>>>(p); break;
+        default: attn_prologue_kernel<8><<<grid, 256, 0, stream>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace kb

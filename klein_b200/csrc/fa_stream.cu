@@ -176,10 +176,13 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
             epoch = *reinterpret_cast<volatile int*>(flags + n_parts) + 1;
             const uint64_t t0 = globaltimer_ns();
             for (int p = 0; p < n_parts && ready; ++p) {
+                // a source's flag counts its pushed chunks: epoch * PUSH_CHUNKS once this epoch's push is complete
+                // (compared as a wrapping difference)
+                const unsigned target = (unsigned) epoch * (unsigned) PUSH_CHUNKS;
                 for (;;) {
-                    int v;
-                    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
-                    if (v - epoch >= 0) break;
+                    unsigned v;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
+                    if ((int) (v - target) >= 0) break;
                     if (globaltimer_ns() - t0 > wait_ns) {
                         record_error(err, DEV_ERR_WAIT_PEER);
                         ready = 0;

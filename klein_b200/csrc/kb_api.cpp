@@ -650,6 +650,72 @@ kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tenso
     return kb::launch_set_rows(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 
+kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const kb_tensor* vcur, const kb_tensor* pos,
+                           const kb_tensor* kv_idx, const kb_tensor* q_norm, const kb_tensor* k_norm, float rms_eps,
+                           const kb_rope_params* rope, const kb_tensor* q_out, const kb_tensor* gate_out,
+                           const kb_tensor* k_cache, const kb_tensor* v_cache, void* stream) {
+    if (!qfull || !kcur || !vcur || !pos || !kv_idx || !q_norm || !k_norm || !rope || !q_out || !gate_out || !k_cache ||
+        !v_cache)
+        return KB_ERR_ARG;
+    if (!rows_f32(qfull) || !rows_f32(kcur) || !rows_f32(vcur) || !contiguous_f32(q_norm) || !contiguous_f32(k_norm) ||
+        !contiguous_f32(q_out) || !contiguous_f32(gate_out))
+        return KB_ERR_UNSUPPORTED;
+    if (pos->type != KB_TYPE_I32 || kv_idx->type != KB_TYPE_I64) return KB_ERR_UNSUPPORTED;
+    const int64_t hd = q_norm->ne[0];
+    if (hd != 64 && hd != 128 && hd != 256) return KB_ERR_UNSUPPORTED;
+    const int64_t n = qfull->ne[1];
+    if (qfull->ne[0] % (2 * hd) != 0 || kcur->ne[0] % hd != 0) return KB_ERR_BAD_SHAPE;
+    const int64_t nh = qfull->ne[0] / (2 * hd), nkv = kcur->ne[0] / hd;
+    if (nh <= 0 || nkv <= 0 || k_norm->ne[0] != hd || vcur->ne[0] != kcur->ne[0] || kcur->ne[1] != n ||
+        vcur->ne[1] != n || pos->ne[0] < 4 * n || kv_idx->ne[0] != n)
+        return KB_ERR_BAD_SHAPE;
+    if (q_out->ne[0] != hd || q_out->ne[1] != nh || q_out->ne[2] != n || gate_out->ne[0] != hd * nh || gate_out->ne[1] != n)
+        return KB_ERR_BAD_SHAPE;
+    const int ct = k_cache->type;
+    if ((ct != KB_TYPE_F16 && ct != KB_TYPE_Q8_0) || v_cache->type != ct) return KB_ERR_UNSUPPORTED;
+    if (k_cache->ne[0] != hd * nkv || v_cache->ne[0] != hd * nkv || v_cache->ne[1] != k_cache->ne[1]) return KB_ERR_BAD_SHAPE;
+    if (k_cache->nb[0] != (ct == KB_TYPE_F16 ? 2u : 34u) || v_cache->nb[0] != k_cache->nb[0]) return KB_ERR_BAD_SHAPE;
+    if (rope->n_rot <= 0 || rope->n_rot % 64 != 0 || rope->n_rot > hd) return KB_ERR_UNSUPPORTED;
+    if (rope->mode != 40 && rope->mode != 8) return KB_ERR_UNSUPPORTED;
+    const int sect = rope->sections[0] + rope->sections[1] + rope->sections[2] + rope->sections[3];
+    if (sect <= 0 || rope->sections[0] < 0 || rope->sections[1] < 0 || rope->sections[2] < 0 || rope->sections[3] < 0)
+        return KB_ERR_BAD_SHAPE;
+    if (n == 0) return KB_OK;
+    kb::PrologueParams p{};
+    p.qfull = static_cast<const char*>(qfull->data);
+    p.q_nb1 = (int64_t) qfull->nb[1];
+    p.kcur = static_cast<const char*>(kcur->data);
+    p.vcur = static_cast<const char*>(vcur->data);
+    p.k_nb1 = (int64_t) kcur->nb[1];
+    p.v_nb1 = (int64_t) vcur->nb[1];
+    p.pos = static_cast<const int32_t*>(pos->data);
+    p.kv_idx = static_cast<const int64_t*>(kv_idx->data);
+    p.q_norm = static_cast<const float*>(q_norm->data);
+    p.k_norm = static_cast<const float*>(k_norm->data);
+    p.q_out = static_cast<float*>(q_out->data);
+    p.gate_out = static_cast<float*>(gate_out->data);
+    p.k_cache = static_cast<char*>(k_cache->data);
+    p.v_cache = static_cast<char*>(v_cache->data);
+    p.kc_nb1 = (int64_t) k_cache->nb[1];
+    p.vc_nb1 = (int64_t) v_cache->nb[1];
+    p.n_cells = k_cache->ne[1];
+    p.cache_type = ct;
+    p.n = (int) n;
+    p.nh = (int) nh;
+    p.nkv = (int) nkv;
+    p.eps = rms_eps;
+    p.n_rot = rope->n_rot;
+    for (int i = 0; i < 4; ++i) p.sections[i] = rope->sections[i];
+    p.sect_dims = sect;
+    p.imrope = rope->mode == 40;
+    // ggml: theta_scale = powf(freq_base, -2.0f / n_dims) (ops.cpp:6371)
+    p.theta_scale = std::pow(rope->freq_base, -2.0f / (float) rope->n_rot);
+    p.freq_scale = rope->freq_scale;
+    p.attn_factor = rope->attn_factor;
+    p.err = kb::device_error_word();
+    return kb::launch_attn_prologue(p, (int) hd, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
 kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t conv_row, const void* const* snap,
                                 int32_t snap_type, float* const* ssm, int64_t ssm_row, int32_t s, int32_t n_snapshots,
                                 void* stream) {

@@ -102,7 +102,34 @@ struct PeerPushParams {
     int* flags[MAX_PEERS];               // each rank's flag array [n_ranks flags | epoch counter | done counter]
     int rank, n_ranks;
 };
+constexpr int PUSH_CHUNKS = 32;  // CTAs per destination of a push; a complete push counts this many in its flag
 cudaError_t launch_partials_push(const PeerPushParams& p, cudaStream_t stream);
+
+// Parameters of the attention prologue (attn_prologue.cu): Q/gate split, RMS norms, M-RoPE, KV-cache writes.
+struct PrologueParams {
+    const char* qfull;               // f32 [n][nh][2 hd]: q then gate per head
+    int64_t q_nb1;
+    const char* kcur;                // f32 [n][nkv][hd]
+    const char* vcur;
+    int64_t k_nb1, v_nb1;
+    const int32_t* pos;              // [4][n], section-major
+    const int64_t* kv_idx;           // [n]
+    const float* q_norm;             // [hd]
+    const float* k_norm;
+    float* q_out;                    // f32 [n][nh][hd]
+    float* gate_out;                 // f32 [n][nh][hd]
+    char* k_cache;                   // f16 / q8_0 rows of nkv * hd values
+    char* v_cache;
+    int64_t kc_nb1, vc_nb1, n_cells;
+    int cache_type;                  // KB_TYPE_F16 or KB_TYPE_Q8_0
+    int n, nh, nkv;
+    float eps;
+    int n_rot, sect_dims, imrope;
+    int sections[4];
+    float theta_scale, freq_scale, attn_factor;
+    int* err;
+};
+cudaError_t launch_attn_prologue(const PrologueParams& p, int hd, cudaStream_t stream);
 
 int* device_error_word();
 

@@ -93,6 +93,9 @@ def ref():
         lib.kbref_set_rows.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int]
         lib.kbref_cpy.restype = c_int
         lib.kbref_cpy.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int64]
+        lib.kbref_attn_prologue.restype = c_int
+        lib.kbref_attn_prologue.argtypes = [c_void_p] * 7 + [c_int] * 4 + [c_float, c_int, c_void_p, c_int, c_float, c_int] + \
+            [c_void_p] * 4 + [c_int, c_int64, c_int]
         _ref = lib
     return _ref
 
@@ -241,6 +244,33 @@ def ref_set_rows(cache: np.ndarray, dst_type: int, row_elems: int, src: np.ndarr
                                 n_threads)
 
 
+def ref_attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, eps, n_rot, sections, mode, freq_base,
+                      k_cache, v_cache, cache_type, n_ctx_orig=262144, n_threads=1):
+    """Builder::attention's prologue on the reference ggml CPU ops (graph.cpp:94-112). qfull f32 [n][nh * 2 hd],
+    kcur / vcur f32 [n][nkv * hd], pos i32 [4 n], kv_idx i64 [n], q_norm / k_norm f32 [hd]; the caches (numpy
+    byte or f16 arrays [n_cells][row]) are written in place. Returns (q [n][nh][hd], gate [n][nh * hd])."""
+    qfull = np.ascontiguousarray(qfull, dtype=np.float32)
+    kcur = np.ascontiguousarray(kcur, dtype=np.float32)
+    vcur = np.ascontiguousarray(vcur, dtype=np.float32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    kv_idx = np.ascontiguousarray(kv_idx, dtype=np.int64)
+    q_norm = np.ascontiguousarray(q_norm, dtype=np.float32)
+    k_norm = np.ascontiguousarray(k_norm, dtype=np.float32)
+    hd = q_norm.shape[0]
+    n = qfull.shape[0]
+    nh = qfull.shape[1] // (2 * hd)
+    nkv = kcur.shape[1] // hd
+    sec = np.ascontiguousarray(sections, dtype=np.int32)
+    q_out = np.zeros((n, nh, hd), np.float32)
+    gate = np.zeros((n, nh * hd), np.float32)
+    rc = ref().kbref_attn_prologue(_ptr(qfull), _ptr(kcur), _ptr(vcur), _ptr(pos), _ptr(kv_idx), _ptr(q_norm),
+                                   _ptr(k_norm), hd, nh, nkv, n, eps, n_rot, _ptr(sec), mode, freq_base, n_ctx_orig,
+                                   _ptr(q_out), _ptr(gate), _ptr(k_cache), _ptr(v_cache), cache_type, k_cache.shape[0],
+                                   n_threads)
+    assert rc == 0
+    return q_out, gate
+
+
 def ref_cpy(src: np.ndarray, src_type: int, dst: np.ndarray, dst_type: int) -> int:
     return ref().kbref_cpy(_ptr(src), src_type, _ptr(dst), dst_type, src.size)
 
@@ -308,3 +338,57 @@ def q_round_f16(q: np.ndarray) -> np.ndarray:
 def q_round_q8_0(q: np.ndarray) -> np.ndarray:
     """Q as the q8_0 K dot type sees it, with quantize_row_q8_0_ref rounding."""
     return rs_dequantize_q8_0(rs_quantize_q8_0(q))
+
+
+def rs_attn_prologue(qfull, kcur, pos, q_norm, k_norm, eps, n_rot, sections, mode, freq_base):
+    """Restatement of the attention prologue's arithmetic (TEST INFRASTRUCTURE): RMS norm with weight
+    (ggml-cpu/ops.cpp:4107-4167) and ggml_rope_multi (ops.cpp:6219-6306, 6376-6450) on q and k. The rope angles
+    follow ggml's running f32 product theta_{i+1} = theta_i * theta_scale; the rest is float64.
+    Returns (q [n][nh][hd], k [n][nkv][hd], gate [n][nh * hd])."""
+    hd = q_norm.shape[0]
+    n = qfull.shape[0]
+    nh = qfull.shape[1] // (2 * hd)
+    nkv = kcur.shape[1] // hd
+    qg = qfull.reshape(n, nh, 2, hd).astype(np.float64)
+    q, gate = qg[:, :, 0, :], qg[:, :, 1, :].reshape(n, nh * hd)
+    k = kcur.reshape(n, nkv, hd).astype(np.float64)
+
+    def rms(x, w):
+        ms = (x * x).mean(-1, keepdims=True)
+        return x / np.sqrt(ms + eps) * w.astype(np.float64)
+
+    q, k = rms(q, q_norm), rms(k, k_norm)
+    half = n_rot // 2
+    sect = sum(sections)
+    theta_scale = np.float32(np.power(np.float32(freq_base), np.float32(-2.0) / np.float32(n_rot)))
+    cos = np.zeros((n, half))
+    sin = np.zeros((n, half))
+    for t in range(n):
+        th = [np.float32(pos[c * n + t]) for c in range(4)]
+        for i in range(half):
+            sector = i % sect
+            if mode == 40:
+                if sector % 3 == 1 and sector < 3 * sections[1]:
+                    c = 1
+                elif sector % 3 == 2 and sector < 3 * sections[2]:
+                    c = 2
+                elif sector % 3 == 0 and sector < 3 * sections[0]:
+                    c = 0
+                else:
+                    c = 3
+            else:
+                sw = sections[0] + sections[1]
+                c = 1 if sections[0] <= sector < sw else 2 if sw <= sector < sw + sections[2] else 3 if sector >= sw + sections[2] else 0
+            cos[t, i] = np.cos(np.float64(th[c]))
+            sin[t, i] = np.sin(np.float64(th[c]))
+            th = [np.float32(x * theta_scale) for x in th]
+
+    def rope(x):
+        y = x.copy()
+        x0, x1 = x[..., :half], x[..., half:n_rot]
+        c, s_ = cos[:, None, :], sin[:, None, :]
+        y[..., :half] = x0 * c - x1 * s_
+        y[..., half:n_rot] = x0 * s_ + x1 * c
+        return y
+
+    return rope(q), rope(k), gate

@@ -12,6 +12,9 @@
 //   kbref_quantize_q8_0    ggml_quantize_chunk(Q8_0) -> quantize_row_q8_0_ref (ggml-quants.c:276-299)
 //   kbref_set_rows         ggml_set_rows as in src/graph.cpp:111-112; CPU op ops.cpp:5446-5530
 //   kbref_cpy              ggml_cpy f32<->f16 (snapshot write graph.cpp:179-184, rollback state.cpp:162-183)
+//   kbref_attn_prologue    the ops between the projections and the attention in Builder::attention
+//                          (src/graph.cpp:94-112): q / gate views, ggml_rms_norm * weight, ggml_rope_multi,
+//                          ggml_cont of the gate, ggml_set_rows of K and V into the caches
 //
 // use_ref = 1 selects ggml's vec-only reference path (no split-KV, no tiling; ops.cpp:9487-9550),
 // which makes results independent of the thread count.
@@ -137,6 +140,56 @@ int kbref_cpy(const void* src, int src_type, void* dst, int dst_type, int64_t n)
     ggml_tensor* d = bind(c.ctx, (ggml_type) dst_type, n, 1, 1, 1, dst);
     ggml_tensor* r = ggml_cpy(c.ctx, s, d);
     return compute(c.ctx, r, 1, 0);
+}
+
+// Builder::attention's prologue for n tokens (graph.cpp:94-112). qfull f32 [n][nh][2 hd] (q then gate per head),
+// kcur / vcur f32 [n][nkv][hd], pos i32 [4][n] (section-major), kv_idx i64 [n], q_norm / k_norm f32 [hd];
+// outputs q_out f32 [n][nh][hd] (normed, roped), gate_out f32 [n][nh][hd], rows kv_idx of the caches
+// (cache_type, [n_cells][nkv * hd]) written.
+int kbref_attn_prologue(const float* qfull, const float* kcur, const float* vcur, const int32_t* pos,
+                        const int64_t* kv_idx, const float* q_norm, const float* k_norm, int hd, int nh, int nkv, int n,
+                        float eps, int n_rot, const int32_t* sections, int mode, float freq_base, int n_ctx_orig,
+                        float* q_out, float* gate_out, void* k_cache, void* v_cache, int cache_type, int64_t n_cells,
+                        int n_threads) {
+    init_once();
+    const size_t mem = (size_t) 16 * (2 * (size_t) hd * nh + 2 * (size_t) hd * nkv) * (size_t) n * 4 + ((size_t) 8 << 20);
+    ggml_init_params ip{mem, nullptr, false};
+    ggml_context* ctx = ggml_init(ip);
+    if (!ctx) return 1;
+    auto bindx = [&](ggml_type t, int64_t n0, int64_t n1, int64_t n2, const void* data) {
+        ggml_tensor* x = ggml_new_tensor_3d(ctx, t, n0, n1, n2);
+        x->data = const_cast<void*>(data);
+        return x;
+    };
+    ggml_tensor* qf = bindx(GGML_TYPE_F32, (int64_t) 2 * hd * nh, n, 1, qfull);
+    const size_t es = sizeof(float);
+    ggml_tensor* q = ggml_view_3d(ctx, qf, hd, nh, n, es * hd * 2, es * hd * 2 * nh, 0);
+    ggml_tensor* qn = bindx(GGML_TYPE_F32, hd, 1, 1, q_norm);
+    ggml_tensor* kn = bindx(GGML_TYPE_F32, hd, 1, 1, k_norm);
+    q = ggml_mul(ctx, ggml_rms_norm(ctx, q, eps), qn);
+    ggml_tensor* gate = ggml_view_3d(ctx, qf, hd, nh, n, es * hd * 2, es * hd * 2 * nh, es * hd);
+    gate = ggml_cont_2d(ctx, gate, (int64_t) hd * nh, n);
+    ggml_tensor* k = bindx(GGML_TYPE_F32, hd, nkv, n, kcur);
+    ggml_tensor* v = bindx(GGML_TYPE_F32, hd, nkv, n, vcur);
+    k = ggml_mul(ctx, ggml_rms_norm(ctx, k, eps), kn);
+    ggml_tensor* pt = bindx(GGML_TYPE_I32, (int64_t) 4 * n, 1, 1, pos);
+    int sec[4] = {sections[0], sections[1], sections[2], sections[3]};
+    q = ggml_rope_multi(ctx, q, pt, nullptr, n_rot, sec, mode, n_ctx_orig, freq_base, 1.0f, 0.0f, 1.0f, 32.0f, 1.0f);
+    k = ggml_rope_multi(ctx, k, pt, nullptr, n_rot, sec, mode, n_ctx_orig, freq_base, 1.0f, 0.0f, 1.0f, 32.0f, 1.0f);
+    ggml_tensor* ck = bindx((ggml_type) cache_type, (int64_t) hd * nkv, n_cells, 1, k_cache);
+    ggml_tensor* cv = bindx((ggml_type) cache_type, (int64_t) hd * nkv, n_cells, 1, v_cache);
+    ggml_tensor* it = bindx(GGML_TYPE_I64, n, 1, 1, kv_idx);
+    ggml_cgraph* gf = ggml_new_graph(ctx);
+    ggml_build_forward_expand(gf, ggml_set_rows(ctx, ck, ggml_reshape_2d(ctx, k, (int64_t) hd * nkv, n), it));
+    ggml_build_forward_expand(gf, ggml_set_rows(ctx, cv, ggml_reshape_2d(ctx, v, (int64_t) hd * nkv, n), it));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, q, bindx(GGML_TYPE_F32, hd, nh, n, q_out)));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, gate, bindx(GGML_TYPE_F32, (int64_t) hd * nh, n, 1, gate_out)));
+    ggml_cplan plan = ggml_graph_plan(gf, n_threads > 0 ? n_threads : 1, nullptr);
+    std::vector<uint8_t> work(plan.work_size + 64);
+    plan.work_data = plan.work_size ? work.data() : nullptr;
+    const int rc = ggml_graph_compute(gf, &plan) == GGML_STATUS_SUCCESS ? 0 : 1;
+    ggml_free(ctx);
+    return rc;
 }
 
 }  // extern "C"

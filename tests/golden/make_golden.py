@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference's own ggml CPU ops.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [attn_prologue]   (one fixture only with its name)
 
 Needs oracle/_ref (built by `make -C oracle ref` from the reference sources). Every fixture holds seeded
 inputs and the reference's outputs for them; tests/test_oracle.py checks the C restatement against them
@@ -29,8 +29,44 @@ def q8_edge_rows():
     return x
 
 
-def main():
+# qwen35 full-attention rope: 64 of 256 dims rotated, interleaved M-RoPE sections, theta base 1e7
+PROLOGUE_ROPE = dict(n_rot=64, sections=[11, 11, 10, 0], mode=40, freq_base=1e7)
+
+
+def make_prologue_inputs(seed, n, nh=24, nkv=4, hd=256, max_pos=262143):
+    """Seeded inputs of the attention prologue: projections ~N(0, 1), norm weights ~1 + N(0, 0.1), text positions
+    (t = h = w, extra 0) spread up to max_pos, distinct cache cells of a 64-cell ring (n <= 64)."""
+    rng = np.random.default_rng(seed)
+    qfull = rng.standard_normal((n, nh * 2 * hd)).astype(np.float32)
+    kcur = rng.standard_normal((n, nkv * hd)).astype(np.float32)
+    vcur = rng.standard_normal((n, nkv * hd)).astype(np.float32)
+    p = np.sort(rng.integers(0, max_pos + 1, n)).astype(np.int32)
+    pos = np.concatenate([p, p, p, np.zeros(n, np.int32)]).astype(np.int32)
+    kv_idx = (np.arange(n, dtype=np.int64) + seed) % 64  # distinct cells (a token owns its cell)
+    q_norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    k_norm = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    return qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm
+
+
+def prologue_fixture():
+    qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm = make_prologue_inputs(11, 3, nh=4, nkv=2)
+    kv_idx = np.array([5, 17, 63], dtype=np.int64)
+    c16k = np.zeros((64, 2 * 256 * 2), np.uint8)
+    c16v = np.zeros_like(c16k)
+    q, gate = O.ref_attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, 1e-6, k_cache=c16k, v_cache=c16v,
+                                  cache_type=O.GGML_F16, **PROLOGUE_ROPE)
+    return dict(qfull=qfull, kcur=kcur, vcur=vcur, pos=pos, kv_idx=kv_idx, q_norm=q_norm, k_norm=k_norm, q=q,
+                gate=gate, k_cache=c16k, v_cache=c16v)
+
+
+def main(only=None):
     out = {}
+    if only == "attn_prologue":
+        out["attn_prologue"] = prologue_fixture()
+        for name, arrays in out.items():
+            np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
+            print(name, sum(a.nbytes for a in arrays.values()))
+        return
     # flash attention: decode f16, verify f16 with klein's causal mask, verify q8_0 with mask
     for name, n_q, n_kv, kvt in [("fa_decode_f16", 1, 64, O.GGML_F16), ("fa_verify_f16", 4, 48, O.GGML_F16),
                                  ("fa_verify_q8_0", 4, 80, O.GGML_Q8_0)]:
@@ -62,10 +98,11 @@ def main():
     h = np.zeros(xs.size, dtype=np.uint16)
     O.ref_cpy(xs, O.GGML_F32, h, O.GGML_F16)
     out["cpy_f32_f16"] = dict(x=xs, y=h)
+    out["attn_prologue"] = prologue_fixture()
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
         print(name, sum(a.nbytes for a in arrays.values()))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else None)

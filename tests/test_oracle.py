@@ -182,3 +182,46 @@ def test_live_set_rows_q8_0_matches_cpu_path():
     assert (a != b).mean() < 1e-3
     d = a.reshape(64, 32, 34)[:, :, :2].copy().view(np.float16).astype(np.float32)
     assert np.all(np.abs(da - db).reshape(64, 32, 32) <= d + 1e-12)
+
+
+# ---------------------------------------------------------------------------------------------- attention prologue
+
+def assert_f16_near(cache_f16, x64):
+    """K rows in f16 against the float64 restatement: the reference rounds its float32 value, so the two can sit on
+    either side of an f16 rounding boundary (one f16 ulp apart), rarely."""
+    a = cache_f16.astype(np.float64)
+    b = x64.astype(np.float32).astype(np.float16).astype(np.float64)
+    ulp = np.spacing(np.abs(b).astype(np.float16)).astype(np.float64)
+    assert np.all(np.abs(a - b) <= ulp)
+    assert np.mean(a != b) < 1e-2
+
+
+def test_golden_attn_prologue():
+    """RMS norm * weight and interleaved M-RoPE (64 of 256 dims, base 1e7) of the restatement against the
+    reference's graph (graph.cpp:94-112) on positions up to 262,143; the gate and V rows pass through."""
+    g = gold("attn_prologue")
+    q, k, gate = O.rs_attn_prologue(g["qfull"], g["kcur"], g["pos"], g["q_norm"], g["k_norm"], 1e-6, 64,
+                                    [11, 11, 10, 0], 40, 1e7)
+    assert np.abs(q - g["q"]).max() <= 1e-6 * np.abs(g["q"]).max()
+    assert np.array_equal(gate.astype(np.float32), g["gate"])
+    kc = g["k_cache"].view(np.float16).reshape(64, -1, 256)[g["kv_idx"]]
+    assert_f16_near(kc, k)
+    vc = g["v_cache"].view(np.float16).reshape(64, -1)[g["kv_idx"]]
+    assert np.array_equal(vc, g["vcur"].astype(np.float16))
+
+
+@ref_only
+def test_live_attn_prologue_qwen35_shapes():
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import PROLOGUE_ROPE, make_prologue_inputs
+
+    qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm = make_prologue_inputs(12, 5)
+    kc = np.zeros((64, 4 * 256 * 2), np.uint8)
+    vc = np.zeros_like(kc)
+    q_ref, gate_ref = O.ref_attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, 1e-6, k_cache=kc, v_cache=vc,
+                                          cache_type=O.GGML_F16, **PROLOGUE_ROPE)
+    q, k, gate = O.rs_attn_prologue(qfull, kcur, pos, q_norm, k_norm, 1e-6, **PROLOGUE_ROPE)
+    assert np.abs(q - q_ref).max() <= 1e-6 * np.abs(q_ref).max()
+    assert np.array_equal(gate.astype(np.float32), gate_ref)
+    assert_f16_near(kc.view(np.float16).reshape(64, 4, 256)[kv_idx], k)
