@@ -214,6 +214,16 @@ kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t co
 kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream);
 
 /*
+ * kb_flash_attn_ext followed by klein's output gate (graph.cpp:124: ggml_mul(o, ggml_sigmoid(gate))), fused into the
+ * attention's final store: dst = o * 1 / (1 + expf(-gate)). gate f32 [D, H, n_q, ne3] (klein's contiguous gate
+ * [D * H, n_q], e.g. kb_attn_prologue's gate_out), nb[0] = 4. Scratch as for kb_flash_attn_ext
+ * (kb_flash_attn_ext_scratch_bytes).
+ */
+kb_status kb_flash_attn_ext_gated(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                  const kb_fa_params* params, const kb_tensor* gate, const kb_tensor* dst, void* scratch,
+                                  size_t scratch_bytes, void* stream);
+
+/*
  * The attention prologue of klein's Builder::attention (src/graph.cpp:94-112) in one launch: the q / gate split of
  * the interleaved query projection, ggml_rms_norm(eps) * q_norm / k_norm on every head row, ggml_rope_multi on q and
  * k, ggml_cont of the gate, and ggml_set_rows of the K and V rows into the caches. Operands (ggml ne / nb):

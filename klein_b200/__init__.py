@@ -47,6 +47,7 @@ EXPORTED = [
     "kb_partials_push",
     "kb_lse_combine_wait",
     "kb_attn_prologue",
+    "kb_flash_attn_ext_gated",
 ]
 
 
@@ -107,6 +108,9 @@ def lib():
                                             c_int32, c_void_p]
         L.kb_set_rows.restype = c_int32
         L.kb_set_rows.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), c_void_p]
+        L.kb_flash_attn_ext_gated.restype = c_int32
+        L.kb_flash_attn_ext_gated.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
+                                              P(KbTensor), P(KbTensor), c_void_p, c_size_t, c_void_p]
         L.kb_attn_prologue.restype = c_int32
         L.kb_attn_prologue.argtypes = [P(KbTensor)] * 7 + [ctypes.c_float, P(KbRopeParams)] + [P(KbTensor)] * 4 + [c_void_p]
         L.kb_device_error.restype = c_int32
@@ -194,12 +198,13 @@ def fa_params(scale: float, max_bias=0.0, softcap=0.0, causal=False, pos0=0, kv_
 
 
 def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bias=0.0, softcap=0.0, causal=False,
-                   pos0=0, kv_lo=0, ring=0, out=None, stream=None):
+                   pos0=0, kv_lo=0, ring=0, out=None, stream=None, gate=None):
     """GGML_OP_FLASH_ATTN_EXT through kb_flash_attn_ext.
 
     q: torch f32 on the GPU, token-major [ne3][n_q][H][D] (or [n_q][H][D]); passed as klein's permuted
     view [D, n_q, H, ne3]. k, v: kb_tensor cache views (kv_cache_view). mask: torch f16 [n_q'][n_kv] or
-    None. Returns f32 [ne3][n_q][H][D] (ggml's permuted result [D, H, n_q, ne3]).
+    None. Returns f32 [ne3][n_q][H][D] (ggml's permuted result [D, H, n_q, ne3]). gate: torch f32 of the output's
+    shape, or None; with a gate the result is o * sigmoid(gate) (kb_flash_attn_ext_gated).
     """
     import torch
 
@@ -221,10 +226,18 @@ def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bia
     nbytes = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(prm))
     scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
-    rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(mt) if mt is not None else None,
-                             ctypes.byref(prm), ctypes.byref(dt), c_void_p(scratch.data_ptr()), c_size_t(nbytes),
-                             c_void_p(st))
-    check("kb_flash_attn_ext", rc)
+    if gate is not None:
+        g = gate if gate.dim() == 4 else gate.reshape((ne3, n_q, H, D))
+        gt = from_torch(g)
+        rc = L.kb_flash_attn_ext_gated(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v),
+                                       ctypes.byref(mt) if mt is not None else None, ctypes.byref(prm), ctypes.byref(gt),
+                                       ctypes.byref(dt), c_void_p(scratch.data_ptr()), c_size_t(nbytes), c_void_p(st))
+        check("kb_flash_attn_ext_gated", rc)
+    else:
+        rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v),
+                                 ctypes.byref(mt) if mt is not None else None, ctypes.byref(prm), ctypes.byref(dt),
+                                 c_void_p(scratch.data_ptr()), c_size_t(nbytes), c_void_p(st))
+        check("kb_flash_attn_ext", rc)
     out._kb_scratch = scratch  # keep alive until the stream has used it
     return out
 

@@ -428,11 +428,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_ld32(lane_addr + TM_O + grp * OPT + c * 32, ov);
                 tmem_wait_ld();
                 if (qi < p.n_q) {
+                    // klein's output gate (graph.cpp:124): o * sigmoid(gate), ggml's 1 / (1 + expf(-x))
+                    const float* gr = p.gate ? reinterpret_cast<const float*>(p.gate + h * p.g_nb1 + (int64_t) qi * p.g_nb2 +
+                                                                            b * p.g_nb3) + grp * OPT + c * 32
+                                             : nullptr;
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4*>(out + c * 32 + e) =
-                            make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
-                                        __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
+                    for (int e = 0; e < 32; e += 4) {
+                        float4 o4 = make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
+                                                __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
+                        if (gr) {
+                            o4.x *= 1.0f / (1.0f + expf(-gr[e]));
+                            o4.y *= 1.0f / (1.0f + expf(-gr[e + 1]));
+                            o4.z *= 1.0f / (1.0f + expf(-gr[e + 2]));
+                            o4.w *= 1.0f / (1.0f + expf(-gr[e + 3]));
+                        }
+                        *reinterpret_cast<float4*>(out + c * 32 + e) = o4;
+                    }
                 }
             }
         } else if (nb == 0 && qi < p.n_q) {

@@ -62,6 +62,11 @@ __device__ __forceinline__ float masked_score(const FaStreamParams& p, float x, 
 }
 
 // final store of one output element: normalised, or (o, m, l) partial for a cross-device combine
+// klein's attention output gate (graph.cpp:124): o * sigmoid(gate), ggml_vec_sigmoid_f32's 1 / (1 + expf(-x))
+__device__ __forceinline__ float gate_sigmoid(const char* g) {
+    return 1.0f / (1.0f + expf(-*reinterpret_cast<const float*>(g)));
+}
+
 __device__ __forceinline__ void store_row(const FaStreamParams& p, int qi, int h, int b, int d, float O, float M, float L) {
     float* dst = reinterpret_cast<float*>(p.dst + (int64_t) d * 4 + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
     if (p.partial_out) {
@@ -72,7 +77,9 @@ __device__ __forceinline__ void store_row(const FaStreamParams& p, int qi, int h
             ml[1] = L;
         }
     } else {
-        *dst = L > 0.0f ? O / L : 0.0f;
+        float o = L > 0.0f ? O / L : 0.0f;
+        if (p.gate) o *= gate_sigmoid(p.gate + (int64_t) d * 4 + h * p.g_nb1 + qi * p.g_nb2 + b * p.g_nb3);
+        *dst = o;
     }
 }
 
@@ -86,7 +93,8 @@ constexpr int MERGE_THREADS = 256;
 constexpr int MERGE_MAX_PARTS = 1024;
 
 __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const float* __restrict__ ml, int64_t ml_stride,
-                          int n, int Dd, float* __restrict__ out_row, float* __restrict__ ml_out) {
+                          int n, int Dd, float* __restrict__ out_row, float* __restrict__ ml_out,
+                          const char* __restrict__ gate_row = nullptr) {
     __shared__ float f[MERGE_MAX_PARTS];
     __shared__ float red[MERGE_THREADS / 32];
     __shared__ float acc_s[MERGE_THREADS / 32][256 + 4];
@@ -137,7 +145,8 @@ __device__ void merge_row(const float* __restrict__ o, int64_t o_stride, const f
             float t = 0.0f;
 #pragma unroll
             for (int wi = 0; wi < MERGE_THREADS / 32; ++wi) t += acc_s[wi][tid];
-            out_row[d0 + tid] = ml_out ? t : t * inv;  // partial output stays unnormalised
+            // a partial output stays unnormalised; a final one takes the output gate when there is one
+            out_row[d0 + tid] = ml_out ? t : gate_row ? t * inv * gate_sigmoid(gate_row + (int64_t) (d0 + tid) * 4) : t * inv;
         }
         __syncthreads();
     }
@@ -156,8 +165,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) fa_combine_kernel(const FaStrea
     const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
     float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
     float* ml_out = p.partial_out ? p.dst_ml + (((int64_t) b * p.n_q + qi) * p.n_head + h) * 2 : nullptr;
+    const char* gate_row = p.gate && !p.partial_out ? p.gate + h * p.g_nb1 + qi * p.g_nb2 + b * p.g_nb3 : nullptr;
     merge_row(p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + (base * RPC + r) * 2, (int64_t) RPC * 2,
-              p.n_splits, D, out, ml_out);
+              p.n_splits, D, out, ml_out, gate_row);
 }
 
 // Merges partial results computed over disjoint KV ranges (e.g. one per GPU), one row per block.

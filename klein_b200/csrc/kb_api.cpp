@@ -183,13 +183,17 @@ namespace {
 
 kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                   const kb_fa_params* prm, const kb_tensor* dst, float* dst_ml, void* scratch, size_t scratch_bytes,
-                  void* stream) {
+                  void* stream, const kb_tensor* gate = nullptr) {
     if (!prm || !dst) return KB_ERR_ARG;
     FaShape s;
     kb_status st = check_fa(q, k, v, mask, &s);
     if (st != KB_OK) return st;
     if (dst->type != KB_TYPE_F32 || dst->nb[0] != 4) return KB_ERR_BAD_SHAPE;
     if (dst->ne[0] != s.D || dst->ne[1] != s.H || dst->ne[2] != s.n_q || dst->ne[3] != s.ne3) return KB_ERR_BAD_SHAPE;
+    if (gate && (gate->type != KB_TYPE_F32 || gate->nb[0] != 4 || gate->ne[0] != s.D || gate->ne[1] != s.H ||
+                 gate->ne[2] != s.n_q || gate->ne[3] != s.ne3))
+        return KB_ERR_BAD_SHAPE;
+    if (gate && dst_ml) return KB_ERR_ARG;  // the gate applies to final outputs, not to partials
     if (prm->logit_softcap != 0.0f && !(std::isfinite(prm->logit_softcap))) return KB_ERR_ARG;
     if (prm->max_bias > 0.0f && !mask) return KB_ERR_ARG;  // ggml: ALiBi needs a mask
     if (prm->causal && prm->ring < 0) return KB_ERR_ARG;
@@ -235,6 +239,10 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         pp.causal = prm->causal, pp.pos0 = prm->pos0, pp.kv_lo = prm->kv_lo;
         pp.dst = static_cast<char*>(dst->data);
         pp.d_nb1 = (int64_t) dst->nb[1], pp.d_nb2 = (int64_t) dst->nb[2], pp.d_nb3 = (int64_t) dst->nb[3];
+        if (gate) {
+            pp.gate = static_cast<const char*>(gate->data);
+            pp.g_nb1 = (int64_t) gate->nb[1], pp.g_nb2 = (int64_t) gate->nb[2], pp.g_nb3 = (int64_t) gate->nb[3];
+        }
         pp.err = kb::device_error_word();
         pp.wait_ns = g_wait_ns;
         CUtensorMap tK, tV;
@@ -298,6 +306,10 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     p.d_nb1 = (int64_t) dst->nb[1];
     p.d_nb2 = (int64_t) dst->nb[2];
     p.d_nb3 = (int64_t) dst->nb[3];
+    if (gate) {
+        p.gate = static_cast<const char*>(gate->data);
+        p.g_nb1 = (int64_t) gate->nb[1], p.g_nb2 = (int64_t) gate->nb[2], p.g_nb3 = (int64_t) gate->nb[3];
+    }
     p.partial_out = dst_ml != nullptr;
     p.dst_ml = dst_ml;
     p.err = kb::device_error_word();
@@ -327,6 +339,13 @@ size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb
 }  // namespace kb
 
 extern "C" {
+
+kb_status kb_flash_attn_ext_gated(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                  const kb_fa_params* params, const kb_tensor* gate, const kb_tensor* dst, void* scratch,
+                                  size_t scratch_bytes, void* stream) {
+    if (!gate) return KB_ERR_ARG;
+    return fa_impl(q, k, v, mask, params, dst, nullptr, scratch, scratch_bytes, stream, gate);
+}
 
 kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                             const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,

@@ -43,6 +43,8 @@ struct FaStreamParams {
     int64_t d_nb1, d_nb2, d_nb3;
     int partial_out;                 // write (o, m, l) partials instead of the normalised output
     float* dst_ml;                   // partial_out: f32 [ne3][n_q][H][2] = (max in log2 units, sum)
+    const char* gate;                // null, or f32 [D, H, n_q, ne3]: the output is o * sigmoid(gate) (not partials)
+    int64_t g_nb1, g_nb2, g_nb3;
     int* err;                        // device error word
     uint64_t wait_ns;                // budget of every bounded wait
 };
@@ -72,6 +74,8 @@ struct FaPrefillParams {
     int64_t pos0, kv_lo;
     char* dst;                       // f32 [D, H, n_q, ne3]
     int64_t d_nb1, d_nb2, d_nb3;
+    const char* gate;                // null, or f32 [D, H, n_q, ne3]: the output is o * sigmoid(gate)
+    int64_t g_nb1, g_nb2, g_nb3;
     int* err;
     uint64_t wait_ns;
 };

@@ -246,3 +246,37 @@ def test_q8_0_long_verify_262144(kb, cuda):
     mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
     gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q)
     check_attention(gpu, exact_np(O.q_round_q8_0(q), kd, vd, mask))
+
+
+# ---------------------------------------------------------------------------------------------- output gate
+
+@pytest.mark.parametrize("kvt,n_q,n_kv", [("f16", 4, 8192), ("f16", 1, 100), ("q8_0", 4, 8192), ("bf16", 256, 512)])
+def test_output_gate_fused(kb, cuda, kvt, n_q, n_kv):
+    """kb_flash_attn_ext_gated = kb_flash_attn_ext * sigmoid(gate) (graph.cpp:124) on the split-combine path, the
+    single-split store, the q8_0 kernel and the prefill kernel."""
+    import torch
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(n_q * 7 + n_kv)
+    H, H_kv, D = 24, 4, 256
+    q = torch.randn(1, n_q, H, D, device=cuda, generator=g)
+    if kvt == "bf16":
+        q = q.bfloat16().float()
+    kf = torch.randn(n_kv, H_kv * D, device=cuda, generator=g)
+    vf = torch.randn(n_kv, H_kv * D, device=cuda, generator=g)
+    if kvt == "q8_0":
+        kc = torch.from_numpy(O.rs_quantize_q8_0(kf.cpu().numpy())).to(cuda)
+        vc = torch.from_numpy(O.rs_quantize_q8_0(vf.cpu().numpy())).to(cuda)
+        t = kb.Q8_0
+    elif kvt == "bf16":
+        kc, vc, t = kf.bfloat16(), vf.bfloat16(), kb.BF16
+    else:
+        kc, vc, t = kf.half(), vf.half(), kb.F16
+    kv, vv = kb.kv_cache_view(kc, t, H_kv, D), kb.kv_cache_view(vc, t, H_kv, D)
+    gate = torch.randn(1, n_q, H, D, device=cuda, generator=g) * 3
+    plain = kb.flash_attn_ext(q, kv, vv, 1 / 16, causal=True, pos0=n_kv - n_q)
+    gated = kb.flash_attn_ext(q, kv, vv, 1 / 16, causal=True, pos0=n_kv - n_q, gate=gate)
+    torch.cuda.synchronize()
+    assert kb.device_error() == 0
+    want = plain * (1.0 / (1.0 + torch.exp(-gate)))
+    assert float((gated - want).abs().max()) <= 1e-6 * float(want.abs().max()) + 1e-30

@@ -44,7 +44,7 @@ def test_prologue_f16_cache_matches_reference(kb, cuda, n):
     assert np.array_equal(vc, rv)
     # K rows: identical f16 except where the float value sits on a rounding boundary (one ulp at most)
     a, b = kc.view(np.float16).astype(np.float32), rk.view(np.float16).astype(np.float32)
-    ulp = np.abs(np.spacing(np.abs(b).astype(np.float16).astype(np.float32)))
+    ulp = np.spacing(np.abs(b).astype(np.float16)).astype(np.float32)  # one f16 ulp at each value
     assert np.all(np.abs(a - b) <= ulp)
     assert np.mean(a != b) < 1e-3
 
