@@ -249,6 +249,31 @@ kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const 
                            const kb_tensor* k_cache, const kb_tensor* v_cache, void* stream);
 
 /*
+ * The DeltaNet input side of klein's Builder::deltanet (src/graph.cpp:136-165) in one launch:
+ *   beta = sigmoid(beta_raw), g = softplus(alpha + dt_bias) * a                     (the GDN gates)
+ *   conv = silu(ggml_ssm_conv([conv state | qkv], conv_w))  over the kc = 4 wide window of each channel
+ *   q, k = l2(conv[q heads]), l2(conv[k heads]) with l2(x) = rms_norm(x, eps / S) / sqrt(S); v = conv[v heads]
+ *   conv state snapshots: slot s <- the kc - 1 inputs before token n - s (clamped at the stored state), for
+ *   s < K, skipping slots s >= n other than 0 (the rollback slots of State::rollback_recurrent)
+ * Operands (ggml ne): qkv f32 [ch, n], ch = 2 S H_k + S H_v (q heads, k heads, v heads); conv_state f32
+ * [(kc - 1) ch, K] (slot 0 = the state, channel-major); conv_w f32 [kc, ch]; beta_raw, alpha f32 [H_v, n] or both
+ * NULL (then dt_bias, a, beta_out, g_out are ignored); dt_bias, a f32 [H_v]; q_out, k_out f32 [S, H_k, n];
+ * v_out f32 [S, H_v, n]; beta_out, g_out f32 [H_v, n] (the GDN op's shapes with their trailing 1s). All
+ * contiguous; S is 64 or 128.
+ */
+kb_status kb_gdn_input(const kb_tensor* qkv, const kb_tensor* conv_state, const kb_tensor* conv_w,
+                       const kb_tensor* beta_raw, const kb_tensor* alpha, const kb_tensor* dt_bias, const kb_tensor* a,
+                       int32_t S, int32_t H_k, float rms_eps, const kb_tensor* q_out, const kb_tensor* k_out,
+                       const kb_tensor* v_out, const kb_tensor* beta_out, const kb_tensor* g_out, void* stream);
+
+/*
+ * The DeltaNet output side (graph.cpp:186-190): dst = rms_norm(x, eps) * w * silu(z) on every [S] row.
+ * x f32 [S, H, n] (GDN's attention output), z f32 [S H, n], w f32 [S], dst f32 [S H, n]; contiguous, S 64 or 128.
+ */
+kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_tensor* w, float rms_eps,
+                            const kb_tensor* dst, void* stream);
+
+/*
  * Size of the device buffer built into the library for kb_flash_attn_ext_noalloc (per GPU, held from the
  * library's load until the process exits).
  */

@@ -48,6 +48,8 @@ EXPORTED = [
     "kb_lse_combine_wait",
     "kb_attn_prologue",
     "kb_flash_attn_ext_gated",
+    "kb_gdn_input",
+    "kb_gdn_gated_norm",
 ]
 
 
@@ -111,6 +113,10 @@ def lib():
         L.kb_flash_attn_ext_gated.restype = c_int32
         L.kb_flash_attn_ext_gated.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
                                               P(KbTensor), P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_gdn_input.restype = c_int32
+        L.kb_gdn_input.argtypes = [P(KbTensor)] * 7 + [c_int32, c_int32, ctypes.c_float] + [P(KbTensor)] * 5 + [c_void_p]
+        L.kb_gdn_gated_norm.restype = c_int32
+        L.kb_gdn_gated_norm.argtypes = [P(KbTensor)] * 3 + [ctypes.c_float, P(KbTensor), c_void_p]
         L.kb_attn_prologue.restype = c_int32
         L.kb_attn_prologue.argtypes = [P(KbTensor)] * 7 + [ctypes.c_float, P(KbRopeParams)] + [P(KbTensor)] * 4 + [c_void_p]
         L.kb_device_error.restype = c_int32
@@ -362,6 +368,46 @@ def attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, rms_eps: float
                                 ctypes.byref(v_cache), c_void_p(_stream(qfull, stream)))
     check("kb_attn_prologue", rc)
     return q, gate
+
+
+def gdn_input(qkv, conv_state, conv_w, S: int, H_k: int, rms_eps: float, beta_raw=None, alpha=None, dt_bias=None,
+              a=None, stream=None):
+    """klein's DeltaNet input side (graph.cpp:136-165) through kb_gdn_input. qkv torch f32 [n][ch], conv_state
+    f32 [K][(kc - 1) ch] (updated in place), conv_w f32 [ch][kc]; beta_raw / alpha f32 [n][H_v] and dt_bias / a
+    f32 [H_v] optional. Returns (q [n][H_k][S], k [n][H_k][S], v [n][H_v][S], beta [n][H_v] | None, g | None)."""
+    import torch
+
+    n, ch = qkv.shape
+    H_v = (ch - 2 * S * H_k) // S
+    dev = qkv.device
+    q = torch.empty((n, H_k, S), dtype=torch.float32, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty((n, H_v, S), dtype=torch.float32, device=dev)
+    beta = g = None
+    gate_args = [None, None, None, None]
+    if beta_raw is not None:
+        beta = torch.empty((n, H_v), dtype=torch.float32, device=dev)
+        g = torch.empty_like(beta)
+        gate_args = [ctypes.byref(from_torch(x)) for x in (beta_raw, alpha, dt_bias, a)]
+    rc = lib().kb_gdn_input(ctypes.byref(from_torch(qkv)), ctypes.byref(from_torch(conv_state)),
+                            ctypes.byref(from_torch(conv_w)), *gate_args, S, H_k, ctypes.c_float(rms_eps),
+                            ctypes.byref(from_torch(q)), ctypes.byref(from_torch(k)), ctypes.byref(from_torch(v)),
+                            ctypes.byref(from_torch(beta)) if beta is not None else None,
+                            ctypes.byref(from_torch(g)) if g is not None else None, c_void_p(_stream(qkv, stream)))
+    check("kb_gdn_input", rc)
+    return q, k, v, beta, g
+
+
+def gdn_gated_norm(x, z, w, rms_eps: float, stream=None):
+    """klein's DeltaNet output norm (graph.cpp:186-190) through kb_gdn_gated_norm: rms_norm(x) * w * silu(z)."""
+    import torch
+
+    dst = torch.empty_like(x)
+    rc = lib().kb_gdn_gated_norm(ctypes.byref(from_torch(x)), ctypes.byref(from_torch(z.reshape(x.shape))),
+                                 ctypes.byref(from_torch(w)), ctypes.c_float(rms_eps), ctypes.byref(from_torch(dst)),
+                                 c_void_p(_stream(x, stream)))
+    check("kb_gdn_gated_norm", rc)
+    return dst
 
 
 def cache_rows(cache, kv_type: int) -> KbTensor:

@@ -1,0 +1,179 @@
+// The ops on either side of GGML_OP_GATED_DELTA_NET in klein's Builder::deltanet, one launch each:
+//
+// input side (graph.cpp:136-165):
+//   beta  = sigmoid(beta_raw)                      ggml_sigmoid: 1 / (1 + expf(-x))
+//   g     = softplus(alpha + dt_bias) * a          ggml_softplus: x > 20 ? x : logf(1 + expf(x))
+//   conv  = silu(ssm_conv([state | qkv], w))       per channel c and token t: sum_j in[t + j][c] * w[j][c] over the
+//                                                  kernel width kc, in[] = the kc - 1 stored inputs then the batch
+//                                                  (ops.cpp:9931-9982), silu = x / (1 + expf(-x))
+//   q, k  = l2(conv[q], conv[k]) per head          rms_norm(x, eps / S) * (1 / sqrt(S)) (graph.cpp:41-44)
+//   v     = conv[v]
+//   state = conv-state snapshots: slot s <- the kc - 1 inputs before token n - s (clamped at 0), for s < K,
+//           skipping slots s >= n other than 0 (graph.cpp:147-155)
+// output side (graph.cpp:186-190): o = rms_norm(attn, eps) * w * silu(z) per head row.
+//
+// Layout of the input kernel: one warp per (chunk of tokens, head slot of S channels: the H_k q heads, the H_k k
+// heads, the H_v v heads); lane l holds channels l, l + 32, ... of the slot and slides the conv window over the
+// chunk's tokens in registers. Only the chunk-0 warps read the stored state, and they write the snapshots after
+// reading it, so no warp reads a state slot another writes.
+#include "kb_common.cuh"
+#include "kb_internal.h"
+
+namespace kb {
+
+namespace {
+
+constexpr int GIN_CHUNK = 16;  // tokens per warp
+constexpr int KC = 4;          // conv kernel width (qwen35's ssm_conv_kernel); others are rejected by the host
+static_assert(GIN_CHUNK > KC - 1, "only the first chunk reads the stored state");
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+template <int CPL>  // channels per lane: S / 32
+__global__ void __launch_bounds__(256) gdn_input_kernel(const GdnInputParams p) {
+    constexpr int S = 32 * CPL;
+    constexpr int KM1 = KC - 1;
+    const int lane = threadIdx.x & 31;
+    const int slots = 2 * p.H_k + p.H_v;
+    const int64_t task = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int n_chunks = (p.n + GIN_CHUNK - 1) / GIN_CHUNK;
+    // the beta / g rows ride along: one warp per token after the conv tasks
+    const int64_t conv_tasks = (int64_t) n_chunks * slots;
+    if (task >= conv_tasks) {
+        const int64_t t = task - conv_tasks;
+        if (t >= p.n || !p.beta_raw) return;
+        for (int h = lane; h < p.H_v; h += 32) {
+            const float b = p.beta_raw[t * p.H_v + h];
+            p.beta_out[t * p.H_v + h] = 1.0f / (1.0f + expf(-b));
+            const float x = p.alpha[t * p.H_v + h] + p.dt_bias[h];
+            const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
+            p.g_out[t * p.H_v + h] = sp * p.a[h];
+        }
+        return;
+    }
+    const int chunk = (int) (task / slots), slot = (int) (task % slots);
+    const int c0 = slot * S;  // first channel of the slot
+    const int t0 = chunk * GIN_CHUNK, t1 = min(p.n, t0 + GIN_CHUNK);
+    // win[i][j]: the KC - 1 inputs before token t0 of channel c0 + lane + 32 i; old[i][j]: the stored state
+    float win[CPL][KM1], old[CPL][KM1], w[CPL][KC];
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+        const int64_t c = c0 + lane + 32 * i;
+#pragma unroll
+        for (int j = 0; j < KC; ++j) w[i][j] = p.conv_w[c * KC + j];
+#pragma unroll
+        for (int j = 0; j < KM1; ++j) {
+            // only the first chunk's window reaches into the stored state (GIN_CHUNK > KC - 1)
+            old[i][j] = t0 == 0 ? p.state[c * KM1 + j] : 0.0f;
+            win[i][j] = t0 == 0 ? old[i][j] : p.qkv[(int64_t) (t0 - KM1 + j) * p.qkv_ld + c];
+        }
+    }
+    // output row of this slot: q (slot < H_k), k, or v
+    const bool is_q = slot < p.H_k, is_k = !is_q && slot < 2 * p.H_k;
+    float* out = is_q ? p.q_out + (int64_t) slot * S : is_k ? p.k_out + (int64_t) (slot - p.H_k) * S
+                                                               : p.v_out + (int64_t) (slot - 2 * p.H_k) * S;
+    const int64_t out_ld = (int64_t) (is_q || is_k ? p.H_k : p.H_v) * S;
+    for (int t = t0; t < t1; ++t) {
+        float y[CPL];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const float x = p.qkv[(int64_t) t * p.qkv_ld + c0 + lane + 32 * i];
+            // ggml's order: sum over the window oldest first, one multiply-add per tap
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < KM1; ++j) acc += win[i][j] * w[i][j];
+            acc += x * w[i][KM1];
+            y[i] = silu_f(acc);
+#pragma unroll
+            for (int j = 0; j + 1 < KM1; ++j) win[i][j] = win[i][j + 1];
+            win[i][KM1 - 1] = x;
+        }
+        if (is_q || is_k) {
+            // l2: rms_norm with eps / S (sum of squares in double, as ggml), then * 1 / sqrt(S)
+            double ss = 0.0;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) ss += (double) (y[i] * y[i]);
+#pragma unroll
+            for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float mean = (float) (ss / S);
+            const float scale = 1.0f / sqrtf(mean + p.l2_eps);
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) y[i] = y[i] * scale * p.inv_sqrt_s;
+        }
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) out[(int64_t) t * out_ld + lane + 32 * i] = y[i];
+    }
+    if (chunk != 0) return;
+    // conv-state snapshots of this lane's channels: slot s <- in[n - s .. n - s + KC - 2] (in = old state | batch),
+    // the window after n - s tokens, clamped at the start of in[]; the old state is in registers (read above)
+    for (int s = 0; s < p.K; ++s) {
+        if (s >= p.n && s > 0) continue;
+        const int start = max(0, p.n - s);
+        float* dst = p.state + (int64_t) s * p.state_ld;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int64_t c = c0 + lane + 32 * i;
+#pragma unroll
+            for (int j = 0; j < KM1; ++j) {
+                const int ii = start + j;
+                float v = 0.0f;
+#pragma unroll
+                for (int jj = 0; jj < KM1; ++jj)
+                    if (ii == jj) v = old[i][jj];
+                if (ii >= KM1) v = p.qkv[(int64_t) (ii - KM1) * p.qkv_ld + c];
+                dst[c * KM1 + j] = v;
+            }
+        }
+    }
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const GdnNormParams p) {
+    constexpr int S = 32 * CPL;
+    const int lane = threadIdx.x & 31;
+    const int64_t task = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (task >= (int64_t) p.n * p.H) return;
+    const float* x = p.x + task * S;
+    const float* z = p.z + task * S;
+    float* o = p.dst + task * S;
+    float v[CPL];
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+        v[i] = x[lane + 32 * i];
+        ss += (double) (v[i] * v[i]);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float mean = (float) (ss / S);
+    const float scale = 1.0f / sqrtf(mean + p.eps);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) o[lane + 32 * i] = v[i] * scale * p.w[lane + 32 * i] * silu_f(z[lane + 32 * i]);
+}
+
+}  // namespace
+
+cudaError_t launch_gdn_input(const GdnInputParams& p, int S, cudaStream_t stream) {
+    const int n_chunks = (p.n + GIN_CHUNK - 1) / GIN_CHUNK;
+    const int64_t tasks = (int64_t) n_chunks * (2 * p.H_k + p.H_v) + p.n;
+    if (tasks == 0) return cudaSuccess;
+    const unsigned grid = (unsigned) ((tasks + 7) / 8);
+    switch (S) {
+        case 64: gdn_input_kernel<2><<<grid, 256, 0, stream>>>(p); break;
+        default: gdn_input_kernel<4><<<grid, 256, 0, stream>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream) {
+    const int64_t tasks = (int64_t) p.n * p.H;
+    if (tasks == 0) return cudaSuccess;
+    const unsigned grid = (unsigned) ((tasks + 7) / 8);
+    switch (S) {
+        case 64: gdn_gated_norm_kernel<2><<<grid, 256, 0, stream>>>(p); break;
+        default: gdn_gated_norm_kernel<4><<<grid, 256, 0, stream>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace kb

@@ -735,6 +735,83 @@ kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const 
     return kb::launch_attn_prologue(p, (int) hd, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 
+kb_status kb_gdn_input(const kb_tensor* qkv, const kb_tensor* conv_state, const kb_tensor* conv_w,
+                       const kb_tensor* beta_raw, const kb_tensor* alpha, const kb_tensor* dt_bias, const kb_tensor* a,
+                       int32_t S, int32_t H_k, float rms_eps, const kb_tensor* q_out, const kb_tensor* k_out,
+                       const kb_tensor* v_out, const kb_tensor* beta_out, const kb_tensor* g_out, void* stream) {
+    if (!qkv || !conv_state || !conv_w || !q_out || !k_out || !v_out) return KB_ERR_ARG;
+    if (!!beta_raw != !!alpha) return KB_ERR_ARG;
+    if (beta_raw && (!dt_bias || !a || !beta_out || !g_out)) return KB_ERR_ARG;
+    if (S != 64 && S != 128) return KB_ERR_UNSUPPORTED;
+    for (const kb_tensor* t : {qkv, conv_state, conv_w, q_out, k_out, v_out})
+        if (!contiguous_f32(t)) return KB_ERR_UNSUPPORTED;
+    const int64_t ch = qkv->ne[0], n = qkv->ne[1];
+    if (H_k <= 0 || ch <= 2 * (int64_t) S * H_k || (ch - 2 * (int64_t) S * H_k) % S != 0) return KB_ERR_BAD_SHAPE;
+    const int64_t H_v = (ch - 2 * (int64_t) S * H_k) / S;
+    const int64_t kc = conv_w->ne[0];
+    if (kc != 4) return KB_ERR_UNSUPPORTED;
+    if (conv_w->ne[1] != ch || conv_state->ne[0] != (kc - 1) * ch || conv_state->ne[1] < 1) return KB_ERR_BAD_SHAPE;
+    if (q_out->ne[0] != S || q_out->ne[1] != H_k || q_out->ne[2] != n || k_out->ne[0] != S || k_out->ne[1] != H_k ||
+        k_out->ne[2] != n || v_out->ne[0] != S || v_out->ne[1] != H_v || v_out->ne[2] != n)
+        return KB_ERR_BAD_SHAPE;
+    if (beta_raw) {
+        for (const kb_tensor* t : {beta_raw, alpha, dt_bias, a, beta_out, g_out})
+            if (!contiguous_f32(t)) return KB_ERR_UNSUPPORTED;
+        for (const kb_tensor* t : {beta_raw, alpha, beta_out, g_out})
+            if (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != H_v * n || t->ne[0] != H_v && t->ne[1] != H_v)
+                return KB_ERR_BAD_SHAPE;
+        if (dt_bias->ne[0] * dt_bias->ne[1] != H_v || a->ne[0] * a->ne[1] != H_v) return KB_ERR_BAD_SHAPE;
+    }
+    if (n == 0) return KB_OK;
+    kb::GdnInputParams p{};
+    p.qkv = static_cast<const float*>(qkv->data);
+    p.qkv_ld = ch;
+    p.state = static_cast<float*>(conv_state->data);
+    p.state_ld = conv_state->ne[0];
+    p.conv_w = static_cast<const float*>(conv_w->data);
+    if (beta_raw) {
+        p.beta_raw = static_cast<const float*>(beta_raw->data);
+        p.alpha = static_cast<const float*>(alpha->data);
+        p.dt_bias = static_cast<const float*>(dt_bias->data);
+        p.a = static_cast<const float*>(a->data);
+        p.beta_out = static_cast<float*>(beta_out->data);
+        p.g_out = static_cast<float*>(g_out->data);
+    }
+    p.q_out = static_cast<float*>(q_out->data);
+    p.k_out = static_cast<float*>(k_out->data);
+    p.v_out = static_cast<float*>(v_out->data);
+    p.n = (int) n;
+    p.H_k = H_k;
+    p.H_v = (int) H_v;
+    p.K = (int) conv_state->ne[1];
+    // l2 (graph.cpp:41-44): rms_norm with eps / n, then a scale of 1 / sqrt(n), n = S (computed as klein does)
+    p.l2_eps = rms_eps / (float) S;
+    p.inv_sqrt_s = 1.0f / std::sqrt((float) S);
+    return kb::launch_gdn_input(p, S, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
+kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_tensor* w, float rms_eps,
+                            const kb_tensor* dst, void* stream) {
+    if (!x || !z || !w || !dst) return KB_ERR_ARG;
+    for (const kb_tensor* t : {x, z, w, dst})
+        if (!contiguous_f32(t)) return KB_ERR_UNSUPPORTED;
+    const int64_t S = w->ne[0];
+    if (S != 64 && S != 128) return KB_ERR_UNSUPPORTED;
+    const int64_t total = x->ne[0] * x->ne[1] * x->ne[2] * x->ne[3];
+    if (x->ne[0] != S || total % S != 0 || z->ne[0] * z->ne[1] * z->ne[2] * z->ne[3] != total ||
+        dst->ne[0] * dst->ne[1] * dst->ne[2] * dst->ne[3] != total)
+        return KB_ERR_BAD_SHAPE;
+    kb::GdnNormParams p{};
+    p.x = static_cast<const float*>(x->data);
+    p.z = static_cast<const float*>(z->data);
+    p.w = static_cast<const float*>(w->data);
+    p.dst = static_cast<float*>(dst->data);
+    p.H = (int) x->ne[1];
+    p.n = (int) (total / (S * x->ne[1]));
+    p.eps = rms_eps;
+    return kb::launch_gdn_gated_norm(p, (int) S, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
 kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t conv_row, const void* const* snap,
                                 int32_t snap_type, float* const* ssm, int64_t ssm_row, int32_t s, int32_t n_snapshots,
                                 void* stream) {

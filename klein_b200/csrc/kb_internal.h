@@ -135,6 +135,38 @@ struct PrologueParams {
 };
 cudaError_t launch_attn_prologue(const PrologueParams& p, int hd, cudaStream_t stream);
 
+// Parameters of the DeltaNet input side (gdn_io.cu): conv + SiLU + L2 norms + conv-state snapshots, beta and g.
+struct GdnInputParams {
+    const float* qkv;                // [n][qkv_ld]: channels 2 S H_k + S H_v (q heads, k heads, v heads)
+    int64_t qkv_ld;
+    float* state;                    // conv state slots [K][state_ld]: channel-major (kc - 1) inputs per channel
+    int64_t state_ld;
+    const float* conv_w;             // [ch][kc]
+    const float* beta_raw;           // [n][H_v] or null (then alpha, dt_bias, a, beta_out, g_out are unused)
+    const float* alpha;              // [n][H_v]
+    const float* dt_bias;            // [H_v]
+    const float* a;                  // [H_v]
+    float* q_out;                    // [n][H_k][S]
+    float* k_out;                    // [n][H_k][S]
+    float* v_out;                    // [n][H_v][S]
+    float* beta_out;                 // [n][H_v]
+    float* g_out;                    // [n][H_v]
+    int n, H_k, H_v, K;
+    float l2_eps, inv_sqrt_s;
+};
+cudaError_t launch_gdn_input(const GdnInputParams& p, int S, cudaStream_t stream);
+
+// Parameters of the DeltaNet gated RMS norm (gdn_io.cu): dst = rms_norm(x, eps) * w * silu(z) per [S] row.
+struct GdnNormParams {
+    const float* x;                  // [n][H][S]
+    const float* z;                  // [n][H][S]
+    const float* w;                  // [S]
+    float* dst;                      // [n][H][S]
+    int n, H;
+    float eps;
+};
+cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream);
+
 int* device_error_word();
 
 // kb_flash_attn_ext with caller-chosen scratch, and its scratch size (shared by the C-ABI entry points)

@@ -93,6 +93,10 @@ def ref():
         lib.kbref_set_rows.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int]
         lib.kbref_cpy.restype = c_int
         lib.kbref_cpy.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int64]
+        lib.kbref_gdn_input.restype = c_int
+        lib.kbref_gdn_input.argtypes = [c_void_p] * 7 + [c_int] * 6 + [c_float] + [c_void_p] * 5 + [c_int]
+        lib.kbref_gdn_gated_norm.restype = c_int
+        lib.kbref_gdn_gated_norm.argtypes = [c_void_p] * 3 + [c_int] * 3 + [c_float, c_void_p, c_int]
         lib.kbref_attn_prologue.restype = c_int
         lib.kbref_attn_prologue.argtypes = [c_void_p] * 7 + [c_int] * 4 + [c_float, c_int, c_void_p, c_int, c_float, c_int] + \
             [c_void_p] * 4 + [c_int, c_int64, c_int]
@@ -271,6 +275,40 @@ def ref_attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, eps, n_rot
     return q_out, gate
 
 
+def ref_gdn_input(qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a, S, H_k, eps, n_threads=1):
+    """Builder::deltanet's input side on the reference ggml CPU ops (graph.cpp:136-165). qkv f32 [n][ch],
+    conv_state f32 [K][(kc - 1) ch] (written in place), conv_w f32 [ch][kc], beta_raw / alpha f32 [n][H_v],
+    dt_bias / a f32 [H_v]. Returns (q [n][H_k][S], k, v [n][H_v][S], beta [n][H_v], g [n][H_v])."""
+    f = lambda x: np.ascontiguousarray(x, dtype=np.float32)
+    qkv, conv_w, beta_raw, alpha, dt_bias, a = map(f, (qkv, conv_w, beta_raw, alpha, dt_bias, a))
+    assert conv_state.dtype == np.float32 and conv_state.flags.c_contiguous
+    n, ch = qkv.shape
+    H_v = (ch - 2 * S * H_k) // S
+    kc = conv_w.shape[1]
+    K = conv_state.shape[0]
+    q = np.zeros((n, H_k, S), np.float32)
+    k = np.zeros_like(q)
+    v = np.zeros((n, H_v, S), np.float32)
+    beta = np.zeros((n, H_v), np.float32)
+    g = np.zeros_like(beta)
+    rc = ref().kbref_gdn_input(_ptr(qkv), _ptr(conv_state), _ptr(conv_w), _ptr(beta_raw), _ptr(alpha), _ptr(dt_bias),
+                               _ptr(a), S, H_k, H_v, kc, K, n, eps, _ptr(q), _ptr(k), _ptr(v), _ptr(beta), _ptr(g),
+                               n_threads)
+    assert rc == 0
+    return q, k, v, beta, g
+
+
+def ref_gdn_gated_norm(x, z, w, eps, n_threads=1):
+    """rms_norm(x, eps) * w * silu(z) on the reference's ops (graph.cpp:186-190); x, z f32 [n][H][S], w f32 [S]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    z = np.ascontiguousarray(z, dtype=np.float32).reshape(x.shape)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, H, S = x.shape
+    dst = np.zeros_like(x)
+    assert ref().kbref_gdn_gated_norm(_ptr(x), _ptr(z), _ptr(w), S, H, n, eps, _ptr(dst), n_threads) == 0
+    return dst
+
+
 def ref_cpy(src: np.ndarray, src_type: int, dst: np.ndarray, dst_type: int) -> int:
     return ref().kbref_cpy(_ptr(src), src_type, _ptr(dst), dst_type, src.size)
 
@@ -392,3 +430,43 @@ def rs_attn_prologue(qfull, kcur, pos, q_norm, k_norm, eps, n_rot, sections, mod
         return y
 
     return rope(q), rope(k), gate
+
+
+def rs_gdn_input(qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a, S, H_k, eps):
+    """Restatement of the DeltaNet input side (TEST INFRASTRUCTURE; graph.cpp:136-165 with ggml's ops):
+    float64 conv over [state | batch] (ops.cpp:9931-9982), silu, l2 = rms_norm(eps / S) / sqrt(S), the gates,
+    and the conv-state snapshot rule. Returns (q, k, v, beta, g, new_state)."""
+    n, ch = qkv.shape
+    H_v = (ch - 2 * S * H_k) // S
+    kc = conv_w.shape[1]
+    K = conv_state.shape[0]
+    old = conv_state[0].reshape(ch, kc - 1).astype(np.float64)
+    seq = np.concatenate([old, qkv.T.astype(np.float64)], axis=1)  # [ch][kc - 1 + n]
+    w = conv_w.astype(np.float64)
+    conv = np.stack([(seq[:, t:t + kc] * w).sum(1) for t in range(n)], 0)  # [n][ch]
+    conv = conv / (1.0 + np.exp(-conv))
+    q = conv[:, :S * H_k].reshape(n, H_k, S)
+    k = conv[:, S * H_k:2 * S * H_k].reshape(n, H_k, S)
+    v = conv[:, 2 * S * H_k:].reshape(n, H_v, S)
+
+    def l2(x):
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + eps / S) / np.sqrt(S)
+
+    beta = 1.0 / (1.0 + np.exp(-beta_raw.astype(np.float64)))
+    xg = alpha.astype(np.float64) + dt_bias.astype(np.float64)
+    g = np.where(xg > 20.0, xg, np.log1p(np.exp(np.minimum(xg, 20.0)))) * a.astype(np.float64)
+    state = conv_state.copy()
+    for s_ in range(K):
+        if s_ >= n and s_ > 0:
+            continue
+        start = max(0, n - s_)
+        state[s_] = seq[:, start:start + kc - 1].astype(np.float32).reshape(-1)
+    return l2(q), l2(k), v, beta, g, state
+
+
+def rs_gdn_gated_norm(x, z, w, eps):
+    """rms_norm(x, eps) * w * silu(z) in float64 (graph.cpp:186-190)."""
+    x = x.astype(np.float64)
+    z = z.astype(np.float64).reshape(x.shape)
+    y = x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * w.astype(np.float64)
+    return y * z / (1.0 + np.exp(-z))

@@ -15,9 +15,14 @@
 //   kbref_attn_prologue    the ops between the projections and the attention in Builder::attention
 //                          (src/graph.cpp:94-112): q / gate views, ggml_rms_norm * weight, ggml_rope_multi,
 //                          ggml_cont of the gate, ggml_set_rows of K and V into the caches
+//   kbref_gdn_input        the DeltaNet input side of Builder::deltanet (src/graph.cpp:136-165): sigmoid,
+//                          softplus gates, conv-state concat + snapshot copies, ggml_ssm_conv + silu, l2 norms
+//   kbref_gdn_gated_norm   the DeltaNet output norm (src/graph.cpp:186-190): rms_norm * w * silu(z)
 //
 // use_ref = 1 selects ggml's vec-only reference path (no split-KV, no tiling; ops.cpp:9487-9550),
 // which makes results independent of the thread count.
+#include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <vector>
@@ -184,6 +189,97 @@ int kbref_attn_prologue(const float* qfull, const float* kcur, const float* vcur
     ggml_build_forward_expand(gf, ggml_set_rows(ctx, cv, ggml_reshape_2d(ctx, v, (int64_t) hd * nkv, n), it));
     ggml_build_forward_expand(gf, ggml_cpy(ctx, q, bindx(GGML_TYPE_F32, hd, nh, n, q_out)));
     ggml_build_forward_expand(gf, ggml_cpy(ctx, gate, bindx(GGML_TYPE_F32, (int64_t) hd * nh, n, 1, gate_out)));
+    ggml_cplan plan = ggml_graph_plan(gf, n_threads > 0 ? n_threads : 1, nullptr);
+    std::vector<uint8_t> work(plan.work_size + 64);
+    plan.work_data = plan.work_size ? work.data() : nullptr;
+    const int rc = ggml_graph_compute(gf, &plan) == GGML_STATUS_SUCCESS ? 0 : 1;
+    ggml_free(ctx);
+    return rc;
+}
+
+// Builder::deltanet's input side for n tokens (graph.cpp:136-165). qkv f32 [n][ch] (ch = 2 S H_k + S H_v),
+// conv_state f32 [K][(kc - 1) ch] (read and written), conv_w f32 [ch][kc], beta_raw / alpha f32 [n][H_v],
+// dt_bias / a f32 [H_v]; outputs q_out, k_out f32 [n][H_k][S], v_out f32 [n][H_v][S], beta_out, g_out [n][H_v].
+int kbref_gdn_input(const float* qkv, float* conv_state, const float* conv_w, const float* beta_raw, const float* alpha,
+                    const float* dt_bias, const float* a, int S, int H_k, int H_v, int kc, int K, int n, float eps,
+                    float* q_out, float* k_out, float* v_out, float* beta_out, float* g_out, int n_threads) {
+    init_once();
+    const int64_t ch = 2 * (int64_t) S * H_k + (int64_t) S * H_v;
+    const size_t mem = (size_t) 16 * (size_t) (ch * (n + kc) + (int64_t) H_v * n) * 4 + ((size_t) 16 << 20);
+    ggml_init_params ip{mem, nullptr, false};
+    ggml_context* ctx = ggml_init(ip);
+    if (!ctx) return 1;
+    auto bindx = [&](ggml_type t, int64_t n0, int64_t n1, int64_t n2, const void* data) {
+        ggml_tensor* x = ggml_new_tensor_3d(ctx, t, n0, n1, n2);
+        x->data = const_cast<void*>(data);
+        return x;
+    };
+    ggml_cgraph* gf = ggml_new_graph(ctx);
+    ggml_tensor* qkv_t = bindx(GGML_TYPE_F32, ch, n, 1, qkv);
+    ggml_tensor* beta = ggml_sigmoid(ctx, bindx(GGML_TYPE_F32, H_v, n, 1, beta_raw));
+    ggml_tensor* g = ggml_mul(ctx, ggml_softplus(ctx, ggml_add(ctx, bindx(GGML_TYPE_F32, H_v, n, 1, alpha),
+                                                                bindx(GGML_TYPE_F32, H_v, 1, 1, dt_bias))),
+                              bindx(GGML_TYPE_F32, H_v, 1, 1, a));
+    ggml_tensor* cs_all = bindx(GGML_TYPE_F32, (int64_t) (kc - 1) * ch, K, 1, conv_state);
+    ggml_tensor* cs = ggml_view_1d(ctx, cs_all, cs_all->ne[0], 0);
+    cs = ggml_reshape_3d(ctx, cs, kc - 1, ch, 1);
+    ggml_tensor* xt = ggml_transpose(ctx, ggml_reshape_3d(ctx, qkv_t, ch, n, 1));
+    ggml_tensor* conv_in = ggml_concat(ctx, cs, xt, 0);  // [kc - 1 + n, ch, 1]
+    for (int t = 1; t <= K; ++t) {
+        const int64_t s_idx = std::max<int64_t>(0, conv_in->ne[0] - (kc - 1) - K + t);
+        const int slot = K - t;
+        if (slot >= n && slot > 0) continue;
+        ggml_tensor* src = ggml_view_3d(ctx, conv_in, kc - 1, ch, 1, conv_in->nb[1], conv_in->nb[2],
+                                        ggml_row_size(conv_in->type, s_idx));
+        ggml_tensor* dst = ggml_view_1d(ctx, cs_all, cs_all->ne[0], (size_t) slot * cs_all->nb[1]);
+        ggml_build_forward_expand(gf, ggml_cpy(ctx, src, dst));
+    }
+    ggml_tensor* conv = ggml_silu(ctx, ggml_ssm_conv(ctx, conv_in, bindx(GGML_TYPE_F32, kc, ch, 1, conv_w)));
+    const int64_t nb1 = ggml_row_size(conv->type, ch);
+    ggml_tensor* q = ggml_view_4d(ctx, conv, S, H_k, n, 1, ggml_row_size(conv->type, S), nb1, nb1 * n, 0);
+    ggml_tensor* k = ggml_view_4d(ctx, conv, S, H_k, n, 1, ggml_row_size(conv->type, S), nb1, nb1 * n,
+                                  ggml_row_size(conv->type, (int64_t) S * H_k));
+    ggml_tensor* v = ggml_view_4d(ctx, conv, S, H_v, n, 1, ggml_row_size(conv->type, S), nb1, nb1 * n,
+                                  ggml_row_size(conv->type, 2 * (int64_t) S * H_k));
+    auto l2 = [&](ggml_tensor* x) {
+        const float nn = (float) x->ne[0];
+        return ggml_scale(ctx, ggml_rms_norm(ctx, x, eps / nn), 1.0f / std::sqrt(nn));
+    };
+    q = l2(q);
+    k = l2(k);
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, q, bindx(GGML_TYPE_F32, S, H_k, n, q_out)));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, k, bindx(GGML_TYPE_F32, S, H_k, n, k_out)));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, v, bindx(GGML_TYPE_F32, S, H_v, n, v_out)));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, beta, bindx(GGML_TYPE_F32, H_v, n, 1, beta_out)));
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, g, bindx(GGML_TYPE_F32, H_v, n, 1, g_out)));
+    ggml_cplan plan = ggml_graph_plan(gf, n_threads > 0 ? n_threads : 1, nullptr);
+    std::vector<uint8_t> work(plan.work_size + 64);
+    plan.work_data = plan.work_size ? work.data() : nullptr;
+    const int rc = ggml_graph_compute(gf, &plan) == GGML_STATUS_SUCCESS ? 0 : 1;
+    ggml_free(ctx);
+    return rc;
+}
+
+// Builder::deltanet's output norm (graph.cpp:186-190): dst = rms_norm(x, eps) * w * silu(z); x, z, dst f32
+// [n][H][S], w f32 [S].
+int kbref_gdn_gated_norm(const float* x, const float* z, const float* w, int S, int H, int n, float eps, float* dst,
+                         int n_threads) {
+    init_once();
+    const size_t mem = (size_t) 8 * (size_t) S * H * n * 4 + ((size_t) 4 << 20);
+    ggml_init_params ip{mem, nullptr, false};
+    ggml_context* ctx = ggml_init(ip);
+    if (!ctx) return 1;
+    ggml_tensor* xt = ggml_new_tensor_3d(ctx, GGML_TYPE_F32, S, H, n);
+    xt->data = const_cast<float*>(x);
+    ggml_tensor* zt = ggml_new_tensor_3d(ctx, GGML_TYPE_F32, S, H, n);
+    zt->data = const_cast<float*>(z);
+    ggml_tensor* wt = ggml_new_tensor_1d(ctx, GGML_TYPE_F32, S);
+    wt->data = const_cast<float*>(w);
+    ggml_tensor* dt = ggml_new_tensor_3d(ctx, GGML_TYPE_F32, S, H, n);
+    dt->data = dst;
+    ggml_tensor* o = ggml_mul(ctx, ggml_mul(ctx, ggml_rms_norm(ctx, xt, eps), wt), ggml_silu(ctx, zt));
+    ggml_cgraph* gf = ggml_new_graph(ctx);
+    ggml_build_forward_expand(gf, ggml_cpy(ctx, o, dt));
     ggml_cplan plan = ggml_graph_plan(gf, n_threads > 0 ? n_threads : 1, nullptr);
     std::vector<uint8_t> work(plan.work_size + 64);
     plan.work_data = plan.work_size ? work.data() : nullptr;

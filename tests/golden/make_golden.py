@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference's own ggml CPU ops.
 
-    python tests/golden/make_golden.py [attn_prologue]   (one fixture only with its name)
+    python tests/golden/make_golden.py [attn_prologue | gdn_io]   (one fixture only with its name)
 
 Needs oracle/_ref (built by `make -C oracle ref` from the reference sources). Every fixture holds seeded
 inputs and the reference's outputs for them; tests/test_oracle.py checks the C restatement against them
@@ -59,10 +59,39 @@ def prologue_fixture():
                 gate=gate, k_cache=c16k, v_cache=c16v)
 
 
+def make_gdn_io_inputs(seed, n, S=128, H_k=16, H_v=48, K=4, kc=4):
+    """Seeded inputs of the DeltaNet input / output sides: projections ~N(0, 1), conv weights ~N(0, 0.5),
+    a stored conv state ~N(0, 1) in slot 0 (older slots hold a sentinel), gate inputs ~N(0, 1), a < 0."""
+    rng = np.random.default_rng(seed)
+    ch = 2 * S * H_k + S * H_v
+    qkv = rng.standard_normal((n, ch)).astype(np.float32)
+    conv_state = np.full((K, (kc - 1) * ch), 7.0, np.float32)
+    conv_state[0] = rng.standard_normal((kc - 1) * ch).astype(np.float32)
+    conv_w = (0.5 * rng.standard_normal((ch, kc))).astype(np.float32)
+    beta_raw = rng.standard_normal((n, H_v)).astype(np.float32)
+    alpha = rng.standard_normal((n, H_v)).astype(np.float32)
+    dt_bias = rng.standard_normal(H_v).astype(np.float32)
+    a = -np.exp(rng.standard_normal(H_v)).astype(np.float32)
+    return qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a
+
+
+def gdn_io_fixture():
+    qkv, cs, w, br, al, dt, a = make_gdn_io_inputs(21, 3, S=64, H_k=2, H_v=4)
+    cs_out = cs.copy()
+    q, k, v, beta, g = O.ref_gdn_input(qkv, cs_out, w, br, al, dt, a, 64, 2, 1e-6)
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((3, 4, 64)).astype(np.float32)
+    z = rng.standard_normal((3, 4, 64)).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal(64)).astype(np.float32)
+    o = O.ref_gdn_gated_norm(x, z, nw, 1e-6)
+    return dict(qkv=qkv, conv_state=cs, conv_w=w, beta_raw=br, alpha=al, dt_bias=dt, a=a, q=q, k=k, v=v, beta=beta,
+                g=g, conv_state_out=cs_out, x=x, z=z, norm_w=nw, o=o)
+
+
 def main(only=None):
     out = {}
-    if only == "attn_prologue":
-        out["attn_prologue"] = prologue_fixture()
+    if only in ("attn_prologue", "gdn_io"):
+        out[only] = prologue_fixture() if only == "attn_prologue" else gdn_io_fixture()
         for name, arrays in out.items():
             np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
             print(name, sum(a.nbytes for a in arrays.values()))
@@ -99,6 +128,7 @@ def main(only=None):
     O.ref_cpy(xs, O.GGML_F32, h, O.GGML_F16)
     out["cpy_f32_f16"] = dict(x=xs, y=h)
     out["attn_prologue"] = prologue_fixture()
+    out["gdn_io"] = gdn_io_fixture()
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
         print(name, sum(a.nbytes for a in arrays.values()))

@@ -225,3 +225,34 @@ def test_live_attn_prologue_qwen35_shapes():
     assert np.abs(q - q_ref).max() <= 1e-6 * np.abs(q_ref).max()
     assert np.array_equal(gate.astype(np.float32), gate_ref)
     assert_f16_near(kc.view(np.float16).reshape(64, 4, 256)[kv_idx], k)
+
+
+# ---------------------------------------------------------------------------------------------- DeltaNet input / output sides
+
+def test_golden_gdn_io():
+    """conv + silu + l2 norms, the gates, the conv-state snapshot rule and the gated output norm of the
+    restatement against the reference's graph (graph.cpp:136-165, 186-190)."""
+    g = gold("gdn_io")
+    q, k, v, beta, gg, state = O.rs_gdn_input(g["qkv"], g["conv_state"], g["conv_w"], g["beta_raw"], g["alpha"],
+                                              g["dt_bias"], g["a"], 64, 2, 1e-6)
+    for a, b in ((q, g["q"]), (k, g["k"]), (v, g["v"]), (beta, g["beta"]), (gg, g["g"])):
+        assert np.abs(a - b).max() <= 1e-6 * np.abs(b).max()
+    assert np.array_equal(state, g["conv_state_out"])
+    o = O.rs_gdn_gated_norm(g["x"], g["z"], g["norm_w"], 1e-6)
+    assert np.abs(o - g["o"]).max() <= 1e-6 * np.abs(g["o"]).max()
+
+
+@ref_only
+@pytest.mark.parametrize("n", [1, 2, 5])
+def test_live_gdn_input_qwen35_shapes(n):
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import make_gdn_io_inputs
+
+    qkv, cs, w, br, al, dt, a = make_gdn_io_inputs(30 + n, n)
+    cs_ref = cs.copy()
+    ref = O.ref_gdn_input(qkv, cs_ref, w, br, al, dt, a, 128, 16, 1e-6)
+    rs = O.rs_gdn_input(qkv, cs, w, br, al, dt, a, 128, 16, 1e-6)
+    for x, y in zip(rs[:5], ref):
+        assert np.abs(x - y).max() <= 1e-6 * np.abs(y).max()
+    assert np.array_equal(rs[5], cs_ref)
