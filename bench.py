@@ -299,6 +299,79 @@ def bench_gdn(kb, torch, dev, steps, warmup):
                          "traffic": ncu_traffic("gdn_recurrent_verify")}}
 
 
+def bench_io_ops(kb, torch, dev, steps, warmup):
+    """The ops around the two attention kinds at config[2]'s 4,096-token prefill (qwen35 shapes, f16 cache):
+    kb_attn_prologue (Q/gate split, RMS norms, M-RoPE, K/V cache writes), kb_gdn_input (conv, SiLU, L2 norms, gates,
+    conv-state snapshots) and kb_gdn_gated_norm; plus the same three at the 4-token verify. HBM-bound: bytes = what
+    each op must read and write once. Timed with CUDA events, each op alone in a loop (inputs > L2 at 4,096 tokens)."""
+    import ctypes  # noqa: F401
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    hd, nh, nkv, S, Hk, Hv = D, H, H_KV, 128, 16, 48
+    ch = 2 * S * Hk + S * Hv
+    pk, _ = measured_peaks()
+    res = {}
+    for T in (4096, 4):
+        qfull = torch.randn(T, nh * 2 * hd, device=dev, generator=g)
+        kcur = torch.randn(T, nkv * hd, device=dev, generator=g)
+        vcur = torch.randn(T, nkv * hd, device=dev, generator=g)
+        p = torch.arange(T, dtype=torch.int32, device=dev)
+        pos = torch.cat([p, p, p, torch.zeros_like(p)])
+        kv_idx = torch.arange(T, dtype=torch.int64, device=dev)
+        qn = torch.ones(hd, device=dev)
+        kcache = torch.zeros(T, nkv * hd, dtype=torch.float16, device=dev)
+        vcache = torch.zeros_like(kcache)
+        kc, vc = kb.cache_rows(kcache, kb.F16), kb.cache_rows(vcache, kb.F16)
+        qkv = torch.randn(T, ch, device=dev, generator=g)
+        state = torch.randn(4, 3 * ch, device=dev, generator=g)
+        cw = torch.randn(ch, 4, device=dev, generator=g) * 0.5
+        br = torch.randn(T, Hv, device=dev, generator=g)
+        al = torch.randn(T, Hv, device=dev, generator=g)
+        dt = torch.randn(Hv, device=dev, generator=g)
+        aa = -torch.rand(Hv, device=dev, generator=g) - 0.1
+        x = torch.randn(T, Hv, S, device=dev, generator=g)
+        z = torch.randn(T, Hv, S, device=dev, generator=g)
+        nw = torch.ones(S, device=dev)
+        ops = {
+            "attn_prologue": (lambda: kb.attn_prologue(qfull, kcur, vcur, pos, kv_idx, qn, qn, 1e-6, 64, [11, 11, 10, 0], 40,
+                                                       1e7, kc, vc),
+                              T * (nh * 2 * hd + 2 * nkv * hd) * 4 + T * (2 * nh * hd * 4 + 2 * nkv * hd * 2)),
+            "gdn_input": (lambda: kb.gdn_input(qkv, state, cw, S, Hk, 1e-6, beta_raw=br, alpha=al, dt_bias=dt, a=aa),
+                          T * ch * 4 * 2 + T * Hv * 4 * 4 + 4 * 3 * ch * 4),
+            "gdn_gated_norm": (lambda: kb.gdn_gated_norm(x, z, nw, 1e-6), T * Hv * S * 4 * 3),
+        }
+        for name, (fn, nbytes) in ops.items():
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            # 10 calls per CUDA graph (as a captured forward launches them), so host overhead is not timed
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cap):
+                for _ in range(10):
+                    fn()
+            torch.cuda.current_stream(dev).wait_stream(cap)
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = max(2, steps // 10)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del graph
+            us = e0.elapsed_time(e1) * 1e3 / (reps * 10)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            res[f"{name}_{T}"] = {"value": round(us, 2), "unit": "us", "tokens": T,
+                                  "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
+                                               "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
+                                               "algorithmic_bytes_per_launch": nbytes}}
+    return res
+
+
 def bench_gdn_prefill(kb, torch, dev, steps, warmup):
     """config[2] DeltaNet half: 4,096 tokens in 64-token chunks from a zero state (48 value / 16 key heads, d 128,
     K = 4 slots) through kb_gated_delta_net with scratch (tcgen05 prep + state kernels, the last 3 tokens
@@ -585,6 +658,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         secondary["prefill_bf16_4096"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
+        secondary["io_ops"] = bench_io_ops(kb, torch, dev, max(20, args.steps // 2), args.warmup)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

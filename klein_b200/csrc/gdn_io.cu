@@ -73,11 +73,21 @@ __global__ void __launch_bounds__(256) gdn_input_kernel(const GdnInputParams p) 
     float* out = is_q ? p.q_out + (int64_t) slot * S : is_k ? p.k_out + (int64_t) (slot - p.H_k) * S
                                                                : p.v_out + (int64_t) (slot - 2 * p.H_k) * S;
     const int64_t out_ld = (int64_t) (is_q || is_k ? p.H_k : p.H_v) * S;
-    for (int t = t0; t < t1; ++t) {
+    // the chunk's inputs first, all loads in flight together
+    float xs[GIN_CHUNK][CPL];
+#pragma unroll
+    for (int u = 0; u < GIN_CHUNK; ++u)
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            xs[u][i] = t0 + u < t1 ? p.qkv[(int64_t) (t0 + u) * p.qkv_ld + c0 + lane + 32 * i] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < GIN_CHUNK; ++u) {
+        const int t = t0 + u;
+        if (t >= t1) break;
         float y[CPL];
 #pragma unroll
         for (int i = 0; i < CPL; ++i) {
-            const float x = p.qkv[(int64_t) t * p.qkv_ld + c0 + lane + 32 * i];
+            const float x = xs[u][i];
             // ggml's order: sum over the window oldest first, one multiply-add per tap
             float acc = 0.0f;
 #pragma unroll
