@@ -468,6 +468,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     L = kb.lib()
     need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]), ctypes.byref(layers[0][3]),
                                              ctypes.byref(prm))
+    if world > 1:  # the fused exchange needs its counter as well
+        need = max(need, L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]),
+                                                                ctypes.byref(layers[0][3]), ctypes.byref(prm)))
     scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
     sp = ctypes.c_void_p(scratch.data_ptr())
     st = ctypes.c_void_p(stream.cuda_stream)
@@ -498,13 +501,15 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             if rc != 0:
                 raise kb.KbError("kb_flash_attn_ext", rc)
             return
+        if xchg is not None:
+            # the partial attention writes its rows straight into every rank's gather buffer, then the merge
+            xchg.attend_and_combine(qt, layers[l][2], layers[l][3], prm, sp.value, need, rows, D, out.data_ptr(),
+                                    st.value)
+            return
         rc = L.kb_flash_attn_ext_partial(ctypes.byref(qt), ctypes.byref(layers[l][2]), ctypes.byref(layers[l][3]), None,
                                          ctypes.byref(prm), ctypes.byref(pt), ml_ptr, sp, ctypes.c_size_t(need), st)
         if rc != 0:
             raise kb.KbError("kb_flash_attn_ext_partial", rc)
-        if xchg is not None:
-            xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), st.value)
-            return
         dist.all_gather_into_tensor(gathered, part)
         rc = L.kb_lse_combine(g_o, g_ml, ctypes.c_int64(pf), world, ctypes.c_int64(rows), D,
                               ctypes.c_void_p(out.data_ptr()), st)
@@ -599,6 +604,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         # the q8_0 kernel plans its own row chunks and splits: size the scratch for it
         need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]), ctypes.byref(layers[0][3]),
                                                  ctypes.byref(prm))
+        if world > 1:
+            need = max(need, L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]),
+                                                                    ctypes.byref(layers[0][3]), ctypes.byref(prm)))
         del scratch
         scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
         sp = ctypes.c_void_p(scratch.data_ptr())

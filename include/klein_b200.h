@@ -146,6 +146,21 @@ kb_status kb_partials_push(const float* part, int64_t part_floats, float* const*
 kb_status kb_lse_combine_wait(const float* gather, int64_t part_stride, int64_t slot_set_floats, int32_t n_parts,
                               int64_t rows, int32_t head_dim, int32_t* flags, float* dst, void* stream);
 
+/*
+ * kb_flash_attn_ext_partial and kb_partials_push in one call: the split combine of this rank's partial attention
+ * writes every merged row (o unnormalised, m, l) straight into slot `rank` of every rank's gather buffer, in the
+ * packed layout kb_partials_push uses (o [n_q * H][D], then (m, l) [n_q * H][2]; part_floats >= n_q * H * (D + 2),
+ * a multiple of 4), and its last CTA counts the exchange in every rank's flags exactly as a push does; the next
+ * call on this rank is kb_lse_combine_wait. Operands as kb_flash_attn_ext_partial (ne3 = 1, at least one cell);
+ * scratch of kb_flash_attn_ext_push_scratch_bytes bytes.
+ */
+size_t kb_flash_attn_ext_push_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                            const kb_fa_params* params);
+kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                 const kb_fa_params* params, int64_t part_floats, float* const* gather,
+                                 int64_t slot_set_floats, int32_t* const* flags, int32_t rank, int32_t n_ranks,
+                                 void* scratch, size_t scratch_bytes, void* stream);
+
 /* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
  * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,

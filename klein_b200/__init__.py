@@ -50,6 +50,8 @@ EXPORTED = [
     "kb_flash_attn_ext_gated",
     "kb_gdn_input",
     "kb_gdn_gated_norm",
+    "kb_flash_attn_ext_push",
+    "kb_flash_attn_ext_push_scratch_bytes",
 ]
 
 
@@ -113,6 +115,11 @@ def lib():
         L.kb_flash_attn_ext_gated.restype = c_int32
         L.kb_flash_attn_ext_gated.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
                                               P(KbTensor), P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_flash_attn_ext_push.restype = c_int32
+        L.kb_flash_attn_ext_push.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams), c_int64,
+                                             c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_size_t, c_void_p]
+        L.kb_flash_attn_ext_push_scratch_bytes.restype = c_size_t
+        L.kb_flash_attn_ext_push_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
         L.kb_gdn_input.restype = c_int32
         L.kb_gdn_input.argtypes = [P(KbTensor)] * 7 + [c_int32, c_int32, ctypes.c_float] + [P(KbTensor)] * 5 + [c_void_p]
         L.kb_gdn_gated_norm.restype = c_int32
@@ -474,6 +481,20 @@ class PeerExchange:
         L = lib()
         check("kb_partials_push", L.kb_partials_push(c_void_p(part_ptr), self.pf, self._g, self.set_floats, self._f,
                                                      self.rank, self.n, c_void_p(stream)))
+        check("kb_lse_combine_wait", L.kb_lse_combine_wait(c_void_p(self.gbuf), self.pf, self.set_floats, self.n, rows,
+                                                           head_dim, c_void_p(self.fbuf), c_void_p(dst_ptr),
+                                                           c_void_p(stream)))
+
+    def attend_and_combine(self, qt, k: KbTensor, v: KbTensor, prm, scratch_ptr: int, scratch_bytes: int, rows: int,
+                           head_dim: int, dst_ptr: int, stream: int) -> None:
+        """kb_flash_attn_ext_push (this rank's partial attention, its rows written straight into every rank's gather
+        buffer) then kb_lse_combine_wait into dst: the whole sequence-split attention of one layer in two kernels of
+        this library plus the attention's own. qt / prm: kb_tensor q and KbFaParams as for kb_flash_attn_ext."""
+        L = lib()
+        check("kb_flash_attn_ext_push", L.kb_flash_attn_ext_push(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), None,
+                                                                 ctypes.byref(prm), self.pf, self._g, self.set_floats,
+                                                                 self._f, self.rank, self.n, c_void_p(scratch_ptr),
+                                                                 c_size_t(scratch_bytes), c_void_p(stream)))
         check("kb_lse_combine_wait", L.kb_lse_combine_wait(c_void_p(self.gbuf), self.pf, self.set_floats, self.n, rows,
                                                            head_dim, c_void_p(self.fbuf), c_void_p(dst_ptr),
                                                            c_void_p(stream)))

@@ -166,8 +166,39 @@ __global__ void __launch_bounds__(MERGE_THREADS) fa_combine_kernel(const FaStrea
     float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + qi * p.d_nb2 + b * p.d_nb3);
     float* ml_out = p.partial_out ? p.dst_ml + (((int64_t) b * p.n_q + qi) * p.n_head + h) * 2 : nullptr;
     const char* gate_row = p.gate && !p.partial_out ? p.gate + h * p.g_nb1 + qi * p.g_nb2 + b * p.g_nb3 : nullptr;
+    if (!p.push) {
+        merge_row(p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + (base * RPC + r) * 2, (int64_t) RPC * 2,
+                  p.n_splits, D, out, ml_out, gate_row);
+        return;
+    }
+    // fused exchange: this rank's merged partial row (o unnormalised, m, l) into slot `rank` of the slot set of this
+    // exchange's epoch in every rank's gather buffer (packed part: o [rows][D], then (m, l) [rows][2])
+    const int epoch = *reinterpret_cast<volatile const int*>(p.flags[p.rank] + p.n_ranks) + 1;
+    const int64_t rows = (int64_t) p.n_q * p.n_head, ro = (int64_t) qi * p.n_head + h;
+    const int64_t off = (int64_t) (epoch & 1) * p.slot_set_floats + (int64_t) p.rank * p.part_floats;
+    float* own = p.gather[p.rank] + off;
     merge_row(p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + (base * RPC + r) * 2, (int64_t) RPC * 2,
-              p.n_splits, D, out, ml_out, gate_row);
+              p.n_splits, D, own + ro * D, own + rows * D + ro * 2);
+    __syncthreads();
+    for (int d = 0; d < p.n_ranks; ++d) {
+        if (d == p.rank) continue;
+        float* dst = p.gather[d] + off;
+        for (int i = threadIdx.x; i < D; i += blockDim.x) dst[ro * D + i] = own[ro * D + i];
+        if (threadIdx.x < 2) dst[rows * D + ro * 2 + threadIdx.x] = own[rows * D + ro * 2 + threadIdx.x];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int total = (int) (gridDim.x * gridDim.y * gridDim.z);
+        if (atomicAdd(p.push_counter, 1) == total - 1) {
+            // the last CTA: every row is in place on every rank (each CTA fenced before counting itself)
+            *p.push_counter = 0;
+            __threadfence_system();
+            for (int d = 0; d < p.n_ranks; ++d)
+                asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p.flags[d] + p.rank), "r"(PUSH_CHUNKS)
+                             : "memory");
+        }
+    }
 }
 
 // Merges partial results computed over disjoint KV ranges (e.g. one per GPU), one row per block.
@@ -375,6 +406,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
     const int rows = min(N, p.R - row0);
     const int kb3 = b / p.rk3;
 
+    if (p.push && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) *p.push_counter = 0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < KRAW; ++s) {
             mbar_init(&sm.kfull[s], 1);
@@ -833,7 +865,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < N; ++e)
                         if (e == r) O = __uint_as_float(ov[e]);
-                    if (p.n_splits == 1) {
+                    if (p.n_splits == 1 && !p.push) {
                         store_row(p, sm.row_qi[r], sm.row_h[r], b, d, O, M, L);
                     } else {
                         p.o_part[(part_row0 + r) * D + d] = O;
@@ -882,7 +914,7 @@ cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUt
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
     kern<<<grid, tc::Roles<Q8>::THREADS, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
-    if (e != cudaSuccess || p.n_splits == 1) return e;
+    if (e != cudaSuccess || (p.n_splits == 1 && !p.push)) return e;
     dim3 cgrid(p.R, p.n_head_kv, p.ne3);
     fa_combine_kernel<N><<<cgrid, MERGE_THREADS, 0, stream>>>(p);
     return cudaGetLastError();

@@ -109,7 +109,8 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     return KB_OK;
 }
 
-FaPlan plan_fa(const FaShape& s) {
+// push: the fused exchange (kb_flash_attn_ext_push) always runs the split combine and needs a counter
+FaPlan plan_fa(const FaShape& s, bool push = false) {
     FaPlan pl;
     pl.rpc = kb::fa_tc_rpc(s.R);
     pl.n_row_chunks = (s.R + pl.rpc - 1) / pl.rpc;
@@ -128,9 +129,10 @@ FaPlan plan_fa(const FaShape& s) {
         pl.keys_per_split = tps * unit;
         pl.n_splits = (int) ((tiles + tps - 1) / tps);
     }
-    if (pl.n_splits > 1) {
+    if (pl.n_splits > 1 || push) {
         const size_t rows = (size_t) base * pl.n_splits * pl.rpc;
         pl.scratch = rows * kb::FA_D * 4 + 256 + rows * 2 * 4;
+        if (push) pl.scratch = (pl.scratch + 255) / 256 * 256 + 256;  // the combine's CTA counter
     }
     return pl;
 }
@@ -181,9 +183,17 @@ size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, c
 
 namespace {
 
+// the destinations of the fused exchange
+struct PushArgs {
+    float* const* gather;
+    int32_t* const* flags;
+    int64_t slot_set_floats, part_floats;
+    int rank, n_ranks;
+};
+
 kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                   const kb_fa_params* prm, const kb_tensor* dst, float* dst_ml, void* scratch, size_t scratch_bytes,
-                  void* stream, const kb_tensor* gate = nullptr) {
+                  void* stream, const kb_tensor* gate = nullptr, const PushArgs* push = nullptr) {
     if (!prm || !dst) return KB_ERR_ARG;
     FaShape s;
     kb_status st = check_fa(q, k, v, mask, &s);
@@ -194,10 +204,12 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
                  gate->ne[2] != s.n_q || gate->ne[3] != s.ne3))
         return KB_ERR_BAD_SHAPE;
     if (gate && dst_ml) return KB_ERR_ARG;  // the gate applies to final outputs, not to partials
+    if (push && (gate || s.ne3 != 1)) return KB_ERR_ARG;
     if (prm->logit_softcap != 0.0f && !(std::isfinite(prm->logit_softcap))) return KB_ERR_ARG;
     if (prm->max_bias > 0.0f && !mask) return KB_ERR_ARG;  // ggml: ALiBi needs a mask
     if (prm->causal && prm->ring < 0) return KB_ERR_ARG;
 
+    if (s.n_kv == 0 && push) return KB_ERR_UNSUPPORTED;  // nothing to attend: exchange l = 0 partials another way
     if (s.n_kv == 0) {
         // no cells: every row's softmax sum is 0, so the output is 0 (ops.cpp:9066); partials get l = 0
         const size_t row = (size_t) s.D * 4;
@@ -209,7 +221,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         return KB_OK;
     }
     const float log2e_ = 1.4426950408889634f;
-    if (use_prefill(s, prm, dst_ml != nullptr)) {
+    if (use_prefill(s, prm, dst_ml != nullptr || push != nullptr)) {
         const bool qv4 = aligned16(reinterpret_cast<uintptr_t>(q->data)) && aligned16(q->nb[1]) && aligned16(q->nb[2]) &&
                          aligned16(q->nb[3]);
         if (!qv4 || !aligned16(dst->nb[1]) || !aligned16(dst->nb[2]) || !aligned16(dst->nb[3]) ||
@@ -252,7 +264,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
     }
     if (s.kv_type == KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;  // bf16 caches: prefill shapes only
-    const FaPlan pl = plan_fa(s);
+    const FaPlan pl = plan_fa(s, push != nullptr);
     if (pl.scratch > 0 && (!scratch || scratch_bytes < pl.scratch)) return KB_ERR_SCRATCH;
 
     kb::FaStreamParams p{};
@@ -310,8 +322,20 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         p.gate = static_cast<const char*>(gate->data);
         p.g_nb1 = (int64_t) gate->nb[1], p.g_nb2 = (int64_t) gate->nb[2], p.g_nb3 = (int64_t) gate->nb[3];
     }
-    p.partial_out = dst_ml != nullptr;
+    p.partial_out = dst_ml != nullptr || push != nullptr;
     p.dst_ml = dst_ml;
+    if (push) {
+        p.push = 1;
+        p.rank = push->rank;
+        p.n_ranks = push->n_ranks;
+        p.slot_set_floats = push->slot_set_floats;
+        p.part_floats = push->part_floats;
+        for (int r = 0; r < push->n_ranks; ++r) {
+            p.gather[r] = push->gather[r];
+            p.flags[r] = push->flags[r];
+        }
+        p.push_counter = reinterpret_cast<int*>(static_cast<char*>(scratch) + pl.scratch - 256);
+    }
     p.err = kb::device_error_word();
     p.wait_ns = g_wait_ns;
 
@@ -339,6 +363,34 @@ size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb
 }  // namespace kb
 
 extern "C" {
+
+size_t kb_flash_attn_ext_push_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                            const kb_fa_params* params) {
+    (void) params;
+    FaShape s;
+    if (check_fa(q, k, v, nullptr, &s) != KB_OK) return 0;
+    return plan_fa(s, true).scratch;
+}
+
+kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                 const kb_fa_params* params, int64_t part_floats, float* const* gather,
+                                 int64_t slot_set_floats, int32_t* const* flags, int32_t rank, int32_t n_ranks,
+                                 void* scratch, size_t scratch_bytes, void* stream) {
+    if (!q || !gather || !flags || n_ranks < 1 || n_ranks > KB_MAX_PEERS || rank < 0 || rank >= n_ranks) return KB_ERR_ARG;
+    // the packed partial of kb_partials_push: o [n_q * H][D], then (m, l) [n_q * H][2]
+    const int64_t rows = q->ne[1] * q->ne[2], D = q->ne[0];
+    if (part_floats < rows * D + rows * 2 || part_floats % 4 != 0 || slot_set_floats < n_ranks * part_floats)
+        return KB_ERR_BAD_SHAPE;
+    for (int r = 0; r < n_ranks; ++r)
+        if (!gather[r] || !flags[r]) return KB_ERR_ARG;
+    // a shape-only destination (nothing is stored through it in this mode)
+    kb_tensor dst{};
+    dst.type = KB_TYPE_F32;
+    dst.ne[0] = D, dst.ne[1] = q->ne[2], dst.ne[2] = q->ne[1], dst.ne[3] = q->ne[3];
+    dst.nb[0] = 4, dst.nb[1] = (size_t) D * 4, dst.nb[2] = dst.nb[1] * dst.ne[1], dst.nb[3] = dst.nb[2] * dst.ne[2];
+    PushArgs pa{gather, flags, slot_set_floats, part_floats, rank, n_ranks};
+    return fa_impl(q, k, v, mask, params, &dst, nullptr, scratch, scratch_bytes, stream, nullptr, &pa);
+}
 
 kb_status kb_flash_attn_ext_gated(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                                   const kb_fa_params* params, const kb_tensor* gate, const kb_tensor* dst, void* scratch,

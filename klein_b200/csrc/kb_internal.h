@@ -45,6 +45,14 @@ struct FaStreamParams {
     float* dst_ml;                   // partial_out: f32 [ne3][n_q][H][2] = (max in log2 units, sum)
     const char* gate;                // null, or f32 [D, H, n_q, ne3]: the output is o * sigmoid(gate) (not partials)
     int64_t g_nb1, g_nb2, g_nb3;
+    // fused exchange (kb_flash_attn_ext_push): the split combine writes each merged partial row into slot `rank` of
+    // every rank's gather buffer, and its last CTA counts the exchange in their flags (as kb_partials_push does)
+    int push;
+    int rank, n_ranks;
+    int64_t slot_set_floats, part_floats;
+    float* gather[16];
+    int* flags[16];
+    int* push_counter;               // in the scratch: combine CTAs done (zeroed by the attention kernel)
     int* err;                        // device error word
     uint64_t wait_ns;                // budget of every bounded wait
 };

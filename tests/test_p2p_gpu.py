@@ -16,7 +16,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, fused):
     import torch
     import torch.distributed as dist
 
@@ -53,10 +53,20 @@ def _rank_main(rank, world, port, out_dir):
     stream = torch.cuda.current_stream(dev).cuda_stream
     errs = []
     kb.device_error(clear=True)
+    L = kb.lib()
+    import ctypes
+    prm = kb.fa_params(1 / 16, causal=True, pos0=pos0, kv_lo=kv_lo)
     for q, ref in zip(qs, full):
         out = torch.empty(1, n_q, H, D, device=dev)
-        kb.flash_attn_ext_partial(q, kv, vv, 1 / 16, part, causal=True, pos0=pos0, kv_lo=kv_lo)
-        xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), stream)
+        if fused:
+            qt = kb.kb_tensor(q.data_ptr(), kb.F32, [D, n_q, H, 1], [4, q.stride(1) * 4, q.stride(2) * 4, q.stride(0) * 4])
+            nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv),
+                                                        ctypes.byref(prm))
+            scratch = torch.empty(nb, dtype=torch.uint8, device=dev)
+            xchg.attend_and_combine(qt, kv, vv, prm, scratch.data_ptr(), nb, rows, D, out.data_ptr(), stream)
+        else:
+            kb.flash_attn_ext_partial(q, kv, vv, 1 / 16, part, causal=True, pos0=pos0, kv_lo=kv_lo)
+            xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), stream)
         torch.cuda.synchronize()
         errs.append(float((out - ref).abs().max() / ref.abs().max()))
     code = kb.device_error()
@@ -68,14 +78,15 @@ def _rank_main(rank, world, port, out_dir):
     np.save(os.path.join(out_dir, f"r{rank}.npy"), np.array(errs + [code], dtype=np.float64))
 
 
-def test_two_gpu_exchange_matches_single_gpu(kb, cuda, tmp_path):
+@pytest.mark.parametrize("fused", [False, True], ids=["push", "fused"])
+def test_two_gpu_exchange_matches_single_gpu(kb, cuda, tmp_path, fused):
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     port = _free_port()
-    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path), fused), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         res = np.load(tmp_path / f"r{r}.npy")
         errs, code = res[:-1], res[-1]
