@@ -36,6 +36,7 @@ typedef enum kb_status {
 enum {
     KB_TYPE_F32 = 0,
     KB_TYPE_F16 = 1,
+    KB_TYPE_Q4_0 = 2, /* blocks of 32: f16 scale d then 16 bytes of 4-bit values (ggml-common.h block_q4_0) */
     KB_TYPE_Q8_0 = 8, /* blocks of 32: f16 scale d then 32 int8 (ggml-common.h block_q8_0) */
     KB_TYPE_I32 = 26,
     KB_TYPE_I64 = 27,
@@ -246,7 +247,7 @@ kb_status kb_flash_attn_ext_gated(const kb_tensor* q, const kb_tensor* k, const 
  *   kcur, vcur  f32 [hd nkv, n]            pos  i32 [4 n] (section-major: t..., h..., w..., extra...)
  *   kv_idx i64 [n] (cache cell of each token)              q_norm, k_norm  f32 [hd]
  *   q_out  f32 [hd, nh, n] contiguous      gate_out  f32 [hd nh, n] contiguous
- *   k_cache, v_cache  f16 or q8_0 [hd nkv, n_cells] (klein's cache rows)
+ *   k_cache, v_cache  f16, q8_0 or q4_0 [hd nkv, n_cells] (klein's cache rows)
  * hd is 64, 128 or 256; rope->n_rot a multiple of 64, at most hd. A kv_idx outside [0, n_cells) skips that row
  * and sets the device error word.
  */

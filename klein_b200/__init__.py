@@ -17,9 +17,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libklein_b200.so")
 
 # element types (numbered as enum ggml_type)
-F32, F16, Q8_0, I32, I64, BF16 = 0, 1, 8, 26, 27, 30
+F32, F16, Q4_0, Q8_0, I32, I64, BF16 = 0, 1, 2, 8, 26, 27, 30
 TYPE_SIZE = {F32: 4, F16: 2, I32: 4, I64: 8, BF16: 2}
 Q8_0_BLOCK_BYTES = 34
+Q4_0_BLOCK_BYTES = 18
+BLOCK_BYTES = {Q8_0: Q8_0_BLOCK_BYTES, Q4_0: Q4_0_BLOCK_BYTES}
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # KB_NOALLOC_SCRATCH_BYTES
 
@@ -191,9 +193,9 @@ def kv_cache_view(cache, kv_type: int, n_head_kv: int, head_dim: int, n_kv: int 
     ggml tensor [head_dim, n_kv, n_head_kv] with nb1 = row bytes, nb2 = one head's bytes."""
     rows = cache.shape[0] if n_kv is None else n_kv
     row_bytes = cache.stride(0) * cache.element_size()
-    if kv_type == Q8_0:
-        head_bytes = head_dim // 32 * Q8_0_BLOCK_BYTES
-        es = Q8_0_BLOCK_BYTES  # nb0 of a q8_0 tensor is the block size
+    if kv_type in BLOCK_BYTES:
+        head_bytes = head_dim // 32 * BLOCK_BYTES[kv_type]
+        es = BLOCK_BYTES[kv_type]  # nb0 of a block-quantised tensor is the block size
     else:
         es = TYPE_SIZE[kv_type]
         head_bytes = head_dim * es
@@ -420,9 +422,10 @@ def gdn_gated_norm(x, z, w, rms_eps: float, stream=None):
 def cache_rows(cache, kv_type: int) -> KbTensor:
     """kb_tensor of a whole cache as ggml's 2-d rows tensor [row elements, n_cells] (the set_rows destination)."""
     row_bytes = cache.stride(0) * cache.element_size()
-    if kv_type == Q8_0:
-        return kb_tensor(cache.data_ptr(), kv_type, [row_bytes // Q8_0_BLOCK_BYTES * 32, cache.shape[0], 1, 1],
-                         [Q8_0_BLOCK_BYTES, row_bytes, row_bytes * cache.shape[0], row_bytes * cache.shape[0]])
+    if kv_type in BLOCK_BYTES:
+        bb = BLOCK_BYTES[kv_type]
+        return kb_tensor(cache.data_ptr(), kv_type, [row_bytes // bb * 32, cache.shape[0], 1, 1],
+                         [bb, row_bytes, row_bytes * cache.shape[0], row_bytes * cache.shape[0]])
     es = TYPE_SIZE[kv_type]
     return kb_tensor(cache.data_ptr(), kv_type, [row_bytes // es, cache.shape[0], 1, 1],
                      [es, row_bytes, row_bytes * cache.shape[0], row_bytes * cache.shape[0]])

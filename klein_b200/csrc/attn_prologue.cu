@@ -8,7 +8,8 @@
 //              component its sector selects times theta_scale^i (the same running f32 product), no YaRN ramp
 //   gate     = ggml_cont of the gate half
 //   caches   = ggml_set_rows of the normed, roped K rows and the V rows at kv_idx, f32 -> f16 (round to
-//              nearest) or q8_0 (per 32 values: d = amax / 127, q = roundf(x / d), as kb_set_rows)
+//              nearest), q8_0 (per 32 values: d = amax / 127, q = roundf(x / d)) or q4_0 (quantize_row_q4_0_ref),
+//              as kb_set_rows
 //
 // Layout: one warp per (token, row), rows = the nh query heads, then the nkv K heads, then the nkv V heads.
 // Lane l holds dims l, l + 32, ..., so a 32-dim q8_0 block is one register across the warp and a rope pair
@@ -108,6 +109,10 @@ __global__ void __launch_bounds__(256) attn_prologue_kernel(const PrologueParams
         __half* d = reinterpret_cast<__half*>(row) + (int64_t) kh * HD;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) d[lane + 32 * k] = __float2half_rn(x[k]);
+    } else if (p.cache_type == 2) {  // q4_0: block k of this head = lanes 0-31 of register k
+        unsigned char* hb = reinterpret_cast<unsigned char*>(row) + (int64_t) kh * (HD / 32) * 18;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) store_block_q4_0(x[k], lane, hb + k * 18);
     } else {  // q8_0: block k of this head = lanes 0-31 of register k
         char* hb = row + (int64_t) kh * (HD / 32) * 34;
 #pragma unroll

@@ -30,6 +30,7 @@ constexpr int TILE = FA_TILE;
 constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 cells][64 dims] f16, 128B-swizzled
 constexpr int QROW = D / 32 * 34;              // bytes of one head's row in a q8_0 cache (272)
 constexpr int QTILE_RAW = TILE * QROW;         // 17,408 B of raw blocks per tile
+constexpr int Q4ROW = D / 32 * 18;             // bytes of one head's row in a q4_0 cache (144)
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {
     if (p.max_bias <= 0.0f) return 1.0f;
@@ -286,7 +287,12 @@ constexpr int KRAW = 4, VRAW = 3;
 // and pass it at once (a parity wait sees only the last two phases).
 static_assert(KRAW % 2 == 0, "K ring slots carry tiles of one parity");
 // warp roles: q8_0 adds the 8 dequantisation warps (4-11)
-template <bool Q8>
+// cache kinds of the kernel
+constexpr int KT_F16 = 0, KT_Q8 = 1, KT_Q4 = 2;
+template <int KT>
+constexpr int raw_row() { return KT == KT_Q8 ? QROW : Q4ROW; }
+
+template <bool Q8>  // Q8: a block-quantised cache (q8_0 or q4_0), with dequantisation warps
 struct Roles {
     static constexpr int KDQ = 4, VDQ = 8;
     static constexpr int KTMA = Q8 ? 12 : 4, VTMA = Q8 ? 13 : 5, SMMA = Q8 ? 14 : 6, PVMMA = Q8 ? 15 : 7;
@@ -296,14 +302,15 @@ struct Roles {
 constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
 constexpr float THRESH = 8.0f;  // log2 units
 
-template <int N, bool Q8>
+template <int N, int KT>
 struct Smem {
+    static constexpr int RAWT = TILE * raw_row<KT>();  // bytes of one raw tile (q8_0, q4_0)
     uint8_t v[2][KTILE_F16];        // f16 V tiles [4 dim chunks][64 cells][128 B], 128B-swizzled
     uint8_t q[D / 64][N * 128];     // Q f16, K-major swizzled: the B operand of S^T
     uint8_t p[2][2][N * 128];       // P^T [buffer][64-cell half][N rows][128 B]: the B operand of O^T
-    // q8_0: the raw K ring (272 B per cell); f16: two K blocks [4 dim chunks][128 cells][128 B], the A operand of S^T
-    uint8_t kbuf[Q8 ? KRAW * QTILE_RAW : 2 * 2 * KTILE_F16];
-    uint8_t vraw[Q8 ? VRAW * QTILE_RAW : 16];  // q8_0: the raw V ring
+    // quantised: the raw K ring; f16: two K blocks [4 dim chunks][128 cells][128 B], the A operand of S^T
+    uint8_t kbuf[KT != KT_F16 ? KRAW * RAWT : 2 * 2 * KTILE_F16];
+    uint8_t vraw[KT != KT_F16 ? VRAW * RAWT : 16];  // quantised: the raw V ring
     float red[4][N];                // per-warp row maxima / sums
     float mrow[N];                  // running row maxima (log2 units), shared by all cells
     float nref[N];                  // -(row max) per row: +inf while the row has seen nothing, -inf past the rows
@@ -316,7 +323,8 @@ struct Smem {
     int failed;
 };
 
-static_assert(sizeof(Smem<32, true>) <= 232448 && sizeof(Smem<32, false>) <= 232448, "fits one SM's shared memory");
+static_assert(sizeof(Smem<32, KT_Q8>) <= 232448 && sizeof(Smem<32, KT_Q4>) <= 232448 && sizeof(Smem<32, KT_F16>) <= 232448,
+              "fits one SM's shared memory");
 
 __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaStreamParams& p, volatile int* failed,
                                              int code) {
@@ -374,6 +382,28 @@ __device__ __forceinline__ void q4_to_f16(uint32_t qw, __half2 d2, uint32_t& lo,
     hi = *reinterpret_cast<uint32_t*>(&h2);
 }
 
+// 4 q4_0 bytes -> the f16 pairs of their low nibbles (values j .. j + 3 of the block) and of their high nibbles
+// (values 16 + j .. 19 + j), (n - 8) * d ((n | 0x6400) is 1024 + n exactly; minus 1032)
+__device__ __forceinline__ void n4_to_f16(uint32_t qw, __half2 d2, uint32_t& lo0, uint32_t& lo1, uint32_t& hi0,
+                                          uint32_t& hi1) {
+    const __half2 bias = __floats2half2_rn(1032.0f, 1032.0f);
+    const uint32_t lo = qw & 0x0F0F0F0Fu, hi = (qw >> 4) & 0x0F0F0F0Fu;
+    uint32_t a = __byte_perm(lo, 0x64646464u, 0x4140), b = __byte_perm(lo, 0x64646464u, 0x4342);
+    uint32_t c = __byte_perm(hi, 0x64646464u, 0x4140), e = __byte_perm(hi, 0x64646464u, 0x4342);
+    __half2 ra = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&a), bias), d2);
+    __half2 rb = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&b), bias), d2);
+    __half2 rc = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&c), bias), d2);
+    __half2 re = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&e), bias), d2);
+    lo0 = *reinterpret_cast<uint32_t*>(&ra);
+    lo1 = *reinterpret_cast<uint32_t*>(&rb);
+    hi0 = *reinterpret_cast<uint32_t*>(&rc);
+    hi1 = *reinterpret_cast<uint32_t*>(&re);
+}
+
+// q4_0 V dequantisation slots: 2 sets of 4 blocks whose first nibble words are 0, 1, 2, 3 (mod 4) ({0, 1, 3, 5},
+// {7, 2, 4, 6}), 3 bits each
+constexpr uint32_t V4SLOTS = 0u | (1u << 3) | (3u << 6) | (5u << 9) | (7u << 12) | (2u << 15) | (4u << 18) | (6u << 21);
+
 // V dequantisation slots: slot set ss (0-3) x slot (0-3) -> 2 * block + half, 4 bits each. In every set the
 // first quant words of the 4 slots are 0, 1, 2, 3 (mod 4), so 8 consecutive cells x 4 slots hit 32 distinct banks:
 //   {(0,0) (1,0) (3,0) (5,0)}  {(0,1) (1,1) (3,1) (5,1)}  {(7,0) (2,0) (4,0) (6,0)}  {(7,1) (2,1) (4,1) (6,1)}
@@ -381,10 +411,12 @@ constexpr uint64_t VSLOTS = 0x0ULL | (0ULL << 0) | (2ULL << 4) | (6ULL << 8) | (
                             (7ULL << 24) | (11ULL << 28) | (14ULL << 32) | (4ULL << 36) | (8ULL << 40) | (12ULL << 44) |
                             (15ULL << 48) | (5ULL << 52) | (9ULL << 56) | (13ULL << 60);
 
-template <int N, bool Q8>
-__global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
+template <int N, int KT>
+__global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
     fa_stream_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const FaStreamParams p) {
+    constexpr bool Q8 = KT != KT_F16;  // a block-quantised cache: raw rings and dequantisation warps
+    constexpr int RAWROW = raw_row<KT>(), RAWT = TILE * RAWROW;
     using R_ = Roles<Q8>;
     constexpr int THREADS = R_::THREADS;
     constexpr int W_KDQ = R_::KDQ, W_VDQ = R_::VDQ, W_KTMA = R_::KTMA, W_VTMA = R_::VTMA, W_SMMA = R_::SMMA,
@@ -394,7 +426,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
         if (threadIdx.x == 0) record_error(p.err, DEV_ERR_ALIGN);
         return;
     }
-    Smem<N, Q8>& sm = *reinterpret_cast<Smem<N, Q8>*>(smem_raw);
+    Smem<N, KT>& sm = *reinterpret_cast<Smem<N, KT>*>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, hk = blockIdx.y;
     const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
@@ -487,9 +519,9 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
                     const int s = t % depth;
                     uint64_t* empty = is_v ? &sm.vempty[s] : &sm.kempty[s];
                     uint64_t* fullb = is_v ? &sm.vfull[s] : &sm.kfull[s];
-                    uint8_t* dst = (is_v ? sm.vraw : sm.kbuf) + s * QTILE_RAW;
+                    uint8_t* dst = (is_v ? sm.vraw : sm.kbuf) + s * RAWT;
                     if (t >= depth && !wait_or_fail(empty, ((t / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
-                    mbar_arrive_expect_tx(fullb, QTILE_RAW);
+                    mbar_arrive_expect_tx(fullb, RAWT);
                     tma_load_4d(dst, map, fullb, 0, hk, (int) (key_begin + (int64_t) t * TILE), kb3, pol);
                 }
             } else if (!is_v) {
@@ -591,8 +623,37 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
                 ok = wait_or_fail(&sm.kfull[t % KRAW], (t / KRAW) & 1, p, failed, DEV_ERR_WAIT_FULL);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
-                const uint4* row = reinterpret_cast<const uint4*>(sm.kbuf + (t % KRAW) * QTILE_RAW + cell * QROW);
+                const uint4* row = reinterpret_cast<const uint4*>(sm.kbuf + (t % KRAW) * RAWT + cell * RAWROW);
                 tc_fence_after();
+                if constexpr (KT == KT_Q4) {
+                    // the 144-byte row by 9 aligned 16-byte loads; block b at byte 18 b (scale, then 16 bytes of
+                    // nibbles: low nibbles values 0-15, high nibbles 16-31)
+                    uint32_t w[36];
+#pragma unroll
+                    for (int b4 = 0; b4 < 8; ++b4) {
+                        // two halves of registers: words 0-19 for blocks 0-3 (bytes 0-71), 16-35 for blocks 4-7
+                        if (b4 == 0 || b4 == 4) {
+#pragma unroll
+                            for (int u = (b4 == 0 ? 0 : 4); u < (b4 == 0 ? 5 : 9); ++u) {
+                                const uint4 x = row[u];
+                                w[4 * u] = x.x, w[4 * u + 1] = x.y, w[4 * u + 2] = x.z, w[4 * u + 3] = x.w;
+                            }
+                        }
+                        const uint32_t sw = w[(18 * b4) / 4];
+                        const uint16_t dbits = (18 * b4) % 4 == 0 ? (uint16_t) (sw & 0xffffu) : (uint16_t) (sw >> 16);
+                        const __half dh = __ushort_as_half(dbits);
+                        const __half2 d2 = __halves2half2(dh, dh);
+                        uint32_t out[16];
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            const int byte = 18 * b4 + 2 + 4 * g;
+                            const uint32_t qw =
+                                byte % 4 == 0 ? w[byte / 4] : __funnelshift_r(w[byte / 4], w[byte / 4 + 1], 16);
+                            n4_to_f16(qw, d2, out[2 * g], out[2 * g + 1], out[8 + 2 * g], out[8 + 2 * g + 1]);
+                        }
+                        tmem_st16(lane_base + TM_K + (j & 1) * 128 + 16 * b4, out);
+                    }
+                } else {
                 // two halves of the row, one loop body: bytes [128 hb, 128 hb + 144) by 9 aligned 16-byte loads;
                 // the half's 4 blocks start at byte 8 hb of that window, so the second half is shifted 2 words
 #pragma unroll 1
@@ -622,6 +683,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
                         tmem_st16(lane_base + TM_K + (j & 1) * 128 + 16 * (4 * hb + bl), out);
                     }
                 }
+                }
                 tmem_wait_st();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.kempty[t % KRAW]);
@@ -642,8 +704,49 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
             ok = ok && (t < 2 || wait_or_fail(&sm.v_free[t & 1], ((t >> 1) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY));
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            const uint8_t* raw = sm.vraw + (t % VRAW) * QTILE_RAW;
+            const uint8_t* raw = sm.vraw + (t % VRAW) * RAWT;
             uint8_t* dst = sm.v[t & 1];
+            if constexpr (KT == KT_Q4) {
+                // 4 rounds of 8 consecutive cells x 4 whole blocks per warp (16 rounds per tile over the 4 warps);
+                // round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, block set m / 2 (first nibble words 0-3 mod 4);
+                // two rounds at a time, their loads first
+#pragma unroll 1
+                for (int m0 = 0; m0 < 4; m0 += 2) {
+                    uint32_t W[2][5];
+                    __half dh[2];
+                    const int blk = (int) ((V4SLOTS >> (3 * (4 * (m0 >> 1) + slot))) & 7);
+                    const int qb = 18 * blk + 2, sh = (qb & 3) * 8;
+#pragma unroll
+                    for (int mm = 0; mm < 2; ++mm) {
+                        const uint8_t* rowp = raw + (8 * (i + 4 * mm) + ci) * RAWROW;
+                        const uint32_t* w32 = reinterpret_cast<const uint32_t*>(rowp + (qb & ~3));
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) W[mm][k] = w32[k];
+                        W[mm][4] = sh ? w32[4] : 0u;
+                        dh[mm] = *reinterpret_cast<const __half*>(rowp + 18 * blk);
+                    }
+#pragma unroll
+                    for (int mm = 0; mm < 2; ++mm) {
+                        const int r = 8 * (i + 4 * mm) + ci;
+                        const __half2 d2 = __halves2half2(dh[mm], dh[mm]);
+                        uint32_t lo[8], hi[8];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            n4_to_f16(__funnelshift_r(W[mm][k], W[mm][k + 1], sh), d2, lo[2 * k], lo[2 * k + 1],
+                                      hi[2 * k], hi[2 * k + 1]);
+                        // values 0-15 at dims 32 blk .. + 15 (units u0, u0 + 1), 16-31 at units u0 + 2, u0 + 3
+                        const int u0 = ((32 * blk) & 63) >> 3;
+                        uint8_t* rowd = dst + ((32 * blk) >> 6) * (TILE * 128) + r * 128;
+                        *reinterpret_cast<uint4*>(rowd + ((u0 ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4*>(rowd + (((u0 + 1) ^ (r & 7)) << 4)) =
+                            make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                        *reinterpret_cast<uint4*>(rowd + (((u0 + 2) ^ (r & 7)) << 4)) =
+                            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(rowd + (((u0 + 3) ^ (r & 7)) << 4)) =
+                            make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    }
+                }
+            } else {
             // all 8 rounds' loads first, then the conversions and stores (shared loads are not moved past
             // shared stores). Round i + 4m: cells 8 (i + 4 (m % 2)) .. +7, slot set m / 2.
 #pragma unroll 1
@@ -654,7 +757,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
             for (int mm = 0; mm < 4; ++mm) {
                 const int r = 8 * (i + 4 * (mm & 1)) + ci;
                 const int bh = m0 ? bh_of[2 + (mm >> 1)] : bh_of[mm >> 1], blk = bh >> 1, hf = bh & 1;
-                const uint8_t* rowp = raw + r * QROW;
+                const uint8_t* rowp = raw + r * RAWROW;
                 const int qb = 34 * blk + 2 + 16 * hf;  // first quant byte
                 const uint32_t* w32 = reinterpret_cast<const uint32_t*>(rowp + (qb & ~3));
 #pragma unroll
@@ -677,6 +780,7 @@ __global__ void __launch_bounds__(Roles<Q8>::THREADS, 1)
                 *reinterpret_cast<uint4*>(d0) = make_uint4(o8[0], o8[1], o8[2], o8[3]);
                 // unit u0 + 1 (u0 even): the swizzled address XOR 16
                 *reinterpret_cast<uint4*>(reinterpret_cast<uintptr_t>(d0) ^ 16) = make_uint4(o8[4], o8[5], o8[6], o8[7]);
+            }
             }
             }
             fence_proxy_async_smem();
@@ -904,15 +1008,15 @@ cudaError_t set_smem_once(Kern kern, size_t smem, bool (&done)[64]) {
     return e;
 }
 
-template <int N, bool Q8>
+template <int N, int KT>
 cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t stream) {
     static bool attr_done[64] = {};
-    auto kern = tc::fa_stream_tc_kernel<N, Q8>;
-    const size_t smem = sizeof(tc::Smem<N, Q8>);
+    auto kern = tc::fa_stream_tc_kernel<N, KT>;
+    const size_t smem = sizeof(tc::Smem<N, KT>);
     cudaError_t e = set_smem_once(kern, smem, attr_done);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
-    kern<<<grid, tc::Roles<Q8>::THREADS, smem, stream>>>(tmK, tmV, p);
+    kern<<<grid, tc::Roles<KT != tc::KT_F16>::THREADS, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || (p.n_splits == 1 && !p.push)) return e;
     dim3 cgrid(p.R, p.n_head_kv, p.ne3);
@@ -924,13 +1028,17 @@ cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUt
 
 cudaError_t launch_fa_stream_tc(const FaStreamParams& p, int rpc, int kv_type, const CUtensorMap& tmK,
                                 const CUtensorMap& tmV, cudaStream_t stream) {
-    if (kv_type == 8) return rpc <= 16 ? launch_tc<16, true>(p, tmK, tmV, stream) : launch_tc<32, true>(p, tmK, tmV, stream);
-    return rpc <= 16 ? launch_tc<16, false>(p, tmK, tmV, stream) : launch_tc<32, false>(p, tmK, tmV, stream);
+    using namespace tc;
+    if (kv_type == 8) return rpc <= 16 ? launch_tc<16, KT_Q8>(p, tmK, tmV, stream) : launch_tc<32, KT_Q8>(p, tmK, tmV, stream);
+    if (kv_type == 2) return rpc <= 16 ? launch_tc<16, KT_Q4>(p, tmK, tmV, stream) : launch_tc<32, KT_Q4>(p, tmK, tmV, stream);
+    return rpc <= 16 ? launch_tc<16, KT_F16>(p, tmK, tmV, stream) : launch_tc<32, KT_F16>(p, tmK, tmV, stream);
 }
 
 size_t fa_stream_tc_smem_bytes(int rpc, int kv_type) {
-    if (kv_type == 8) return rpc <= 16 ? sizeof(tc::Smem<16, true>) : sizeof(tc::Smem<32, true>);
-    return rpc <= 16 ? sizeof(tc::Smem<16, false>) : sizeof(tc::Smem<32, false>);
+    using namespace tc;
+    if (kv_type == 8) return rpc <= 16 ? sizeof(Smem<16, KT_Q8>) : sizeof(Smem<32, KT_Q8>);
+    if (kv_type == 2) return rpc <= 16 ? sizeof(Smem<16, KT_Q4>) : sizeof(Smem<32, KT_Q4>);
+    return rpc <= 16 ? sizeof(Smem<16, KT_F16>) : sizeof(Smem<32, KT_F16>);
 }
 
 cudaError_t launch_lse_combine(const float* o_parts, const float* ml_parts, int64_t stride, int n_parts, int64_t rows, int Dd,

@@ -75,7 +75,8 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     if (!q || !k || !v) return KB_ERR_ARG;
     if (q->type != KB_TYPE_F32) return KB_ERR_UNSUPPORTED;
     if (k->type != v->type) return KB_ERR_UNSUPPORTED;
-    if (k->type != KB_TYPE_F16 && k->type != KB_TYPE_Q8_0 && k->type != KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;
+    if (k->type != KB_TYPE_F16 && k->type != KB_TYPE_Q8_0 && k->type != KB_TYPE_Q4_0 && k->type != KB_TYPE_BF16)
+        return KB_ERR_UNSUPPORTED;
     s->D = (int) q->ne[0];
     s->n_q = (int) q->ne[1];
     s->H = (int) q->ne[2];
@@ -88,7 +89,8 @@ kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, c
     if (v->ne[1] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return KB_ERR_BAD_SHAPE;
     if (s->H_kv <= 0 || s->H % s->H_kv != 0 || s->ne3k <= 0 || s->ne3 % s->ne3k != 0) return KB_ERR_BAD_SHAPE;
     if (s->n_q <= 0 || s->H <= 0 || s->ne3 <= 0 || s->n_kv < 0) return KB_ERR_BAD_SHAPE;
-    const size_t kv_es = k->type == KB_TYPE_Q8_0 ? 34 : 2;  // nb[0]: element size, or block size for q8_0
+    // nb[0]: element size, or the block size of a block-quantised type
+    const size_t kv_es = k->type == KB_TYPE_Q8_0 ? 34 : k->type == KB_TYPE_Q4_0 ? 18 : 2;
     s->kv_type = k->type;
     if (q->nb[0] != 4 || k->nb[0] != kv_es || v->nb[0] != kv_es) return KB_ERR_BAD_SHAPE;
     if (s->D != kb::FA_D) return KB_ERR_UNSUPPORTED;
@@ -140,10 +142,10 @@ FaPlan plan_fa(const FaShape& s, bool push = false) {
 kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return KB_ERR_CUDA;
-    if (t->type == KB_TYPE_Q8_0) {
-        // raw blocks: one head's row is ne0/32 blocks of 34 bytes, read as 32-bit words without swizzle;
-        // dims: words of a head row, KV head, cell, batch; box = a whole head row x 64 cells
-        const cuuint64_t words = (cuuint64_t) t->ne[0] / 32 * 34 / 4;
+    if (t->type == KB_TYPE_Q8_0 || t->type == KB_TYPE_Q4_0) {
+        // raw blocks: one head's row is ne0/32 blocks of 34 (q8_0) or 18 (q4_0) bytes, read as 32-bit words without
+        // swizzle; dims: words of a head row, KV head, cell, batch; box = a whole head row x 64 cells
+        const cuuint64_t words = (cuuint64_t) t->ne[0] / 32 * (t->type == KB_TYPE_Q8_0 ? 34 : 18) / 4;
         const cuuint64_t dims[4] = {words, (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[3]};
         const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
         const cuuint32_t box[4] = {(cuuint32_t) words, 1, (cuuint32_t) kb::FA_TILE, 1};
@@ -698,13 +700,15 @@ kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tenso
     if (!rows_f32(src)) return KB_ERR_UNSUPPORTED;
     if (idx->type != KB_TYPE_I64 && idx->type != KB_TYPE_I32) return KB_ERR_UNSUPPORTED;
     const int t = dst->type;
-    if (t != KB_TYPE_F32 && t != KB_TYPE_F16 && t != KB_TYPE_BF16 && t != KB_TYPE_Q8_0) return KB_ERR_UNSUPPORTED;
+    if (t != KB_TYPE_F32 && t != KB_TYPE_F16 && t != KB_TYPE_BF16 && t != KB_TYPE_Q8_0 && t != KB_TYPE_Q4_0)
+        return KB_ERR_UNSUPPORTED;
     const int64_t ne0 = src->ne[0];
-    if (dst->ne[0] != ne0 || ne0 % 32 != 0) return t == KB_TYPE_Q8_0 || dst->ne[0] != ne0 ? KB_ERR_BAD_SHAPE : KB_ERR_UNSUPPORTED;
+    const bool quant = t == KB_TYPE_Q8_0 || t == KB_TYPE_Q4_0;
+    if (dst->ne[0] != ne0 || ne0 % 32 != 0) return quant || dst->ne[0] != ne0 ? KB_ERR_BAD_SHAPE : KB_ERR_UNSUPPORTED;
     if (dst->ne[2] != src->ne[2] || dst->ne[3] != src->ne[3] || idx->ne[0] != src->ne[1]) return KB_ERR_BAD_SHAPE;
     if (idx->ne[1] <= 0 || idx->ne[2] <= 0 || src->ne[2] % idx->ne[1] != 0 || src->ne[3] % idx->ne[2] != 0)
         return KB_ERR_BAD_SHAPE;
-    const size_t es = t == KB_TYPE_F32 ? 4 : t == KB_TYPE_Q8_0 ? 34 : 2;
+    const size_t es = t == KB_TYPE_F32 ? 4 : t == KB_TYPE_Q8_0 ? 34 : t == KB_TYPE_Q4_0 ? 18 : 2;
     if (dst->nb[0] != es) return KB_ERR_BAD_SHAPE;
     kb::SetRowsParams p{};
     p.src = static_cast<const char*>(src->data);
@@ -743,9 +747,10 @@ kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const 
     if (q_out->ne[0] != hd || q_out->ne[1] != nh || q_out->ne[2] != n || gate_out->ne[0] != hd * nh || gate_out->ne[1] != n)
         return KB_ERR_BAD_SHAPE;
     const int ct = k_cache->type;
-    if ((ct != KB_TYPE_F16 && ct != KB_TYPE_Q8_0) || v_cache->type != ct) return KB_ERR_UNSUPPORTED;
+    if ((ct != KB_TYPE_F16 && ct != KB_TYPE_Q8_0 && ct != KB_TYPE_Q4_0) || v_cache->type != ct) return KB_ERR_UNSUPPORTED;
     if (k_cache->ne[0] != hd * nkv || v_cache->ne[0] != hd * nkv || v_cache->ne[1] != k_cache->ne[1]) return KB_ERR_BAD_SHAPE;
-    if (k_cache->nb[0] != (ct == KB_TYPE_F16 ? 2u : 34u) || v_cache->nb[0] != k_cache->nb[0]) return KB_ERR_BAD_SHAPE;
+    if (k_cache->nb[0] != (ct == KB_TYPE_F16 ? 2u : ct == KB_TYPE_Q8_0 ? 34u : 18u) || v_cache->nb[0] != k_cache->nb[0])
+        return KB_ERR_BAD_SHAPE;
     if (rope->n_rot <= 0 || rope->n_rot % 64 != 0 || rope->n_rot > hd) return KB_ERR_UNSUPPORTED;
     if (rope->mode != 40 && rope->mode != 8) return KB_ERR_UNSUPPORTED;
     const int sect = rope->sections[0] + rope->sections[1] + rope->sections[2] + rope->sections[3];

@@ -110,6 +110,27 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 
 // ---------------------------------------------------------------------------------------------- arithmetic
 
+// q4_0 block of 32 values held one per lane (lane j = value j): quantize_row_q4_0_ref (ggml-quants.c:113-148):
+// the value of largest magnitude (the first one on ties) m, d = m / -8, q_j = min(15, (int8)(x_j / d + 8.5)),
+// byte j < 16 = q_j | q_{j+16} << 4. Lanes 0-15 store their byte, lane 0 the f16 d.
+__device__ __forceinline__ void store_block_q4_0(float x, int lane, unsigned char* blk) {
+    float am = fabsf(x);
+    int who = lane;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, am, off);
+        const int ow = __shfl_xor_sync(0xffffffffu, who, off);
+        if (oa > am || (oa == am && ow < who)) am = oa, who = ow;
+    }
+    const float mx = __shfl_sync(0xffffffffu, x, who);
+    const float d = mx / -8.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    const int qi = min(15, (int) (signed char) (x * id + 8.5f));
+    const int hi = __shfl_down_sync(0xffffffffu, qi, 16);
+    if (lane < 16) blk[2 + lane] = (unsigned char) (qi | (hi << 4));
+    if (lane == 0) *reinterpret_cast<__half*>(blk) = __float2half_rn(d);
+}
+
 // packed f32x2 arithmetic: two floats in a 64-bit register pair per instruction
 __device__ __forceinline__ uint64_t f2pack(float a, float b) {
     uint64_t r;

@@ -4,7 +4,7 @@
 // K and V rows of every pass into its cache with it (graph.cpp:111-112). f32 rows are converted to the
 // cache type: f16/bf16 round to nearest even; q8_0 follows quantize_row_q8_0_ref (ggml-quants.c:276-299):
 // per 32 elements d = amax / 127, id = d ? 1/d : 0, q = roundf(x * id), d stored as f16 — the same rule
-// ggml-cuda's set_rows applies (cpy-utils.cuh:137-154), bit for bit.
+// ggml-cuda's set_rows applies (cpy-utils.cuh:137-154), bit for bit; q4_0 follows quantize_row_q4_0_ref.
 //
 // rollback: State::rollback_recurrent (state.cpp:162-183) — after s rejected draft tokens every DeltaNet
 // layer's conv slot s becomes slot 0 (byte copy) and snapshot row s-1 becomes the f32 state (exact
@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(256) set_rows_kernel(const SetRowsParams p) {
         case 0: reinterpret_cast<float*>(drow)[blk * 32 + lane] = x; break;
         case 1: reinterpret_cast<__half*>(drow)[blk * 32 + lane] = __float2half_rn(x); break;
         case 30: reinterpret_cast<__nv_bfloat16*>(drow)[blk * 32 + lane] = __float2bfloat16_rn(x); break;
+        case 2: store_block_q4_0(x, lane, reinterpret_cast<unsigned char*>(drow) + blk * 18); break;
         default: {  // q8_0
             float amax = fabsf(x);
 #pragma unroll

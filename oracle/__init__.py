@@ -22,7 +22,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, "_ref")
 
-GGML_F32, GGML_F16, GGML_Q8_0, GGML_I64, GGML_BF16 = 0, 1, 8, 27, 30
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_I64, GGML_BF16 = 0, 1, 2, 8, 27, 30
 Q8_0_BLOCK = 34
 
 
@@ -121,6 +121,23 @@ def rs_dequantize_q8_0(y: np.ndarray) -> np.ndarray:
     nb = y.shape[-1] // Q8_0_BLOCK
     out = np.empty(y.shape[:-1] + (nb * 32,), dtype=np.float32)
     restate().rs_dequantize_row_q8_0(_ptr(y), _ptr(out), c_int64(out.size))
+    return out
+
+
+def rs_quantize_q4_0(x: np.ndarray) -> np.ndarray:
+    """f32 [..., n] (n % 32 == 0) -> uint8 [..., n/32*18] in ggml's block_q4_0 layout."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.shape[-1]
+    out = np.empty(x.shape[:-1] + (n // 32 * 18,), dtype=np.uint8)
+    restate().rs_quantize_row_q4_0(_ptr(x), _ptr(out), c_int64(x.size))
+    return out
+
+
+def rs_dequantize_q4_0(y: np.ndarray) -> np.ndarray:
+    y = np.ascontiguousarray(y, dtype=np.uint8)
+    nb = y.shape[-1] // 18
+    out = np.empty(y.shape[:-1] + (nb * 32,), dtype=np.float32)
+    restate().rs_dequantize_row_q4_0(_ptr(y), _ptr(out), c_int64(out.size))
     return out
 
 
@@ -344,6 +361,9 @@ def make_fa_inputs(seed: int, n_q: int, n_kv: int, H=24, H_kv=4, D=256, kv_type=
     elif kv_type == GGML_Q8_0:
         kc, vc = rs_quantize_q8_0(kf), rs_quantize_q8_0(vf)
         kd, vd = rs_dequantize_q8_0(kc), rs_dequantize_q8_0(vc)
+    elif kv_type == GGML_Q4_0:
+        kc, vc = rs_quantize_q4_0(kf), rs_quantize_q4_0(vf)
+        kd, vd = rs_dequantize_q4_0(kc), rs_dequantize_q4_0(vc)
     elif kv_type == GGML_BF16:
         kc, vc = f32_to_bf16_bits(kf), f32_to_bf16_bits(vf)
         kd, vd = bf16_bits_to_f32(kc).reshape(kf.shape), bf16_bits_to_f32(vc).reshape(vf.shape)

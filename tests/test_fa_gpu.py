@@ -43,7 +43,7 @@ def run_gpu(kb, cuda, q, kc, vc, H_kv, scale=1.0 / 16, mask=None, **kw):
     qt = torch.from_numpy(q).to(cuda)
     kt = torch.from_numpy(kc).to(cuda)
     vt = torch.from_numpy(vc).to(cuda)
-    kv_type = kb.F16 if kc.dtype == np.float16 else kb.Q8_0
+    kv_type = kb.F16 if kc.dtype == np.float16 else kb.Q8_0 if kc.shape[-1] % 34 == 0 and kc.shape[-1] % 18 != 0 else kb.Q4_0
     kview = kb.kv_cache_view(kt, kv_type, H_kv, D)
     vview = kb.kv_cache_view(vt, kv_type, H_kv, D)
     mt = None if mask is None else torch.from_numpy(mask.astype(np.float16)).to(cuda)
@@ -243,6 +243,39 @@ def test_q8_0_long_verify_262144(kb, cuda):
     """config[3] shape (q8_0): 4 tokens, causal among the last 4, 262,144 cells."""
     n_q, n_kv = 4, 262144
     q, kc, vc, kd, vd = O.make_fa_inputs(4711, n_q, n_kv, kv_type=O.GGML_Q8_0)
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q)
+    check_attention(gpu, exact_np(O.q_round_q8_0(q), kd, vd, mask))
+
+
+# ---------------------------------------------------------------------------------------------- q4_0 cache
+# klein's cache type beyond 131K cells; ggml's vec_dot type for q4_0 K is q8_0, so Q is rounded as for q8_0
+
+@pytest.mark.parametrize("n_q,n_kv", [(1, 4096), (4, 4096), (4, 65), (3, 777)])
+def test_q4_0_causal_analytic(kb, cuda, n_q, n_kv):
+    q, kc, vc, kd, vd = O.make_fa_inputs(3000 + n_q * 7 + n_kv, n_q, n_kv, kv_type=O.GGML_Q4_0)
+    pos0 = n_kv - n_q
+    mask = O.rs_visible_mask(n_q, n_kv, pos0)
+    gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0)
+    exact = exact_np(O.q_round_q8_0(q), kd, vd, mask)
+    ggml = O.ref_flash_attn_ext(q, kc, vc, O.GGML_Q4_0, 4, mask=mask.astype(np.float16), n_threads=4, use_ref=False) \
+        if O.ref_available() else None
+    check_attention(gpu, exact, ggml)
+
+
+def test_q4_0_dense_mask_and_ring(kb, cuda):
+    ring, n_q, pos0 = 2048, 4, 9000
+    q, kc, vc, kd, vd = O.make_fa_inputs(37, n_q, ring, kv_type=O.GGML_Q4_0)
+    mask = O.rs_visible_mask(n_q, ring, pos0, ring=ring)
+    exact = exact_np(O.q_round_q8_0(q), kd, vd, mask)
+    check_attention(run_gpu(kb, cuda, q, kc, vc, 4, mask=mask), exact)
+    check_attention(run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=pos0, ring=ring), exact)
+
+
+def test_q4_0_long_verify_262144(kb, cuda):
+    """config[3] shape over a q4_0 cache: 4 tokens, causal among the last 4, 262,144 cells."""
+    n_q, n_kv = 4, 262144
+    q, kc, vc, kd, vd = O.make_fa_inputs(4713, n_q, n_kv, kv_type=O.GGML_Q4_0)
     mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
     gpu = run_gpu(kb, cuda, q, kc, vc, 4, causal=True, pos0=n_kv - n_q)
     check_attention(gpu, exact_np(O.q_round_q8_0(q), kd, vd, mask))

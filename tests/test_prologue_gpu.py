@@ -20,7 +20,7 @@ def run(kb, cuda, inputs, cache_type, n_cells=64):
     import torch
 
     qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm = [torch.from_numpy(x).to(cuda) for x in inputs]
-    row = 4 * 256 * 2 if cache_type == kb.F16 else 4 * 8 * 34
+    row = {kb.F16: 4 * 256 * 2, kb.Q8_0: 4 * 8 * 34, kb.Q4_0: 4 * 8 * 18}[cache_type]
     kc = torch.zeros((n_cells, row), dtype=torch.uint8, device=cuda)
     vc = torch.zeros_like(kc)
     q, gate = kb.attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, 1e-6, k_cache=kb.cache_rows(kc, cache_type),
@@ -75,3 +75,34 @@ def test_prologue_rejects_bad_cell(kb, cuda):
     kb.attn_prologue(*t, 1e-6, k_cache=kb.cache_rows(kc, kb.F16), v_cache=kb.cache_rows(kc.clone(), kb.F16), **PROLOGUE_ROPE)
     torch.cuda.synchronize()
     assert kb.device_error(clear=True) != 0
+
+
+@ref_only
+def test_prologue_q4_0_cache_matches_reference(kb, cuda):
+    inputs = make_prologue_inputs(8, 9)
+    _, _, kc, vc = run(kb, cuda, inputs, kb.Q4_0)
+    rk = np.zeros((64, 4 * 8 * 18), np.uint8)
+    rv = np.zeros_like(rk)
+    O.ref_attn_prologue(*inputs, 1e-6, k_cache=rk, v_cache=rv, cache_type=O.GGML_Q4_0, **PROLOGUE_ROPE)
+    assert np.array_equal(vc, rv)  # V rows: the same f32 input, quantize_row_q4_0_ref's rule
+    a = O.rs_dequantize_q4_0(kc.reshape(-1, 18)).reshape(64, -1)
+    b = O.rs_dequantize_q4_0(rk.reshape(-1, 18)).reshape(64, -1)
+    d = np.abs(rk.reshape(-1, 18)[:, :2].copy().view(np.float16).astype(np.float32)).reshape(64, -1)
+    assert np.all(np.abs(a - b).reshape(64, -1, 32) <= 1.01 * d[:, :, None] + 1e-30)
+
+
+@ref_only
+def test_set_rows_q4_0_bit_exact(kb, cuda):
+    import torch
+
+    rng = np.random.default_rng(4)
+    src = rng.standard_normal((5, 1024)).astype(np.float32)
+    src[0, :32] = 0.0
+    src[1, 3], src[1, 7] = -4.0, 4.0  # equal magnitudes: the first one sets the scale
+    idx = np.array([3, 0, 9, 5, 1], dtype=np.int64)
+    ref = np.zeros((12, 1024 // 32 * 18), np.uint8)
+    O.ref_set_rows(ref, O.GGML_Q4_0, 1024, src, idx)
+    cache = torch.zeros((12, 1024 // 32 * 18), dtype=torch.uint8, device=cuda)
+    kb.set_rows(kb.cache_rows(cache, kb.Q4_0), torch.from_numpy(src).to(cuda), torch.from_numpy(idx).to(cuda))
+    torch.cuda.synchronize()
+    assert np.array_equal(cache.cpu().numpy(), ref)
