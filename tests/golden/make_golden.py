@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference's own ggml CPU ops.
 
-    python tests/golden/make_golden.py [attn_prologue | gdn_io]   (one fixture only with its name)
+    python tests/golden/make_golden.py [attn_prologue | gdn_io | q4_0]   (one fixture only with its name)
 
 Needs oracle/_ref (built by `make -C oracle ref` from the reference sources). Every fixture holds seeded
 inputs and the reference's outputs for them; tests/test_oracle.py checks the C restatement against them
@@ -88,10 +88,28 @@ def gdn_io_fixture():
                 g=g, conv_state_out=cs_out, x=x, z=z, norm_w=nw, o=o)
 
 
+def q4_0_fixture():
+    """set_rows into a q4_0 cache (quantize_row_q4_0_ref): the q8_0 edge rows plus a block whose largest magnitude
+    appears twice with opposite signs (the first one sets the scale) and one of values that land on x * id + 8.5
+    integer boundaries."""
+    x = q8_edge_rows()
+    x[5, :32] = np.linspace(-1, 1, 32).astype(np.float32)
+    x[5, 3], x[5, 9] = -2.0, 2.0
+    x[5, 32:64] = (np.arange(32) % 16 - 8).astype(np.float32) / 4.0
+    idx = np.array([5, 0, 3, 1, 7, 2], dtype=np.int64)
+    cache = np.zeros((8, 256 // 32 * 18), dtype=np.uint8)
+    O.ref_set_rows(cache, O.GGML_Q4_0, 256, x, idx)
+    return dict(src=x, idx=idx, cache_q4_0=cache)
+
+
+FIXTURES = {"attn_prologue": lambda: prologue_fixture(), "gdn_io": lambda: gdn_io_fixture(),
+            "q4_0": lambda: q4_0_fixture()}
+
+
 def main(only=None):
     out = {}
-    if only in ("attn_prologue", "gdn_io"):
-        out[only] = prologue_fixture() if only == "attn_prologue" else gdn_io_fixture()
+    if only in FIXTURES:
+        out[only] = FIXTURES[only]()
         for name, arrays in out.items():
             np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
             print(name, sum(a.nbytes for a in arrays.values()))
@@ -129,6 +147,7 @@ def main(only=None):
     out["cpy_f32_f16"] = dict(x=xs, y=h)
     out["attn_prologue"] = prologue_fixture()
     out["gdn_io"] = gdn_io_fixture()
+    out["q4_0"] = q4_0_fixture()
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
         print(name, sum(a.nbytes for a in arrays.values()))

@@ -33,6 +33,15 @@ def test_golden_set_rows_bit_exact():
     assert np.array_equal(c8, g["cache_q8_0"])
 
 
+def test_golden_q4_0_set_rows_bit_exact():
+    g = gold("q4_0")
+    c4 = np.zeros_like(g["cache_q4_0"])
+    assert O.rs_set_rows(c4, O.GGML_Q4_0, 256, g["src"], g["idx"]) == 0
+    assert np.array_equal(c4, g["cache_q4_0"])
+    rows = O.rs_quantize_q4_0(g["src"])
+    assert np.array_equal(rows, g["cache_q4_0"][g["idx"]])
+
+
 def test_golden_f16_conversion_bit_exact():
     g = gold("cpy_f32_f16")
     assert np.array_equal(g["x"].astype(np.float16).view(np.uint16), g["y"])

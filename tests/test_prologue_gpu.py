@@ -91,18 +91,13 @@ def test_prologue_q4_0_cache_matches_reference(kb, cuda):
     assert np.all(np.abs(a - b).reshape(64, -1, 32) <= 1.01 * d[:, :, None] + 1e-30)
 
 
-@ref_only
 def test_set_rows_q4_0_bit_exact(kb, cuda):
+    """kb_set_rows into a q4_0 cache equals ggml's set_rows (quantize_row_q4_0_ref) on the golden rows: an all-zero
+    block, a tie of opposite-signed maxima (the first sets the scale), .5 boundaries, tiny and large magnitudes."""
     import torch
 
-    rng = np.random.default_rng(4)
-    src = rng.standard_normal((5, 1024)).astype(np.float32)
-    src[0, :32] = 0.0
-    src[1, 3], src[1, 7] = -4.0, 4.0  # equal magnitudes: the first one sets the scale
-    idx = np.array([3, 0, 9, 5, 1], dtype=np.int64)
-    ref = np.zeros((12, 1024 // 32 * 18), np.uint8)
-    O.ref_set_rows(ref, O.GGML_Q4_0, 1024, src, idx)
-    cache = torch.zeros((12, 1024 // 32 * 18), dtype=torch.uint8, device=cuda)
-    kb.set_rows(kb.cache_rows(cache, kb.Q4_0), torch.from_numpy(src).to(cuda), torch.from_numpy(idx).to(cuda))
+    g = dict(np.load(os.path.join(GOLD, "q4_0.npz")))
+    cache = torch.zeros(g["cache_q4_0"].shape, dtype=torch.uint8, device=cuda)
+    kb.set_rows(kb.cache_rows(cache, kb.Q4_0), torch.from_numpy(g["src"]).to(cuda), torch.from_numpy(g["idx"]).to(cuda))
     torch.cuda.synchronize()
-    assert np.array_equal(cache.cpu().numpy(), ref)
+    assert np.array_equal(cache.cpu().numpy(), g["cache_q4_0"])
