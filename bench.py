@@ -37,7 +37,7 @@ UNIT = "us/layer"
 
 
 def kv_bytes_per_layer(n_kv: int, kv_type: str) -> int:
-    row = H_KV * D * 2 if kv_type == "f16" else H_KV * D // 32 * 34
+    row = {"f16": H_KV * D * 2, "q8_0": H_KV * D // 32 * 34, "q4_0": H_KV * D // 32 * 18}[kv_type]
     return 2 * n_kv * row
 
 
@@ -203,6 +203,22 @@ def quantize_q8_0_rows(torch, x):
     out[:, :, :2] = d.to(torch.float16).view(torch.uint8).view(n, k // 32, 2)
     out[:, :, 2:] = qv.view(torch.uint8)
     return out.view(n, k // 32 * 34)
+
+
+def quantize_q4_0_rows(torch, x):
+    """Device-side q4_0 quantisation of f32 rows [n, k] with quantize_row_q4_0_ref's rule (max = the first value of
+    largest magnitude, d = max / -8 stored as f16, q = min(15, trunc(x / d + 8.5)), byte j = q_j | q_{j+16} << 4);
+    builds the synthetic q4_0 caches of the benchmark."""
+    n, k = x.shape
+    blk = x.view(n, k // 32, 32)
+    mx = torch.gather(blk, -1, blk.abs().argmax(-1, keepdim=True)).squeeze(-1)
+    d = mx / -8.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    qv = torch.clamp(torch.trunc(blk * inv.unsqueeze(-1) + 8.5), max=15).to(torch.uint8)
+    out = torch.empty(n, k // 32, 18, dtype=torch.uint8, device=x.device)
+    out[:, :, :2] = d.to(torch.float16).view(torch.uint8).view(n, k // 32, 2)
+    out[:, :, 2:] = qv[:, :, :16] | (qv[:, :, 16:] << 4)
+    return out.view(n, k // 32 * 18)
 
 
 def bench_prefill(kb, torch, dev, steps, warmup):
@@ -424,8 +440,10 @@ def make_layers(kb, torch, dev, gen, n_kv, kv_type):
         vf = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
         if kv_type == "f16":
             kc, vc, t = kf.half(), vf.half(), kb.F16
-        else:
+        elif kv_type == "q8_0":
             kc, vc, t = quantize_q8_0_rows(torch, kf), quantize_q8_0_rows(torch, vf), kb.Q8_0
+        else:
+            kc, vc, t = quantize_q4_0_rows(torch, kf), quantize_q4_0_rows(torch, vf), kb.Q4_0
         del kf, vf
         layers.append((kc, vc, kb.kv_cache_view(kc, t, H_KV, D), kb.kv_cache_view(vc, t, H_KV, D)))
     return layers
@@ -594,48 +612,50 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     e2e_ms = max(f0.elapsed_time(f1), t_wall * 1e3)
     qt.data = q.data_ptr()
 
-    # secondary: the same verify step over a q8_0 cache (config[3]'s other variant)
+    # secondary: the same verify step over q8_0 and q4_0 caches (config[3]'s other variant; klein's type beyond
+    # 131K cells)
     secondary = {}
     if not args.no_secondary:
-        graphs.clear()  # the f16 graphs refer to the cache about to be freed
-        del layers[:]
-        torch.cuda.empty_cache()
-        layers.extend(make_layers(kb, torch, dev, gen, n_kv, "q8_0"))
-        # the q8_0 kernel plans its own row chunks and splits: size the scratch for it
-        need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]), ctypes.byref(layers[0][3]),
-                                                 ctypes.byref(prm))
-        if world > 1:
-            need = max(need, L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]),
-                                                                    ctypes.byref(layers[0][3]), ctypes.byref(prm)))
-        del scratch
-        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
-        sp = ctypes.c_void_p(scratch.data_ptr())
-        for _ in range(args.warmup):
-            step(st)
-        torch.cuda.synchronize()
-        run_q8 = graphed(step)  # a new capture: the f16 step's graph refers to the freed f16 cache
-        run_q8()
-        torch.cuda.synchronize()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(args.steps):
-            run_q8()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        qms = g0.elapsed_time(g1)
-        if world > 1:
-            t = torch.tensor([qms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            qms = float(t.item())
-        q_us = qms * 1e3 / (args.steps * LAYERS)
-        qbytes = kv_bytes_per_layer(n_kv, "q8_0")
-        pk, _ = measured_peaks()
-        secondary["verify_q8_0"] = {
-            "value": round(q_us, 2), "unit": UNIT, "kv_type": "q8_0",
-            "roofline": {"bound": "hbm", "achieved": round(qbytes / (q_us * 1e-6) / 1e9, 1), "peak": pk["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(qbytes / (q_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
-                         "algorithmic_bytes_per_launch": qbytes,
-                         "traffic": ncu_traffic("fa_stream_q8_0_verify262k")}}
+        for kvt in ("q8_0", "q4_0"):
+            graphs.clear()  # the previous graphs refer to the cache about to be freed
+            del layers[:]
+            torch.cuda.empty_cache()
+            layers.extend(make_layers(kb, torch, dev, gen, n_kv, kvt))
+            # the quantised kernels plan their own row chunks and splits: size the scratch for them
+            need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]),
+                                                     ctypes.byref(layers[0][3]), ctypes.byref(prm))
+            if world > 1:
+                need = max(need, L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(layers[0][2]),
+                                                                        ctypes.byref(layers[0][3]), ctypes.byref(prm)))
+            del scratch
+            scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+            sp = ctypes.c_void_p(scratch.data_ptr())
+            for _ in range(args.warmup):
+                step(st)
+            torch.cuda.synchronize()
+            run_q = graphed(step)  # a new capture: the earlier graphs refer to freed caches
+            run_q()
+            torch.cuda.synchronize()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for _ in range(args.steps):
+                run_q()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            qms = g0.elapsed_time(g1)
+            if world > 1:
+                t = torch.tensor([qms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                qms = float(t.item())
+            q_us = qms * 1e3 / (args.steps * LAYERS)
+            qbytes = kv_bytes_per_layer(n_kv, kvt)
+            pk, _ = measured_peaks()
+            secondary["verify_" + kvt] = {
+                "value": round(q_us, 2), "unit": UNIT, "kv_type": kvt,
+                "roofline": {"bound": "hbm", "achieved": round(qbytes / (q_us * 1e-6) / 1e9, 1), "peak": pk["hbm_gbs"],
+                             "unit": "GB/s", "frac": round(qbytes / (q_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
+                             "algorithmic_bytes_per_launch": qbytes,
+                             "traffic": ncu_traffic(f"fa_stream_{kvt}_verify262k")}}
 
     peaks, peak_kind = measured_peaks()
     bytes_layer = kv_bytes_per_layer(n_kv, "f16")
@@ -723,12 +743,12 @@ def run_case(case: str):
         s0 = (rng.standard_normal((1, 48, 128, 128)) * (0.0 if T > 4 else 0.02)).astype(np.float32)
         args = [torch.from_numpy(a).to(dev) for a in (q, k, v, g, beta, s0)]
         run = lambda: kb.gated_delta_net(*args, 4)
-    elif case in ("verify_f16", "verify_q8_0"):
+    elif case in ("verify_f16", "verify_q8_0", "verify_q4_0"):
         n_kv = 262144
         global LAYERS
         LAYERS = 1
         # keep the cache tensors (the first two entries) alive: the views only hold their pointers
-        kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, "f16" if case == "verify_f16" else "q8_0")[0]
+        kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, case[len("verify_"):])[0]
         q = torch.randn(1, 4, H, D, device=dev, generator=gen)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
     else:
@@ -748,12 +768,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
-    ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 cache)")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 / q4_0 caches, prefill, DeltaNet, I/O ops)")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph per step")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: partials exchange over NVLink peer stores (default) or an NCCL all-gather")
     ap.add_argument("--case", default=None,
-                    choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0"],
+                    choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
+                             "verify_q4_0"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:
