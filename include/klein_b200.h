@@ -77,13 +77,15 @@ typedef struct kb_fa_params {
  * GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext, ggml.h:2476-2495; CPU semantics ops.cpp:8842-9574;
  * replaces ggml_cuda_flash_attn_ext, ggml-cuda/fattn.cu:758-772).
  *   q    f32  [D, n_q, H, ne3]       any byte strides (klein passes a permuted view, graph.cpp:118)
- *   k, v f16/q8_0 [D, n_kv, H_kv, ne3k]  nb[0] = element size (34 = block size for q8_0); H % H_kv == 0,
+ *   k, v f16/q8_0/q4_0 [D, n_kv, H_kv, ne3k]  nb[0] = element size (block size 34 for q8_0, 18 for q4_0);
+ *                                    H % H_kv == 0,
  *                                    ne3 % ne3k == 0; base and nb[1..3] multiples of 16 bytes
  *   mask f16  [n_kv, >= n_q, ne32, ne33] contiguous, or NULL; broadcast over heads as in ggml
  *   dst  f32  [D, H, n_q, ne3]       ("permuted" result); nb[0] = 4
  * Head h reads KV head h / (H / H_kv). A row whose every cell is masked produces zeros.
  * scratch: device memory of at least kb_flash_attn_ext_scratch_bytes(...) bytes (may be NULL when that
- * is 0). Supported here: D = 256, K and V of the same type (f16 or q8_0).
+ * is 0). Supported here: D = 256, K and V of the same type (f16, q8_0 or q4_0). Over a q8_0 or q4_0 cache Q is
+ * rounded to q8_0 first (the vec_dot type of both in ggml's CPU backend).
  */
 kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                             const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
@@ -222,9 +224,10 @@ kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t co
 /*
  * ggml_set_rows (ops.cpp:5446-5500; replaces ggml-cuda/set-rows.cu:8-110), klein's KV-cache write
  * (graph.cpp:111-112): dst row idx[r] <- src row r for every (i2, i3), converted to dst's type.
- *   dst f32 / f16 / bf16 / q8_0 [ne0, n_rows, ne2, ne3]; src f32 [ne0, n_src, ne2, ne3] (rows contiguous);
- *   idx i64 or i32 [n_src, ne11, ne12] broadcast over ne2 % ne11, ne3 % ne12. ne0 % 32 == 0.
- *   q8_0 rounding is quantize_row_q8_0_ref's (ggml-quants.c:276-299), bit for bit.
+ *   dst f32 / f16 / bf16 / q8_0 / q4_0 [ne0, n_rows, ne2, ne3]; src f32 [ne0, n_src, ne2, ne3] (rows
+ *   contiguous); idx i64 or i32 [n_src, ne11, ne12] broadcast over ne2 % ne11, ne3 % ne12. ne0 % 32 == 0.
+ *   q8_0 rounding is quantize_row_q8_0_ref's (ggml-quants.c:276-299), q4_0 quantize_row_q4_0_ref's
+ *   (ggml-quants.c:113-148: the first value of largest magnitude sets d = max / -8), bit for bit.
  * An out-of-range index (ggml asserts) skips that row and sets the device error word (kb_device_error).
  */
 kb_status kb_set_rows(const kb_tensor* dst, const kb_tensor* src, const kb_tensor* idx, void* stream);
