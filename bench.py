@@ -751,6 +751,16 @@ def run_case(case: str):
         kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, case[len("verify_"):])[0]
         q = torch.randn(1, 4, H, D, device=dev, generator=gen)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
+    elif case == "gdn_input_4096":
+        # the DeltaNet input side at config[2]'s 4,096 tokens (qwen35: 16 key / 48 value heads, S 128)
+        T, S, Hk, Hv = 4096, 128, 16, 48
+        ch = 2 * S * Hk + S * Hv
+        qkv = torch.randn(T, ch, device=dev, generator=gen)
+        state = torch.randn(4, 3 * ch, device=dev, generator=gen)
+        cw = torch.randn(ch, 4, device=dev, generator=gen) * 0.5
+        br, al = torch.randn(T, Hv, device=dev, generator=gen), torch.randn(T, Hv, device=dev, generator=gen)
+        dt, aa = torch.randn(Hv, device=dev, generator=gen), -torch.rand(Hv, device=dev, generator=gen) - 0.1
+        run = lambda: kb.gdn_input(qkv, state, cw, S, Hk, 1e-6, beta_raw=br, alpha=al, dt_bias=dt, a=aa)[0]
     else:
         raise SystemExit(f"unknown case {case}")
     for _ in range(3):
@@ -774,7 +784,7 @@ def main():
                     help="N > 1: partials exchange over NVLink peer stores (default) or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
-                             "verify_q4_0"],
+                             "verify_q4_0", "gdn_input_4096"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:

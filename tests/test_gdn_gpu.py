@@ -195,3 +195,27 @@ def test_set_rows_i32_broadcast_and_bad_index(kb, cuda):
     kb.set_rows(dst, st, bad.reshape(1, 1, 3))
     torch.cuda.synchronize()
     assert kb.device_error(clear=True) != 0
+
+
+@pytest.mark.parametrize("T", [4, 130])
+def test_head_shards_equal_whole(kb, cuda, T):
+    """Head sharding (8 ranks' slices of 48 value heads, key heads gathered by gdn_head_shard): each slice through
+    the op equals the same heads of the whole op, for the recurrent verify (T = 4) and the chunked prefill."""
+    import torch
+
+    from klein_b200.kv_split import gdn_head_shard
+
+    K = 4
+    q, k, v, g, beta, s0 = O.make_gdn_inputs(303, T)
+    whole = kb.gated_delta_net(*to_dev(cuda, q, k, v, g, beta[..., None], s0), K)
+    torch.cuda.synchronize()
+    attn, slots = split_packed(whole.cpu().numpy(), 128, 48, T, 1, K)
+    for r in range(8):
+        lo, hi, kidx = gdn_head_shard(16, 48, 8, r)
+        part = kb.gated_delta_net(*to_dev(cuda, q[:, :, kidx], k[:, :, kidx], v[:, :, lo:hi], g[:, :, lo:hi],
+                                          beta[:, :, lo:hi, None], s0[:, lo:hi]), K)
+        torch.cuda.synchronize()
+        a, s = split_packed(part.cpu().numpy(), 128, hi - lo, T, 1, K)
+        scale = np.abs(attn).max()
+        assert np.abs(a - attn[:, :, lo:hi]).max() <= 1e-6 * scale
+        assert np.abs(s - slots[:, :, lo:hi]).max() <= 1e-6 * np.abs(slots).max()
