@@ -501,7 +501,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         pf = packed_part_floats(rows, D)
         part = torch.empty(pf, device=dev)
         gathered = torch.empty(world * pf, device=dev)
-        if args.exchange == "p2p":
+        if args.exchange in ("p2p", "fused"):
             def all_gather_obj(obj):
                 objs = [None] * world
                 dist.all_gather_object(objs, obj)
@@ -519,7 +519,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             if rc != 0:
                 raise kb.KbError("kb_flash_attn_ext", rc)
             return
-        if xchg is not None:
+        if xchg is not None and args.exchange == "fused":
             # the partial attention writes its rows straight into every rank's gather buffer, then the merge
             xchg.attend_and_combine(qt, layers[l][2], layers[l][3], prm, sp.value, need, rows, D, out.data_ptr(),
                                     st.value)
@@ -528,6 +528,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                          ctypes.byref(prm), ctypes.byref(pt), ml_ptr, sp, ctypes.c_size_t(need), st)
         if rc != 0:
             raise kb.KbError("kb_flash_attn_ext_partial", rc)
+        if xchg is not None:
+            # kb_partials_push into every rank's gather buffer, then kb_lse_combine_wait
+            xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), st.value)
+            return
         dist.all_gather_into_tensor(gathered, part)
         rc = L.kb_lse_combine(g_o, g_ml, ctypes.c_int64(pf), world, ctypes.c_int64(rows), D,
                               ctypes.c_void_p(out.data_ptr()), st)
@@ -780,8 +784,9 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 / q4_0 caches, prefill, DeltaNet, I/O ops)")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph per step")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
-                    help="N > 1: partials exchange over NVLink peer stores (default) or an NCCL all-gather")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "fused", "nccl"],
+                    help="N > 1: partials exchange over NVLink peer stores by a push kernel (default), by the split "
+                         "combine itself (fused), or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
                              "verify_q4_0", "gdn_input_4096"],
