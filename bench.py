@@ -384,7 +384,8 @@ def bench_io_ops(kb, torch, dev, steps, warmup):
             res[f"{name}_{T}"] = {"value": round(us, 2), "unit": "us", "tokens": T,
                                   "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
                                                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
-                                               "algorithmic_bytes_per_launch": nbytes}}
+                                               "algorithmic_bytes_per_launch": nbytes,
+                                               "traffic": ncu_traffic(f"{name}_{T}")}}
     return res
 
 
