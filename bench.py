@@ -318,7 +318,8 @@ def bench_gdn(kb, torch, dev, steps, warmup):
 def bench_io_ops(kb, torch, dev, steps, warmup):
     """The ops around the two attention kinds at config[2]'s 4,096-token prefill (qwen35 shapes, f16 cache):
     kb_attn_prologue (Q/gate split, RMS norms, M-RoPE, K/V cache writes), kb_gdn_input (conv, SiLU, L2 norms, gates,
-    conv-state snapshots) and kb_gdn_gated_norm; plus the same three at the 4-token verify. HBM-bound: bytes = what
+    conv-state snapshots) and kb_gdn_gated_norm; plus the same three at the 4-token verify (positions at the end of a
+    262,144-cell context). HBM-bound: bytes = what
     each op must read and write once. Timed with CUDA events, each op alone in a loop (inputs > L2 at 4,096 tokens)."""
     import ctypes  # noqa: F401
 
@@ -332,9 +333,10 @@ def bench_io_ops(kb, torch, dev, steps, warmup):
         qfull = torch.randn(T, nh * 2 * hd, device=dev, generator=g)
         kcur = torch.randn(T, nkv * hd, device=dev, generator=g)
         vcur = torch.randn(T, nkv * hd, device=dev, generator=g)
-        p = torch.arange(T, dtype=torch.int32, device=dev)
+        # the prefill from position 0; the verify step at the end of a 262,144-cell context (long-context angles)
+        p = torch.arange(T, dtype=torch.int32, device=dev) + (0 if T > 4 else 262144 - T)
         pos = torch.cat([p, p, p, torch.zeros_like(p)])
-        kv_idx = torch.arange(T, dtype=torch.int64, device=dev)
+        kv_idx = torch.arange(T, dtype=torch.int64, device=dev)  # cells of a T-cell cache
         qn = torch.ones(hd, device=dev)
         kcache = torch.zeros(T, nkv * hd, dtype=torch.float16, device=dev)
         vcache = torch.zeros_like(kcache)

@@ -21,6 +21,42 @@ namespace kb {
 
 namespace {
 
+// M-RoPE of one head row held as x[k] = dim lane + 32 k: pairs (i, i + n_rot / 2) for i = lane + 32 j, j < OFF
+// (OFF = n_rot / 64), NeoX layout; theta of pair i = the position component its sector selects times theta_scale^i
+// as ggml's running f32 product (ops.cpp:6219-6306)
+template <int EPL, int OFF>
+__device__ __forceinline__ void rope_pairs(float (&x)[EPL], const PrologueParams& p, int t, int lane) {
+    static_assert(2 * OFF <= EPL, "n_rot <= head dim");
+#pragma unroll
+    for (int j = 0; j < OFF; ++j) {
+        const int i = lane + 32 * j;
+        const int sector = i % p.sect_dims;
+        int comp;
+        if (p.imrope) {
+            if (sector % 3 == 1 && sector < 3 * p.sections[1]) comp = 1;
+            else if (sector % 3 == 2 && sector < 3 * p.sections[2]) comp = 2;
+            else if (sector % 3 == 0 && sector < 3 * p.sections[0]) comp = 0;
+            else comp = 3;
+        } else {
+            const int sec_w = p.sections[0] + p.sections[1];
+            if (sector >= p.sections[0] && sector < sec_w) comp = 1;
+            else if (sector >= sec_w && sector < sec_w + p.sections[2]) comp = 2;
+            else if (sector >= sec_w + p.sections[2]) comp = 3;
+            else comp = 0;
+        }
+        float theta = (float) p.pos[(int64_t) comp * p.n + t];
+        for (int s = 0; s < i; ++s) theta *= p.theta_scale;  // ggml's running product, pair by pair
+        theta *= p.freq_scale;
+        // cosf and sinf of one argument in one call (one range reduction: the slow path at long-context angles)
+        float sv, cv;
+        sincosf(theta, &sv, &cv);
+        const float c = cv * p.attn_factor, sn = sv * p.attn_factor;
+        const float x0 = x[j], x1 = x[j + OFF];
+        x[j] = x0 * c - x1 * sn;
+        x[j + OFF] = x0 * sn + x1 * c;
+    }
+}
+
 template <int EPL>  // elements per lane: hd / 32
 __global__ void __launch_bounds__(256) attn_prologue_kernel(const PrologueParams p) {
     constexpr int HD = 32 * EPL;
@@ -56,40 +92,16 @@ __global__ void __launch_bounds__(256) attn_prologue_kernel(const PrologueParams
         const float* w = is_q ? p.q_norm : p.k_norm;
 #pragma unroll
         for (int k = 0; k < EPL; ++k) x[k] = x[k] * scale * w[lane + 32 * k];
-        // M-RoPE over pairs (i, i + n_rot / 2), i = lane + 32 j: element j and its partner j + n_rot / 64
+        // M-RoPE over pairs (i, i + n_rot / 2), i = lane + 32 j: element j and its partner j + n_rot / 64, with
+        // n_rot / 64 a template argument so every index is a constant and x stays in registers
         const int off = p.n_rot / 64;
-#pragma unroll
-        for (int j = 0; j < EPL; ++j) {
-            if (j >= off) break;
-            const int i = lane + 32 * j;
-            const int sector = i % p.sect_dims;
-            int comp;
-            if (p.imrope) {
-                if (sector % 3 == 1 && sector < 3 * p.sections[1]) comp = 1;
-                else if (sector % 3 == 2 && sector < 3 * p.sections[2]) comp = 2;
-                else if (sector % 3 == 0 && sector < 3 * p.sections[0]) comp = 0;
-                else comp = 3;
-            } else {
-                const int sec_w = p.sections[0] + p.sections[1];
-                if (sector >= p.sections[0] && sector < sec_w) comp = 1;
-                else if (sector >= sec_w && sector < sec_w + p.sections[2]) comp = 2;
-                else if (sector >= sec_w + p.sections[2]) comp = 3;
-                else comp = 0;
-            }
-            float theta = (float) p.pos[(int64_t) comp * p.n + t];
-            for (int s = 0; s < i; ++s) theta *= p.theta_scale;  // ggml's running product, pair by pair
-            theta *= p.freq_scale;
-            const float c = cosf(theta) * p.attn_factor, sn = sinf(theta) * p.attn_factor;
-            float x1 = 0.0f;
-#pragma unroll
-            for (int k = 0; k < EPL; ++k)
-                if (k == j + off) x1 = x[k];
-            const float x0 = x[j];
-            const float y1 = x0 * sn + x1 * c;
-            x[j] = x0 * c - x1 * sn;
-#pragma unroll
-            for (int k = 0; k < EPL; ++k)
-                if (k == j + off) x[k] = y1;
+        if (off == 1) rope_pairs<EPL, 1>(x, p, t, lane);
+        if constexpr (EPL >= 4) {
+            if (off == 2) rope_pairs<EPL, 2>(x, p, t, lane);
+        }
+        if constexpr (EPL >= 8) {
+            if (off == 3) rope_pairs<EPL, 3>(x, p, t, lane);
+            if (off == 4) rope_pairs<EPL, 4>(x, p, t, lane);
         }
     }
     if (is_q) {
