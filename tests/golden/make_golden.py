@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference's own ggml CPU ops.
 
-    python tests/golden/make_golden.py [attn_prologue | gdn_io | q4_0]   (one fixture only with its name)
+    python tests/golden/make_golden.py [attn_prologue | gdn_io | q4_0 | fa_verify_q4_0 | ...]   (one fixture only with its name)
 
 Needs oracle/_ref (built by `make -C oracle ref` from the reference sources). Every fixture holds seeded
 inputs and the reference's outputs for them; tests/test_oracle.py checks the C restatement against them
@@ -102,8 +102,21 @@ def q4_0_fixture():
     return dict(src=x, idx=idx, cache_q4_0=cache)
 
 
+def fa_fixture(n_q, n_kv, kvt):
+    q, kc, vc, kd, vd = O.make_fa_inputs(4242 + n_kv, n_q, n_kv, kv_type=kvt)
+    mask = None if n_q == 1 else O.rs_visible_mask(n_q, n_kv, n_kv - n_q).astype(np.float16)
+    ref = O.ref_flash_attn_ext(q, kc, vc, kvt, 4, mask=mask, n_threads=1, use_ref=True)
+    return dict(q=q, k=kc, v=vc, mask=np.zeros((0, 0), np.float16) if mask is None else mask, out=ref,
+                kv_type=np.int32(kvt))
+
+
+# flash attention: decode f16, verify f16 with klein's causal mask, verify q8_0 / q4_0 with mask
+FA_FIXTURES = {"fa_decode_f16": (1, 64, O.GGML_F16), "fa_verify_f16": (4, 48, O.GGML_F16),
+               "fa_verify_q8_0": (4, 80, O.GGML_Q8_0), "fa_verify_q4_0": (4, 72, O.GGML_Q4_0)}
+
 FIXTURES = {"attn_prologue": lambda: prologue_fixture(), "gdn_io": lambda: gdn_io_fixture(),
             "q4_0": lambda: q4_0_fixture()}
+FIXTURES.update({name: (lambda a=args: fa_fixture(*a)) for name, args in FA_FIXTURES.items()})
 
 
 def main(only=None):
@@ -114,14 +127,8 @@ def main(only=None):
             np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
             print(name, sum(a.nbytes for a in arrays.values()))
         return
-    # flash attention: decode f16, verify f16 with klein's causal mask, verify q8_0 with mask
-    for name, n_q, n_kv, kvt in [("fa_decode_f16", 1, 64, O.GGML_F16), ("fa_verify_f16", 4, 48, O.GGML_F16),
-                                 ("fa_verify_q8_0", 4, 80, O.GGML_Q8_0)]:
-        q, kc, vc, kd, vd = O.make_fa_inputs(4242 + n_kv, n_q, n_kv, kv_type=kvt)
-        mask = None if n_q == 1 else O.rs_visible_mask(n_q, n_kv, n_kv - n_q).astype(np.float16)
-        ref = O.ref_flash_attn_ext(q, kc, vc, kvt, 4, mask=mask, n_threads=1, use_ref=True)
-        out[name] = dict(q=q, k=kc, v=vc, mask=np.zeros((0, 0), np.float16) if mask is None else mask, out=ref,
-                         kv_type=np.int32(kvt))
+    for name, (n_q, n_kv, kvt) in FA_FIXTURES.items():
+        out[name] = fa_fixture(n_q, n_kv, kvt)
     # gated delta net (small heads so the fixture stays small): scalar gate and KDA vector gate
     for name, kda in [("gdn_verify", False), ("gdn_verify_kda", True)]:
         q, k, v, g, beta, s0 = O.make_gdn_inputs(77 + kda, T=4, H_k=2, H_v=6, S=32, kda=kda)

@@ -49,7 +49,7 @@ def test_golden_f16_conversion_bit_exact():
     assert np.array_equal(h, g["y"])
 
 
-@pytest.mark.parametrize("name", ["fa_decode_f16", "fa_verify_f16", "fa_verify_q8_0"])
+@pytest.mark.parametrize("name", ["fa_decode_f16", "fa_verify_f16", "fa_verify_q8_0", "fa_verify_q4_0"])
 def test_golden_flash_attention(name):
     g = gold(name)
     kvt = int(g["kv_type"])
@@ -60,9 +60,10 @@ def test_golden_flash_attention(name):
         q = O.q_round_f16(g["q"])
         tol = 2e-2  # ggml accumulates V*softmax in fp16 for f16 V (ops.cpp:8992-9007)
     else:
-        kd = O.rs_dequantize_q8_0(g["k"]).reshape(n_kv, 4, 256)
-        vd = O.rs_dequantize_q8_0(g["v"]).reshape(n_kv, 4, 256)
-        q = O.q_round_q8_0(g["q"])
+        deq = O.rs_dequantize_q8_0 if kvt == O.GGML_Q8_0 else O.rs_dequantize_q4_0
+        kd = deq(g["k"]).reshape(n_kv, 4, 256)
+        vd = deq(g["v"]).reshape(n_kv, 4, 256)
+        q = O.q_round_q8_0(g["q"])  # q8_0 is the vec_dot type of both q8_0 and q4_0 K
         tol = 1e-5  # f32 accumulation: only summation order differs
     mask = g["mask"].astype(np.float32) if g["mask"].size else None
     exact = O.rs_flash_attn_f64(q, kd, vd, mask=mask)
@@ -141,8 +142,17 @@ def test_live_q8_0_bit_exact():
 
 
 @ref_only
+def test_live_q4_0_bit_exact():
+    x = np.random.default_rng(12).standard_normal((128, 1024)).astype(np.float32) * 3
+    y = np.zeros((128, 1024 // 32 * 18), np.uint8)
+    O.ref_set_rows(y, O.GGML_Q4_0, 1024, x, np.arange(128, dtype=np.int64))
+    assert np.array_equal(O.rs_quantize_q4_0(x), y)
+    assert np.array_equal(O.rs_dequantize_q4_0(y).reshape(-1), O.ref_dequantize(O.GGML_Q4_0, y, x.size))
+
+
+@ref_only
 @pytest.mark.parametrize("kvt,n_q,n_kv", [(O.GGML_F16, 1, 4096), (O.GGML_F16, 4, 1000), (O.GGML_Q8_0, 1, 4096),
-                                          (O.GGML_Q8_0, 4, 1000)])
+                                          (O.GGML_Q8_0, 4, 1000), (O.GGML_Q4_0, 1, 4096), (O.GGML_Q4_0, 4, 1000)])
 def test_live_flash_attention(kvt, n_q, n_kv):
     q, kc, vc, kd, vd = O.make_fa_inputs(900 + n_q + n_kv, n_q, n_kv, kv_type=kvt)
     mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
