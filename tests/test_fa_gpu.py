@@ -313,3 +313,26 @@ def test_output_gate_fused(kb, cuda, kvt, n_q, n_kv):
     assert kb.device_error() == 0
     want = plain * (1.0 / (1.0 + torch.exp(-gate)))
     assert float((gated - want).abs().max()) <= 1e-6 * float(want.abs().max()) + 1e-30
+
+
+# ---------------------------------------------------------------------------------------------- golden fixtures
+# the reference's own ggml CPU outputs, committed (tests/golden/make_golden.py): the GPU path against them with the
+# three-way rule, with no reference build needed on the GPU machine
+
+@pytest.mark.parametrize("name", ["fa_decode_f16", "fa_verify_f16", "fa_verify_q8_0", "fa_verify_q4_0"])
+def test_golden_fixture(kb, cuda, name):
+    import os
+
+    g = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", name + ".npz")))
+    kvt = int(g["kv_type"])
+    n_kv = g["k"].shape[0]
+    if kvt == O.GGML_F16:
+        kd, vd = (g[x].astype(np.float32).reshape(n_kv, 4, 256) for x in ("k", "v"))
+        q = O.q_round_f16(g["q"])
+    else:
+        deq = O.rs_dequantize_q8_0 if kvt == O.GGML_Q8_0 else O.rs_dequantize_q4_0
+        kd, vd = (deq(g[x]).reshape(n_kv, 4, 256) for x in ("k", "v"))
+        q = O.q_round_q8_0(g["q"])
+    mask = g["mask"] if g["mask"].size else None
+    gpu = run_gpu(kb, cuda, g["q"], g["k"], g["v"], 4, mask=mask)
+    check_attention(gpu, exact_np(q, kd, vd, mask=mask), g["out"])
