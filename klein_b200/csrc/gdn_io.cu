@@ -167,6 +167,53 @@ __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const GdnNormParams
     for (int i = 0; i < CPL; ++i) o[lane + 32 * i] = v[i] * scale * p.w[lane + 32 * i] * silu_f(z[lane + 32 * i]);
 }
 
+// The same op with lane l holding the CPL consecutive channels l CPL .. l CPL + CPL - 1 (one 16- or 8-byte access
+// per array) and RPW rows per warp, their reductions interleaved; for 16-byte aligned rows
+template <int CPL, int RPW>
+__global__ void __launch_bounds__(256) gdn_gated_norm_vec_kernel(const GdnNormParams p) {
+    static_assert(CPL == 2 || CPL == 4, "8- or 16-byte accesses");
+    constexpr int S = 32 * CPL;
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = (int64_t) p.n * p.H;
+    const int64_t r0 = ((int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+    if (r0 >= rows) return;
+    auto load = [](const float* src, float (&v)[CPL]) {
+        if constexpr (CPL == 4) {
+            const float4 a = *reinterpret_cast<const float4*>(src);
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+        } else {
+            const float2 a = *reinterpret_cast<const float2*>(src);
+            v[0] = a.x, v[1] = a.y;
+        }
+    };
+    float wv[CPL], xv[RPW][CPL], zv[RPW][CPL];
+    load(p.w + lane * CPL, wv);
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+        const int64_t row = min(r0 + rr, rows - 1);  // a missing row repeats the last one and is not stored
+        load(p.x + row * S + lane * CPL, xv[rr]);
+        load(p.z + row * S + lane * CPL, zv[rr]);
+    }
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) ss += (double) (xv[rr][i] * xv[rr][i]);
+#pragma unroll
+        for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float mean = (float) (ss / S);
+        const float scale = 1.0f / sqrtf(mean + p.eps);
+        float o[CPL];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) o[i] = xv[rr][i] * scale * wv[i] * silu_f(zv[rr][i]);
+        if (r0 + rr < rows) {
+            float* dst = p.dst + (r0 + rr) * S + lane * CPL;
+            if constexpr (CPL == 4) *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+            else *reinterpret_cast<float2*>(dst) = make_float2(o[0], o[1]);
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_gdn_input(const GdnInputParams& p, int S, cudaStream_t stream) {
@@ -189,6 +236,15 @@ cudaError_t launch_gdn_input(const GdnInputParams& p, int S, cudaStream_t stream
 cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream) {
     const int64_t tasks = (int64_t) p.n * p.H;
     if (tasks == 0) return cudaSuccess;
+    const auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    if (a16(p.x) && a16(p.z) && a16(p.w) && a16(p.dst)) {
+        // rows of S floats stay 16-byte aligned; 2 rows per warp, 8 warps per CTA
+        constexpr int RPW = 2;
+        const unsigned vgrid = (unsigned) ((tasks + 8 * RPW - 1) / (8 * RPW));
+        if (S == 64) gdn_gated_norm_vec_kernel<2, RPW><<<vgrid, 256, 0, stream>>>(p);
+        else gdn_gated_norm_vec_kernel<4, RPW><<<vgrid, 256, 0, stream>>>(p);
+        return cudaGetLastError();
+    }
     const unsigned grid = (unsigned) ((tasks + 7) / 8);
     switch (S) {
         case 64: gdn_gated_norm_kernel<2><<<grid, 256, 0, stream>>>(p); break;

@@ -39,14 +39,23 @@ def test_gdn_input_matches_reference(kb, cuda, n):
 
 
 @ref_only
-def test_gdn_gated_norm_matches_reference(kb, cuda):
+@pytest.mark.parametrize("n,H,S,offset", [(6, 48, 128, 0), (5, 3, 128, 0), (7, 5, 64, 0), (5, 3, 128, 1), (4, 6, 64, 1)])
+def test_gdn_gated_norm_matches_reference(kb, cuda, n, H, S, offset):
+    """Rows of 16-byte aligned buffers take the vectorised kernel (2 rows per warp: odd row counts leave a warp
+    with one row); buffers offset by one float take the one-row-per-warp kernel."""
     import torch
 
-    rng = np.random.default_rng(9)
-    x = rng.standard_normal((6, 48, 128)).astype(np.float32)
-    z = rng.standard_normal((6, 48, 128)).astype(np.float32)
-    w = (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    rng = np.random.default_rng(9 + n + S)
+    x = rng.standard_normal((n, H, S)).astype(np.float32)
+    z = rng.standard_normal((n, H, S)).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(S)).astype(np.float32)
     ref = O.ref_gdn_gated_norm(x, z, w, 1e-6)
-    out = kb.gdn_gated_norm(torch.from_numpy(x).to(cuda), torch.from_numpy(z).to(cuda), torch.from_numpy(w).to(cuda), 1e-6)
+
+    def dev(a):
+        buf = torch.zeros(a.size + offset, dtype=torch.float32, device=cuda)
+        buf[offset:] = torch.from_numpy(a.reshape(-1)).to(cuda)
+        return buf[offset:].view(a.shape)
+
+    out = kb.gdn_gated_norm(dev(x), dev(z), dev(w), 1e-6)
     torch.cuda.synchronize()
     assert np.abs(out.cpu().numpy() - ref).max() <= 2e-6 * np.abs(ref).max()
