@@ -29,8 +29,27 @@ constexpr int KC = 4;  // conv kernel width (qwen35's ssm_conv_kernel); others a
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-// CPL: channels per lane (S / 32); CH: tokens per warp (8 for batches, 4 for the verify step)
-template <int CPL, int CH>
+// CPL consecutive floats in one 16- (CPL 4) or 8-byte (CPL 2) access
+template <int CPL>
+__device__ __forceinline__ void ld_vec(const float* src, float* d) {
+    static_assert(CPL == 2 || CPL == 4, "8- or 16-byte accesses");
+    if constexpr (CPL == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(src);
+        d[0] = a.x, d[1] = a.y, d[2] = a.z, d[3] = a.w;
+    } else {
+        const float2 a = *reinterpret_cast<const float2*>(src);
+        d[0] = a.x, d[1] = a.y;
+    }
+}
+template <int CPL>
+__device__ __forceinline__ void st_vec(float* dst, const float* v) {
+    if constexpr (CPL == 4) *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    else *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+}
+
+// CPL: channels per lane (S / 32); CH: tokens per warp (8 for batches, 4 for the verify step); CONSEC: lane l holds
+// channels c0 + CPL l .. + CPL - 1 with vector accesses (16-byte aligned buffers), else c0 + l, c0 + l + 32, ...
+template <int CPL, int CH, bool CONSEC>
 __global__ void __launch_bounds__(256, 2) gdn_input_kernel(const GdnInputParams p) {
     static_assert(CH > KC - 1, "only the first chunk reads the stored state");
     constexpr int S = 32 * CPL;
@@ -56,25 +75,56 @@ __global__ void __launch_bounds__(256, 2) gdn_input_kernel(const GdnInputParams 
     const int chunk = (int) (task / slots), slot = (int) (task % slots);
     const int c0 = slot * S;  // first channel of the slot
     const int t0 = chunk * CH, t1 = min(p.n, t0 + CH);
-    // win[i][j]: the KC - 1 inputs before token t0 of channel c0 + lane + 32 i (for chunk 0 the stored state)
+    // channel of this lane's element i
+    auto chan = [&](int i) -> int64_t { return CONSEC ? c0 + CPL * lane + i : c0 + lane + 32 * i; };
+    // win[i][j]: the KC - 1 inputs before token t0 of channel chan(i) (for chunk 0 the stored state)
     float win[CPL][KM1], w[CPL][KC];
+    if constexpr (CONSEC) {
+        // the lane's CPL channels are contiguous in conv_w ([ch][KC]) and in the state ([ch][KC - 1])
+        const int64_t cl = chan(0);
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-        const int64_t c = c0 + lane + 32 * i;
+        for (int q = 0; q < KC; ++q) ld_vec<CPL>(p.conv_w + cl * KC + q * CPL, &w[0][0] + q * CPL);
+        if (t0 == 0) {
 #pragma unroll
-        for (int j = 0; j < KC; ++j) w[i][j] = p.conv_w[c * KC + j];
+            for (int q = 0; q < KM1; ++q) ld_vec<CPL>(p.state + cl * KM1 + q * CPL, &win[0][0] + q * CPL);
+        } else {
 #pragma unroll
-        for (int j = 0; j < KM1; ++j)
-            // only the first chunk's window reaches into the stored state (CH > KC - 1)
-            win[i][j] = t0 == 0 ? p.state[c * KM1 + j] : p.qkv[(int64_t) (t0 - KM1 + j) * p.qkv_ld + c];
+            for (int j = 0; j < KM1; ++j) {
+                float v[CPL];
+                ld_vec<CPL>(p.qkv + (int64_t) (t0 - KM1 + j) * p.qkv_ld + cl, v);
+#pragma unroll
+                for (int i = 0; i < CPL; ++i) win[i][j] = v[i];
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int64_t c = chan(i);
+#pragma unroll
+            for (int j = 0; j < KC; ++j) w[i][j] = p.conv_w[c * KC + j];
+#pragma unroll
+            for (int j = 0; j < KM1; ++j)
+                // only the first chunk's window reaches into the stored state (CH > KC - 1)
+                win[i][j] = t0 == 0 ? p.state[c * KM1 + j] : p.qkv[(int64_t) (t0 - KM1 + j) * p.qkv_ld + c];
+        }
     }
     // the chunk's inputs, all loads in flight together (zeros past the batch: computed, never stored)
     float xs[CH][CPL];
 #pragma unroll
-    for (int u = 0; u < CH; ++u)
+    for (int u = 0; u < CH; ++u) {
+        if constexpr (CONSEC) {
+            if (t0 + u < t1) {
+                ld_vec<CPL>(p.qkv + (int64_t) (t0 + u) * p.qkv_ld + chan(0), xs[u]);
+            } else {
 #pragma unroll
-        for (int i = 0; i < CPL; ++i)
-            xs[u][i] = t0 + u < t1 ? p.qkv[(int64_t) (t0 + u) * p.qkv_ld + c0 + lane + 32 * i] : 0.0f;
+                for (int i = 0; i < CPL; ++i) xs[u][i] = 0.0f;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CPL; ++i)
+                xs[u][i] = t0 + u < t1 ? p.qkv[(int64_t) (t0 + u) * p.qkv_ld + chan(i)] : 0.0f;
+        }
+    }
     if (chunk == 0) {
         // conv-state snapshots of this lane's channels: slot s <- in[n - s .. n - s + KC - 2] (in = stored state |
         // batch), the window after n - s tokens, clamped at the start of in[]. The stored state and the chunk's
@@ -83,9 +133,10 @@ __global__ void __launch_bounds__(256, 2) gdn_input_kernel(const GdnInputParams 
             if (s >= p.n && s > 0) continue;
             const int start = max(0, p.n - s);
             float* dst = p.state + (int64_t) s * p.state_ld;
+            float sv[CPL][KM1];
 #pragma unroll
             for (int i = 0; i < CPL; ++i) {
-                const int64_t c = c0 + lane + 32 * i;
+                const int64_t c = chan(i);
 #pragma unroll
                 for (int j = 0; j < KM1; ++j) {
                     const int ii = start + j;  // index into in[]
@@ -97,8 +148,13 @@ __global__ void __launch_bounds__(256, 2) gdn_input_kernel(const GdnInputParams 
                     for (int u = 0; u < CH; ++u)
                         if (ii == KM1 + u) v = xs[u][i];
                     if (ii >= KM1 + CH) v = p.qkv[(int64_t) (ii - KM1) * p.qkv_ld + c];
-                    dst[c * KM1 + j] = v;
+                    sv[i][j] = v;
+                    if constexpr (!CONSEC) dst[c * KM1 + j] = v;
                 }
+            }
+            if constexpr (CONSEC) {
+#pragma unroll
+                for (int q = 0; q < KM1; ++q) st_vec<CPL>(dst + chan(0) * KM1 + q * CPL, &sv[0][0] + q * CPL);
             }
         }
     }
@@ -137,8 +193,12 @@ __global__ void __launch_bounds__(256, 2) gdn_input_kernel(const GdnInputParams 
             for (int i = 0; i < CPL; ++i) xs[u][i] = xs[u][i] * scale * p.inv_sqrt_s;
         }
         if (t0 + u < t1) {
+            if constexpr (CONSEC) {
+                st_vec<CPL>(out + (int64_t) (t0 + u) * out_ld + CPL * lane, xs[u]);
+            } else {
 #pragma unroll
-            for (int i = 0; i < CPL; ++i) out[(int64_t) (t0 + u) * out_ld + lane + 32 * i] = xs[u][i];
+                for (int i = 0; i < CPL; ++i) out[(int64_t) (t0 + u) * out_ld + lane + 32 * i] = xs[u][i];
+            }
         }
     }
 }
@@ -223,12 +283,24 @@ cudaError_t launch_gdn_input(const GdnInputParams& p, int S, cudaStream_t stream
     const int64_t tasks = (int64_t) n_chunks * (2 * p.H_k + p.H_v) + p.n;
     if (tasks == 0) return cudaSuccess;
     const unsigned grid = (unsigned) ((tasks + 7) / 8);
-    if (ch == 4) {
-        if (S == 64) gdn_input_kernel<2, 4><<<grid, 256, 0, stream>>>(p);
-        else gdn_input_kernel<4, 4><<<grid, 256, 0, stream>>>(p);
+    // vector accesses need 16-byte aligned buffers and row / slot strides of whole 16-byte units
+    const auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    const bool vec = a16(p.qkv) && a16(p.state) && a16(p.conv_w) && a16(p.q_out) && a16(p.k_out) && a16(p.v_out) &&
+                     p.qkv_ld % 4 == 0 && p.state_ld % 4 == 0;
+    if (vec) {
+        if (ch == 4) {
+            if (S == 64) gdn_input_kernel<2, 4, true><<<grid, 256, 0, stream>>>(p);
+            else gdn_input_kernel<4, 4, true><<<grid, 256, 0, stream>>>(p);
+        } else {
+            if (S == 64) gdn_input_kernel<2, 8, true><<<grid, 256, 0, stream>>>(p);
+            else gdn_input_kernel<4, 8, true><<<grid, 256, 0, stream>>>(p);
+        }
+    } else if (ch == 4) {
+        if (S == 64) gdn_input_kernel<2, 4, false><<<grid, 256, 0, stream>>>(p);
+        else gdn_input_kernel<4, 4, false><<<grid, 256, 0, stream>>>(p);
     } else {
-        if (S == 64) gdn_input_kernel<2, 8><<<grid, 256, 0, stream>>>(p);
-        else gdn_input_kernel<4, 8><<<grid, 256, 0, stream>>>(p);
+        if (S == 64) gdn_input_kernel<2, 8, false><<<grid, 256, 0, stream>>>(p);
+        else gdn_input_kernel<4, 8, false><<<grid, 256, 0, stream>>>(p);
     }
     return cudaGetLastError();
 }

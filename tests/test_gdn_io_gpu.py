@@ -17,16 +17,23 @@ ref_only = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not bui
 
 
 @ref_only
-@pytest.mark.parametrize("n", [1, 2, 4, 37])
-def test_gdn_input_matches_reference(kb, cuda, n):
+@pytest.mark.parametrize("n,offset", [(1, 0), (2, 0), (4, 0), (37, 0), (4, 1), (37, 1)])
+def test_gdn_input_matches_reference(kb, cuda, n, offset):
+    """16-byte aligned buffers take the vector-access kernel; qkv offset by one float takes the strided one."""
     import torch
 
     qkv, cs, w, br, al, dt, a = make_gdn_io_inputs(50 + n, n)
     cs_ref = cs.copy()
     ref = O.ref_gdn_input(qkv, cs_ref, w, br, al, dt, a, 128, 16, 1e-6)
-    t = lambda x: torch.from_numpy(x).to(cuda)
+
+    def t(x, off=0):
+        buf = torch.zeros(x.size + off, dtype=torch.float32, device=cuda)
+        buf[off:] = torch.from_numpy(np.ascontiguousarray(x).reshape(-1)).to(cuda)
+        return buf[off:].view(x.shape)
+
     cs_gpu = t(cs)
-    q, k, v, beta, g = kb.gdn_input(t(qkv), cs_gpu, t(w), 128, 16, 1e-6, beta_raw=t(br), alpha=t(al), dt_bias=t(dt),
+    qkv_gpu = t(qkv, offset)
+    q, k, v, beta, g = kb.gdn_input(qkv_gpu, cs_gpu, t(w), 128, 16, 1e-6, beta_raw=t(br), alpha=t(al), dt_bias=t(dt),
                                     a=t(a))
     torch.cuda.synchronize()
     assert kb.device_error() == 0
@@ -59,3 +66,21 @@ def test_gdn_gated_norm_matches_reference(kb, cuda, n, H, S, offset):
     out = kb.gdn_gated_norm(dev(x), dev(z), dev(w), 1e-6)
     torch.cuda.synchronize()
     assert np.abs(out.cpu().numpy() - ref).max() <= 2e-6 * np.abs(ref).max()
+
+
+def test_gdn_io_golden_fixture_s64(kb, cuda):
+    """The committed reference outputs (S 64, 2 key / 4 value heads, 3 tokens): the input side and the gated norm."""
+    import torch
+
+    g = dict(np.load(os.path.join(GOLD, "gdn_io.npz")))
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+    cs = t(g["conv_state"])
+    q, k, v, beta, gg = kb.gdn_input(t(g["qkv"]), cs, t(g["conv_w"]), 64, 2, 1e-6, beta_raw=t(g["beta_raw"]),
+                                     alpha=t(g["alpha"]), dt_bias=t(g["dt_bias"]), a=t(g["a"]))
+    o = kb.gdn_gated_norm(t(g["x"]), t(g["z"]), t(g["norm_w"]), 1e-6)
+    torch.cuda.synchronize()
+    assert kb.device_error() == 0
+    for x, name in ((q, "q"), (k, "k"), (v, "v"), (beta, "beta"), (gg, "g"), (o, "o")):
+        y = g[name]
+        assert np.abs(x.cpu().numpy().reshape(y.shape) - y).max() <= 2e-6 * np.abs(y).max(), name
+    assert np.array_equal(cs.cpu().numpy(), g["conv_state_out"])
