@@ -121,3 +121,97 @@ def test_set_rows_and_rollback_validate(kb):
     assert L.kb_rollback_recurrent(1, f(64), 64, f(64), kb.F16, f(64), 64, 0, 4, None) == kb.KB_OK  # s = 0: no-op
     assert L.kb_rollback_recurrent(1, f(64), 64, f(64), kb.F16, f(64), 64, 4, 4, None) == kb.KB_ERR_ARG
     assert L.kb_rollback_recurrent(1, f(64), 64, f(64), 99, f(64), 64, 1, 4, None) == kb.KB_ERR_UNSUPPORTED
+
+
+def test_gated_and_push_reject_bad_arguments(kb):
+    L = kb.lib()
+    prm = kb.fa_params(1 / 16)
+    a = _fa_args(kb)
+    by = ctypes.byref
+    gate = kb.kb_tensor(1 << 20, kb.F32, [256, 24, 4, 1], [4, 256 * 4, 24 * 256 * 4, 4 * 24 * 256 * 4])
+    call = lambda g: L.kb_flash_attn_ext_gated(by(a["q"]), by(a["k"]), by(a["v"]), None, by(prm), g, by(a["dst"]),
+                                               None, 0, None)
+    assert call(None) == kb.KB_ERR_ARG
+    bad = kb.kb_tensor(1 << 20, kb.F32, [256, 24, 3, 1], [4, 256 * 4, 24 * 256 * 4, 3 * 24 * 256 * 4])
+    assert call(by(bad)) == kb.KB_ERR_BAD_SHAPE  # gate must have the output's shape
+    gate.type = kb.F16
+    assert call(by(gate)) == kb.KB_ERR_BAD_SHAPE
+    # push: peers, ranks and the packed partial size are checked first
+    rows, D = 4 * 24, 256
+    pf = rows * D + rows * 2
+    ptrs = (ctypes.POINTER(ctypes.c_float) * 2)()
+    flags = (ctypes.POINTER(ctypes.c_int32) * 2)()
+    push = lambda part, rank, n: L.kb_flash_attn_ext_push(by(a["q"]), by(a["k"]), by(a["v"]), None, by(prm), part, ptrs,
+                                                         2 * pf, flags, rank, n, None, 0, None)
+    assert push(pf, 2, 2) == kb.KB_ERR_ARG  # rank out of range
+    assert push(pf - 4, 0, 2) == kb.KB_ERR_BAD_SHAPE  # part smaller than o + (m, l)
+    assert push(pf, 0, 2) == kb.KB_ERR_ARG  # null gather buffers
+    assert L.kb_flash_attn_ext_push_scratch_bytes(by(a["q"]), by(a["k"]), by(a["v"]), by(prm)) >= \
+        L.kb_flash_attn_ext_scratch_bytes(by(a["q"]), by(a["k"]), by(a["v"]), by(prm))
+
+
+def _prologue_args(torch, kb, n=2, nh=24, nkv=4, hd=256, cache_dtype=None, cache_type=None):
+    qfull, kcur, vcur = torch.zeros(n, nh * 2 * hd), torch.zeros(n, nkv * hd), torch.zeros(n, nkv * hd)
+    pos, kv_idx = torch.zeros(4 * n, dtype=torch.int32), torch.arange(n, dtype=torch.int64)
+    qn = torch.ones(hd)
+    cache = torch.zeros(8, nkv * hd, dtype=cache_dtype or torch.float16)
+    c = kb.cache_rows(cache, cache_type if cache_type is not None else kb.F16)
+    return [qfull, kcur, vcur, pos, kv_idx, qn, qn], c, cache
+
+
+@no_gpu
+def test_prologue_validates(kb):
+    import torch
+
+    def status(args, c, n_rot=64, mode=40, vc=None):
+        try:
+            kb.attn_prologue(*args, 1e-6, n_rot, [11, 11, 10, 0], mode, 1e7, c, vc or c, stream=0)
+        except kb.KbError as e:
+            return e.status
+        return kb.KB_OK
+
+    args, c, _keep = _prologue_args(torch, kb)
+    assert status(args, c) == kb.KB_ERR_CUDA  # validation passed; no device here
+    assert status(args, c, n_rot=32) == kb.KB_ERR_UNSUPPORTED  # pairs must fill whole warps
+    assert status(args, c, mode=0) == kb.KB_ERR_UNSUPPORTED  # M-RoPE modes only
+    bad = list(args)
+    bad[3] = torch.zeros(8, dtype=torch.int64)  # positions are i32
+    assert status(bad, c) == kb.KB_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[1] = torch.zeros(2, 1000)  # K width not a multiple of the head dim
+    assert status(bad, c) == kb.KB_ERR_BAD_SHAPE
+    _, c32, _k32 = _prologue_args(torch, kb, cache_dtype=torch.float32, cache_type=kb.F32)
+    assert status(args, c32) == kb.KB_ERR_UNSUPPORTED  # caches are f16, q8_0 or q4_0
+    q4 = torch.zeros(8, 4 * 8 * 18, dtype=torch.uint8)
+    assert status(args, c, vc=kb.cache_rows(q4, kb.Q4_0)) == kb.KB_ERR_UNSUPPORTED  # K and V of one type
+    assert status(args, kb.cache_rows(q4, kb.Q4_0)) == kb.KB_ERR_CUDA
+
+
+@no_gpu
+def test_gdn_io_validates(kb):
+    import torch
+
+    S, H_k, H_v, n = 128, 16, 48, 2
+    ch = 2 * S * H_k + S * H_v
+    qkv, state, w = torch.zeros(n, ch), torch.zeros(4, 3 * ch), torch.zeros(ch, 4)
+
+    def status(fn):
+        try:
+            fn()
+        except kb.KbError as e:
+            return e.status
+        return kb.KB_OK
+
+    assert status(lambda: kb.gdn_input(qkv, state, w, S, H_k, 1e-6, stream=0)) == kb.KB_ERR_CUDA
+    assert status(lambda: kb.gdn_input(qkv, state, torch.zeros(ch, 3), S, H_k, 1e-6, stream=0)) == \
+        kb.KB_ERR_UNSUPPORTED  # conv kernel width 4 only
+    assert status(lambda: kb.gdn_input(qkv, torch.zeros(4, 3 * ch - 3), w, S, H_k, 1e-6, stream=0)) == \
+        kb.KB_ERR_BAD_SHAPE
+    # 40 key heads leave no value heads: rejected before the device (the empty v output is refused first)
+    assert status(lambda: kb.gdn_input(qkv, state, w, S, 40, 1e-6, stream=0)) in (kb.KB_ERR_BAD_SHAPE,
+                                                                                 kb.KB_ERR_UNSUPPORTED)
+    x = torch.zeros(n, H_v, S)
+    assert status(lambda: kb.gdn_gated_norm(x, x, torch.ones(S), 1e-6, stream=0)) == kb.KB_ERR_CUDA
+    assert status(lambda: kb.gdn_gated_norm(x, x, torch.ones(96), 1e-6, stream=0)) == kb.KB_ERR_UNSUPPORTED
+    y = torch.zeros(n, H_v, 64)
+    assert status(lambda: kb.gdn_gated_norm(y, y, torch.ones(S), 1e-6, stream=0)) == kb.KB_ERR_BAD_SHAPE
