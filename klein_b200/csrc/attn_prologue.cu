@@ -77,8 +77,15 @@ __global__ void __launch_bounds__(256) attn_prologue_kernel(const PrologueParams
         // the gate half, copied as it is
         const float* gsrc = src + HD;
         float* gdst = p.gate_out + ((int64_t) t * p.nh + r) * HD;
+        if (p.gate_vec) {
+            // HD / 4 units of 16 bytes (offsets 2 hd * 4 r + hd * 4 and hd * 4 (t nh + r) keep them aligned)
 #pragma unroll
-        for (int k = 0; k < EPL; ++k) gdst[lane + 32 * k] = gsrc[lane + 32 * k];
+            for (int u = lane; u < HD / 4; u += 32)
+                reinterpret_cast<float4*>(gdst)[u] = reinterpret_cast<const float4*>(gsrc)[u];
+        } else {
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) gdst[lane + 32 * k] = gsrc[lane + 32 * k];
+        }
     }
     if (!is_v) {
         // RMS norm: the sum of squares of float products, accumulated in double as ggml does

@@ -770,6 +770,8 @@ kb_status kb_attn_prologue(const kb_tensor* qfull, const kb_tensor* kcur, const 
     p.k_norm = static_cast<const float*>(k_norm->data);
     p.q_out = static_cast<float*>(q_out->data);
     p.gate_out = static_cast<float*>(gate_out->data);
+    p.gate_vec = aligned16(reinterpret_cast<uintptr_t>(qfull->data)) && aligned16(qfull->nb[1]) &&
+                 aligned16(reinterpret_cast<uintptr_t>(gate_out->data));
     p.k_cache = static_cast<char*>(k_cache->data);
     p.v_cache = static_cast<char*>(v_cache->data);
     p.kc_nb1 = (int64_t) k_cache->nb[1];

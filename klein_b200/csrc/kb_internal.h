@@ -133,7 +133,8 @@ struct PrologueParams {
     char* k_cache;                   // f16 / q8_0 rows of nkv * hd values
     char* v_cache;
     int64_t kc_nb1, vc_nb1, n_cells;
-    int cache_type;                  // KB_TYPE_F16 or KB_TYPE_Q8_0
+    int cache_type;                  // KB_TYPE_F16, KB_TYPE_Q8_0 or KB_TYPE_Q4_0
+    int gate_vec;                    // qfull and gate_out 16-byte aligned (rows too): the gate is copied in 16 B units
     int n, nh, nkv;
     float eps;
     int n_rot, sect_dims, imrope;

@@ -16,10 +16,15 @@ from make_golden import PROLOGUE_ROPE, make_prologue_inputs  # noqa: E402
 ref_only = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
 
 
-def run(kb, cuda, inputs, cache_type, n_cells=64):
+def run(kb, cuda, inputs, cache_type, n_cells=64, offset=0):
+    """offset: qfull placed one float past a 16-byte boundary (offset 1) takes the 4-byte gate copy."""
     import torch
 
     qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm = [torch.from_numpy(x).to(cuda) for x in inputs]
+    if offset:
+        buf = torch.zeros(qfull.numel() + offset, dtype=torch.float32, device=cuda)
+        buf[offset:] = qfull.reshape(-1)
+        qfull = buf[offset:].view(qfull.shape)
     row = {kb.F16: 4 * 256 * 2, kb.Q8_0: 4 * 8 * 34, kb.Q4_0: 4 * 8 * 18}[cache_type]
     kc = torch.zeros((n_cells, row), dtype=torch.uint8, device=cuda)
     vc = torch.zeros_like(kc)
@@ -31,10 +36,10 @@ def run(kb, cuda, inputs, cache_type, n_cells=64):
 
 
 @ref_only
-@pytest.mark.parametrize("n", [1, 4, 37])
-def test_prologue_f16_cache_matches_reference(kb, cuda, n):
+@pytest.mark.parametrize("n,offset", [(1, 0), (4, 0), (37, 0), (4, 1)])
+def test_prologue_f16_cache_matches_reference(kb, cuda, n, offset):
     inputs = make_prologue_inputs(100 + n, n)
-    q, gate, kc, vc = run(kb, cuda, inputs, kb.F16)
+    q, gate, kc, vc = run(kb, cuda, inputs, kb.F16, offset=offset)
     rk = np.zeros((64, 4 * 256 * 2), np.uint8)
     rv = np.zeros_like(rk)
     q_ref, gate_ref = O.ref_attn_prologue(*inputs, 1e-6, k_cache=rk, v_cache=rv, cache_type=O.GGML_F16, **PROLOGUE_ROPE)
