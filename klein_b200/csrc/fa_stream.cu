@@ -9,12 +9,13 @@
 // fattn-common.cuh:924-978). The kernel, its roles and the softmax scheme are described at namespace tc.
 //
 // f16 cache: TMA writes K blocks and V tiles straight into the swizzled layouts the MMAs read.
-// q8_0 cache: TMA brings the raw 34-byte blocks (ggml-common.h block_q8_0), dequantisation warps widen K into
-// TMEM and V into shared memory. Q is quantised to q8_0 as ggml quantises it for a q8_0 K
-// (quantize_row_q8_0_ref, ggml-quants.c:276-299) and widened to f16(q * d).
+// q8_0 / q4_0 cache: TMA brings the raw 34- or 18-byte blocks (ggml-common.h block_q8_0, block_q4_0),
+// dequantisation warps widen K into TMEM and V into shared memory. Q is quantised to q8_0 as ggml quantises it for
+// a q8_0 or q4_0 K (both have q8_0 as their vec_dot type; quantize_row_q8_0_ref, ggml-quants.c:276-299) and
+// widened to f16(q * d).
 //
 // Semantics follow ggml_compute_forward_flash_attn_ext_f16_one_chunk (ops.cpp:8842-9078): Q is rounded to
-// the K dot type (f16 for f16 K, q8_0 for q8_0 K, :8960), scores are scaled, soft-capped, masked (-inf
+// the K dot type (f16 for f16 K, q8_0 for q8_0 and q4_0 K, :8960), scores are scaled, soft-capped, masked (-inf
 // cells skipped), and a row with no visible cell yields zeros (:9066). Accumulation is f32 throughout.
 #include "kb_common.cuh"
 #include "kb_internal.h"
@@ -258,27 +259,28 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
 //
 // One CTA per (split, KV head, row chunk). The rows of a chunk are the N columns (16 or 32) of S^T = K Q^T,
 // computed for 128 cells at a time (M = 128): every K and V byte is read by the tensor core once per CTA, and the
-// softmax needs no per-row exchange within a thread. Roles (q8_0: 16 warps; f16: 8 warps, no dequantisation):
+// softmax needs no per-row exchange within a thread. Roles (q8_0 / q4_0: 16 warps; f16: 8 warps, no
+// dequantisation):
 //   warps 0-3   softmax, thread = cell (TMEM lane) of the 128-cell block: x = score - row max against row maxima
 //               kept in shared memory (+inf for a row that has seen nothing), one barrier reduction per block to
 //               check max x <= 8 (log2 units, so P <= 2^8 in f16); when a row max rises the scores are re-read
 //               from TMEM, the maxima recomputed, O^T and the partial sums rescaled. P^T as f16 into shared
 //               memory; partial row sums per thread, summed once at the end
-//   q8_0 only:
-//   warps 4-7   K dequantisation, thread = cell: its raw q8_0 row (17 aligned 16-byte loads) -> 256 f16 values
-//               f16(q * d) -> TMEM, the A operand of S^T (TS form)
+//   q8_0 / q4_0 only:
+//   warps 4-7   K dequantisation, thread = cell: its raw row (aligned 16-byte loads: 272 B for q8_0, 144 B for
+//               q4_0) -> 256 f16 values f16(q * d) (q4_0: (n - 8) * d) -> TMEM, the A operand of S^T (TS form)
 //   warps 8-11  V dequantisation: raw tile -> f16 [64 cells][256 dims] swizzled tile, the A operand V^T of O^T
 //               (bank-conflict-free assignment: 8 consecutive cells x 4 blocks per warp instruction)
-//   then (q8_0 warps 12-15, f16 warps 4-7):
-//               TMA producers of K and V (q8_0: raw tile rings of 4 and 3; f16: two 128-cell K blocks, the SS-form
+//   then (quantised: warps 12-15, f16: warps 4-7):
+//               TMA producers of K and V (quantised: raw tile rings of 4 and 3; f16: two 128-cell K blocks, the SS-form
 //               A operand of S^T, and two 64-cell V tiles)
 //               S issuer: S^T_j = K_j Q^T (16 MMAs of K 16) into buffer j % 2 once the softmax has read S_{j-2}
 //               PV issuer: O^T += V^T P^T of block j (2 M-halves x 4 K-steps per 64-cell tile) once P_j is
 //               written. Two issuers: the tensor core accepts only a few MMAs ahead, so one thread would hold
 //               S_{j+2} back behind the 16 PV MMAs of block j.
-// TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), q8_0: K f16 2 x 128 at 128.
-// Numerics: f16 K: Q rounded to f16; q8_0 K: Q quantised to q8_0 and widened to f16(q * d), K and V widened to
-// f16(q * d). f32 accumulation, P rounded to f16.
+// TMEM: S^T 2 x N columns at 0, O^T 2 x N at 64 (dims 0-127, 128-255 on the lanes), quantised: K f16 2 x 128 at
+// 128. Numerics: f16 K: Q rounded to f16; q8_0 / q4_0 K: Q quantised to q8_0 and widened to f16(q * d), K and V
+// widened to f16 of their dequantised values. f32 accumulation, P rounded to f16.
 namespace tc {
 constexpr int BLK = 128;  // cells per S^T block
 constexpr int KRAW = 4, VRAW = 3;
@@ -286,8 +288,7 @@ constexpr int KRAW = 4, VRAW = 3;
 // carry tiles of one parity: with an odd depth a pair could wait for a phase two ahead of the slot's current one
 // and pass it at once (a parity wait sees only the last two phases).
 static_assert(KRAW % 2 == 0, "K ring slots carry tiles of one parity");
-// warp roles: q8_0 adds the 8 dequantisation warps (4-11)
-// cache kinds of the kernel
+// cache kinds of the kernel (q8_0 and q4_0 add the 8 dequantisation warps 4-11)
 constexpr int KT_F16 = 0, KT_Q8 = 1, KT_Q4 = 2;
 template <int KT>
 constexpr int raw_row() { return KT == KT_Q8 ? QROW : Q4ROW; }
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
             mbar_init(&sm.vempty[s], 4);
         }
         for (int s = 0; s < 2; ++s) {
-            // q8_0: the 4 dequantisation warps of each kind arrive; f16: the TMA transaction counts
+            // quantised: the 4 dequantisation warps of each kind arrive; f16: the TMA transaction counts
             mbar_init(&sm.k_full[s], Q8 ? 4 : 1);
             mbar_init(&sm.k_free[s], 1);
             mbar_init(&sm.s_full[s], 1);
@@ -486,7 +487,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
         const float qv = roundf(x * id);
         const float dh = __half2float(__float2half_rn(d));
         const int dim = 32 * blk + lane, e = dim & 63;
-        // q8_0 K: Q rounded to q8_0 (ggml's vec_dot type for q8_0), then f16(q * d); f16 K: Q rounded to f16
+        // q8_0 / q4_0 K: Q rounded to q8_0 (ggml's vec_dot type for both), then f16(q * d); f16 K: Q rounded to f16
         *reinterpret_cast<__half*>(sm.q[dim >> 6] + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
             __float2half_rn(Q8 ? qv * dh : x);
     }
