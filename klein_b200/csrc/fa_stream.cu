@@ -30,7 +30,6 @@ constexpr int D = FA_D;
 constexpr int TILE = FA_TILE;
 constexpr int KTILE_F16 = TILE * D * 2;        // 32 KiB: 4 boxes of [64 cells][64 dims] f16, 128B-swizzled
 constexpr int QROW = D / 32 * 34;              // bytes of one head's row in a q8_0 cache (272)
-constexpr int QTILE_RAW = TILE * QROW;         // 17,408 B of raw blocks per tile
 constexpr int Q4ROW = D / 32 * 18;             // bytes of one head's row in a q4_0 cache (144)
 
 __device__ __forceinline__ float slope_of(const FaStreamParams& p, int h) {

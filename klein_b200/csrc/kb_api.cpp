@@ -817,7 +817,7 @@ kb_status kb_gdn_input(const kb_tensor* qkv, const kb_tensor* conv_state, const 
         for (const kb_tensor* t : {beta_raw, alpha, dt_bias, a, beta_out, g_out})
             if (!contiguous_f32(t)) return KB_ERR_UNSUPPORTED;
         for (const kb_tensor* t : {beta_raw, alpha, beta_out, g_out})
-            if (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != H_v * n || t->ne[0] != H_v && t->ne[1] != H_v)
+            if (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != H_v * n || (t->ne[0] != H_v && t->ne[1] != H_v))
                 return KB_ERR_BAD_SHAPE;
         if (dt_bias->ne[0] * dt_bias->ne[1] != H_v || a->ne[0] * a->ne[1] != H_v) return KB_ERR_BAD_SHAPE;
     }
