@@ -44,7 +44,8 @@ def test_golden_q4_0_set_rows_bit_exact():
 
 def test_golden_f16_conversion_bit_exact():
     g = gold("cpy_f32_f16")
-    assert np.array_equal(g["x"].astype(np.float16).view(np.uint16), g["y"])
+    with np.errstate(over="ignore"):  # the fixture holds values beyond f16's range on purpose (they become inf)
+        assert np.array_equal(g["x"].astype(np.float16).view(np.uint16), g["y"])
     h = np.array([O.restate().rs_fp32_to_fp16(O.ctypes_float(x)) for x in g["x"]], dtype=np.uint16)
     assert np.array_equal(h, g["y"])
 
