@@ -76,10 +76,12 @@ def _worker(rank, world, port, n_q, n_kv, result_path):
     dist.destroy_process_group()
 
 
-def test_two_rank_split_matches_full(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_two_rank_split_matches_full(tmp_path, world):
+    """world ranks (2, or 4 with a ragged last range) each attend over their cells; the merge equals the whole."""
     import torch.multiprocessing as mp
 
-    n_q, n_kv, world = 4, 1000, 2
+    n_q, n_kv = 4, 1000
     out = str(tmp_path / "merged.npy")
     mp.start_processes(_worker, args=(world, _free_port(), n_q, n_kv, out), nprocs=world, start_method="spawn")
     merged = np.load(out).reshape(n_q, 24, 64)
