@@ -215,3 +215,21 @@ def test_gdn_io_validates(kb):
     assert status(lambda: kb.gdn_gated_norm(x, x, torch.ones(96), 1e-6, stream=0)) == kb.KB_ERR_UNSUPPORTED
     y = torch.zeros(n, H_v, 64)
     assert status(lambda: kb.gdn_gated_norm(y, y, torch.ones(S), 1e-6, stream=0)) == kb.KB_ERR_BAD_SHAPE
+
+
+def test_plain_c_caller(tmp_path):
+    """tests/abi_check.c: the header compiles as C11 with warnings as errors, links against the library, and the
+    calls' validation answers a C caller without a device."""
+    import shutil
+    import subprocess
+
+    lib_dir = os.path.join(ROOT, "klein_b200")
+    if not shutil.which("gcc") or not os.path.exists(os.path.join(lib_dir, "libklein_b200.so")):
+        pytest.skip("gcc or the built library is missing")
+    exe = str(tmp_path / "abi_check")
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "abi_check.c"), "-L", lib_dir, "-lklein_b200",
+                    "-Wl,-rpath," + lib_dir, "-o", exe], check=True)
+    r = subprocess.run([exe], stdout=subprocess.PIPE, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout
+    assert "abi_check: ok" in r.stdout
