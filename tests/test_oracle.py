@@ -247,6 +247,32 @@ def test_live_attn_prologue_qwen35_shapes():
     assert_f16_near(kc.view(np.float16).reshape(64, 4, 256)[kv_idx], k)
 
 
+@ref_only
+@pytest.mark.parametrize("cache_type", [O.GGML_Q8_0, O.GGML_Q4_0])
+def test_live_attn_prologue_quantised_caches(cache_type):
+    """The reference's quantised cache writes after the prologue: V rows are the restated quantisation of the input
+    rows, bit for bit; K rows that of the restated normed, roped rows, within one quantisation step."""
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import PROLOGUE_ROPE, make_prologue_inputs
+
+    qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm = make_prologue_inputs(13, 6)
+    bb = 34 if cache_type == O.GGML_Q8_0 else 18
+    kc = np.zeros((64, 4 * 8 * bb), np.uint8)
+    vc = np.zeros_like(kc)
+    O.ref_attn_prologue(qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm, 1e-6, k_cache=kc, v_cache=vc,
+                        cache_type=cache_type, **PROLOGUE_ROPE)
+    quant = O.rs_quantize_q8_0 if cache_type == O.GGML_Q8_0 else O.rs_quantize_q4_0
+    deq = O.rs_dequantize_q8_0 if cache_type == O.GGML_Q8_0 else O.rs_dequantize_q4_0
+    assert np.array_equal(vc[kv_idx], quant(vcur))
+    _, k, _ = O.rs_attn_prologue(qfull, kcur, pos, q_norm, k_norm, 1e-6, **PROLOGUE_ROPE)
+    a = deq(kc[kv_idx].reshape(-1, bb)).reshape(-1, 32)
+    b = deq(quant(k.reshape(len(kv_idx), -1).astype(np.float32)).reshape(-1, bb)).reshape(-1, 32)
+    d = np.abs(kc[kv_idx].reshape(-1, bb)[:, :2].copy().view(np.float16).astype(np.float32))
+    assert np.all(np.abs(a - b) <= 1.01 * d + 1e-30)
+    assert np.mean(a != b) < 1e-2
+
+
 # ---------------------------------------------------------------------------------------------- DeltaNet input / output sides
 
 def test_golden_gdn_io():
