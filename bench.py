@@ -63,7 +63,9 @@ def ncu_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    """nvidia-smi clock / throttle-reason samples while the timed region runs. The sampler is started and its
+    first sample awaited before the timed region begins (nvidia-smi takes ~0.5 s to start), then it samples
+    every 20 ms until the region ends."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active," \
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
@@ -72,30 +74,55 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
 
     def __enter__(self):
+        import threading
+
+        # nvidia-smi numbers the GPUs physically; map this process's device through CUDA_VISIBLE_DEVICES
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = str(self.gpu)
+        if vis:
+            ids = [x.strip() for x in vis.split(",") if x.strip()]
+            if self.gpu < len(ids):
+                idx = ids[self.gpu]
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", idx, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._reader, daemon=True)
+        self.thread.start()
+        t_end = time.time() + 5.0
+        while not self.lines and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.skip = len(self.lines)  # samples taken before the timed region
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self.proc is None:
+            return
+        time.sleep(0.05)  # one more sample at the end of the region
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+        self.thread.join(timeout=5)
+        # keep the last pre-region sample too when the region was shorter than the sampling period
+        self.lines = self.lines[max(0, getattr(self, "skip", 0) - 1):]
 
     def summary(self):
         rows = []
-        for l in getattr(self, "lines", []):
+        for l in self.lines:
             f = [x.strip() for x in l.split(",")]
             if len(f) < 10:
                 continue
@@ -122,6 +149,36 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------ CPU arm
+
+def host_cpu():
+    """(physical cores, logical CPUs, model name) of this host from /proc/cpuinfo."""
+    logical = os.cpu_count() or 1
+    model, cores, phys, core = None, set(), None, None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k, v = k.strip(), v.strip()
+                if k == "model name" and model is None:
+                    model = v
+                elif k == "physical id":
+                    phys = v
+                elif k == "core id":
+                    core = v
+                elif not k and phys is not None and core is not None:
+                    cores.add((phys, core))
+                    phys = core = None
+        if phys is not None and core is not None:
+            cores.add((phys, core))
+    except OSError:
+        pass
+    try:
+        avail = len(os.sched_getaffinity(0))
+    except AttributeError:
+        avail = logical
+    physical = len(cores) if cores else logical
+    return min(physical, avail), logical, model or "unknown"
+
 
 def cpu_verify_sample(kv_type: str, threads: int, budget_s: float, min_reps: int = 2):
     """Times ggml's CPU flash attention (the reference build in oracle/_ref) on one layer of the headline
@@ -162,7 +219,7 @@ def run_reference(args, rank: int):
         return
     import numpy as np
 
-    threads = os.cpu_count() or 1
+    threads, logical, model = host_cpu()  # ggml's CPU backend on every physical core
     rng = np.random.default_rng(7)
     q = rng.standard_normal((N_Q, H, D), dtype=np.float32)
     kc = rng.standard_normal((N_KV, H_KV * D), dtype=np.float32).astype(np.float16)
@@ -183,7 +240,9 @@ def run_reference(args, rank: int):
                                "262144-cell f16 KV cache, 24 Q / 4 KV heads, D 256 (ggml CPU flash_attn_ext)",
                    "n_kv": N_KV, "kv_type": "f16", "layers_per_step": 1},
         "cpu_baseline": {"value": round(us, 2), "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} layers of the headline workload on ggml's CPU backend"},
+                         "logical_cpus": logical, "cpu_model": model,
+                         "sample": f"{args.steps} layers of the headline workload on ggml's CPU backend, "
+                                   f"{threads} threads (one per physical core)"},
         "e2e": {"value": round(us, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -221,40 +280,69 @@ def quantize_q4_0_rows(torch, x):
     return out.view(n, k // 32 * 18)
 
 
-def bench_prefill(kb, torch, dev, steps, warmup):
-    """config[2] attention half: causal prefill of 4,096 tokens, 24 Q / 4 KV heads, D 256, bf16 Q/K/V, through
-    kb_flash_attn_ext (tcgen05 kernel). Two independent Q/K/V sets alternate so inputs exceed L2."""
-    T = 4096
+def bench_prefill(kb, torch, dev, steps, warmup, kv="bf16", T=4096, n_kv=4096):
+    """Causal prefill through kb_flash_attn_ext (tcgen05 kernel): T new tokens at positions [n_kv - T, n_kv) over an
+    n_kv-cell cache, 24 Q / 4 KV heads, D 256. bf16 Q/K/V: config[2] (T = n_kv = 4,096). q8_0: klein's 2,048-token
+    prompt chunk over the 4,096-cell cache it has just written, the call widening the visible cells to f16 in its
+    scratch first (timed as part of the call). Two independent input sets alternate so inputs exceed L2."""
+    import ctypes
+
     gen = torch.Generator(device=dev)
     gen.manual_seed(77)
     sets = []
     for _ in range(2):
-        q = torch.randn(1, T, H, D, device=dev, generator=gen).bfloat16().float()
-        k = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
-        v = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
-        sets.append((q, k, v, kb.kv_cache_view(k, kb.BF16, H_KV, D), kb.kv_cache_view(v, kb.BF16, H_KV, D)))
+        q = torch.randn(1, T, H, D, device=dev, generator=gen)
+        kf = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        vf = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        if kv == "bf16":
+            q = q.bfloat16().float()
+            k, v, t = kf.bfloat16(), vf.bfloat16(), kb.BF16
+        else:
+            k, v, t = quantize_q8_0_rows(torch, kf), quantize_q8_0_rows(torch, vf), kb.Q8_0
+        sets.append((q, k, v, kb.kv_cache_view(k, t, H_KV, D), kb.kv_cache_view(v, t, H_KV, D)))
+    pos0 = n_kv - T
     out = torch.empty(1, T, H, D, device=dev)
+    L = kb.lib()
+    q0 = sets[0][0]
+    qt = kb.kb_tensor(q0.data_ptr(), kb.F32, [D, T, H, 1], [4, H * D * 4, D * 4, T * H * D * 4])
+    prm = kb.fa_params(SCALE, causal=True, pos0=pos0)
+    need = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(sets[0][3]), ctypes.byref(sets[0][4]),
+                                             ctypes.byref(prm))
+    scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    dt = kb.kb_tensor(out.data_ptr(), kb.F32, [D, H, T, 1], [4, D * 4, H * D * 4, T * H * D * 4])
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def call(i):
+        q, _, _, kv_, vv_ = sets[i % 2]
+        qt.data = q.data_ptr()
+        rc = L.kb_flash_attn_ext(ctypes.byref(qt), ctypes.byref(kv_), ctypes.byref(vv_), None, ctypes.byref(prm),
+                                 ctypes.byref(dt), ctypes.c_void_p(scratch.data_ptr()), ctypes.c_size_t(need), st)
+        if rc != 0:
+            raise kb.KbError("kb_flash_attn_ext", rc)
+
     for i in range(warmup):
-        q, _, _, kv, vv = sets[i % 2]
-        kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0, out=out)
+        call(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(steps):
-        q, _, _, kv, vv = sets[i % 2]
-        kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0, out=out)
+        call(i)
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / steps
-    flops = 2.0 * D * H * T * (T + 1)  # causal pairs only, QK^T and PV
+    pairs = T * pos0 + T * (T + 1) // 2  # (query, visible cell) pairs
+    flops = 4.0 * D * H * pairs  # QK^T and PV over the causal pairs only
     tf = flops / (us * 1e-6) / 1e12
     pk, kind = measured_peaks()
-    return {"value": round(tf, 1), "unit": "TFLOP/s", "us_per_layer": round(us, 2), "kv_type": "bf16",
-            "workload": "config[2] causal prefill, 4096 tokens, 24 Q / 4 KV heads, D 256, bf16",
+    name = "fa_prefill_bf16_4096" if kv == "bf16" else f"fa_prefill_{kv}_{T}"
+    wl = (f"config[2] causal prefill, {T} tokens, 24 Q / 4 KV heads, D 256, bf16" if kv == "bf16" else
+          f"prompt chunk: {T} new tokens over a {n_kv}-cell {kv} cache (widened to f16 in the call), 24 Q / 4 KV "
+          f"heads, D 256")
+    return {"value": round(tf, 1), "unit": "TFLOP/s", "us_per_layer": round(us, 2), "kv_type": kv, "workload": wl,
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tf / pk["bf16_tflops"], 4), "peak_kind": kind + " burst",
                          "frac_of_sustained": round(tf / pk.get("bf16_tflops_sustained", pk["bf16_tflops"]), 4),
-                         "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic("fa_prefill_bf16_4096")}}
+                         "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic(name)}}
 
 
 def bench_gdn(kb, torch, dev, steps, warmup):
@@ -452,6 +540,99 @@ def make_layers(kb, torch, dev, gen, n_kv, kv_type):
     return layers
 
 
+PARITY_N_KV = 32768  # cells of the sequence-split parity check (4,096 per rank at N = 8)
+
+
+def exact_attention_f64(q, k, v, pos0, scale=SCALE):
+    """Exact causal attention in float64 (numpy): q [n_q][H][D], k / v [n_kv][H_kv][D], query i sees cells
+    [0, pos0 + i]. The checker of the sequence-split parity run (ggml's flash-attention semantics, ops.cpp:8842-9078,
+    with Q rounded to f16 beforehand by the caller)."""
+    import numpy as np
+
+    n_q, h, d = q.shape
+    g = h // k.shape[1]
+    out = np.zeros((n_q, h, d))
+    vis = np.arange(k.shape[0])[None, :] <= (pos0 + np.arange(n_q))[:, None]
+    for hh in range(h):
+        s = (q[:, hh].astype(np.float64) @ k[:, hh // g].T.astype(np.float64)) * scale
+        s = np.where(vis, s, -np.inf)
+        p = np.exp(s - s.max(1, keepdims=True))
+        out[:, hh] = (p @ v[:, hh // g].astype(np.float64)) / p.sum(1, keepdims=True)
+    return out
+
+
+def split_parity(kb, torch, dev, args, rank, world, xchg, dist):
+    """Correctness of the timed path at this N, before timing: the same per-rank calls and the same exchange
+    (push kernel, fused push or NCCL) on a PARITY_N_KV-cell f16 cache split the same way; every rank's merged
+    output must be identical, and rank 0's is compared with exact attention over the whole cache."""
+    import ctypes
+
+    import numpy as np
+
+    from klein_b200.kv_split import kv_range, local_bounds, packed_part_floats
+
+    n_kv = PARITY_N_KV
+    rng = np.random.default_rng(2024)  # the same cache and queries on every rank
+    q = rng.standard_normal((N_Q, H, D), dtype=np.float32)
+    kc = rng.standard_normal((n_kv, H_KV * D), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((n_kv, H_KV * D), dtype=np.float32).astype(np.float16)
+    lo, hi = kv_range(n_kv, world, rank)
+    kt = torch.from_numpy(kc[lo:hi].copy()).to(dev)
+    vt = torch.from_numpy(vc[lo:hi].copy()).to(dev)
+    kv, vv = kb.kv_cache_view(kt, kb.F16, H_KV, D), kb.kv_cache_view(vt, kb.F16, H_KV, D)
+    pos0, kv_lo = local_bounds(lo, n_kv - N_Q, 0)
+    qd = torch.from_numpy(q).to(dev).unsqueeze(0)
+    out = torch.zeros(1, N_Q, H, D, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    rows = N_Q * H
+    kb.device_error(clear=True)
+    if world == 1:
+        kb.flash_attn_ext(qd, kv, vv, SCALE, causal=True, pos0=pos0, out=out)
+    elif args.exchange == "fused":
+        L = kb.lib()
+        qt = kb.kb_tensor(qd.data_ptr(), kb.F32, [D, N_Q, H, 1], [4, H * D * 4, D * 4, N_Q * H * D * 4])
+        prm = kb.fa_params(SCALE, causal=True, pos0=pos0, kv_lo=kv_lo)
+        nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv),
+                                                    ctypes.byref(prm))
+        scratch = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+        xchg.attend_and_combine(qt, kv, vv, prm, scratch.data_ptr(), nb, rows, D, out.data_ptr(), st)
+    else:
+        part = torch.empty(packed_part_floats(rows, D), device=dev)
+        kb.flash_attn_ext_partial(qd, kv, vv, SCALE, part, causal=True, pos0=pos0, kv_lo=kv_lo)
+        if xchg is not None:
+            xchg.exchange_and_combine(part.data_ptr(), rows, D, out.data_ptr(), st)
+        else:
+            gathered = torch.empty(world * part.numel(), device=dev)
+            dist.all_gather_into_tensor(gathered, part)
+            rc = kb.lib().kb_lse_combine(ctypes.c_void_p(gathered.data_ptr()),
+                                         ctypes.c_void_p(gathered.data_ptr() + rows * D * 4), ctypes.c_int64(part.numel()),
+                                         world, ctypes.c_int64(rows), D, ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(st))
+            if rc != 0:
+                raise kb.KbError("kb_lse_combine", rc)
+    torch.cuda.synchronize()
+    code = kb.device_error(clear=True)
+    spread = 0.0
+    if world > 1:
+        ref = out.clone()
+        dist.broadcast(ref, src=0)
+        d = torch.tensor([float((out - ref).abs().max())], device=dev)
+        dist.all_reduce(d, op=dist.ReduceOp.MAX)
+        c = torch.tensor([float(code)], device=dev)
+        dist.all_reduce(c, op=dist.ReduceOp.MAX)
+        spread, code = float(d.item()), int(c.item())
+    res = {"n": world, "n_kv": n_kv, "exchange": args.exchange if world > 1 else "none",
+           "ranks_max_abs_diff": spread, "device_error": code}
+    if rank == 0:
+        qr = q.astype(np.float16).astype(np.float32)  # Q as the f16 K dot type sees it (ops.cpp:8960)
+        exact = exact_attention_f64(qr, kc.astype(np.float32).reshape(n_kv, H_KV, D),
+                                    vc.astype(np.float32).reshape(n_kv, H_KV, D), n_kv - N_Q)
+        gpu = out[0].cpu().numpy().astype(np.float64)
+        res["e_gpu"] = float(np.abs(gpu - exact).max() / np.abs(exact).max())
+        res["ok"] = bool(res["e_gpu"] <= 2e-3 and code == 0 and spread == 0.0)
+    return res
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int):
     import ctypes
 
@@ -558,6 +739,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         graphs.append(g)
         return g.replay
 
+    parity = split_parity(kb, torch, dev, args, rank, world, xchg, dist if world > 1 else None)
+
     graphs = []
     for _ in range(args.warmup):
         step(st)
@@ -662,7 +845,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 "roofline": {"bound": "hbm", "achieved": round(qbytes / (q_us * 1e-6) / 1e9, 1), "peak": pk["hbm_gbs"],
                              "unit": "GB/s", "frac": round(qbytes / (q_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
                              "algorithmic_bytes_per_launch": qbytes,
-                             "traffic": ncu_traffic(f"fa_stream_{kvt}_verify262k")}}
+                             # ncu DRAM bytes of one full-cache launch; a rank of an N-way split streams 1/N of it
+                             "traffic": (lambda t: None if t is None else int(t / world))(
+                                 ncu_traffic(f"fa_stream_{kvt}_verify262k"))}}
 
     peaks, peak_kind = measured_peaks()
     bytes_layer = kv_bytes_per_layer(n_kv, "f16")
@@ -682,6 +867,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                      "traffic": (lambda t: None if t is None else int(t / world))(ncu_traffic("fa_stream_f16_verify262k")),
                      "algorithmic_bytes_per_launch": bytes_layer},
         "gpu_launches": launches,
+        "parity": parity,
         "e2e": {"value": round(e2e_ms * 1e3 / (args.steps * LAYERS), 2), "unit": UNIT,
                 "h2d_bytes_per_step": LAYERS * N_Q * H * D * 4, "d2h_bytes_per_step": LAYERS * N_Q * H * D * 4},
         "clocks": clk.summary(),
@@ -691,6 +877,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         del layers[:]
         torch.cuda.empty_cache()
         secondary["prefill_bf16_4096"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
+        secondary["prefill_q8_0_2048"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup,
+                                                       kv="q8_0", T=2048, n_kv=4096)
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["io_ops"] = bench_io_ops(kb, torch, dev, max(20, args.steps // 2), args.warmup)
@@ -700,11 +888,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         import oracle as O
 
         if O.ref_available():
-            threads = os.cpu_count() or 1
+            threads, logical, model = host_cpu()  # one thread per physical core
             us_cpu, reps = cpu_verify_sample("f16", threads, args.cpu_budget)
             line["cpu_baseline"] = {"value": round(us_cpu, 1), "unit": UNIT, "cores": threads, "kind": "reference",
+                                    "logical_cpus": logical, "cpu_model": model,
                                     "sample": f"{reps} single layers of the headline workload (ggml CPU flash_attn_ext, "
-                                              f"262144 f16 cells, 4 tokens), median"}
+                                              f"262144 f16 cells, 4 tokens), median, {threads} threads"}
         else:
             line["cpu_baseline"] = None
     if rank == 0:
@@ -737,6 +926,13 @@ def run_case(case: str):
         v = torch.randn(T, H_KV * D, device=dev, generator=gen).bfloat16()
         kv, vv = kb.kv_cache_view(k, kb.BF16, H_KV, D), kb.kv_cache_view(v, kb.BF16, H_KV, D)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=0)
+    elif case == "prefill_q8_0_2048":
+        T, n_kv = 2048, 4096
+        q = torch.randn(1, T, H, D, device=dev, generator=gen)
+        k = quantize_q8_0_rows(torch, torch.randn(n_kv, H_KV * D, device=dev, generator=gen))
+        v = quantize_q8_0_rows(torch, torch.randn(n_kv, H_KV * D, device=dev, generator=gen))
+        kv, vv = kb.kv_cache_view(k, kb.Q8_0, H_KV, D), kb.kv_cache_view(v, kb.Q8_0, H_KV, D)
+        run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - T)
     elif case in ("gdn_prefill_4096", "gdn_verify"):
         T = 4096 if case == "gdn_prefill_4096" else 4
         rng = np.random.default_rng(3)
@@ -791,7 +987,7 @@ def main():
                     help="N > 1: partials exchange over NVLink peer stores by a push kernel (default), by the split "
                          "combine itself (fused), or an NCCL all-gather")
     ap.add_argument("--case", default=None,
-                    choices=["prefill_bf16_4096", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
+                    choices=["prefill_bf16_4096", "prefill_q8_0_2048", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
                              "verify_q4_0", "gdn_input_4096"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()

@@ -77,15 +77,21 @@ typedef struct kb_fa_params {
  * GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext, ggml.h:2476-2495; CPU semantics ops.cpp:8842-9574;
  * replaces ggml_cuda_flash_attn_ext, ggml-cuda/fattn.cu:758-772).
  *   q    f32  [D, n_q, H, ne3]       any byte strides (klein passes a permuted view, graph.cpp:118)
- *   k, v f16/q8_0/q4_0 [D, n_kv, H_kv, ne3k]  nb[0] = element size (block size 34 for q8_0, 18 for q4_0);
+ *   k, v f16/bf16/q8_0/q4_0 [D, n_kv, H_kv, ne3k]  nb[0] = element size (block size 34 for q8_0, 18 for q4_0);
  *                                    H % H_kv == 0,
  *                                    ne3 % ne3k == 0; base and nb[1..3] multiples of 16 bytes
  *   mask f16  [n_kv, >= n_q, ne32, ne33] contiguous, or NULL; broadcast over heads as in ggml
  *   dst  f32  [D, H, n_q, ne3]       ("permuted" result); nb[0] = 4
  * Head h reads KV head h / (H / H_kv). A row whose every cell is masked produces zeros.
  * scratch: device memory of at least kb_flash_attn_ext_scratch_bytes(...) bytes (may be NULL when that
- * is 0). Supported here: D = 256, K and V of the same type (f16, q8_0 or q4_0). Over a q8_0 or q4_0 cache Q is
- * rounded to q8_0 first (the vec_dot type of both in ggml's CPU backend).
+ * is 0). Supported here: D = 256, K and V of the same type (f16, bf16, q8_0 or q4_0; bf16 for n_q >= 128 only).
+ * Over a q8_0 or q4_0 cache Q is rounded to q8_0 first (the vec_dot type of both in ggml's CPU backend).
+ * Kernels: n_q >= 128 (prompt chunks) runs the tensor-core prefill kernel. Over a q8_0 / q4_0 cache it first
+ * widens the cells the queries can see into an f16 copy in the scratch (as ggml-cuda converts K and V to f16
+ * for its MMA kernel, fattn-common.cuh:1031-1090); given less scratch than kb_flash_attn_ext_scratch_bytes
+ * asks for but enough for the split partials, such a call runs on the streaming kernel instead (same result
+ * within the parity bound, slower). Fewer query tokens (decode, the verify step), the MTP ring and
+ * kb_flash_attn_ext_partial run the streaming kernel.
  */
 kb_status kb_flash_attn_ext(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                             const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
@@ -165,7 +171,9 @@ kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const k
                                  void* scratch, size_t scratch_bytes, void* stream);
 
 /* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
- * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756). */
+ * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756): the split partials of the
+ * streaming kernel (at most SM count x 32 rows x (256 + 2) x 4 bytes, ~4.9 MB on a 148-SM B200) and, for
+ * n_q >= 128 over a q8_0 / q4_0 cache, the two f16 views (ne3 x n_kv x H_kv x 1,024 bytes). */
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                        const kb_fa_params* params);
 
@@ -304,10 +312,13 @@ kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_ten
  * and foreign-language bindings that pass raw pointers but have no device allocator. Same operands,
  * semantics and errors as kb_flash_attn_ext, but the split-KV partials live in a fixed buffer of
  * KB_NOALLOC_SCRATCH_BYTES compiled into the library, so the call itself allocates nothing.
- *   - A call that would need more partials than the buffer holds returns KB_ERR_SCRATCH
- *     (kb_flash_attn_ext_scratch_bytes gives the need; 262,144 cells x 4 tokens x 24/4 heads needs ~3.7 MB).
- *   - The first call on each device looks up the buffer's device address (cudaGetSymbolAddress); make
- *     that first call before any stream capture on that device.
+ *   - A call that would need more partials than the buffer holds returns KB_ERR_SCRATCH. The split
+ *     partials never exceed SM count x 32 rows x (256 + 2) x 4 bytes (~4.9 MB on a 148-SM B200, e.g.
+ *     262,144 cells x 4 tokens x 24/4 heads). Prompt-length calls over a q8_0 / q4_0 cache, whose f16
+ *     views do not fit, run on the streaming kernel.
+ *   - Every call looks up the buffer's device address (cudaGetSymbolAddress once per device, cached);
+ *     make the first call on a device before any stream capture on that device. The cache assumes each
+ *     device's primary context for the life of the process (no cudaDeviceReset in between).
  *   - All calls on a device share the buffer: calls that overlap on the GPU (other streams, other host
  *     threads) race on it and must be serialised by the caller. Nothing in it needs clearing between calls.
  * This entry point has no counterpart in the reference (ggml-cuda always draws scratch from its pool).

@@ -213,13 +213,14 @@ def fa_params(scale: float, max_bias=0.0, softcap=0.0, causal=False, pos0=0, kv_
 
 
 def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bias=0.0, softcap=0.0, causal=False,
-                   pos0=0, kv_lo=0, ring=0, out=None, stream=None, gate=None):
+                   pos0=0, kv_lo=0, ring=0, out=None, stream=None, gate=None, scratch_bytes=None):
     """GGML_OP_FLASH_ATTN_EXT through kb_flash_attn_ext.
 
     q: torch f32 on the GPU, token-major [ne3][n_q][H][D] (or [n_q][H][D]); passed as klein's permuted
     view [D, n_q, H, ne3]. k, v: kb_tensor cache views (kv_cache_view). mask: torch f16 [n_q'][n_kv] or
     None. Returns f32 [ne3][n_q][H][D] (ggml's permuted result [D, H, n_q, ne3]). gate: torch f32 of the output's
-    shape, or None; with a gate the result is o * sigmoid(gate) (kb_flash_attn_ext_gated).
+    shape, or None; with a gate the result is o * sigmoid(gate) (kb_flash_attn_ext_gated). scratch_bytes: the
+    scratch to pass (default: kb_flash_attn_ext_scratch_bytes).
     """
     import torch
 
@@ -239,6 +240,8 @@ def flash_attn_ext(q, k: KbTensor, v: KbTensor, scale: float, mask=None, max_bia
     prm = fa_params(scale, max_bias, softcap, causal, pos0, kv_lo, ring)
     L = lib()
     nbytes = L.kb_flash_attn_ext_scratch_bytes(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), ctypes.byref(prm))
+    if scratch_bytes is not None:
+        nbytes = scratch_bytes
     scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     st = torch.cuda.current_stream(q.device).cuda_stream if stream is None else stream
     if gate is not None:

@@ -13,6 +13,8 @@
 // between calls; a call whose bounded wait ran out leaves its output undefined (see kb_device_error).
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "../../include/klein_b200.h"
 #include "kb_internal.h"
 
@@ -22,23 +24,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[KB_NOALLOC_SCRA
 
 // Device address of g_noalloc_scratch on the current device. In host code the array's name only stands for
 // the symbol, so the address must come from cudaGetSymbolAddress, once per device, with that device current.
+// The cache is keyed on the device ordinal: the library assumes each device's primary context for the life of
+// the process (no cudaDeviceReset, no other current context). Threads that race on the first lookup store the
+// same address; the atomics make that explicit.
 void* scratch_address(kb_status* st) {
-    static void* addr[64] = {};
+    static std::atomic<void*> addr[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         *st = KB_ERR_CUDA;
         return nullptr;
     }
-    if (!addr[dev]) {
-        void* p = nullptr;
+    void* p = addr[dev].load(std::memory_order_acquire);
+    if (!p) {
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
             *st = KB_ERR_CUDA;
             return nullptr;
         }
-        addr[dev] = p;
+        addr[dev].store(p, std::memory_order_release);
     }
     *st = KB_OK;
-    return addr[dev];
+    return p;
 }
 
 }  // namespace
@@ -46,13 +51,13 @@ void* scratch_address(kb_status* st) {
 extern "C" kb_status kb_flash_attn_ext_noalloc(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                                const kb_tensor* mask, const kb_fa_params* params, const kb_tensor* dst,
                                                void* stream) {
-    const size_t need = kb::flash_attn_scratch_bytes(q, k, v, params);
-    if (need > KB_NOALLOC_SCRATCH_BYTES) return KB_ERR_SCRATCH;  // more partials than the built-in buffer holds
+    // the address lookup runs on every call, so the first call on a device always does it, whatever its shape
     kb_status st = KB_OK;
-    void* scratch = nullptr;
-    if (need > 0) {
-        scratch = scratch_address(&st);
-        if (st != KB_OK) return st;
-    }
+    void* scratch = scratch_address(&st);
+    if (st != KB_OK) return st;
+    // the least scratch with which the call runs (the split partials of the streaming kernel); a larger
+    // preferred size (the f16 view of a quantised cache for prefill) falls back to that kernel
+    const size_t need = kb::flash_attn_min_scratch_bytes(q, k, v, params);
+    if (need > KB_NOALLOC_SCRATCH_BYTES) return KB_ERR_SCRATCH;  // more partials than the built-in buffer holds
     return kb::flash_attn_with_scratch(q, k, v, mask, params, dst, scratch, KB_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -1,5 +1,7 @@
 // Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM): GGML_OP_FLASH_ATTN_EXT with
-// many query tokens over an f16 or bf16 KV cache (klein's prompt chunks; config[2]'s 4,096-token prefill).
+// many query tokens over an f16 or bf16 KV cache (klein's prompt chunks; config[2]'s 4,096-token prefill), and over
+// the f16 widening of a q8_0 / q4_0 cache (kv_widen.cu writes it; Q is then rounded to q8_0 first, as ggml's CPU op
+// rounds it to the vec_dot type of a q8_0 or q4_0 K, ops.cpp:8960).
 //
 // One CTA computes a 128-query tile of one head. Roles (8 warps):
 //   warps 0-3  softmax, one thread per query row (row r = TMEM lane r, all 64 cells of a block): stage Q, run the
@@ -85,10 +87,13 @@ __device__ __forceinline__ float prefill_score(const FaPrefillParams& p, float x
     return v;
 }
 
-template <int FMT>  // 0 = f16, 1 = bf16 (K, V, and the rounding of Q and P)
+// FMT: 0 = f16 K/V, 1 = bf16 K/V (the type of K, V, and of the rounding of Q and P); 2 = f16 K/V widened from a
+// q8_0 / q4_0 cache, with Q quantised to q8_0 (quantize_row_q8_0_ref's rule) and widened to f16(q * d)
+template <int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const FaPrefillParams p) {
+    constexpr int OPF = FMT == 1 ? 1 : 0;  // operand format of the MMAs: f16 or bf16
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte alignment; the dynamic window starts there (checked, not assumed)
     if (smem_u32(smem_raw) & 1023) {
@@ -151,11 +156,33 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (qi < p.n_q) {
                 const float4* src =
                     reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3) + (grp * OPT + c * 64) / 4;
+                if constexpr (FMT == 2) {
+                    // two q8_0 blocks of 32 dims: d = amax / 127, q = round(x / d), then f16(q * f16(d))
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const float4 a = src[u];
-                    qv[2 * u] = FMT == 0 ? pack_half2(a.x, a.y) : pack_bf162(a.x, a.y);
-                    qv[2 * u + 1] = FMT == 0 ? pack_half2(a.z, a.w) : pack_bf162(a.z, a.w);
+                    for (int hb = 0; hb < 2; ++hb) {
+                        float4 a[8];
+                        float amax = 0.0f;
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            a[u] = src[8 * hb + u];
+                            amax = fmaxf(amax, max3f(fabsf(a[u].x), fabsf(a[u].y), fmaxf(fabsf(a[u].z), fabsf(a[u].w))));
+                        }
+                        const float d = amax / 127.0f;
+                        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                        const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            qv[16 * hb + 2 * u] = pack_half2(roundf(a[u].x * id) * dh, roundf(a[u].y * id) * dh);
+                            qv[16 * hb + 2 * u + 1] = pack_half2(roundf(a[u].z * id) * dh, roundf(a[u].w * id) * dh);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        const float4 a = src[u];
+                        qv[2 * u] = OPF == 0 ? pack_half2(a.x, a.y) : pack_bf162(a.x, a.y);
+                        qv[2 * u + 1] = OPF == 0 ? pack_half2(a.z, a.w) : pack_bf162(a.z, a.w);
+                    }
                 }
             } else {
 #pragma unroll
@@ -207,7 +234,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // completed. A separate PV issuer keeps PV from waiting behind these 16 MMAs: the tensor core accepts only
         // a few MMAs ahead of the one executing, so issuing them takes about as long as running them.
         if (lane == 0 && nb > 0) {
-            constexpr uint32_t idS = umma_idesc_f16(FMT, BM, BN, false, false);
+            constexpr uint32_t idS = umma_idesc_f16(OPF, BM, BN, false, false);
             for (int j = 0; j < nb; ++j) {
                 const int s = j % NSTAGE, ks_ = j % KSTAGE;
                 if (!wait_or_fail(&sm.k_full[ks_], (j / KSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
@@ -239,7 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // -------------------------------------------------------------------------------- PV issuer
         // O += P_i V_i as soon as the softmax has written P_i (into the first half of S_i's columns)
         if (lane == 0 && nb > 0) {
-            constexpr uint32_t idO = umma_idesc_f16(FMT, BM, D, false, true);
+            constexpr uint32_t idO = umma_idesc_f16(OPF, BM, D, false, true);
             for (int i = 0; i < nb; ++i) {
                 const int s = i % NSTAGE, vs = i % VSTAGE;
                 if (!wait_or_fail(&sm.p_full[s], (i / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
@@ -383,8 +410,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const float p0 = ex2_ftz(x0), p1 = ex2_ftz(x1), p2 = ex2_ftz(x2), p3 = ex2_ftz(x3);
                     acc0 = fadd2(acc0, f2pack(p0, p1));
                     acc1 = fadd2(acc1, f2pack(p2, p3));
-                    pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
-                    pk[(e >> 1) + 1] = FMT == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
+                    pk[e >> 1] = OPF == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
+                    pk[(e >> 1) + 1] = OPF == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
                 }
                 f2unpack(fadd2(acc0, acc1), s0, s1);
             } else {
@@ -393,8 +420,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const float p0 = exp2f(__uint_as_float(sv[e]) - mref), p1 = exp2f(__uint_as_float(sv[e + 1]) - mref);
                     const float p2 = exp2f(__uint_as_float(sv[e + 2]) - mref), p3 = exp2f(__uint_as_float(sv[e + 3]) - mref);
                     s0 += p0, s1 += p1, s2 += p2, s3 += p3;
-                    pk[e >> 1] = FMT == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
-                    pk[(e >> 1) + 1] = FMT == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
+                    pk[e >> 1] = OPF == 0 ? pack_half2(p0, p1) : pack_bf162(p0, p1);
+                    pk[(e >> 1) + 1] = OPF == 0 ? pack_half2(p2, p3) : pack_bf162(p2, p3);
                 }
             }
             l += (s0 + s1) + (s2 + s3);
@@ -462,11 +489,12 @@ size_t fa_prefill_smem_bytes() { return sizeof(Smem); }
 
 cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorMap& tmK, const CUtensorMap& tmV,
                               cudaStream_t stream) {
-    static bool attr_done[2][64] = {};
+    static bool attr_done[3][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    auto kern = fmt == 0 ? fa_prefill_kernel<0> : fa_prefill_kernel<1>;
+    if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+    auto kern = fmt == 0 ? fa_prefill_kernel<0> : fmt == 1 ? fa_prefill_kernel<1> : fa_prefill_kernel<2>;
     const size_t smem = fa_prefill_smem_bytes();
     if (dev < 0 || dev >= 64 || !attr_done[fmt][dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);

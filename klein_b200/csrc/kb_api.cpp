@@ -66,10 +66,20 @@ struct FaShape {
 
 // Prefill (tcgen05) kernel: 128-query tiles of one head; f16 or bf16 K/V; whole-output calls only.
 constexpr int PREFILL_MIN_Q = 128;
-bool use_prefill(const FaShape& s, const kb_fa_params* prm, bool partial) {
-    return !partial && s.n_q >= PREFILL_MIN_Q && (s.kv_type == KB_TYPE_F16 || s.kv_type == KB_TYPE_BF16) &&
-           !(prm && prm->causal && prm->ring > 0);
+bool prefill_shape(const FaShape& s, const kb_fa_params* prm, bool partial) {
+    return !partial && s.n_q >= PREFILL_MIN_Q && !(prm && prm->causal && prm->ring > 0);
 }
+bool use_prefill(const FaShape& s, const kb_fa_params* prm, bool partial) {
+    return prefill_shape(s, prm, partial) && (s.kv_type == KB_TYPE_F16 || s.kv_type == KB_TYPE_BF16);
+}
+// Prefill over a q8_0 / q4_0 cache: the visible cells are widened to an f16 copy in the scratch (kv_widen.cu), then
+// the f16 prefill kernel runs on it with Q rounded to q8_0. Without that much scratch the call runs on the streaming
+// kernel instead (same results within the parity bound, slower for long prompts).
+bool prefill_quant_shape(const FaShape& s, const kb_fa_params* prm, bool partial) {
+    return prefill_shape(s, prm, partial) && (s.kv_type == KB_TYPE_Q8_0 || s.kv_type == KB_TYPE_Q4_0);
+}
+// bytes of one f16 view [ne3k][n_kv][H_kv][256] (K or V); the V view follows the K view
+size_t widen_view_bytes(const FaShape& s) { return (size_t) s.ne3k * (size_t) s.n_kv * s.H_kv * kb::FA_D * 2; }
 
 kb_status check_fa(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask, FaShape* s) {
     if (!q || !k || !v) return KB_ERR_ARG;
@@ -174,11 +184,13 @@ const char* kb_version(void) { return "klein_b200 0.1"; }
 
 size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
                                        const kb_fa_params* params) {
-    (void) params;
     FaShape s;
     if (check_fa(q, k, v, nullptr, &s) != KB_OK) return 0;
-    if (use_prefill(s, params, false)) return 0;
-    return plan_fa(s).scratch;
+    // the streaming kernel's split partials: what kb_flash_attn_ext_partial needs for any shape (the f16 / bf16
+    // prefill kernel takes none), plus, for prefill shapes over a q8_0 / q4_0 cache, the two f16 views
+    const size_t stream_need = plan_fa(s).scratch;
+    if (prefill_quant_shape(s, params, false)) return std::max(2 * widen_view_bytes(s), stream_need);
+    return stream_need;
 }
 
 }  // extern "C"
@@ -223,7 +235,11 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         return KB_OK;
     }
     const float log2e_ = 1.4426950408889634f;
-    if (use_prefill(s, prm, dst_ml != nullptr || push != nullptr)) {
+    const bool partial = dst_ml != nullptr || push != nullptr;
+    const bool quant_prefill =
+        prefill_quant_shape(s, prm, partial) && scratch && scratch_bytes >= 2 * widen_view_bytes(s) &&
+        aligned16(reinterpret_cast<uintptr_t>(scratch));
+    if (use_prefill(s, prm, partial) || quant_prefill) {
         const bool qv4 = aligned16(reinterpret_cast<uintptr_t>(q->data)) && aligned16(q->nb[1]) && aligned16(q->nb[2]) &&
                          aligned16(q->nb[3]);
         if (!qv4 || !aligned16(dst->nb[1]) || !aligned16(dst->nb[2]) || !aligned16(dst->nb[3]) ||
@@ -260,9 +276,41 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         pp.err = kb::device_error_word();
         pp.wait_ns = g_wait_ns;
         CUtensorMap tK, tV;
+        cudaStream_t cs = static_cast<cudaStream_t>(stream);
+        if (quant_prefill) {
+            // widen the cells the query tiles read (whole 64-cell blocks from kv_lo's block up to the last tile's
+            // causal bound; every cell without causal bounds) into f16 views [ne3k][n_kv][H_kv][256] in the scratch
+            int64_t c0 = 0, c1 = s.n_kv;
+            if (prm->causal) {
+                c0 = std::max<int64_t>(0, prm->kv_lo) / 64 * 64;
+                const int64_t hi = std::min<int64_t>(s.n_kv, prm->pos0 + (int64_t) pp.n_qtiles * 128);
+                c1 = hi > c0 ? std::min<int64_t>(s.n_kv, (hi + 63) / 64 * 64) : c0;
+            }
+            kb_tensor fv[2];
+            const kb_tensor* src[2] = {k, v};
+            for (int i = 0; i < 2; ++i) {
+                kb_tensor& f = fv[i];
+                f = kb_tensor{};
+                f.type = KB_TYPE_F16;
+                f.ne[0] = kb::FA_D, f.ne[1] = s.n_kv, f.ne[2] = s.H_kv, f.ne[3] = s.ne3k;
+                f.nb[0] = 2, f.nb[2] = (size_t) kb::FA_D * 2, f.nb[1] = f.nb[2] * s.H_kv, f.nb[3] = f.nb[1] * s.n_kv;
+                f.data = static_cast<char*>(scratch) + i * widen_view_bytes(s);
+                if (c1 > c0) {
+                    kb::KvWidenParams wp{};
+                    wp.src = static_cast<const char*>(src[i]->data);
+                    wp.s_nb1 = (int64_t) src[i]->nb[1], wp.s_nb2 = (int64_t) src[i]->nb[2], wp.s_nb3 = (int64_t) src[i]->nb[3];
+                    wp.dst = static_cast<__half*>(f.data);
+                    wp.n_kv = s.n_kv, wp.c0 = c0, wp.c1 = c1, wp.H_kv = s.H_kv, wp.ne3 = s.ne3k;
+                    if (kb::launch_kv_widen(wp, s.kv_type, cs) != cudaSuccess) return KB_ERR_CUDA;
+                }
+            }
+            if ((st = encode_kv_map(&fv[0], &tK)) != KB_OK) return st;
+            if ((st = encode_kv_map(&fv[1], &tV)) != KB_OK) return st;
+            return kb::launch_fa_prefill(pp, 2, tK, tV, cs) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+        }
         if ((st = encode_kv_map(k, &tK)) != KB_OK) return st;
         if ((st = encode_kv_map(v, &tV)) != KB_OK) return st;
-        cudaError_t e = kb::launch_fa_prefill(pp, s.kv_type == KB_TYPE_BF16 ? 1 : 0, tK, tV, static_cast<cudaStream_t>(stream));
+        cudaError_t e = kb::launch_fa_prefill(pp, s.kv_type == KB_TYPE_BF16 ? 1 : 0, tK, tV, cs);
         return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
     }
     if (s.kv_type == KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;  // bf16 caches: prefill shapes only
@@ -360,6 +408,14 @@ kb_status flash_attn_with_scratch(const kb_tensor* q, const kb_tensor* k, const 
 
 size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_fa_params* params) {
     return kb_flash_attn_ext_scratch_bytes(q, k, v, params);
+}
+
+size_t flash_attn_min_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                    const kb_fa_params* params) {
+    FaShape s;
+    if (check_fa(q, k, v, nullptr, &s) != KB_OK) return 0;
+    if (use_prefill(s, params, false)) return 0;
+    return plan_fa(s).scratch;
 }
 
 }  // namespace kb

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -89,9 +90,20 @@ struct FaPrefillParams {
 };
 
 size_t fa_prefill_smem_bytes();
-// fmt: 0 = f16 K/V, 1 = bf16 K/V
+// fmt: 0 = f16 K/V, 1 = bf16 K/V, 2 = f16 K/V widened from q8_0 / q4_0 (Q rounded to q8_0 first)
 cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorMap& tmK, const CUtensorMap& tmV,
                               cudaStream_t stream);
+
+// Widening of cells [c0, c1) of a q8_0 / q4_0 cache view [D = 256, n_kv, H_kv, ne3] (kv_widen.cu) into a contiguous
+// f16 copy [ne3][n_kv][H_kv][256] (cells outside [c0, c1) are not written).
+struct KvWidenParams {
+    const char* src;                 // raw rows; every head row 16-byte aligned
+    int64_t s_nb1, s_nb2, s_nb3;
+    __half* dst;
+    int64_t n_kv, c0, c1;
+    int H_kv, ne3;
+};
+cudaError_t launch_kv_widen(const KvWidenParams& p, int kv_type, cudaStream_t stream);
 
 // merges n_parts partial results: o_p [rows][D] at o_parts + p*stride, ml_p [rows][2] at ml_parts + p*stride
 // Plain merge: flags == nullptr. Exchange merge: flags = this rank's flag array [n_parts flags | epoch counter |
@@ -176,12 +188,16 @@ struct GdnNormParams {
 };
 cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream);
 
-int* device_error_word();
+int* device_error_word();  // address of the current device's error word (null on failure)
 
 // kb_flash_attn_ext with caller-chosen scratch, and its scratch size (shared by the C-ABI entry points)
 kb_status flash_attn_with_scratch(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                                   const kb_fa_params* params, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
                                   void* stream);
-size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_fa_params* params);  // address of the current device's error word (null on failure)
+size_t flash_attn_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_fa_params* params);
+// the least scratch with which kb_flash_attn_ext runs these operands (the streaming kernel's split partials); the
+// preferred size above can be larger (the f16 view for prefill over a quantised cache)
+size_t flash_attn_min_scratch_bytes(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v,
+                                    const kb_fa_params* params);
 
 }  // namespace kb
