@@ -6,7 +6,8 @@ config[3] — 4 query tokens per layer, causal among the 4 new cells, over a 262
 (4 KV heads x 256, f16) in each of 16 full-attention layers. One step = the 16 layers. value = us per
 layer of the whole job (max over ranks), lower is better. With --gpus N the KV sequence of every layer is
 split into N contiguous ranges, one per rank (strong scaling); each rank computes unnormalised partials
-(o, m, l) of its range and the partials are merged with a log-sum-exp combine after an NCCL all-gather.
+(o, m, l) of its range, and the attention kernel itself exchanges them over NVLink and merges them with a
+log-sum-exp combine (one launch per layer and rank).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
@@ -588,14 +589,17 @@ def split_parity(kb, torch, dev, args, rank, world, xchg, dist):
     kb.device_error(clear=True)
     if world == 1:
         kb.flash_attn_ext(qd, kv, vv, SCALE, causal=True, pos0=pos0, out=out)
-    elif args.exchange == "fused":
+    elif args.exchange in ("fused", "kernel"):
         L = kb.lib()
         qt = kb.kb_tensor(qd.data_ptr(), kb.F32, [D, N_Q, H, 1], [4, H * D * 4, D * 4, N_Q * H * D * 4])
         prm = kb.fa_params(SCALE, causal=True, pos0=pos0, kv_lo=kv_lo)
         nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv),
                                                     ctypes.byref(prm))
         scratch = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
-        xchg.attend_and_combine(qt, kv, vv, prm, scratch.data_ptr(), nb, rows, D, out.data_ptr(), st)
+        if args.exchange == "kernel":
+            xchg.attend_exchange(qt, kv, vv, prm, scratch.data_ptr(), nb, kb.from_torch(out), st)
+        else:
+            xchg.attend_and_combine(qt, kv, vv, prm, scratch.data_ptr(), nb, rows, D, out.data_ptr(), st)
     else:
         part = torch.empty(packed_part_floats(rows, D), device=dev)
         kb.flash_attn_ext_partial(qd, kv, vv, SCALE, part, causal=True, pos0=pos0, kv_lo=kv_lo)
@@ -685,7 +689,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         pf = packed_part_floats(rows, D)
         part = torch.empty(pf, device=dev)
         gathered = torch.empty(world * pf, device=dev)
-        if args.exchange in ("p2p", "fused"):
+        if args.exchange in ("p2p", "fused", "kernel"):
             def all_gather_obj(obj):
                 objs = [None] * world
                 dist.all_gather_object(objs, obj)
@@ -702,6 +706,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                      ctypes.byref(prm), ctypes.byref(dt), sp, ctypes.c_size_t(need), st)
             if rc != 0:
                 raise kb.KbError("kb_flash_attn_ext", rc)
+            return
+        if xchg is not None and args.exchange == "kernel":
+            # the partial attention, the exchange over NVLink and the final merge in one launch
+            xchg.attend_exchange(qt, layers[l][2], layers[l][3], prm, sp.value, need, dt, st.value)
             return
         if xchg is not None and args.exchange == "fused":
             # the partial attention writes its rows straight into every rank's gather buffer, then the merge
@@ -768,7 +776,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         ms = float(t.item())
     ms_per_step = ms / args.steps
     us_per_layer = ms_per_step * 1e3 / LAYERS
-    kernels_per_call = (2 if need > 0 else 1) + (1 if world > 1 else 0)
+    # this library's kernels per layer: attention (+ split combine when the plan splits the cells), then at N > 1
+    # push + merge-wait (p2p), merge-wait (fused: the combine pushes), merge (nccl; NCCL's own kernel not counted);
+    # the in-kernel exchange is one launch
+    combine = 1 if need > 0 else 0
+    kernels_per_call = {1: 1 + combine}.get(world) if world == 1 else \
+        {"kernel": 1, "p2p": 1 + combine + 2, "fused": 3, "nccl": 1 + combine + 1}[args.exchange]
     launches = args.steps * LAYERS * kernels_per_call
 
     # end to end through the C ABI: per layer, pinned host Q -> device, attention, output -> pinned host
@@ -983,9 +996,10 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 / q4_0 caches, prefill, DeltaNet, I/O ops)")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph per step")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "fused", "nccl"],
-                    help="N > 1: partials exchange over NVLink peer stores by a push kernel (default), by the split "
-                         "combine itself (fused), or an NCCL all-gather")
+    ap.add_argument("--exchange", default="kernel", choices=["kernel", "p2p", "fused", "nccl"],
+                    help="N > 1: the partials exchange over NVLink inside the attention kernel (kernel, default: one "
+                         "launch per layer), by a push kernel after the split combine (p2p), by the split combine "
+                         "itself (fused), or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "prefill_q8_0_2048", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
                              "verify_q4_0", "gdn_input_4096"],

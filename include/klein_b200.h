@@ -170,6 +170,31 @@ kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const k
                                  int64_t slot_set_floats, int32_t* const* flags, int32_t rank, int32_t n_ranks,
                                  void* scratch, size_t scratch_bytes, void* stream);
 
+/*
+ * The whole sequence-split attention of one layer on this rank in ONE launch: the partial attention over this
+ * rank's cells, then, inside the same kernel (a cooperative launch, every CTA resident), the merge of its splits,
+ * stores of the merged rows into slot `rank` of every rank's gather buffer over NVLink, a per-slot release flag in
+ * every rank's flag array, a bounded wait for the same slots from every rank and the final log-sum-exp merge into
+ * dst (with klein's output gate when gate != NULL, as kb_flash_attn_ext_gated). Replaces kb_flash_attn_ext_partial +
+ * kb_partials_push + kb_lse_combine_wait (ggml's split-KV partials and reduce, ops.cpp:9489-9520, 9370-9438,
+ * across devices).
+ *   q, k, v, mask, params  as kb_flash_attn_ext_partial (causal / ring bounds in this rank's cell coordinates; ne3 = 1,
+ *                          at least one cell); every rank passes the same n_q and heads
+ *   gather, slot_set_floats, part_floats  as kb_partials_push (two slot sets of n_ranks packed partials per rank)
+ *   flags   per rank an int32 array of kb_exchange_flag_bytes(n_ranks) bytes, zero at start (kb_peer_alloc); its
+ *           first n_ranks + 2 words are the push / wait exchange's, so both can share one array
+ *   dst     f32 [D, H, n_q, 1], rows 16-byte aligned; scratch of kb_flash_attn_ext_push_scratch_bytes bytes
+ * Returns KB_ERR_UNSUPPORTED when the split plan needs more CTAs than the GPU has SMs or n_q * H exceeds 512
+ * rows. A wait that runs out (a rank that never arrives) sets the device error word after
+ * 1 s; the call returns without hanging. Captured in a CUDA graph, successive replays advance the device-side epoch.
+ */
+size_t kb_exchange_flag_bytes(int32_t n_ranks);
+kb_status kb_flash_attn_ext_exchange(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                     const kb_fa_params* params, const kb_tensor* gate, int64_t part_floats,
+                                     float* const* gather, int64_t slot_set_floats, int32_t* const* flags, int32_t rank,
+                                     int32_t n_ranks, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                                     void* stream);
+
 /* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
  * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756): the split partials of the
  * streaming kernel (at most SM count x 32 rows x (256 + 2) x 4 bytes, ~4.9 MB on a 148-SM B200) and, for

@@ -54,6 +54,8 @@ EXPORTED = [
     "kb_gdn_gated_norm",
     "kb_flash_attn_ext_push",
     "kb_flash_attn_ext_push_scratch_bytes",
+    "kb_flash_attn_ext_exchange",
+    "kb_exchange_flag_bytes",
 ]
 
 
@@ -122,6 +124,12 @@ def lib():
                                              c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_size_t, c_void_p]
         L.kb_flash_attn_ext_push_scratch_bytes.restype = c_size_t
         L.kb_flash_attn_ext_push_scratch_bytes.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
+        L.kb_flash_attn_ext_exchange.restype = c_int32
+        L.kb_flash_attn_ext_exchange.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
+                                                 P(KbTensor), c_int64, c_void_p, c_int64, c_void_p, c_int32, c_int32,
+                                                 P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_exchange_flag_bytes.restype = c_size_t
+        L.kb_exchange_flag_bytes.argtypes = [c_int32]
         L.kb_gdn_input.restype = c_int32
         L.kb_gdn_input.argtypes = [P(KbTensor)] * 7 + [c_int32, c_int32, ctypes.c_float] + [P(KbTensor)] * 5 + [c_void_p]
         L.kb_gdn_gated_norm.restype = c_int32
@@ -475,7 +483,8 @@ class PeerExchange:
         self.rank, self.n, self.pf = rank, n_ranks, part_floats
         self.set_floats = n_ranks * part_floats
         self.gbuf, gh = peer_alloc(2 * self.set_floats * 4)  # two slot sets
-        self.fbuf, fh = peer_alloc(max(256, (n_ranks + 2) * 4))
+        # flag words of both exchanges (push / wait: n_ranks + 2; in-kernel: kb_exchange_flag_bytes)
+        self.fbuf, fh = peer_alloc(max(256, (n_ranks + 2) * 4, lib().kb_exchange_flag_bytes(n_ranks)))
         handles = exchange_handles((gh, fh))
         self.gather = [self.gbuf if r == rank else peer_open(handles[r][0]) for r in range(n_ranks)]
         self.flags = [self.fbuf if r == rank else peer_open(handles[r][1]) for r in range(n_ranks)]
@@ -504,6 +513,17 @@ class PeerExchange:
         check("kb_lse_combine_wait", L.kb_lse_combine_wait(c_void_p(self.gbuf), self.pf, self.set_floats, self.n, rows,
                                                            head_dim, c_void_p(self.fbuf), c_void_p(dst_ptr),
                                                            c_void_p(stream)))
+
+    def attend_exchange(self, qt, k: KbTensor, v: KbTensor, prm, scratch_ptr: int, scratch_bytes: int, dt, stream: int,
+                        gate=None) -> None:
+        """kb_flash_attn_ext_exchange: this rank's partial attention, the exchange and the final merge into dt (a
+        kb_tensor [D, H, n_q, 1]) in one launch. gate: a kb_tensor of dt's shape, or None."""
+        L = lib()
+        check("kb_flash_attn_ext_exchange",
+              L.kb_flash_attn_ext_exchange(ctypes.byref(qt), ctypes.byref(k), ctypes.byref(v), None, ctypes.byref(prm),
+                                           ctypes.byref(gate) if gate is not None else None, self.pf, self._g,
+                                           self.set_floats, self._f, self.rank, self.n, ctypes.byref(dt),
+                                           c_void_p(scratch_ptr), c_size_t(scratch_bytes), c_void_p(stream)))
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after every rank has finished its last exchange)."""

@@ -254,6 +254,205 @@ __global__ void __launch_bounds__(MERGE_THREADS) lse_combine_kernel(const float*
     merge_row(o_parts + r * Dd, stride, ml_parts + r * 2, stride, n_parts, Dd, dst + r * Dd, nullptr);
 }
 
+// ------------------------------------------------------------------------------------------------ in-kernel exchange
+//
+// The sequence-split exchange at the end of the attention kernel itself (kb_flash_attn_ext_exchange), so a layer is
+// one launch on every rank. After its main loop each CTA has written its split's partials (o, m, l) to the scratch:
+//   1. grid barrier (cooperative launch: all CTAs resident) so every split of every row is in place;
+//   2. output row ro (of n_q * H, in dst order) belongs to CTAs ro, ro + G, ... (the same rows on every rank,
+//      whatever its grid); the CTA merges the row over the splits (log-sum-exp, as fa_combine_kernel: each warp a
+//      share of the splits, lanes 8 dims each, the warps' sums meeting in shared memory) and stores the merged
+//      partial (o unnormalised, m, l) into slot `rank` of every rank's gather buffer (plain stores to peer memory over
+//      NVLink); after one system-scope fence its thread 0 writes the epoch into flag word (rank, ro) of every rank;
+//   3. the CTA waits (acquire polls, bounded) until every source's flag word for its row holds the epoch, then merges
+//      the n_ranks partials of the row from its local gather buffer the same way and stores the normalised (gated)
+//      output row;
+//   4. the last CTA to finish resets the barrier counters and advances the epoch.
+// Slot sets alternate by epoch parity; a rank cannot start epoch e + 2 before every rank has pushed epoch e + 1, which
+// each does only in a launch after the one that consumed epoch e, so a slot set is never overwritten while read.
+// Shared memory: the attention's buffers are free by then (every TMA and MMA has completed before the dealloc).
+
+// Log-sum-exp merge of one row (D dims) over n partials by the whole CTA: part s has o at o + s * o_stride and
+// (m, l) at ml + s * ml_stride. Leaves the weighted sum of o in sh_out[D] and returns (M, L) through sh_ml (the row
+// max over parts with l > 0, and sum_s 2^(m_s - M) l_s). sh: >= 256 + 2 * WARPS + WARPS * D floats of shared memory.
+// Loads go through L2 (ld.global.cg): the parts were written by other CTAs or GPUs during this kernel.
+template <int WARPS>
+__device__ void cta_merge_row(float* sh, const float* o, int64_t o_stride, const float* ml, int64_t ml_stride, int n,
+                              float* sh_out, float* sh_ml) {
+    float* f = sh;                     // [256] weights
+    float* red = sh + 256;             // [2 WARPS]
+    float* acc = sh + 256 + 2 * WARPS;  // [WARPS][D]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // the first PF parts of this warp (w, w + WARPS, ...) are loaded together with the (m, l) pairs, before the
+    // weights are known: one round trip to L2 for up to PF * WARPS parts (48)
+    constexpr int PF = WARPS <= 8 ? 6 : 3;
+    float4 xa[PF], xb[PF];
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+        const int sp = warp + k * WARPS;
+        xa[k] = xb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sp < n) {
+            const float4* src = reinterpret_cast<const float4*>(o + (int64_t) sp * o_stride + lane * 8);
+            xa[k] = __ldcg(src);
+            xb[k] = __ldcg(src + 1);
+        }
+    }
+    float mx = -INFINITY;
+    float2 v0 = make_float2(-INFINITY, 0.0f);
+    if (tid < n) {
+        v0 = __ldcg(reinterpret_cast<const float2*>(ml + (int64_t) tid * ml_stride));
+        if (v0.y > 0.0f) mx = v0.x;
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < WARPS; ++w) M = fmaxf(M, red[w]);
+    float lw = 0.0f;
+    if (tid < n) {
+        const float w = (v0.y > 0.0f && M != -INFINITY) ? exp2f(v0.x - M) : 0.0f;
+        f[tid] = w;
+        lw = w * v0.y;
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+    if (lane == 0) red[WARPS + warp] = lw;
+    __syncthreads();
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    auto fma8 = [&](float w, const float4& x, const float4& y) {
+        a[0] = fmaf(w, x.x, a[0]), a[1] = fmaf(w, x.y, a[1]), a[2] = fmaf(w, x.z, a[2]), a[3] = fmaf(w, x.w, a[3]);
+        a[4] = fmaf(w, y.x, a[4]), a[5] = fmaf(w, y.y, a[5]), a[6] = fmaf(w, y.z, a[6]), a[7] = fmaf(w, y.w, a[7]);
+    };
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+        const int sp = warp + k * WARPS;
+        if (sp < n) fma8(f[sp], xa[k], xb[k]);
+    }
+#pragma unroll 4
+    for (int sp = warp + PF * WARPS; sp < n; sp += WARPS) {
+        const float4* src = reinterpret_cast<const float4*>(o + (int64_t) sp * o_stride + lane * 8);
+        fma8(f[sp], __ldcg(src), __ldcg(src + 1));
+    }
+    *reinterpret_cast<float4*>(acc + warp * D + lane * 8) = make_float4(a[0], a[1], a[2], a[3]);
+    *reinterpret_cast<float4*>(acc + warp * D + lane * 8 + 4) = make_float4(a[4], a[5], a[6], a[7]);
+    __syncthreads();
+    for (int d = tid; d < D; d += WARPS * 32) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) t += acc[w * D + d];
+        sh_out[d] = t;
+    }
+    if (tid == 0) {
+        float L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) L += red[WARPS + w];
+        sh_ml[0] = M;
+        sh_ml[1] = L;
+    }
+    __syncthreads();
+}
+
+template <int RPC, int WARPS>
+__device__ void exchange_tail(const FaStreamParams& p, float* sh) {
+    __shared__ int s_epoch;
+    __shared__ volatile int s_ok;
+    const int G = (int) (gridDim.x * gridDim.y * gridDim.z);
+    const int cta = (int) (blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    int* my = p.flags[p.rank];
+    int* bar = my + p.n_ranks + 2;
+    int* done = my + p.n_ranks + 3;
+    float* sh_row = sh + 256 + 2 * WARPS + WARPS * D;  // [D] merged row, then (M, L)
+    float* sh_ml = sh_row + D;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();  // the CTA's split partials (ordered before it by the barrier) are visible device-wide
+        s_epoch = *reinterpret_cast<volatile int*>(my + p.n_ranks) + 1;
+        s_ok = 1;
+        atomicAdd(bar, 1);
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(bar) < G) {
+            if (globaltimer_ns() - t0 > p.wait_ns) {
+                record_error(p.err, DEV_ERR_WAIT_GRID);
+                s_ok = 0;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    const int e = s_epoch;
+    const int rows = p.n_q * p.n_head;
+    const int64_t set_off = (int64_t) (e & 1) * p.slot_set_floats;
+    const int64_t own_off = set_off + (int64_t) p.rank * p.part_floats;
+    if (s_ok) {
+        for (int ro = cta; ro < rows; ro += G) {
+            const int h = ro % p.n_head, qi = ro / p.n_head;
+            const int hk = h / p.gqa, gr = qi * p.gqa + h % p.gqa, chunk = gr / RPC, r = gr % RPC;
+            const int64_t base = ((int64_t) hk * p.n_row_chunks + chunk) * p.n_splits;
+            cta_merge_row<WARPS>(sh, p.o_part + (base * RPC + r) * D, (int64_t) RPC * D, p.ml_part + base * RPC * 2 + r * 2,
+                                 (int64_t) RPC * 2, p.n_splits, sh_row, sh_ml);
+            // the merged partial of this rank into every rank's gather buffer: o row, then (m, l)
+            for (int i = threadIdx.x; i < p.n_ranks * (D / 4 + 1); i += WARPS * 32) {
+                const int d = i / (D / 4 + 1), k = i % (D / 4 + 1);
+                float* g = p.gather[d] + own_off;
+                if (k < D / 4)
+                    *reinterpret_cast<float4*>(g + (int64_t) ro * D + 4 * k) = *reinterpret_cast<const float4*>(sh_row + 4 * k);
+                else
+                    *reinterpret_cast<float2*>(g + (int64_t) rows * D + (int64_t) ro * 2) = make_float2(sh_ml[0], sh_ml[1]);
+            }
+            // one system-scope fence per CTA: the barrier orders every thread's stores before thread 0's fence
+            // (cumulativity), and the flag stores after it publish them
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence_system();
+                for (int d = 0; d < p.n_ranks; ++d)
+                    st_relaxed_sys(p.flags[d] + XCHG_FLAG_BASE + p.rank * XCHG_MAX_SLOTS + ro, e);
+            }
+        }
+        for (int ro = cta; ro < rows; ro += G) {
+            if (threadIdx.x < p.n_ranks) {
+                const int* f = my + XCHG_FLAG_BASE + threadIdx.x * XCHG_MAX_SLOTS + ro;
+                const uint64_t t0 = globaltimer_ns();
+                while ((int) ((unsigned) ld_acquire_sys(f) - (unsigned) e) < 0) {  // wrapping comparison
+                    if (globaltimer_ns() - t0 > p.wait_ns) {
+                        record_error(p.err, DEV_ERR_WAIT_PEER);
+                        s_ok = 0;
+                        break;
+                    }
+                    __nanosleep(20);
+                }
+            }
+            __syncthreads();
+            if (!s_ok) break;
+            const float* g = p.gather[p.rank] + set_off;
+            cta_merge_row<WARPS>(sh, g + (int64_t) ro * D, p.part_floats, g + (int64_t) rows * D + (int64_t) ro * 2,
+                                 p.part_floats, p.n_ranks, sh_row, sh_ml);
+            const int h = ro % p.n_head, qi = ro / p.n_head;
+            const float L = sh_ml[1];
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + qi * p.d_nb2);
+            for (int d = threadIdx.x; d < D; d += WARPS * 32) {
+                float v = sh_row[d] * inv;
+                if (p.gate) v *= gate_sigmoid(p.gate + h * p.g_nb1 + qi * p.g_nb2 + (int64_t) d * 4);
+                out[d] = v;
+            }
+            __syncthreads();
+        }
+    }
+    // the last CTA resets the counters and advances the epoch (every CTA has read the epoch before counting itself)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(done, 1) == G - 1) {
+            *reinterpret_cast<volatile int*>(bar) = 0;
+            *reinterpret_cast<volatile int*>(done) = 0;
+            __threadfence();
+            atomicAdd(my + p.n_ranks, 1);
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ tcgen05 kernel
 //
 // One CTA per (split, KV head, row chunk). The rows of a chunk are the N columns (16 or 32) of S^T = K Q^T,
@@ -430,8 +629,8 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, hk = blockIdx.y;
     const int chunk = blockIdx.z % p.n_row_chunks, b = blockIdx.z / p.n_row_chunks;
-    const int64_t key_begin = (int64_t) split * p.keys_per_split;
-    const int64_t key_end = min(p.n_kv, key_begin + p.keys_per_split);
+    const int64_t key_begin = ((int64_t) split * p.blocks_base + min(split, p.blocks_extra)) * BLK;
+    const int64_t key_end = min(p.n_kv, key_begin + (p.blocks_base + (split < p.blocks_extra ? 1 : 0)) * BLK);
     const int n_tiles = key_end > key_begin ? (int) ((key_end - key_begin + TILE - 1) / TILE) : 0;
     const int nblk = (n_tiles + 1) / 2;
     const int row0 = chunk * N;
@@ -467,43 +666,69 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
         tmem_alloc(&sm.tmem_base, R_::TMEM_COLS);
         tmem_relinquish();
     }
-    // Q quantised like quantize_row_q8_0_ref, stored as f16(q * d) in the swizzled K-major image; rows past the
-    // chunk are zero
-    for (int task = warp; task < N * (D / 32); task += THREADS / 32) {
-        const int r = task / (D / 32), blk = task % (D / 32);
-        float x = 0.0f;
-        if (r < rows) {
-            const int gr = row0 + r;
-            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-            x = *reinterpret_cast<const float*>(p.q + (int64_t) (32 * blk + lane) * 4 + qi * p.q_nb1 + h * p.q_nb2 +
-                                                b * p.q_nb3);
-        }
-        float amax = fabsf(x);
-#pragma unroll
-        for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float d = amax / 127.0f;
-        const float id = d != 0.0f ? 1.0f / d : 0.0f;
-        const float qv = roundf(x * id);
-        const float dh = __half2float(__float2half_rn(d));
-        const int dim = 32 * blk + lane, e = dim & 63;
-        // q8_0 / q4_0 K: Q rounded to q8_0 (ggml's vec_dot type for both), then f16(q * d); f16 K: Q rounded to f16
-        *reinterpret_cast<__half*>(sm.q[dim >> 6] + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
-            __float2half_rn(Q8 ? qv * dh : x);
-    }
-    if (threadIdx.x < N) {
-        const int r = threadIdx.x;
-        const int gr = row0 + min(r, max(rows - 1, 0));
-        const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
-        sm.row_qi[r] = qi;
-        sm.row_h[r] = h;
-        sm.row_slope[r] = slope_of(p, h);
-    }
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
+    // Q staging by every warp but the TMA producers, which start streaming K and V once the Q loads are issued (so that
+    // these are not queued behind the first K / V tiles). Q rounded to f16 (f16 K), or quantised like
+    // quantize_row_q8_0_ref and widened to f16(q * d) (q8_0 / q4_0 K), into the swizzled K-major image; rows past the
+    // chunk are zero. Thread t takes float4s t, t + QT, ... of the [N rows][64 float4] block, all loaded before any is
+    // converted; a 32-dim q8_0 block is 8 consecutive threads (QT is a multiple of 8).
+    constexpr int QT = THREADS - 64, NF = N * (D / 4), PER = (NF + QT - 1) / QT;
+    const bool q_stager = warp != W_KTMA && warp != W_VTMA;
+    const int tq = warp < W_KTMA ? (int) threadIdx.x : (int) threadIdx.x - 64;
+    float4 qv[PER];
+#pragma unroll
+    for (int i = 0; i < PER && q_stager; ++i) {
+        const int f = i * QT + tq, r = f / (D / 4);
+        qv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (f < NF && r < rows) {
+            const int gr = row0 + r;
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            const char* src = p.q + (int64_t) (f % (D / 4)) * 16 + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3;
+            if (p.q_vec4) {
+                qv[i] = *reinterpret_cast<const float4*>(src);
+            } else {
+                const float* s4 = reinterpret_cast<const float*>(src);
+                qv[i] = make_float4(s4[0], s4[1], s4[2], s4[3]);
+            }
+        }
+    }
+    named_bar_sync(3, THREADS);  // the Q loads are issued (their data may still be in flight)
+    if (q_stager) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int f = i * QT + tq, r = f / (D / 4);
+            float x0 = qv[i].x, x1 = qv[i].y, x2 = qv[i].z, x3 = qv[i].w;
+            if constexpr (Q8) {
+                // amax over the 8 threads of this 32-dim block (every thread of the warp takes part)
+                float amax = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                const float d = amax / 127.0f;
+                const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                const float dh = __half2float(__float2half_rn(d));
+                x0 = roundf(x0 * id) * dh, x1 = roundf(x1 * id) * dh, x2 = roundf(x2 * id) * dh, x3 = roundf(x3 * id) * dh;
+            }
+            if (f < NF) {
+                const int dim = (f % (D / 4)) * 4, e = dim & 63;
+                *reinterpret_cast<uint2*>(sm.q[dim >> 6] + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
+                    make_uint2(pack_half2(x0, x1), pack_half2(x2, x3));
+            }
+        }
+        if (threadIdx.x < N) {
+            const int r = threadIdx.x;
+            const int gr = row0 + min(r, max(rows - 1, 0));
+            const int qi = gr / p.gqa, h = hk * p.gqa + gr % p.gqa;
+            sm.row_qi[r] = qi;
+            sm.row_h[r] = h;
+            sm.row_slope[r] = slope_of(p, h);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2, THREADS - 64);
+    }
 
     if (warp == W_KTMA || warp == W_VTMA) {
         // ------------------------------------------------------------------------ TMA producers
@@ -961,15 +1186,13 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
                     tmem_wait_ld();
                 }
                 const int d = 128 * hh + c;
-#pragma unroll 4
-                for (int r = 0; r < rows; ++r) {
+#pragma unroll
+                for (int r = 0; r < N; ++r) {
+                    if (r >= rows) break;
                     const float L = (sm.red[0][r] + sm.red[1][r]) + (sm.red[2][r] + sm.red[3][r]);
                     const float M = nblk > 0 ? sm.mrow[r] : -INFINITY;
-                    float O = 0.0f;
-#pragma unroll
-                    for (int e = 0; e < N; ++e)
-                        if (e == r) O = __uint_as_float(ov[e]);
-                    if (p.n_splits == 1 && !p.push) {
+                    const float O = __uint_as_float(ov[r]);
+                    if (p.n_splits == 1 && !p.push && !p.xchg) {
                         store_row(p, sm.row_qi[r], sm.row_h[r], b, d, O, M, L);
                     } else {
                         p.o_part[(part_row0 + r) * D + d] = O;
@@ -991,6 +1214,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == W_SMMA) tmem_dealloc(tmem, R_::TMEM_COLS);
+    if (p.xchg) exchange_tail<N, THREADS / 32>(p, reinterpret_cast<float*>(smem_raw));
 }
 
 }  // namespace tc
@@ -1016,6 +1240,20 @@ cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUt
     cudaError_t e = set_smem_once(kern, smem, attr_done);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
+    if (p.xchg) {
+        // the in-kernel exchange waits on a grid barrier: every CTA must be resident at once
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(tc::Roles<KT != tc::KT_F16>::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, tmK, tmV, p);
+    }
     kern<<<grid, tc::Roles<KT != tc::KT_F16>::THREADS, smem, stream>>>(tmK, tmV, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || (p.n_splits == 1 && !p.push)) return e;

@@ -55,7 +55,8 @@ bool aligned16(size_t x) { return (x & 15) == 0; }
 // The split-KV plan of one streaming attention call.
 struct FaPlan {
     int rpc = 32, n_row_chunks = 1, n_splits = 1;
-    int64_t keys_per_split = 0;
+    int64_t blocks_base = 0;  // 128-cell blocks per split (the first blocks_extra splits take one more)
+    int blocks_extra = 0;
     size_t scratch = 0;
 };
 
@@ -135,11 +136,12 @@ FaPlan plan_fa(const FaShape& s, bool push = false) {
     if (target < 1) target = 1;
     if (tiles == 0) {
         pl.n_splits = 1;
-        pl.keys_per_split = unit;
+        pl.blocks_base = 1;
     } else {
-        const int64_t tps = (tiles + target - 1) / target;
-        pl.keys_per_split = tps * unit;
-        pl.n_splits = (int) ((tiles + tps - 1) / tps);
+        // as many splits as SMs allow, their block counts within one of each other (a CTA's time is its blocks)
+        pl.n_splits = (int) std::min<int64_t>(target, tiles);
+        pl.blocks_base = tiles / pl.n_splits;
+        pl.blocks_extra = (int) (tiles % pl.n_splits);
     }
     if (pl.n_splits > 1 || push) {
         const size_t rows = (size_t) base * pl.n_splits * pl.rpc;
@@ -205,9 +207,11 @@ struct PushArgs {
     int rank, n_ranks;
 };
 
+// push: the fused push exchange (partials into the gather buffers); xchg: with push, the whole exchange in the
+// attention kernel (kb_flash_attn_ext_exchange), dst the final output
 kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
                   const kb_fa_params* prm, const kb_tensor* dst, float* dst_ml, void* scratch, size_t scratch_bytes,
-                  void* stream, const kb_tensor* gate = nullptr, const PushArgs* push = nullptr) {
+                  void* stream, const kb_tensor* gate = nullptr, const PushArgs* push = nullptr, bool xchg = false) {
     if (!prm || !dst) return KB_ERR_ARG;
     FaShape s;
     kb_status st = check_fa(q, k, v, mask, &s);
@@ -218,7 +222,7 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
                  gate->ne[2] != s.n_q || gate->ne[3] != s.ne3))
         return KB_ERR_BAD_SHAPE;
     if (gate && dst_ml) return KB_ERR_ARG;  // the gate applies to final outputs, not to partials
-    if (push && (gate || s.ne3 != 1)) return KB_ERR_ARG;
+    if (push && ((gate && !xchg) || s.ne3 != 1)) return KB_ERR_ARG;
     if (prm->logit_softcap != 0.0f && !(std::isfinite(prm->logit_softcap))) return KB_ERR_ARG;
     if (prm->max_bias > 0.0f && !mask) return KB_ERR_ARG;  // ggml: ALiBi needs a mask
     if (prm->causal && prm->ring < 0) return KB_ERR_ARG;
@@ -316,6 +320,15 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     if (s.kv_type == KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;  // bf16 caches: prefill shapes only
     const FaPlan pl = plan_fa(s, push != nullptr);
     if (pl.scratch > 0 && (!scratch || scratch_bytes < pl.scratch)) return KB_ERR_SCRATCH;
+    if (xchg) {
+        // every CTA resident at once (one per SM), and the exchange's slots of rows within the flag array
+        const int64_t slots = (int64_t) s.n_q * s.H;  // one flag word per output row and source rank
+        const int64_t grid = (int64_t) pl.n_splits * s.H_kv * pl.n_row_chunks;
+        const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
+        if (slots > kb::XCHG_MAX_SLOTS || grid > sms || (gate && !aligned16(gate->nb[1]))) return KB_ERR_UNSUPPORTED;
+        if (!aligned16(dst->nb[1]) || !aligned16(dst->nb[2]) || (reinterpret_cast<uintptr_t>(dst->data) & 7) != 0)
+            return KB_ERR_UNSUPPORTED;
+    }
 
     kb::FaStreamParams p{};
     p.q = static_cast<const char*>(q->data);
@@ -356,7 +369,8 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
     p.kv_lo = prm->kv_lo;
     p.ring = prm->causal ? prm->ring : 0;
     p.n_splits = pl.n_splits;
-    p.keys_per_split = pl.keys_per_split;
+    p.blocks_base = pl.blocks_base;
+    p.blocks_extra = pl.blocks_extra;
     p.n_row_chunks = pl.n_row_chunks;
     if (pl.scratch > 0) {
         const size_t rows = (size_t) s.H_kv * pl.n_row_chunks * s.ne3 * pl.n_splits * pl.rpc;
@@ -372,10 +386,11 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         p.gate = static_cast<const char*>(gate->data);
         p.g_nb1 = (int64_t) gate->nb[1], p.g_nb2 = (int64_t) gate->nb[2], p.g_nb3 = (int64_t) gate->nb[3];
     }
-    p.partial_out = dst_ml != nullptr || push != nullptr;
+    p.partial_out = dst_ml != nullptr || (push != nullptr && !xchg);
     p.dst_ml = dst_ml;
     if (push) {
-        p.push = 1;
+        p.push = xchg ? 0 : 1;
+        p.xchg = xchg ? 1 : 0;
         p.rank = push->rank;
         p.n_ranks = push->n_ranks;
         p.slot_set_floats = push->slot_set_floats;
@@ -448,6 +463,31 @@ kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const k
     dst.nb[0] = 4, dst.nb[1] = (size_t) D * 4, dst.nb[2] = dst.nb[1] * dst.ne[1], dst.nb[3] = dst.nb[2] * dst.ne[2];
     PushArgs pa{gather, flags, slot_set_floats, part_floats, rank, n_ranks};
     return fa_impl(q, k, v, mask, params, &dst, nullptr, scratch, scratch_bytes, stream, nullptr, &pa);
+}
+
+size_t kb_exchange_flag_bytes(int32_t n_ranks) {
+    if (n_ranks < 1 || n_ranks > KB_MAX_PEERS) return 0;
+    return (size_t) (kb::XCHG_FLAG_BASE + n_ranks * kb::XCHG_MAX_SLOTS) * sizeof(int32_t);
+}
+
+kb_status kb_flash_attn_ext_exchange(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                     const kb_fa_params* params, const kb_tensor* gate, int64_t part_floats,
+                                     float* const* gather, int64_t slot_set_floats, int32_t* const* flags, int32_t rank,
+                                     int32_t n_ranks, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
+                                     void* stream) {
+    if (!q || !dst || !gather || !flags || n_ranks < 1 || n_ranks > KB_MAX_PEERS || rank < 0 || rank >= n_ranks)
+        return KB_ERR_ARG;
+    const int64_t rows = q->ne[1] * q->ne[2], D = q->ne[0];
+    if (part_floats < rows * D + rows * 2 || part_floats % 4 != 0 || slot_set_floats < n_ranks * part_floats ||
+        slot_set_floats % 4 != 0)
+        return KB_ERR_BAD_SHAPE;
+    for (int r = 0; r < n_ranks; ++r) {
+        if (!gather[r] || !flags[r]) return KB_ERR_ARG;
+        if ((reinterpret_cast<uintptr_t>(gather[r]) & 15) != 0 || (reinterpret_cast<uintptr_t>(flags[r]) & 3) != 0)
+            return KB_ERR_ARG;
+    }
+    PushArgs pa{gather, flags, slot_set_floats, part_floats, rank, n_ranks};
+    return fa_impl(q, k, v, mask, params, dst, nullptr, scratch, scratch_bytes, stream, gate, &pa, true);
 }
 
 kb_status kb_flash_attn_ext_gated(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,

@@ -10,10 +10,37 @@
 namespace kb {
 
 // error codes written to the device error word (kb_device_error)
-enum : int { DEV_ERR_NONE = 0, DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_WAIT_PEER = 3, DEV_ERR_ALIGN = 5 };
+enum : int {
+    DEV_ERR_NONE = 0,
+    DEV_ERR_WAIT_FULL = 1,
+    DEV_ERR_WAIT_EMPTY = 2,
+    DEV_ERR_WAIT_PEER = 3,
+    DEV_ERR_ALIGN = 5,
+    DEV_ERR_WAIT_GRID = 6  // a grid-wide barrier of a cooperative launch ran out of time
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(int* p, int v) {
+    asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -34,8 +34,9 @@ struct FaStreamParams {
     int causal;
     int64_t pos0, kv_lo, ring;
     // KV split
-    int n_splits;
-    int64_t keys_per_split;          // multiple of FA_TC_BLOCK
+    int n_splits;                    // split s: 128-cell blocks [s base + min(s, extra), + base + (s < extra))
+    int64_t blocks_base;
+    int blocks_extra;
     int n_row_chunks;                // CTAs along the rows of one KV head (16 or 32 rows each at most)
     // outputs
     float* o_part;                   // scratch: [ne3][H_kv][chunk][split][RPC][D]
@@ -54,6 +55,11 @@ struct FaStreamParams {
     float* gather[16];
     int* flags[16];
     int* push_counter;               // in the scratch: combine CTAs done (zeroed by the attention kernel)
+    // in-kernel exchange (kb_flash_attn_ext_exchange): after a grid barrier the kernel merges its splits, stores the
+    // merged rows into every rank's gather buffer, flags each slot of rows in every rank's flag array, waits for the
+    // same slot from every rank and writes the final output (gather / flags / rank / n_ranks / slot_set_floats /
+    // part_floats as for push). Launched cooperatively: every CTA is resident at once.
+    int xchg;
     int* err;                        // device error word
     uint64_t wait_ns;                // budget of every bounded wait
 };
@@ -127,6 +133,11 @@ struct PeerPushParams {
     int rank, n_ranks;
 };
 constexpr int PUSH_CHUNKS = 32;  // CTAs per destination of a push; a complete push counts this many in its flag
+// Flag array words of the in-kernel exchange: [n_ranks] epoch (shared with the push / wait exchange), [n_ranks + 2]
+// grid-barrier arrivals, [n_ranks + 3] CTAs done, and from XCHG_FLAG_BASE one word per (source rank, output row)
+// holding the last epoch that source has delivered for that row.
+constexpr int XCHG_FLAG_BASE = 64;
+constexpr int XCHG_MAX_SLOTS = 512;
 cudaError_t launch_partials_push(const PeerPushParams& p, cudaStream_t stream);
 
 // Parameters of the attention prologue (attn_prologue.cu): Q/gate split, RMS norms, M-RoPE, KV-cache writes.

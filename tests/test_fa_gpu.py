@@ -336,3 +336,78 @@ def test_golden_fixture(kb, cuda, name):
     mask = g["mask"] if g["mask"].size else None
     gpu = run_gpu(kb, cuda, g["q"], g["k"], g["v"], 4, mask=mask)
     check_attention(gpu, exact_np(q, kd, vd, mask=mask), g["out"])
+
+
+# ---------------------------------------------------------------------------------------------- in-kernel exchange
+# kb_flash_attn_ext_exchange with one rank: the same kernel path the N-GPU sequence split runs (grid barrier, split
+# merge, stores into the gather buffer, per-slot release flags, bounded waits, final merge, device-side epochs), with
+# every peer being this GPU itself
+
+@pytest.mark.parametrize("kvt,n_q,n_kv,gated", [("f16", 4, 262144, False), ("f16", 1, 4096, False),
+                                                ("f16", 4, 9000, True), ("q8_0", 4, 70001, False),
+                                                ("q4_0", 4, 20000, False)])
+def test_exchange_single_rank(kb, cuda, kvt, n_q, n_kv, gated):
+    import ctypes
+    import torch
+
+    from klein_b200.kv_split import packed_part_floats
+
+    gt = {"f16": O.GGML_F16, "q8_0": O.GGML_Q8_0, "q4_0": O.GGML_Q4_0}[kvt]
+    t = {"f16": kb.F16, "q8_0": kb.Q8_0, "q4_0": kb.Q4_0}[kvt]
+    q, kc, vc, kd, vd = O.make_fa_inputs(4242 + n_q + n_kv, n_q, n_kv, kv_type=gt)
+    H, D = 24, 256
+    kt, vt = torch.from_numpy(kc).to(cuda), torch.from_numpy(vc).to(cuda)
+    kv, vv = kb.kv_cache_view(kt, t, 4, D), kb.kv_cache_view(vt, t, 4, D)
+    qd = torch.from_numpy(q).to(cuda).unsqueeze(0)
+    qt = kb.kb_tensor(qd.data_ptr(), kb.F32, [D, n_q, H, 1], [4, H * D * 4, D * 4, n_q * H * D * 4])
+    prm = kb.fa_params(1 / 16, causal=True, pos0=n_kv - n_q)
+    gate = torch.randn(1, n_q, H, D, device=cuda) * 2 if gated else None
+    rows = n_q * H
+    xchg = kb.PeerExchange(0, 1, packed_part_floats(rows, D), lambda obj: [obj])
+    L = kb.lib()
+    nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(prm))
+    scratch = torch.empty(max(nb, 1), dtype=torch.uint8, device=cuda)
+    outs = [torch.full((1, n_q, H, D), float("nan"), device=cuda) for _ in range(4)]
+    dts = [kb.from_torch(o.view(1, n_q, H, D)) for o in outs]
+    for dt in dts:
+        dt.ne[:] = [D, H, n_q, 1]
+        dt.nb[:] = [4, D * 4, H * D * 4, n_q * H * D * 4]
+    gt_t = None
+    if gated:
+        gt_t = kb.from_torch(gate)
+        gt_t.ne[:] = [D, H, n_q, 1]
+        gt_t.nb[:] = [4, D * 4, H * D * 4, n_q * H * D * 4]
+    kb.device_error(clear=True)
+    st = torch.cuda.current_stream(cuda).cuda_stream
+    # two eager calls, then two replays of a captured call (the epoch lives on the device)
+    for i in range(2):
+        xchg.attend_exchange(qt, kv, vv, prm, scratch.data_ptr(), nb, dts[i], st, gate=gt_t)
+    torch.cuda.synchronize()
+    graphs = []
+    for i in (2, 3):
+        side = torch.cuda.Stream(cuda)
+        side.wait_stream(torch.cuda.current_stream(cuda))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            xchg.attend_exchange(qt, kv, vv, prm, scratch.data_ptr(), nb, dts[i], side.cuda_stream, gate=gt_t)
+        torch.cuda.current_stream(cuda).wait_stream(side)
+        graphs.append(g)
+    for g in graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    assert kb.device_error() == 0
+    plain = kb.flash_attn_ext(qd, kv, vv, 1 / 16, causal=True, pos0=n_kv - n_q, gate=gate)
+    torch.cuda.synchronize()
+    mask = O.rs_visible_mask(n_q, n_kv, n_kv - n_q)
+    qr = O.q_round_f16(q) if kvt == "f16" else O.q_round_q8_0(q)
+    exact = exact_np(qr, kd, vd, mask)
+    if gated:
+        exact = exact / (1.0 + np.exp(-gate[0].double().cpu().numpy()))
+    ref = plain[0].cpu().numpy()
+    for o in outs:
+        got = o[0].cpu().numpy()
+        check_attention(got, exact)
+        # the same merge arithmetic as the split combine, in another order: f32 rounding differences only
+        assert np.abs(got - ref).max() <= 1e-5 * np.abs(exact).max()
+    del graphs
+    xchg.close()

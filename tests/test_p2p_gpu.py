@@ -1,6 +1,7 @@
 """The KV-sequence split across 2, 4 and 8 GPUs with the NVLink partials exchange: one process per GPU, IPC
-handles exchanged over a gloo group. Two exchanges: kb_partials_push + kb_lse_combine_wait ("push"), and the
-split combine of kb_flash_attn_ext_push storing into the peers' gather buffers itself ("fused"). Every exchange
+handles exchanged over a gloo group. Three exchanges: kb_partials_push + kb_lse_combine_wait ("push"), the split
+combine of kb_flash_attn_ext_push storing into the peers' gather buffers itself ("fused"), and the whole exchange
+inside the attention kernel, kb_flash_attn_ext_exchange ("exchange"). Every exchange
 of a run (several in a row, so both slot sets and the device-side epochs are exercised) is checked against
 exact f64 attention over the whole cache (the checker, tests/parity.py's bound) and against the single-GPU
 attention; all ranks must hold the same merged output. Cases need as many GPUs as ranks and are skipped
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir, fused):
+def _rank_main(rank, world, port, out_dir, mode):
     import ctypes
 
     import torch
@@ -67,7 +68,13 @@ def _rank_main(rank, world, port, out_dir, fused):
     outs, vs_single = [], []
     for q, ref in zip(qs, full):
         out = torch.empty(1, N_Q, H, D, device=dev)
-        if fused:
+        if mode == "exchange":
+            qt = kb.kb_tensor(q.data_ptr(), kb.F32, [D, N_Q, H, 1], [4, q.stride(1) * 4, q.stride(2) * 4, q.stride(0) * 4])
+            nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv),
+                                                        ctypes.byref(prm))
+            scratch = torch.empty(nb, dtype=torch.uint8, device=dev)
+            xchg.attend_exchange(qt, kv, vv, prm, scratch.data_ptr(), nb, kb.from_torch(out), stream)
+        elif mode == "fused":
             qt = kb.kb_tensor(q.data_ptr(), kb.F32, [D, N_Q, H, 1], [4, q.stride(1) * 4, q.stride(2) * 4, q.stride(0) * 4])
             nb = L.kb_flash_attn_ext_push_scratch_bytes(ctypes.byref(qt), ctypes.byref(kv), ctypes.byref(vv),
                                                         ctypes.byref(prm))
@@ -91,8 +98,8 @@ def _rank_main(rank, world, port, out_dir, fused):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("fused", [False, True], ids=["push", "fused"])
-def test_sequence_split_exchange(kb, cuda, tmp_path, world, fused):
+@pytest.mark.parametrize("mode", ["push", "fused", "exchange"])
+def test_sequence_split_exchange(kb, cuda, tmp_path, world, mode):
     import torch
     import torch.multiprocessing as mp
 
@@ -102,7 +109,7 @@ def test_sequence_split_exchange(kb, cuda, tmp_path, world, fused):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
-    mp.start_processes(_rank_main, args=(world, port, str(tmp_path), fused), nprocs=world, join=True,
+    mp.start_processes(_rank_main, args=(world, port, str(tmp_path), mode), nprocs=world, join=True,
                        start_method="spawn")
     res = [dict(np.load(tmp_path / f"r{r}.npz")) for r in range(world)]
     r0 = res[0]
