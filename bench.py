@@ -525,6 +525,240 @@ def bench_gdn_prefill(kb, torch, dev, steps, warmup):
                          "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic("gdn_chunk_prefill_4096")}}
 
 
+# ------------------------------------------------------------------------------------------------ whole stack
+
+HIDDEN = 5120  # qwen35 27B n_embd
+
+
+def bench_stack(kb, torch, dev, steps, warmup, contexts=(4096, 32768, 131072, 262144)):
+    """config[4]: the whole 64-layer attention stack of a 27B qwen35 model (48 gated DeltaNet + 16 GQA full-attention
+    layers, hidden 5120; random-init bf16 projections, 7.25 B parameters, distinct per layer; the FFN blocks are not
+    part of the attention stack and are left out) over klein's State in HBM (kb_state, caches of klein's --kv auto type:
+    q8_0 up to 131,072 cells, q4_0 beyond, engine.cpp:114; 4 recurrent slots, f16 snapshots). Per context: batch-1
+    decode and the 4-token verify step, each one CUDA graph of 64 layers (RMS norm, projections by cuBLAS through
+    torch, kb_layer_attention / kb_layer_deltanet, output projection, residual), timed whole and with the projections
+    and norms removed (the attention-path ops alone, fed by fixed projection outputs). Plus the MTP head's attention
+    over its full 16,384-cell ring and the 16,384-token prefill in klein's 2,048-token chunks."""
+    import ctypes  # noqa: F401
+
+    from klein_b200.state import State
+
+    HD, NH, NKV, S, HK, HV = D, H, H_KV, 128, 16, 48
+    CH = 2 * S * HK + S * HV
+    eps = 1e-6
+    dims = kb.qwen35_dims()
+    n_layer = dims.n_layer
+    attn_layer = [((il + 1) % dims.full_attn_interval) == 0 for il in range(n_layer)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(27)
+    bf = torch.bfloat16
+
+    def randw(i, o):
+        return (torch.randn(i, o, device=dev, generator=gen) * (i ** -0.5)).to(bf)
+
+    W = []
+    for il in range(n_layer + 1):  # + the MTP block's attention (index n_layer)
+        if il == n_layer or attn_layer[il]:
+            W.append({"wq": randw(HIDDEN, 2 * NH * HD), "wk": randw(HIDDEN, NKV * HD), "wv": randw(HIDDEN, NKV * HD),
+                      "wo": randw(NH * HD, HIDDEN), "norm": torch.ones(HIDDEN, device=dev),
+                      "q_norm": torch.ones(HD, device=dev), "k_norm": torch.ones(HD, device=dev)})
+        else:
+            W.append({"wqkv": randw(HIDDEN, CH), "wz": randw(HIDDEN, HV * S), "wb": randw(HIDDEN, HV),
+                      "wa": randw(HIDDEN, HV), "wout": randw(HV * S, HIDDEN), "norm": torch.ones(HIDDEN, device=dev),
+                      "conv_w": torch.randn(CH, 4, device=dev, generator=gen) * 0.5,
+                      "dt": torch.randn(HV, device=dev, generator=gen), "a": -torch.rand(HV, device=dev, generator=gen) - 0.1,
+                      "ssm_norm": torch.ones(S, device=dev)})
+    n_params = sum(t.numel() for w in W[:n_layer] for t in w.values() if t.dtype == bf)
+    rope = kb.KbRopeParams(64, (ctypes.c_int32 * 4)(11, 11, 10, 0), 40, 1e7, 1.0, 1.0)
+
+    def rms(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+    def timed(fn, reps):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(max(1, warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    def fill_caches(st, n_cells, kv_type):
+        # ~N(0,1) rows quantised once (klein's set_rows rounding), copied into every attention layer's K and V
+        rows = torch.randn(min(n_cells, 65536), NKV * HD, device=dev, generator=gen)
+        qr = quantize_q8_0_rows(torch, rows) if kv_type == kb.Q8_0 else quantize_q4_0_rows(torch, rows)
+        del rows
+        for il in range(n_layer + 1):
+            if il < n_layer and not attn_layer[il]:
+                continue
+            lay = st.layer(il)
+            for t in (lay.k, lay.v):
+                view = st.view(t)
+                for c0 in range(0, view.shape[0], qr.shape[0]):
+                    c1 = min(view.shape[0], c0 + qr.shape[0])
+                    view[c0:c1].copy_(qr[:c1 - c0])
+        del qr
+
+    def layer_ops(st, n, p, pos, kv_idx, scratch_a, scratch_g, proj, outs, mtp=False):
+        """the attention-path ops of every layer for one pass, fed by proj[il] (the projection outputs)"""
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for il in ([n_layer] if mtp else range(n_layer)):
+            w, pr = W[il], proj[il]
+            if il == n_layer or attn_layer[il]:
+                st.attention(il, p, pr["qfull"], pr["kcur"], pr["vcur"], pos, kv_idx, w["q_norm"], w["k_norm"], eps, rope,
+                             outs["attn"], scratch_a, stream)
+            else:
+                st.deltanet(il, n, pr["qkv"], pr["z"], pr["b"], pr["a"], w["dt"], w["a"], w["conv_w"], w["ssm_norm"], eps,
+                            outs["gdn"], scratch_g, stream)
+
+    def full_step(st, n, p, pos, kv_idx, scratch_a, scratch_g, x, outs, mtp=False):
+        """one forward pass of n tokens through the stack: norms, projections, the layer ops, output projections and
+        residuals (x updated in place)"""
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for il in ([n_layer] if mtp else range(n_layer)):
+            w = W[il]
+            hb = rms(x, w["norm"]).to(bf)
+            if il == n_layer or attn_layer[il]:
+                qfull = (hb @ w["wq"]).float()
+                kcur, vcur = (hb @ w["wk"]).float(), (hb @ w["wv"]).float()
+                st.attention(il, p, qfull, kcur, vcur, pos, kv_idx, w["q_norm"], w["k_norm"], eps, rope, outs["attn"],
+                             scratch_a, stream)
+                x.add_((outs["attn"].to(bf) @ w["wo"]).float())
+            else:
+                qkv, z = (hb @ w["wqkv"]).float(), (hb @ w["wz"]).float()
+                br, al = (hb @ w["wb"]).float(), (hb @ w["wa"]).float()
+                st.deltanet(il, n, qkv, z, br, al, w["dt"], w["a"], w["conv_w"], w["ssm_norm"], eps, outs["gdn"],
+                            scratch_g, stream)
+                x.add_((outs["gdn"].to(bf) @ w["wout"]).float())
+
+    def proj_inputs(n):
+        pr = []
+        for il in range(n_layer + 1):
+            if il == n_layer or attn_layer[il]:
+                pr.append({"qfull": torch.randn(n, 2 * NH * HD, device=dev, generator=gen),
+                           "kcur": torch.randn(n, NKV * HD, device=dev, generator=gen),
+                           "vcur": torch.randn(n, NKV * HD, device=dev, generator=gen)})
+            else:
+                pr.append({"qkv": torch.randn(n, CH, device=dev, generator=gen),
+                           "z": torch.randn(n, HV * S, device=dev, generator=gen),
+                           "b": torch.randn(n, HV, device=dev, generator=gen),
+                           "a": torch.randn(n, HV, device=dev, generator=gen)})
+        return pr
+
+    def pass_inputs(st, n, mtp=False, cell0=None, kv_lo=0):
+        p, idx = st.plan(n, kv_lo=kv_lo, mtp=mtp, cell0=cell0)
+        posv = torch.arange(n, dtype=torch.int32, device=dev) + int(p.cell0)
+        pos = torch.cat([posv, posv, posv, torch.zeros_like(posv)])
+        return p, pos, torch.from_numpy(idx).to(dev)
+
+    pk, _ = measured_peaks()
+    res = {"workload": "config[4] whole attention stack, qwen35 27B shapes: 48 gated DeltaNet + 16 GQA layers (24 / 4 "
+                       "heads x 256), hidden 5120, random-init bf16 projections (FFN blocks excluded), klein's State in "
+                       "HBM with --kv auto cache types, 4 recurrent slots",
+           "projection_params": n_params, "decode": {}, "verify": {}}
+    reps = max(3, steps)
+    for ctx_len in contexts:
+        kv_type = kb.Q8_0 if ctx_len <= 131072 else kb.Q4_0
+        cfg = kb.state_config(ctx_len, kv_type, kv_type, 4, kb.F16, 16384)
+        st = State(dims, cfg, dev)
+        fill_caches(st, ctx_len, kv_type)
+        for mode, n in (("decode", 1), ("verify", 4)):
+            st.n_past = ctx_len - n  # the pass writes the last n cells of the context
+            p, pos, kv_idx = pass_inputs(st, n)
+            scratch_a = torch.empty(max(st.attention_scratch_bytes(n_layer - 1, p), 1), dtype=torch.uint8, device=dev)
+            scratch_g = torch.empty(max(st.deltanet_scratch_bytes(0, n), 1), dtype=torch.uint8, device=dev)
+            outs = {"attn": torch.empty(n, NH * HD, device=dev), "gdn": torch.empty(n, HV * S, device=dev)}
+            x = torch.randn(n, HIDDEN, device=dev, generator=gen)
+            proj = proj_inputs(n)
+            t_full = timed(lambda: full_step(st, n, p, pos, kv_idx, scratch_a, scratch_g, x, outs), reps)
+            t_attn = timed(lambda: layer_ops(st, n, p, pos, kv_idx, scratch_a, scratch_g, proj, outs), reps)
+            kvb = kv_bytes_per_layer(int(p.n_kv), "q8_0" if kv_type == kb.Q8_0 else "q4_0")
+            gdn_b = S * S * HV * 4 * 2 + 3 * S * S * HV * 2  # state read + slot 0 write + 3 f16 snapshots
+            att_bytes = 16 * kvb + 48 * gdn_b
+            res[mode][str(ctx_len)] = {
+                "kv_type": "q8_0" if kv_type == kb.Q8_0 else "q4_0", "step_us": round(t_full, 1),
+                "attention_us": round(t_attn, 1), "projections_and_norms_us": round(t_full - t_attn, 1),
+                "attention_bytes": att_bytes,
+                "attention_hbm_frac": round(att_bytes / (t_attn * 1e-6) / 1e9 / pk["hbm_gbs"], 4)}
+            del proj, outs, scratch_a, scratch_g
+        st.close()
+        del st
+        torch.cuda.empty_cache()
+
+    # the MTP head's attention: decode over its full 16,384-cell ring at a position past several wraps
+    cfg = kb.state_config(131072, kb.Q8_0, kb.Q8_0, 4, kb.F16, 16384)
+    st = State(dims, cfg, dev)
+    fill_caches(st, 16384, kb.Q8_0)
+    p, pos, kv_idx = pass_inputs(st, 1, mtp=True, cell0=70001, kv_lo=1)
+    scratch_a = torch.empty(st.attention_scratch_bytes(n_layer, p), dtype=torch.uint8, device=dev)
+    outs = {"attn": torch.empty(1, NH * HD, device=dev), "gdn": torch.empty(1, HV * S, device=dev)}
+    x = torch.randn(1, HIDDEN, device=dev, generator=gen)
+    proj = proj_inputs(1)
+    t_full = timed(lambda: full_step(st, 1, p, pos, kv_idx, scratch_a, None, x, outs, mtp=True), reps)
+    t_attn = timed(lambda: layer_ops(st, 1, p, pos, kv_idx, scratch_a, None, proj, outs, mtp=True), reps)
+    res["mtp_16k"] = {"ring_cells": int(p.ring), "n_kv": int(p.n_kv), "layer_us": round(t_full, 1),
+                      "attention_us": round(t_attn, 1), "kv_type": "q8_0"}
+    st.close()
+    del st, proj, outs, scratch_a
+    torch.cuda.empty_cache()
+
+    # the 16,384-token prefill: 8 chunks of 2,048 (klein's n_ubatch) through the 64 layers, q8_0 caches
+    T, CHUNK = 16384, 2048
+    cfg = kb.state_config(T, kb.Q8_0, kb.Q8_0, 4, kb.F16, 16384)
+    st = State(dims, cfg, dev)
+    x = torch.randn(CHUNK, HIDDEN, device=dev, generator=gen)
+    outs = {"attn": torch.empty(CHUNK, NH * HD, device=dev), "gdn": torch.empty(CHUNK, HV * S, device=dev)}
+    passes = []
+    for c in range(T // CHUNK):
+        st.n_past = c * CHUNK
+        passes.append(pass_inputs(st, CHUNK))
+    sa = max(st.attention_scratch_bytes(n_layer - 1, pp[0]) for pp in passes)
+    scratch_a = torch.empty(sa, dtype=torch.uint8, device=dev)
+    scratch_g = torch.empty(st.deltanet_scratch_bytes(0, CHUNK), dtype=torch.uint8, device=dev)
+    proj = proj_inputs(CHUNK)
+
+    def prefill(attn_only):
+        st.clear(torch.cuda.current_stream(dev).cuda_stream)
+        for p, pos, kv_idx in passes:
+            if attn_only:
+                layer_ops(st, CHUNK, p, pos, kv_idx, scratch_a, scratch_g, proj, outs)
+            else:
+                full_step(st, CHUNK, p, pos, kv_idx, scratch_a, scratch_g, x, outs)
+
+    times = {}
+    for attn_only in (False, True):
+        prefill(attn_only)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        prefill(attn_only)
+        e1.record()
+        torch.cuda.synchronize()
+        times[attn_only] = e0.elapsed_time(e1)
+    flops = 16 * 4.0 * D * H * T * (T + 1) / 2 + 48 * T * HV * (10 * 64 * S + 6 * S * S)
+    res["prefill_16384"] = {"chunk": CHUNK, "kv_type": "q8_0", "total_ms": round(times[False], 2),
+                            "attention_ms": round(times[True], 2),
+                            "projections_and_norms_ms": round(times[False] - times[True], 2),
+                            "attention_algorithmic_tflop": round(flops / 1e12, 2),
+                            "attention_tflops": round(flops / (times[True] * 1e-3) / 1e12, 1)}
+    st.close()
+    del st, proj, outs, scratch_a, scratch_g, W
+    torch.cuda.empty_cache()
+    return res
+
+
 def make_layers(kb, torch, dev, gen, n_kv, kv_type):
     layers = []
     for _ in range(LAYERS):
@@ -895,6 +1129,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["io_ops"] = bench_io_ops(kb, torch, dev, max(20, args.steps // 2), args.warmup)
+        if not args.no_stack:
+            secondary["stack_27b"] = bench_stack(kb, torch, dev, max(3, args.steps // 4), args.warmup)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -995,6 +1231,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU timing for cpu_baseline")
     ap.add_argument("--layers", type=int, default=16, help="full-attention layers per step (16 = the headline)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary measurements (q8_0 / q4_0 caches, prefill, DeltaNet, I/O ops)")
+    ap.add_argument("--no-stack", action="store_true", help="skip the whole-stack (config[4]) secondary")
+    ap.add_argument("--stack-only", action="store_true", help="run only the whole-stack (config[4]) measurement")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph per step")
     ap.add_argument("--exchange", default="kernel", choices=["kernel", "p2p", "fused", "nccl"],
                     help="N > 1: the partials exchange over NVLink inside the attention kernel (kernel, default: one "
@@ -1007,6 +1245,15 @@ def main():
     args = ap.parse_args()
     if args.case:
         run_case(args.case)
+        return
+    if args.stack_only:
+        import torch
+
+        import klein_b200 as kb
+
+        dev = torch.device("cuda:0")
+        torch.cuda.set_device(dev)
+        print(json.dumps({"stack_27b": bench_stack(kb, torch, dev, max(3, args.steps // 4), max(args.warmup, 3))}), flush=True)
         return
     global LAYERS
     LAYERS = args.layers

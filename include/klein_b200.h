@@ -325,6 +325,109 @@ kb_status kb_gdn_input(const kb_tensor* qkv, const kb_tensor* conv_state, const 
 kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_tensor* w, float rms_eps,
                             const kb_tensor* dst, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * klein's per-sequence State, resident in HBM (replaces src/state.h / src/state.cpp's tensors; klein's mapped host
+ * KV cache and its bulk host view, state.cpp:110-134, are not needed when the cache lives in device memory), the
+ * per-pass indexing of Engine::run (engine.cpp:254-326), the accept / rollback of Engine::generate's verify step
+ * (engine.cpp:584-590), and Builder::attention / Builder::deltanet (graph.cpp:87-191) bound to the state without
+ * their weight GEMMs (the caller's projections feed them and consume their outputs).
+ */
+
+/* qwen35's shapes (src/model.h HParams). Layer il < n_layer is full attention iff (il + 1) % full_attn_interval
+ * == 0, DeltaNet otherwise; with_mtp adds the MTP layer (index n_layer), full attention over a ring of cells. */
+typedef struct kb_qwen35_dims {
+    int32_t n_layer, full_attn_interval;
+    int32_t n_head, n_head_kv, head_dim;
+    int32_t ssm_conv_kernel, ssm_d_state, ssm_n_group, ssm_dt_rank;
+    int32_t with_mtp;
+} kb_qwen35_dims;
+
+/* src/state.h StateConfig: cache types (f16, bf16, q8_0 or q4_0), recurrent slots (1 + max drafts) and their
+ * snapshot type (f16, bf16 or f32), and the MTP ring's cells (min(n_ctx, mtp_window), state.cpp:17). */
+typedef struct kb_state_config {
+    int32_t n_ctx;
+    int32_t type_k, type_v;
+    int32_t n_snapshots;
+    int32_t snap_type;
+    int32_t mtp_window;
+} kb_state_config;
+
+typedef struct kb_state kb_state;
+
+/* One layer's tensors (State::k / v / conv / ssm / ssm_snap): attention layers get k, v [kv_row, cells] (their
+ * other fields are zero), DeltaNet layers conv [(kc - 1) * channels, n_snapshots] f32, ssm [d_state^2 * dt_rank, 1]
+ * f32 and ssm_snap [d_state^2 * dt_rank, n_snapshots - 1] (data NULL when n_snapshots == 1). */
+typedef struct kb_state_layer {
+    kb_tensor k, v, conv, ssm, ssm_snap;
+} kb_state_layer;
+
+/* One forward pass over n_tokens cells from cell0 (Engine::run): ring (MTP only, 0 otherwise), the cells attended
+ * n_kv (graph.cpp:16-19 padded_n_kv, at most the ring), and the visibility rule as analytic bounds (scale
+ * 1 / sqrt(head_dim), causal, pos0 = cell0, kv_lo, ring), the same cells klein's dense mask admits. */
+typedef struct kb_pass {
+    int32_t n_tokens, mtp;
+    int64_t cell0, kv_lo, ring, n_kv;
+    kb_fa_params fa;
+} kb_pass;
+
+/* Byte counts of state_kv_bytes / state_mtp_kv_bytes / state_recurrent_bytes (state.cpp:20-35). */
+kb_status kb_state_sizes(const kb_qwen35_dims* dims, const kb_state_config* cfg, size_t* kv_bytes,
+                         size_t* mtp_kv_bytes, size_t* recurrent_bytes);
+/* State::State: one device allocation on the current device, zeroed; kb_state_destroy frees it. */
+kb_status kb_state_create(const kb_qwen35_dims* dims, const kb_state_config* cfg, kb_state** out);
+/* The same inside the caller's device memory (e.g. a ggml backend buffer, as klein's State allocates its tensors),
+ * at least kb_state_required_bytes bytes, 256-byte aligned, zeroed here; kb_state_destroy then frees nothing. */
+size_t kb_state_required_bytes(const kb_qwen35_dims* dims, const kb_state_config* cfg);
+kb_status kb_state_create_in(const kb_qwen35_dims* dims, const kb_state_config* cfg, void* base, size_t bytes,
+                             kb_state** out);
+kb_status kb_state_destroy(kb_state* state);
+size_t kb_state_device_bytes(const kb_state* state);
+kb_status kb_state_get_layer(const kb_state* state, int32_t il, kb_state_layer* out);
+/* State::n_past / n_past_mtp (mtp != 0). */
+int64_t kb_state_n_past(const kb_state* state, int32_t mtp);
+kb_status kb_state_set_n_past(kb_state* state, int32_t mtp, int64_t n_past);
+/* State::clear (state.cpp:148-160): recurrent states and snapshots to zero, n_past = n_past_mtp = 0. */
+kb_status kb_state_clear(kb_state* state, void* stream);
+/* State::rollback_recurrent (state.cpp:162-183): slot s -> current, every DeltaNet layer, one launch. */
+kb_status kb_state_rollback(kb_state* state, int32_t s, void* stream);
+/* Engine::run's pass indexing; kv_idx (host, n_tokens entries, may be NULL) receives each token's cache row
+ * ((cell0 + i) mod ring for the MTP layer). Fails with KB_ERR_ARG when the pass does not fit the context. */
+kb_status kb_plan_pass(const kb_qwen35_dims* dims, const kb_state_config* cfg, int32_t mtp, int32_t n_tokens,
+                       int64_t cell0, int64_t kv_lo, kb_pass* out, int64_t* kv_idx);
+/* the same from the state's n_past (or n_past_mtp) */
+kb_status kb_state_plan_pass(const kb_state* state, int32_t mtp, int32_t n_tokens, int64_t kv_lo, kb_pass* out,
+                             int64_t* kv_idx);
+/* After a verify pass of n_batch cells from base: n_past = base + accepted + 1, and the DeltaNet states roll back
+ * past the (n_batch - 1 - accepted) rejected drafts (Engine::generate, engine.cpp:584-590). */
+kb_status kb_state_accept(kb_state* state, int64_t base, int32_t n_batch, int32_t accepted, void* stream);
+
+/*
+ * Builder::attention without its GEMMs (graph.cpp:94-124) for attention layer il (or the MTP layer, pass->mtp): the
+ * prologue (q / gate split, Q / K RMS norms, M-RoPE, K and V rows written into the state's cache at kv_idx) and the
+ * gated flash attention over pass->n_kv cells. qfull, kcur, vcur, pos, kv_idx, q_norm, k_norm and rope as
+ * kb_attn_prologue (kv_idx: device copy of kb_plan_pass's); out f32 [head_dim * n_head, n_tokens] contiguous (the
+ * input of wo). scratch: kb_layer_attention_scratch_bytes bytes, 256-byte aligned (the prologue's Q and gate, then the
+ * attention's scratch).
+ */
+size_t kb_layer_attention_scratch_bytes(const kb_state* state, int32_t il, const kb_pass* pass);
+kb_status kb_layer_attention(kb_state* state, int32_t il, const kb_pass* pass, const kb_tensor* qfull,
+                             const kb_tensor* kcur, const kb_tensor* vcur, const kb_tensor* pos, const kb_tensor* kv_idx,
+                             const kb_tensor* q_norm, const kb_tensor* k_norm, float rms_eps, const kb_rope_params* rope,
+                             const kb_tensor* out, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * Builder::deltanet without its GEMMs (graph.cpp:134-190) for DeltaNet layer il: kb_gdn_input on the state's conv
+ * slots, the recurrence into the state's ssm and snapshot rows (kb_gated_delta_net_cache with K = n_snapshots), and
+ * the gated RMS norm. qkv, beta_raw, alpha, dt_bias, a, conv_w as kb_gdn_input; z and ssm_norm as kb_gdn_gated_norm;
+ * out f32 [d_state * dt_rank, n_tokens] (the input of ssm_out). scratch: kb_layer_deltanet_scratch_bytes bytes,
+ * 256-byte aligned (q, k, v, beta, g, the attention rows, then the chunked form's records for long passes).
+ */
+size_t kb_layer_deltanet_scratch_bytes(const kb_state* state, int32_t il, int32_t n_tokens);
+kb_status kb_layer_deltanet(kb_state* state, int32_t il, int32_t n_tokens, const kb_tensor* qkv, const kb_tensor* z,
+                            const kb_tensor* beta_raw, const kb_tensor* alpha, const kb_tensor* dt_bias,
+                            const kb_tensor* a, const kb_tensor* conv_w, const kb_tensor* ssm_norm, float rms_eps,
+                            const kb_tensor* out, void* scratch, size_t scratch_bytes, void* stream);
+
 /*
  * Size of the device buffer built into the library for kb_flash_attn_ext_noalloc (per GPU, held from the
  * library's load until the process exits).

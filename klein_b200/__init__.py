@@ -56,6 +56,24 @@ EXPORTED = [
     "kb_flash_attn_ext_push_scratch_bytes",
     "kb_flash_attn_ext_exchange",
     "kb_exchange_flag_bytes",
+    "kb_state_sizes",
+    "kb_state_create",
+    "kb_state_required_bytes",
+    "kb_state_create_in",
+    "kb_state_destroy",
+    "kb_state_device_bytes",
+    "kb_state_get_layer",
+    "kb_state_n_past",
+    "kb_state_set_n_past",
+    "kb_state_clear",
+    "kb_state_rollback",
+    "kb_plan_pass",
+    "kb_state_plan_pass",
+    "kb_state_accept",
+    "kb_layer_attention_scratch_bytes",
+    "kb_layer_attention",
+    "kb_layer_deltanet_scratch_bytes",
+    "kb_layer_deltanet",
 ]
 
 
@@ -78,6 +96,39 @@ class KbRopeParams(ctypes.Structure):
 class KbFaParams(ctypes.Structure):
     _fields_ = [("scale", c_float), ("max_bias", c_float), ("logit_softcap", c_float), ("prec", c_int32),
                 ("causal", c_int32), ("pos0", c_int64), ("kv_lo", c_int64), ("ring", c_int64)]
+
+
+class KbQwen35Dims(ctypes.Structure):
+    _fields_ = [("n_layer", c_int32), ("full_attn_interval", c_int32), ("n_head", c_int32), ("n_head_kv", c_int32),
+                ("head_dim", c_int32), ("ssm_conv_kernel", c_int32), ("ssm_d_state", c_int32), ("ssm_n_group", c_int32),
+                ("ssm_dt_rank", c_int32), ("with_mtp", c_int32)]
+
+
+class KbStateConfig(ctypes.Structure):
+    _fields_ = [("n_ctx", c_int32), ("type_k", c_int32), ("type_v", c_int32), ("n_snapshots", c_int32),
+                ("snap_type", c_int32), ("mtp_window", c_int32)]
+
+
+class KbStateLayer(ctypes.Structure):
+    _fields_ = [("k", KbTensor), ("v", KbTensor), ("conv", KbTensor), ("ssm", KbTensor), ("ssm_snap", KbTensor)]
+
+
+class KbPass(ctypes.Structure):
+    _fields_ = [("n_tokens", c_int32), ("mtp", c_int32), ("cell0", c_int64), ("kv_lo", c_int64), ("ring", c_int64),
+                ("n_kv", c_int64), ("fa", KbFaParams)]
+
+
+def qwen35_dims(n_layer=64, with_mtp=1, full_attn_interval=4, n_head=24, n_head_kv=4, head_dim=256, conv_kernel=4,
+                d_state=128, n_group=16, dt_rank=48) -> KbQwen35Dims:
+    """qwen35 27B's attention shapes (model.h HParams; 64 decoder layers, every 4th full attention, 24 / 4 heads of
+    256, DeltaNet 16 key / 48 value heads of 128, conv kernel 4) unless given otherwise."""
+    return KbQwen35Dims(n_layer, full_attn_interval, n_head, n_head_kv, head_dim, conv_kernel, d_state, n_group, dt_rank,
+                        with_mtp)
+
+
+def state_config(n_ctx, type_k=None, type_v=None, n_snapshots=4, snap_type=None, mtp_window=16384) -> KbStateConfig:
+    return KbStateConfig(n_ctx, Q8_0 if type_k is None else type_k, Q8_0 if type_v is None else type_v, n_snapshots,
+                         F16 if snap_type is None else snap_type, mtp_window)
 
 
 _lib = None
@@ -130,6 +181,45 @@ def lib():
                                                  P(KbTensor), c_void_p, c_size_t, c_void_p]
         L.kb_exchange_flag_bytes.restype = c_size_t
         L.kb_exchange_flag_bytes.argtypes = [c_int32]
+        L.kb_state_sizes.restype = c_int32
+        L.kb_state_sizes.argtypes = [P(KbQwen35Dims), P(KbStateConfig), P(c_size_t), P(c_size_t), P(c_size_t)]
+        L.kb_state_create.restype = c_int32
+        L.kb_state_create.argtypes = [P(KbQwen35Dims), P(KbStateConfig), P(c_void_p)]
+        L.kb_state_required_bytes.restype = c_size_t
+        L.kb_state_required_bytes.argtypes = [P(KbQwen35Dims), P(KbStateConfig)]
+        L.kb_state_create_in.restype = c_int32
+        L.kb_state_create_in.argtypes = [P(KbQwen35Dims), P(KbStateConfig), c_void_p, c_size_t, P(c_void_p)]
+        L.kb_state_destroy.restype = c_int32
+        L.kb_state_destroy.argtypes = [c_void_p]
+        L.kb_state_device_bytes.restype = c_size_t
+        L.kb_state_device_bytes.argtypes = [c_void_p]
+        L.kb_state_get_layer.restype = c_int32
+        L.kb_state_get_layer.argtypes = [c_void_p, c_int32, P(KbStateLayer)]
+        L.kb_state_n_past.restype = c_int64
+        L.kb_state_n_past.argtypes = [c_void_p, c_int32]
+        L.kb_state_set_n_past.restype = c_int32
+        L.kb_state_set_n_past.argtypes = [c_void_p, c_int32, c_int64]
+        L.kb_state_clear.restype = c_int32
+        L.kb_state_clear.argtypes = [c_void_p, c_void_p]
+        L.kb_state_rollback.restype = c_int32
+        L.kb_state_rollback.argtypes = [c_void_p, c_int32, c_void_p]
+        L.kb_plan_pass.restype = c_int32
+        L.kb_plan_pass.argtypes = [P(KbQwen35Dims), P(KbStateConfig), c_int32, c_int32, c_int64, c_int64, P(KbPass),
+                                   c_void_p]
+        L.kb_state_plan_pass.restype = c_int32
+        L.kb_state_plan_pass.argtypes = [c_void_p, c_int32, c_int32, c_int64, P(KbPass), c_void_p]
+        L.kb_state_accept.restype = c_int32
+        L.kb_state_accept.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_void_p]
+        L.kb_layer_attention_scratch_bytes.restype = c_size_t
+        L.kb_layer_attention_scratch_bytes.argtypes = [c_void_p, c_int32, P(KbPass)]
+        L.kb_layer_attention.restype = c_int32
+        L.kb_layer_attention.argtypes = [c_void_p, c_int32, P(KbPass)] + [P(KbTensor)] * 7 + \
+            [ctypes.c_float, P(KbRopeParams), P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_layer_deltanet_scratch_bytes.restype = c_size_t
+        L.kb_layer_deltanet_scratch_bytes.argtypes = [c_void_p, c_int32, c_int32]
+        L.kb_layer_deltanet.restype = c_int32
+        L.kb_layer_deltanet.argtypes = [c_void_p, c_int32, c_int32] + [P(KbTensor)] * 8 + \
+            [ctypes.c_float, P(KbTensor), c_void_p, c_size_t, c_void_p]
         L.kb_gdn_input.restype = c_int32
         L.kb_gdn_input.argtypes = [P(KbTensor)] * 7 + [c_int32, c_int32, ctypes.c_float] + [P(KbTensor)] * 5 + [c_void_p]
         L.kb_gdn_gated_norm.restype = c_int32
