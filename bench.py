@@ -525,6 +525,139 @@ def bench_gdn_prefill(kb, torch, dev, steps, warmup):
                          "algorithmic_flops_per_launch": flops, "traffic": ncu_traffic("gdn_chunk_prefill_4096")}}
 
 
+# ------------------------------------------------------------------------------------------------ head shards
+
+def bench_head_shards(kb, torch, dev, steps, warmup, rank, world, dist):
+    """N > 1: the paths that shard by heads with no collective (kv_split.gdn_head_shard / fa_head_shard), each rank
+    running the single-GPU op on its heads: config[1]'s DeltaNet verify step (48 layers per CUDA graph), config[2]'s
+    4,096-token prefill attention (bf16) and its chunked DeltaNet prefill. Strong scaling: the whole op's work is split
+    over the N ranks; the time is the max over ranks (device events), throughput = the whole op's work / that time."""
+    import ctypes
+
+    import numpy as np
+
+    from klein_b200.kv_split import fa_head_shard, gdn_head_shard
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_graph(fn, reps):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(max(1, warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    pk, kind = measured_peaks()
+    res = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(55)
+    # DeltaNet verify step on this rank's value heads (key heads gathered, H_k = H_v = local heads)
+    L_, T, K, S = 48, 4, 4, 128
+    lo, hi, kidx = gdn_head_shard(16, 48, world, rank)
+    n = hi - lo
+    q = torch.nn.functional.normalize(torch.randn(1, T, 16, S, device=dev, generator=gen), dim=-1)[:, :, kidx].contiguous()
+    k = torch.nn.functional.normalize(torch.randn(1, T, 16, S, device=dev, generator=gen), dim=-1)[:, :, kidx].contiguous()
+    v = torch.randn(1, T, n, S, device=dev, generator=gen)
+    g = -torch.nn.functional.softplus(torch.randn(1, T, n, 1, device=dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(1, T, n, 1, device=dev, generator=gen))
+    states = [torch.randn(1, n, S, S, device=dev, generator=gen) * 0.02 for _ in range(L_)]
+    snaps = [torch.zeros(K - 1, S * S * n, dtype=torch.float16, device=dev) for _ in range(L_)]
+    attn = torch.empty(1, T, n, S, device=dev)
+    L = kb.lib()
+    ins = [kb.from_torch(x) for x in (q, k, v, g, beta)]
+    outs = [(kb.from_torch(states[l]), kb.from_torch(snaps[l])) for l in range(L_)]
+    at = kb.from_torch(attn)
+
+    def gdn_step():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        for l in range(L_):
+            rc = L.kb_gated_delta_net_cache(*[ctypes.byref(x) for x in ins], ctypes.byref(outs[l][0]),
+                                            ctypes.byref(outs[l][1]), K, ctypes.byref(at), None, 0, ctypes.c_void_p(st))
+            if rc != 0:
+                raise kb.KbError("kb_gated_delta_net_cache", rc)
+
+    us = max_over_ranks(time_graph(gdn_step, max(3, steps)) / L_)
+    nbytes = S * S * 48 * 4 * 2 + (K - 1) * S * S * 48 * 2 + (2 * T * 16 * S + 2 * T * 48 * S + 2 * T * 48) * 4
+    res["gdn_verify_heads"] = {"value": round(us, 2), "unit": "us/layer", "heads_per_rank": n,
+                               "workload": "config[1] DeltaNet verify step (48 layers per graph), value heads split "
+                                           "over the ranks, max over ranks",
+                               "roofline": {"bound": "hbm", "achieved": round(nbytes / (us * 1e-6) / 1e9, 1),
+                                            "peak": pk["hbm_gbs"] * world, "unit": "GB/s (all ranks)",
+                                            "frac": round(nbytes / (us * 1e-6) / 1e9 / (pk["hbm_gbs"] * world), 4)}}
+    del states, snaps, q, k, v, g, beta, attn
+    # prefill attention (config[2], bf16) on this rank's query heads and the KV heads they read
+    TT = 4096
+    q_lo, q_hi, kv_lo, kv_hi = fa_head_shard(H, H_KV, world, rank)
+    nq, nkv = q_hi - q_lo, kv_hi - kv_lo
+    qp = torch.randn(1, TT, nq, D, device=dev, generator=gen).bfloat16().float()
+    kk = torch.randn(TT, nkv * D, device=dev, generator=gen).bfloat16()
+    vv = torch.randn(TT, nkv * D, device=dev, generator=gen).bfloat16()
+    kv_, vv_ = kb.kv_cache_view(kk, kb.BF16, nkv, D), kb.kv_cache_view(vv, kb.BF16, nkv, D)
+    outp = torch.empty(1, TT, nq, D, device=dev)
+
+    def prefill():
+        kb.flash_attn_ext(qp, kv_, vv_, SCALE, causal=True, pos0=0, out=outp,
+                          stream=torch.cuda.current_stream(dev).cuda_stream)
+
+    us = max_over_ranks(time_graph(prefill, max(3, steps // 4)))
+    flops = 2.0 * D * H * TT * (TT + 1)
+    tf = flops / (us * 1e-6) / 1e12
+    res["prefill_bf16_4096_heads"] = {"value": round(tf, 1), "unit": "TFLOP/s (all ranks)", "us_per_layer": round(us, 2),
+                                      "q_heads_per_rank": nq, "kv_heads_per_rank": nkv,
+                                      "roofline": {"bound": "tensor", "achieved": round(tf, 1),
+                                                   "peak": pk["bf16_tflops"] * world, "unit": "TFLOP/s (all ranks)",
+                                                   "frac": round(tf / (pk["bf16_tflops"] * world), 4)}}
+    del qp, kk, vv, outp
+    # chunked DeltaNet prefill (config[2]) on this rank's value heads
+    rng = np.random.default_rng(4096)
+    qn = rng.standard_normal((1, TT, 16, S), dtype=np.float32)
+    kn = rng.standard_normal((1, TT, 16, S), dtype=np.float32)
+    qn /= np.linalg.norm(qn, axis=-1, keepdims=True)
+    kn /= np.linalg.norm(kn, axis=-1, keepdims=True)
+    vn = rng.standard_normal((1, TT, 48, S), dtype=np.float32)
+    bn = (1.0 / (1.0 + np.exp(-rng.standard_normal((1, TT, 48, 1))))).astype(np.float32)
+    gn = (-np.logaddexp(0.0, rng.standard_normal((1, TT, 48, 1)))).astype(np.float32)
+    args = [torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in
+            (qn[:, :, kidx], kn[:, :, kidx], vn[:, :, lo:hi], gn[:, :, lo:hi], bn[:, :, lo:hi],
+             np.zeros((1, n, S, S), dtype=np.float32))]
+    nb = L.kb_gated_delta_net_scratch_bytes(ctypes.byref(kb.from_torch(args[2])), ctypes.byref(kb.from_torch(args[3])), 4)
+    scratch = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+
+    def gdn_prefill():
+        kb.gated_delta_net(*args, 4, scratch=scratch, stream=torch.cuda.current_stream(dev).cuda_stream)
+
+    us = max_over_ranks(time_graph(gdn_prefill, max(3, steps // 4)))
+    flops = TT * 48 * (10 * 64 * S + 6 * S * S)
+    tf = flops / (us * 1e-6) / 1e12
+    res["gdn_prefill_4096_heads"] = {"value": round(us, 1), "unit": "us/layer", "heads_per_rank": n,
+                                     "tflops_algorithmic": round(tf, 2),
+                                     "roofline": {"bound": "tensor", "achieved": round(tf, 2),
+                                                  "peak": pk["bf16_tflops"] * world, "unit": "TFLOP/s (all ranks)",
+                                                  "frac": round(tf / (pk["bf16_tflops"] * world), 4)}}
+    return res
+
+
 # ------------------------------------------------------------------------------------------------ whole stack
 
 HIDDEN = 5120  # qwen35 27B n_embd
@@ -1095,6 +1228,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                              # ncu DRAM bytes of one full-cache launch; a rank of an N-way split streams 1/N of it
                              "traffic": (lambda t: None if t is None else int(t / world))(
                                  ncu_traffic(f"fa_stream_{kvt}_verify262k"))}}
+
+    if not args.no_secondary and world > 1:
+        graphs.clear()
+        del layers[:]
+        torch.cuda.empty_cache()
+        secondary.update(bench_head_shards(kb, torch, dev, args.steps, args.warmup, rank, world, dist))
 
     peaks, peak_kind = measured_peaks()
     bytes_layer = kv_bytes_per_layer(n_kv, "f16")
