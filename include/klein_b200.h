@@ -195,6 +195,12 @@ kb_status kb_flash_attn_ext_exchange(const kb_tensor* q, const kb_tensor* k, con
                                      int32_t n_ranks, const kb_tensor* dst, void* scratch, size_t scratch_bytes,
                                      void* stream);
 
+/* 1 when kb_flash_attn_ext accepts these operands (shapes, types, strides, params; data pointers may still be NULL,
+ * as in ggml-cuda's supports_op, ggml-cuda.cu:5775-5776), 0 otherwise. Alignment of the data pointers themselves and
+ * of dst are checked by the call. */
+int32_t kb_flash_attn_ext_supported(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                    const kb_fa_params* params);
+
 /* Scratch needed by kb_flash_attn_ext / kb_flash_attn_ext_partial for these operands on the current
  * device (the role of ggml_cuda_flash_attn_ext_get_alloc_size, fattn.cu:722-756): the split partials of the
  * streaming kernel (at most SM count x 32 rows x (256 + 2) x 4 bytes, ~4.9 MB on a 148-SM B200) and, for

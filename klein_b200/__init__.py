@@ -56,6 +56,7 @@ EXPORTED = [
     "kb_flash_attn_ext_push_scratch_bytes",
     "kb_flash_attn_ext_exchange",
     "kb_exchange_flag_bytes",
+    "kb_flash_attn_ext_supported",
     "kb_state_sizes",
     "kb_state_create",
     "kb_state_required_bytes",
@@ -179,6 +180,8 @@ def lib():
         L.kb_flash_attn_ext_exchange.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams),
                                                  P(KbTensor), c_int64, c_void_p, c_int64, c_void_p, c_int32, c_int32,
                                                  P(KbTensor), c_void_p, c_size_t, c_void_p]
+        L.kb_flash_attn_ext_supported.restype = c_int32
+        L.kb_flash_attn_ext_supported.argtypes = [P(KbTensor), P(KbTensor), P(KbTensor), P(KbTensor), P(KbFaParams)]
         L.kb_exchange_flag_bytes.restype = c_size_t
         L.kb_exchange_flag_bytes.argtypes = [c_int32]
         L.kb_state_sizes.restype = c_int32

@@ -465,6 +465,20 @@ kb_status kb_flash_attn_ext_push(const kb_tensor* q, const kb_tensor* k, const k
     return fa_impl(q, k, v, mask, params, &dst, nullptr, scratch, scratch_bytes, stream, nullptr, &pa);
 }
 
+int32_t kb_flash_attn_ext_supported(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, const kb_tensor* mask,
+                                    const kb_fa_params* params) {
+    FaShape s;
+    if (!params || check_fa(q, k, v, mask, &s) != KB_OK) return 0;
+    if (params->logit_softcap != 0.0f && !std::isfinite(params->logit_softcap)) return 0;
+    if (params->max_bias > 0.0f && !mask) return 0;
+    if (params->causal && params->ring < 0) return 0;
+    const bool prefill = use_prefill(s, params, false) || prefill_quant_shape(s, params, false);
+    if (s.kv_type == KB_TYPE_BF16 && !prefill) return 0;  // bf16 caches: prefill shapes only
+    // the prefill kernel loads Q rows and stores output rows in 16-byte units
+    if (prefill && (!aligned16(q->nb[1]) || !aligned16(q->nb[2]) || !aligned16(q->nb[3]))) return 0;
+    return 1;
+}
+
 size_t kb_exchange_flag_bytes(int32_t n_ranks) {
     if (n_ranks < 1 || n_ranks > KB_MAX_PEERS) return 0;
     return (size_t) (kb::XCHG_FLAG_BASE + n_ranks * kb::XCHG_MAX_SLOTS) * sizeof(int32_t);
