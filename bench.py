@@ -404,6 +404,78 @@ def bench_gdn(kb, torch, dev, steps, warmup):
                          "traffic": ncu_traffic("gdn_recurrent_verify")}}
 
 
+def bench_gdn_layer(kb, torch, dev, steps, warmup):
+    """A whole DeltaNet layer of the decode step (1 token) and the 4-token verify step between its GEMMs — conv input
+    side, recurrence with K = 4 f16 snapshots in klein's cache form, gated norm — as kb_gdn_step's single launch and
+    as the three calls it replaces (kb_gdn_input, kb_gated_delta_net_cache, kb_gdn_gated_norm), each over 48 layers
+    with their own states in one CUDA graph (the states, 151 MB, exceed L2)."""
+    L_, K, S, Hv, Hk = 48, 4, 128, 48, 16
+    ch = 2 * S * Hk + S * Hv
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(9)
+    pk, _ = measured_peaks()
+    conv_w = torch.randn(ch, 4, device=dev, generator=gen) * 0.5
+    dt, aa = torch.randn(Hv, device=dev, generator=gen), -torch.rand(Hv, device=dev, generator=gen) - 0.1
+    nw = 1 + 0.1 * torch.randn(S, device=dev, generator=gen)
+    convs = [torch.randn(K, 3 * ch, device=dev, generator=gen) * 0.5 for _ in range(L_)]
+    ssms = [torch.randn(1, Hv, S, S, device=dev, generator=gen) * 0.02 for _ in range(L_)]
+    snaps = [torch.zeros(K - 1, S * S * Hv, dtype=torch.float16, device=dev) for _ in range(L_)]
+    sync = torch.zeros(L_, Hk, dtype=torch.int32, device=dev)
+    res = {}
+    for T in (1, 4):
+        qkv = torch.randn(T, ch, device=dev, generator=gen)
+        z = torch.randn(T, Hv * S, device=dev, generator=gen)
+        br, al = torch.randn(T, Hv, device=dev, generator=gen), torch.randn(T, Hv, device=dev, generator=gen)
+        out = torch.empty(T, Hv * S, device=dev)
+
+        def fused():
+            for l in range(L_):
+                kb.gdn_step(qkv, convs[l], conv_w, br, al, dt, aa, ssms[l], snaps[l], K, z, nw, 1e-6, sync[l], out=out)
+
+        def chain():
+            for l in range(L_):
+                q, k, v, beta, g = kb.gdn_input(qkv, convs[l], conv_w, S, Hk, 1e-6, beta_raw=br, alpha=al, dt_bias=dt, a=aa)
+                attn = kb.gated_delta_net_cache(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), g.view(1, T, Hv, 1),
+                                                beta.view(1, T, Hv), ssms[l], snaps[l], K)
+                kb.gdn_gated_norm(attn.view(T, Hv, S), z, nw, 1e-6)
+
+        times = {}
+        for name, fn in (("fused", fused), ("chain", chain)):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            for _ in range(warmup):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del graph
+            times[name] = e0.elapsed_time(e1) * 1e3 / (steps * L_)
+        # bytes one layer must move: the state read and written back, the T - 1 f16 snapshots, the conv state slots
+        # (read slot 0, write min(T, K) slots), the T rows of qkv, z, beta, alpha and the output
+        nbytes = (S * S * Hv * 4 * 2 + (min(T, K) - 1) * S * S * Hv * 2 + 3 * ch * 4 * (1 + min(T, K)) +
+                  T * (ch + 2 * Hv * S + 2 * Hv) * 4)
+        gbs = nbytes / (times["fused"] * 1e-6) / 1e9
+        res[f"gdn_layer_{T}"] = {
+            "value": round(times["fused"], 2), "unit": "us/layer", "tokens": T, "three_calls_us": round(times["chain"], 2),
+            "workload": f"one DeltaNet layer between its GEMMs, {T} token(s): conv input side, recurrence with K = 4 "
+                        "f16 snapshots, gated norm (48/16 heads, d 128), 48 layers per CUDA graph",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes_per_launch": nbytes,
+                         "traffic": ncu_traffic(f"gdn_step_{T}")}}
+    return res
+
+
 def bench_io_ops(kb, torch, dev, steps, warmup):
     """The ops around the two attention kinds at config[2]'s 4,096-token prefill (qwen35 shapes, f16 cache):
     kb_attn_prologue (Q/gate split, RMS norms, M-RoPE, K/V cache writes), kb_gdn_input (conv, SiLU, L2 norms, gates,
@@ -1266,6 +1338,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         secondary["prefill_q8_0_2048"] = bench_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup,
                                                        kv="q8_0", T=2048, n_kv=4096)
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
+        secondary.update(bench_gdn_layer(kb, torch, dev, max(3, args.steps // 20), args.warmup))
         secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["io_ops"] = bench_io_ops(kb, torch, dev, max(20, args.steps // 2), args.warmup)
         if not args.no_stack:
@@ -1342,6 +1415,19 @@ def run_case(case: str):
         kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, case[len("verify_"):])[0]
         q = torch.randn(1, 4, H, D, device=dev, generator=gen)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
+    elif case in ("gdn_step_1", "gdn_step_4"):
+        # one DeltaNet layer of the decode / verify step in one launch (kb_gdn_step), K = 4 f16 snapshots
+        T, S, Hk, Hv = int(case[-1]), 128, 16, 48
+        ch = 2 * S * Hk + S * Hv
+        conv = torch.randn(4, 3 * ch, device=dev, generator=gen)
+        ssm = torch.randn(1, Hv, S, S, device=dev, generator=gen) * 0.02
+        snap = torch.zeros(3, S * S * Hv, dtype=torch.float16, device=dev)
+        cw = torch.randn(ch, 4, device=dev, generator=gen) * 0.5
+        qkv, z = torch.randn(T, ch, device=dev, generator=gen), torch.randn(T, Hv * S, device=dev, generator=gen)
+        br, al = torch.randn(T, Hv, device=dev, generator=gen), torch.randn(T, Hv, device=dev, generator=gen)
+        dt, aa = torch.randn(Hv, device=dev, generator=gen), -torch.rand(Hv, device=dev, generator=gen) - 0.1
+        nw, sync = torch.ones(S, device=dev), torch.zeros(Hk, dtype=torch.int32, device=dev)
+        run = lambda: kb.gdn_step(qkv, conv, cw, br, al, dt, aa, ssm, snap, 4, z, nw, 1e-6, sync)
     elif case == "gdn_input_4096":
         # the DeltaNet input side at config[2]'s 4,096 tokens (qwen35: 16 key / 48 value heads, S 128)
         T, S, Hk, Hv = 4096, 128, 16, 48
@@ -1379,7 +1465,7 @@ def main():
                          "itself (fused), or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "prefill_q8_0_2048", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
-                             "verify_q4_0", "gdn_input_4096"],
+                             "verify_q4_0", "gdn_input_4096", "gdn_step_1", "gdn_step_4"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:

@@ -331,6 +331,25 @@ kb_status kb_gdn_input(const kb_tensor* qkv, const kb_tensor* conv_state, const 
 kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_tensor* w, float rms_eps,
                             const kb_tensor* dst, void* stream);
 
+/*
+ * A whole DeltaNet layer of a decode / verify pass between its GEMMs (graph.cpp:136-190) in one launch, for n_tokens
+ * 1..4: kb_gdn_input on the conv state slots, the recurrence into ssm (slot 0, in place) and ssm_snap (slots 1..,
+ * kb_gated_delta_net_cache with K = n_snapshots) and kb_gdn_gated_norm, with bit-identical results.
+ *   qkv, beta_raw, alpha, dt_bias, a, conv_w, conv_state  as kb_gdn_input (S = 128, conv width 4)
+ *   ssm       f32 [S * S * H_v]; ssm_snap [S * S * H_v, n_snapshots - 1] of f32 / f16 / bf16, or null when
+ *             n_snapshots is 1
+ *   z, ssm_norm, out  as kb_gdn_gated_norm
+ *   sync      device int32 [H_k] (kb_gdn_step_sync_bytes), zero before the first call; every call leaves it zero.
+ *             Calls that share it must not run concurrently.
+ * Every buffer contiguous and 16-byte aligned (ssm_snap 8-byte). KB_ERR_UNSUPPORTED for shapes outside this form
+ * (the three calls above cover them).
+ */
+size_t kb_gdn_step_sync_bytes(int32_t H_k);
+kb_status kb_gdn_step(const kb_tensor* qkv, const kb_tensor* conv_state, const kb_tensor* conv_w,
+                      const kb_tensor* beta_raw, const kb_tensor* alpha, const kb_tensor* dt_bias, const kb_tensor* a,
+                      const kb_tensor* ssm, const kb_tensor* ssm_snap, int32_t n_snapshots, const kb_tensor* z,
+                      const kb_tensor* ssm_norm, float rms_eps, int32_t* sync, const kb_tensor* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * klein's per-sequence State, resident in HBM (replaces src/state.h / src/state.cpp's tensors; klein's mapped host
  * KV cache and its bulk host view, state.cpp:110-134, are not needed when the cache lives in device memory), the

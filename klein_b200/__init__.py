@@ -52,6 +52,8 @@ EXPORTED = [
     "kb_flash_attn_ext_gated",
     "kb_gdn_input",
     "kb_gdn_gated_norm",
+    "kb_gdn_step_sync_bytes",
+    "kb_gdn_step",
     "kb_flash_attn_ext_push",
     "kb_flash_attn_ext_push_scratch_bytes",
     "kb_flash_attn_ext_exchange",
@@ -227,6 +229,11 @@ def lib():
         L.kb_gdn_input.argtypes = [P(KbTensor)] * 7 + [c_int32, c_int32, ctypes.c_float] + [P(KbTensor)] * 5 + [c_void_p]
         L.kb_gdn_gated_norm.restype = c_int32
         L.kb_gdn_gated_norm.argtypes = [P(KbTensor)] * 3 + [ctypes.c_float, P(KbTensor), c_void_p]
+        L.kb_gdn_step_sync_bytes.restype = ctypes.c_size_t
+        L.kb_gdn_step_sync_bytes.argtypes = [c_int32]
+        L.kb_gdn_step.restype = c_int32
+        L.kb_gdn_step.argtypes = [P(KbTensor)] * 9 + [c_int32] + [P(KbTensor)] * 2 + [ctypes.c_float, c_void_p,
+                                                                                       P(KbTensor), c_void_p]
         L.kb_attn_prologue.restype = c_int32
         L.kb_attn_prologue.argtypes = [P(KbTensor)] * 7 + [ctypes.c_float, P(KbRopeParams)] + [P(KbTensor)] * 4 + [c_void_p]
         L.kb_device_error.restype = c_int32
@@ -521,6 +528,29 @@ def gdn_gated_norm(x, z, w, rms_eps: float, stream=None):
                                  c_void_p(_stream(x, stream)))
     check("kb_gdn_gated_norm", rc)
     return dst
+
+
+def gdn_step(qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a, ssm, snap, n_snapshots: int, z, ssm_norm,
+             rms_eps: float, sync, out=None, stream=None):
+    """A whole DeltaNet layer of a decode / verify pass (1..4 tokens) in one launch through kb_gdn_step: the input
+    side on conv_state (f32 [n_snapshots][3 ch], updated in place), the recurrence into ssm (f32, H_v S S values,
+    slot 0 in place) and snap (f16 / bf16 / f32 [n_snapshots - 1][S S H_v] or None), and the gated norm with z
+    (f32 [n][H_v S]). sync: torch int32 [H_k] of zeros on the device (left zero). Returns out f32 [n][H_v S]."""
+    import torch
+
+    n = qkv.shape[0]
+    if out is None:
+        out = torch.empty(z.shape, dtype=torch.float32, device=qkv.device)
+    tensors = [from_torch(x) for x in (qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a)]
+    ssm_t = from_torch(ssm.reshape(-1))
+    snap_t = from_torch(snap.reshape(snap.shape[0], -1)) if snap is not None else None
+    rc = lib().kb_gdn_step(*[ctypes.byref(t) for t in tensors], ctypes.byref(ssm_t),
+                           ctypes.byref(snap_t) if snap_t is not None else None, n_snapshots,
+                           ctypes.byref(from_torch(z.reshape(n, -1))), ctypes.byref(from_torch(ssm_norm)),
+                           ctypes.c_float(rms_eps), c_void_p(sync.data_ptr()), ctypes.byref(from_torch(out.view(n, -1))),
+                           c_void_p(_stream(qkv, stream)))
+    check("kb_gdn_step", rc)
+    return out
 
 
 def cache_rows(cache, kv_type: int) -> KbTensor:

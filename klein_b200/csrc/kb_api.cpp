@@ -981,6 +981,75 @@ kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_ten
     return kb::launch_gdn_gated_norm(p, (int) S, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
 }
 
+size_t kb_gdn_step_sync_bytes(int32_t H_k) { return H_k > 0 ? (size_t) H_k * sizeof(int32_t) : 0; }
+
+kb_status kb_gdn_step(const kb_tensor* qkv, const kb_tensor* conv_state, const kb_tensor* conv_w,
+                      const kb_tensor* beta_raw, const kb_tensor* alpha, const kb_tensor* dt_bias, const kb_tensor* a,
+                      const kb_tensor* ssm, const kb_tensor* ssm_snap, int32_t n_snapshots, const kb_tensor* z,
+                      const kb_tensor* ssm_norm, float rms_eps, int32_t* sync, const kb_tensor* out, void* stream) {
+    if (!qkv || !conv_state || !conv_w || !beta_raw || !alpha || !dt_bias || !a || !ssm || !z || !ssm_norm || !sync ||
+        !out)
+        return KB_ERR_ARG;
+    if (n_snapshots < 1 || (n_snapshots > 1 && !ssm_snap)) return KB_ERR_ARG;
+    constexpr int64_t S = 128;
+    for (const kb_tensor* t : {qkv, conv_state, conv_w, beta_raw, alpha, dt_bias, a, ssm, z, ssm_norm, out})
+        if (!contiguous_f32(t) || !aligned16(reinterpret_cast<uintptr_t>(t->data))) return KB_ERR_UNSUPPORTED;
+    const int64_t n = qkv->ne[1], ch = qkv->ne[0];
+    if (n < 1 || n > 4 || qkv->ne[2] * qkv->ne[3] != 1) return KB_ERR_UNSUPPORTED;
+    if (ssm_norm->ne[0] * ssm_norm->ne[1] != S) return KB_ERR_UNSUPPORTED;
+    const int64_t H_v = ssm->ne[0] * ssm->ne[1] * ssm->ne[2] * ssm->ne[3] / (S * S);
+    if (H_v < 1 || H_v * S * S != ssm->ne[0] * ssm->ne[1] * ssm->ne[2] * ssm->ne[3]) return KB_ERR_BAD_SHAPE;
+    const int64_t qk = ch - S * H_v;  // 2 S H_k
+    if (qk <= 0 || qk % (2 * S)) return KB_ERR_BAD_SHAPE;
+    const int64_t H_k = qk / (2 * S);
+    if (H_v % H_k) return KB_ERR_UNSUPPORTED;
+    if (conv_w->ne[0] != 4) return KB_ERR_UNSUPPORTED;
+    if (conv_w->ne[1] != ch || conv_state->ne[0] != 3 * ch || conv_state->ne[1] != n_snapshots) return KB_ERR_BAD_SHAPE;
+    for (const kb_tensor* t : {beta_raw, alpha})
+        if (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != H_v * n || (t->ne[0] != H_v && t->ne[1] != H_v))
+            return KB_ERR_BAD_SHAPE;
+    if (dt_bias->ne[0] * dt_bias->ne[1] != H_v || a->ne[0] * a->ne[1] != H_v) return KB_ERR_BAD_SHAPE;
+    const int64_t rows = S * H_v * n;
+    if (z->ne[0] * z->ne[1] * z->ne[2] * z->ne[3] != rows || out->ne[0] * out->ne[1] * out->ne[2] * out->ne[3] != rows)
+        return KB_ERR_BAD_SHAPE;
+    kb::GdnStepParams p{};
+    const int64_t n_written = n < n_snapshots ? n : n_snapshots;
+    if (n_written > 1) {
+        const int code = snap_code(ssm_snap->type);
+        if (code < 0) return KB_ERR_UNSUPPORTED;
+        const size_t es = code == 0 ? 4 : 2;
+        if (ssm_snap->ne[0] != S * S * H_v || ssm_snap->ne[1] < n_written - 1 || ssm_snap->nb[0] != es)
+            return KB_ERR_BAD_SHAPE;
+        if ((reinterpret_cast<uintptr_t>(ssm_snap->data) & 7) || (ssm_snap->nb[1] & 7)) return KB_ERR_UNSUPPORTED;
+        p.snap = static_cast<char*>(ssm_snap->data);
+        p.snap_stride = (int64_t) ssm_snap->nb[1];
+        p.snap_type = code;
+    }
+    if (reinterpret_cast<uintptr_t>(sync) & 3) return KB_ERR_ARG;
+    p.qkv = static_cast<const float*>(qkv->data);
+    p.qkv_ld = ch;
+    p.conv_state = static_cast<float*>(conv_state->data);
+    p.conv_ld = conv_state->ne[0];
+    p.conv_w = static_cast<const float*>(conv_w->data);
+    p.beta_raw = static_cast<const float*>(beta_raw->data);
+    p.alpha = static_cast<const float*>(alpha->data);
+    p.dt_bias = static_cast<const float*>(dt_bias->data);
+    p.a = static_cast<const float*>(a->data);
+    p.state = static_cast<float*>(ssm->data);
+    p.z = static_cast<const float*>(z->data);
+    p.norm_w = static_cast<const float*>(ssm_norm->data);
+    p.out = static_cast<float*>(out->data);
+    p.sync = sync;
+    p.T = (int) n, p.H_k = (int) H_k, p.H_v = (int) H_v, p.K = n_snapshots;
+    // as kb_gdn_input (graph.cpp:41-44) and kb_gdn_gated_norm
+    p.l2_eps = rms_eps / (float) S;
+    p.inv_sqrt_s = 1.0f / std::sqrt((float) S);
+    p.eps = rms_eps;
+    p.err = kb::device_error_word();
+    p.wait_ns = g_wait_ns;
+    return kb::launch_gdn_step(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+}
+
 kb_status kb_rollback_recurrent(int32_t n_layers, float* const* conv, int64_t conv_row, const void* const* snap,
                                 int32_t snap_type, float* const* ssm, int64_t ssm_row, int32_t s, int32_t n_snapshots,
                                 void* stream) {

@@ -199,6 +199,33 @@ struct GdnNormParams {
 };
 cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream);
 
+// One DeltaNet layer of a decode / verify pass in one launch (gdn_step.cu): S = 128, conv width 4, 1 <= T <= 4;
+// every buffer contiguous and 16-byte aligned (the snapshot rows 8-byte aligned).
+struct GdnStepParams {
+    const float* qkv;                // [T][qkv_ld]: q heads, k heads, v heads
+    int64_t qkv_ld;
+    float* conv_state;               // [K][conv_ld] conv state slots
+    int64_t conv_ld;
+    const float* conv_w;             // [ch][4]
+    const float* beta_raw;           // [T][H_v]
+    const float* alpha;              // [T][H_v]
+    const float* dt_bias;            // [H_v]
+    const float* a;                  // [H_v]
+    float* state;                    // [H_v][S][S] f32, transposed; slot 0 in place
+    char* snap;                      // slots 1..K-1 of snap_type (0 f32, 1 f16, 2 bf16)
+    int64_t snap_stride;             // bytes
+    int snap_type;
+    const float* z;                  // [T][H_v][S]
+    const float* norm_w;             // [S]
+    float* out;                      // [T][H_v][S]
+    int* sync;                       // [H_k] counters, zero between calls
+    int T, H_k, H_v, K;
+    float l2_eps, inv_sqrt_s, eps;
+    int* err;                        // device error word
+    uint64_t wait_ns;                // budget of the bounded wait for the cluster's partial sums
+};
+cudaError_t launch_gdn_step(const GdnStepParams& p, cudaStream_t stream);
+
 int* device_error_word();  // address of the current device's error word (null on failure)
 
 // kb_flash_attn_ext with caller-chosen scratch, and its scratch size (shared by the C-ABI entry points)

@@ -89,10 +89,11 @@ kb_tensor f32_tensor(void* data, int64_t n0, int64_t n1, int64_t n2 = 1, int64_t
 
 struct Layer {
     int64_t cells = 0;  // attention layers: cache rows (0 for a DeltaNet layer)
-    size_t k_off = 0, v_off = 0, conv_off = 0, ssm_off = 0, snap_off = 0;
+    size_t k_off = 0, v_off = 0, conv_off = 0, ssm_off = 0, snap_off = 0, sync_off = 0;
     bool has_snap = false;
     void *k = nullptr, *v = nullptr;                        // attention layers
     void *conv = nullptr, *ssm = nullptr, *snap = nullptr;  // DeltaNet layers
+    int32_t* sync = nullptr;                                // DeltaNet layers: kb_gdn_step's counters (ssm_n_group)
 };
 
 }  // namespace
@@ -146,6 +147,9 @@ bool plan_state(const kb_qwen35_dims* d, const kb_state_config* c, kb_state* st,
                              rs * (size_t) (c->n_snapshots - 1);
         }
     }
+    // kb_gdn_step's counters, one set per DeltaNet layer (zero between calls)
+    for (Layer& l : L)
+        if (!l.cells) l.sync_off = take((size_t) d->ssm_n_group * sizeof(int32_t));
     pl->total = off;
     if (st) {
         st->row_k = rk, st->row_v = rv, st->snap_row = rs;
@@ -217,6 +221,7 @@ kb_status make_state(const kb_qwen35_dims* dims, const kb_state_config* cfg, voi
             l.conv = b + l.conv_off;
             l.ssm = b + l.ssm_off;
             l.snap = l.has_snap ? b + l.snap_off : nullptr;
+            l.sync = reinterpret_cast<int32_t*>(b + l.sync_off);
         }
     }
     // State::State clears every buffer (state.cpp:140); the KV cells beyond n_past are masked anyway
@@ -496,11 +501,18 @@ kb_status kb_layer_deltanet(kb_state* st, int32_t il, int32_t n_tokens, const kb
     const kb_qwen35_dims& d = st->dims;
     const int64_t S = d.ssm_d_state, Hk = d.ssm_n_group, Hv = d.ssm_dt_rank, n = n_tokens;
     if (!qkv || qkv->ne[1] != n) return KB_ERR_BAD_SHAPE;
+    kb_state_layer lv;
+    kb_state_get_layer(st, il, &lv);
+    if (n <= 4) {
+        // decode / verify passes: the whole layer in one launch (same results as the three calls below)
+        const kb_status s = kb_gdn_step(qkv, &lv.conv, conv_w, beta_raw, alpha, dt_bias, a, &lv.ssm,
+                                        lv.ssm_snap.data ? &lv.ssm_snap : nullptr, st->cfg.n_snapshots, z, ssm_norm,
+                                        rms_eps, st->layers[il].sync, out, stream);
+        if (s != KB_ERR_UNSUPPORTED) return s;
+    }
     const GdnScratch sc = gdn_scratch(st, n_tokens);
     if (!scratch || scratch_bytes < sc.total || (reinterpret_cast<uintptr_t>(scratch) & (ALIGN - 1))) return KB_ERR_SCRATCH;
     char* b = static_cast<char*>(scratch);
-    kb_state_layer lv;
-    kb_state_get_layer(st, il, &lv);
     const kb_tensor q = f32_tensor(b + sc.q, S, Hk, n), k = f32_tensor(b + sc.k, S, Hk, n);
     const kb_tensor v = f32_tensor(b + sc.v, S, Hv, n);
     const kb_tensor beta = f32_tensor(b + sc.beta, Hv, n), g = f32_tensor(b + sc.g, Hv, n);
