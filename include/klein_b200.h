@@ -341,7 +341,7 @@ kb_status kb_gdn_gated_norm(const kb_tensor* x, const kb_tensor* z, const kb_ten
  *   z, ssm_norm, out  as kb_gdn_gated_norm
  *   sync      device int32 [H_k] (kb_gdn_step_sync_bytes), zero before the first call; every call leaves it zero.
  *             Calls that share it must not run concurrently.
- * Every buffer contiguous and 16-byte aligned (ssm_snap 8-byte). KB_ERR_UNSUPPORTED for shapes outside this form
+ * Every buffer contiguous and 16-byte aligned. KB_ERR_UNSUPPORTED for shapes outside this form
  * (the three calls above cover them).
  */
 size_t kb_gdn_step_sync_bytes(int32_t H_k);

@@ -9,15 +9,16 @@
 //
 // Grid: one cluster of 8 CTAs per value head h (thread block clusters, distributed shared memory); CTA r of the
 // cluster owns value columns [16 r, 16 r + 16) of the head's 128 x 128 state (stored transposed, M[j][i]).
-//   1. the CTA's state columns are loaded first (the longest loads), then the input side, warp-specialised:
-//      warp 0 the q channels and warp 1 the k channels of key head h % H_k (lane l: channels 4 l .. 4 l + 3, conv +
-//      SiLU + L2 norm), warp 2 lanes 0-3 the CTA's 16 v channels, warp 3 beta = sigmoid(beta_raw) and
-//      exp(g), g = softplus(alpha + dt_bias) * a; all into shared memory.
+//   1. the CTA's state columns are loaded first (the longest loads), then the input side, spread over all four
+//      warps (so over the SM's four schedulers): thread t the conv + SiLU of q channel t and k channel t of key
+//      head h % H_k, 16 threads the CTA's v channels, T threads beta = sigmoid(beta_raw) and exp(g),
+//      g = softplus(alpha + dt_bias) * a; then the 2 T L2 norms of the q / k rows, one row per warp at a time (lane l:
+//      channels 4 l .. 4 l + 3); all in shared memory.
 //      Conv-state snapshots (slot s <- the 3 inputs before token T - s, clamped at the stored state, for s < K,
 //      skipping s >= T other than 0): a CTA writes its own v channels; the q / k channels of a key head are read by
 //      the 24 CTAs of its value heads, so the last of them to have read (a counter per key head in `sync`, zero
 //      before the call and left at zero) writes them.
-//   2. the recurrence, warp w on columns 16 r + 4 w .. + 3 (lane l: rows 4 l .. 4 l + 3 as float4): slot 0 back into
+//   2. the recurrence (gdn_rec.cuh), warp w on columns 16 r + 4 w .. + 3 with 8 lanes per column: slot 0 back into
 //      the f32 state in place, slots 1.. into the snapshot rows (f32 / f16 / bf16).
 //   3. the gated norm: each CTA's 4 lane partial sums of squares per token are pushed into every CTA of the cluster
 //      (st.async into distributed shared memory, completing on the receiver's mbarrier: no cluster-wide barrier,
@@ -27,6 +28,7 @@
 
 #include "kb_common.cuh"
 #include "kb_internal.h"
+#include "gdn_rec.cuh"
 
 namespace kb {
 
@@ -38,12 +40,6 @@ constexpr int S = 128, KC = 4, KM1 = KC - 1, CPL = 4, TMAX = 4, CLUSTER = 8, COL
 constexpr int LPC = COLS / CPL;  // lanes of a row's butterfly per CTA
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-    for (int off = 16; off; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
-    return x;
-}
 
 __device__ __forceinline__ double warp_sum_d(double x) {
 #pragma unroll
@@ -85,45 +81,42 @@ __device__ __forceinline__ void st4(float* dst, const float* v) {
     *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
 }
 
-__device__ __forceinline__ void store4(char* base, int type, int64_t elem, float4 v) {
-    if (type == 0) {
-        *reinterpret_cast<float4*>(base + elem * 4) = v;
-    } else if (type == 1) {
-        __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-        *reinterpret_cast<uint2*>(base + elem * 2) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-    } else {
-        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-        *reinterpret_cast<uint2*>(base + elem * 2) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+// conv + SiLU of one channel for tokens 0..T-1 over in[] = [stored window (KM1) | x (T)], ggml's order: the window
+// oldest first, one multiply-add per tap
+template <int T>
+__device__ __forceinline__ void conv_silu(const float (&win)[KM1], const float (&x)[TMAX], const float (&w)[KC],
+                                          float (&y)[TMAX]) {
+#pragma unroll
+    for (int u = 0; u < T; ++u) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KM1; ++j)
+            acc += (u - KM1 + j >= 0 ? x[u - KM1 + j < 0 ? 0 : u - KM1 + j] : win[u + j < KM1 ? u + j : 0]) * w[j];
+        acc += x[u] * w[KM1];
+        y[u] = silu_f(acc);
     }
 }
 
-// the conv-state snapshots of a lane's 4 channels from cl on: slot s <- in[start .. start + KM1), in = [stored window
-// (KM1) | the T inputs], start = T - s clamped at 0
+// the conv-state snapshots of channel c: slot s <- in[start .. start + KM1), start = T - s clamped at 0
 template <int T>
-__device__ __forceinline__ void write_conv_slots(const GdnStepParams& p, int64_t cl, const float (&win)[CPL][KM1],
-                                                 const float (&xs)[TMAX][CPL]) {
+__device__ __forceinline__ void write_conv_slots(const GdnStepParams& p, int64_t c, const float (&win)[KM1],
+                                                 const float (&x)[TMAX]) {
     for (int s = 0; s < p.K; ++s) {
         if (s >= T && s > 0) continue;
         const int start = max(0, T - s);
-        float sv[CPL][KM1];
+        float* dst = p.conv_state + (int64_t) s * p.conv_ld + c * KM1;
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) {
+        for (int j = 0; j < KM1; ++j) {
+            const int ii = start + j;
+            float v = 0.0f;
 #pragma unroll
-            for (int j = 0; j < KM1; ++j) {
-                const int ii = start + j;
-                float v = 0.0f;
+            for (int jj = 0; jj < KM1; ++jj)
+                if (ii == jj) v = win[jj];
 #pragma unroll
-                for (int jj = 0; jj < KM1; ++jj)
-                    if (ii == jj) v = win[i][jj];
-#pragma unroll
-                for (int u = 0; u < T; ++u)
-                    if (ii == KM1 + u) v = xs[u][i];
-                sv[i][j] = v;
-            }
+            for (int u = 0; u < T; ++u)
+                if (ii == KM1 + u) v = x[u];
+            dst[j] = v;
         }
-        float* dst = p.conv_state + (int64_t) s * p.conv_ld + cl * KM1;
-#pragma unroll
-        for (int q = 0; q < KM1; ++q) st4(dst + q * CPL, &sv[0][0] + q * CPL);
     }
 }
 
@@ -151,10 +144,12 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS) gdn_s
     }
     cluster_arrive_relaxed();  // paired with the wait before the first push: every CTA's barrier is initialised
 
+    // this lane's state column and first row (the token step's layout, gdn_rec.cuh)
+    const int col = j0 + (lane >> 3), r8 = lane & 7;
     float4 M[4];
-    const float* s0 = p.state + (int64_t) h * S * S;
+    const float* s0 = p.state + (int64_t) h * S * S + (int64_t) col * S;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) M[c] = *reinterpret_cast<const float4*>(s0 + (int64_t) (j0 + c) * S + 4 * lane);
+    for (int d = 0; d < 4; ++d) M[d] = *reinterpret_cast<const float4*>(s0 + gdn_row(r8, d));
     // the gated norm's operands, needed last: loaded now so their latency overlaps everything else
     float zv[CPL], wv[CPL];
     const bool norm_lane = warp < T && lane < LPC;
@@ -164,60 +159,38 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS) gdn_s
     }
 
     // ------------------------------------------------------------------------------------ 1. input side
-    // the lane's first channel: q / k of key head hk (warps 0 / 1), 4 of the CTA's v channels (warp 2, lanes 0-3)
-    int64_t cl = -1;
-    if (warp < 2) cl = (int64_t) (warp * p.H_k + hk) * S + CPL * lane;
-    else if (warp == 2 && lane < LPC) cl = 2 * (int64_t) p.H_k * S + (int64_t) h * S + j_base + CPL * lane;
-    float win[CPL][KM1], xs[TMAX][CPL];
-    if (cl >= 0) {
-        float w[CPL][KC], y[TMAX][CPL];
+    // conv + SiLU: thread t takes q channel t and k channel t of key head hk, warp 2's lanes 0-15 also the CTA's 16 v
+    // channels, warp 3's lanes < T beta and exp(g) of token `lane`; the raw q / k rows go to shared memory
+    const int64_t cq = (int64_t) hk * S + tid, ck = (int64_t) (p.H_k + hk) * S + tid;
+    float winq[KM1], wink[KM1], xq[TMAX], xk[TMAX];
+    {
+        float wq[KC], wk[KC], yq[TMAX], yk[TMAX];
+        ld4(p.conv_w + cq * KC, wq);
+        ld4(p.conv_w + ck * KC, wk);
 #pragma unroll
-        for (int q = 0; q < KC; ++q) ld4(p.conv_w + cl * KC + q * CPL, &w[0][0] + q * CPL);
-#pragma unroll
-        for (int q = 0; q < KM1; ++q) ld4(p.conv_state + cl * KM1 + q * CPL, &win[0][0] + q * CPL);
+        for (int j = 0; j < KM1; ++j) winq[j] = p.conv_state[cq * KM1 + j], wink[j] = p.conv_state[ck * KM1 + j];
 #pragma unroll
         for (int u = 0; u < TMAX; ++u) {
-            if (u < T) {
-                ld4(p.qkv + (int64_t) u * p.qkv_ld + cl, xs[u]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < CPL; ++i) xs[u][i] = 0.0f;
-            }
+            xq[u] = u < T ? p.qkv[(int64_t) u * p.qkv_ld + cq] : 0.0f;
+            xk[u] = u < T ? p.qkv[(int64_t) u * p.qkv_ld + ck] : 0.0f;
         }
-        // conv + SiLU, ggml's order: the window oldest first, one multiply-add per tap
+        conv_silu<T>(winq, xq, wq, yq);
+        conv_silu<T>(wink, xk, wk, yk);
 #pragma unroll
-        for (int u = 0; u < T; ++u) {
+        for (int u = 0; u < T; ++u) qs[u][tid] = yq[u], ks[u][tid] = yk[u];
+    }
+    if (warp == 2 && lane < COLS) {
+        const int64_t cv = 2 * (int64_t) p.H_k * S + (int64_t) h * S + j_base + lane;
+        float w[KC], win[KM1], x[TMAX], y[TMAX];
+        ld4(p.conv_w + cv * KC, w);
 #pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-                float acc = 0.0f;
+        for (int j = 0; j < KM1; ++j) win[j] = p.conv_state[cv * KM1 + j];
 #pragma unroll
-                for (int j = 0; j < KM1; ++j)
-                    acc += (u - KM1 + j >= 0 ? xs[u - KM1 + j < 0 ? 0 : u - KM1 + j][i] : win[i][u + j < KM1 ? u + j : 0]) *
-                           w[i][j];
-                acc += xs[u][i] * w[i][KM1];
-                y[u][i] = silu_f(acc);
-            }
-        }
-        if (warp < 2) {
-            // l2: rms_norm with eps / S (sum of squares in double), then * 1 / sqrt(S)
-            float(*dst)[S] = warp == 0 ? qs : ks;
+        for (int u = 0; u < TMAX; ++u) x[u] = u < T ? p.qkv[(int64_t) u * p.qkv_ld + cv] : 0.0f;
+        conv_silu<T>(win, x, w, y);
 #pragma unroll
-            for (int u = 0; u < T; ++u) {
-                double ss = 0.0;
-#pragma unroll
-                for (int i = 0; i < CPL; ++i) ss += (double) (y[u][i] * y[u][i]);
-                ss = warp_sum_d(ss);
-                const float mean = (float) (ss / S);
-                const float scale = 1.0f / sqrtf(mean + p.l2_eps);
-#pragma unroll
-                for (int i = 0; i < CPL; ++i) y[u][i] = y[u][i] * scale * p.inv_sqrt_s;
-                st4(&dst[u][CPL * lane], y[u]);
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < T; ++u) st4(&vs[u][CPL * lane], y[u]);
-            write_conv_slots<T>(p, cl, win, xs);  // the CTA's own channels, read above by this thread only
-        }
+        for (int u = 0; u < T; ++u) vs[u][lane] = y[u];
+        write_conv_slots<T>(p, cv, win, x);  // the CTA's own channel, read above by this thread only
     } else if (warp == 3 && lane < T) {
         const float b = p.beta_raw[(int64_t) lane * p.H_v + h];
         beta_s[lane] = 1.0f / (1.0f + expf(-b));
@@ -225,6 +198,24 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS) gdn_s
         const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
         const float g = __fmul_rn(sp, p.a[h]);  // rounded on its own, as when it is stored and read back
         eg_s[lane] = expf(g);
+    }
+    __syncthreads();
+    // l2 of the q and k rows of every token, one row per warp at a time: rms_norm with eps / S (lane l's 4 consecutive
+    // channels summed in double, then the butterfly), then * 1 / sqrt(S)
+#pragma unroll
+    for (int task = warp; task < 2 * T; task += THREADS / 32) {
+        float* row = task < T ? qs[task] : ks[task - T];
+        float y[CPL];
+        ld4(row + CPL * lane, y);
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) ss += (double) (y[i] * y[i]);
+        ss = warp_sum_d(ss);
+        const float mean = (float) (ss / S);
+        const float scale = 1.0f / sqrtf(mean + p.l2_eps);
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) y[i] = y[i] * scale * p.inv_sqrt_s;
+        st4(row + CPL * lane, y);
     }
     __syncthreads();
     // every read of the key head's stored window by this CTA is behind the barrier above: count this CTA among its
@@ -236,52 +227,22 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS) gdn_s
     // ------------------------------------------------------------------------------------ 2. recurrence
     {
         const float scale = rsqrtf((float) S);
-        const int64_t e0 = (int64_t) h * S * S;
+        const int64_t elem = ((int64_t) h * S + col) * S;
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-            const float4 k4 = *reinterpret_cast<const float4*>(&ks[t][4 * lane]);
-            const float4 q4 = *reinterpret_cast<const float4*>(&qs[t][4 * lane]);
-            const float beta = beta_s[t];
-            const float eg = eg_s[t];
-            float vj[4];
+            float4 k[4], q[4], e[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) vj[c] = vs[t][4 * warp + c];
-            float sk[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                M[c].x *= eg;
-                M[c].y *= eg;
-                M[c].z *= eg;
-                M[c].w *= eg;
-                sk[c] = M[c].x * k4.x + M[c].y * k4.y + M[c].z * k4.z + M[c].w * k4.w;
+            for (int d = 0; d < 4; ++d) {
+                k[d] = *reinterpret_cast<const float4*>(&ks[t][gdn_row(r8, d)]);
+                q[d] = *reinterpret_cast<const float4*>(&qs[t][gdn_row(r8, d)]);
+                e[d] = make_float4(eg_s[t], eg_s[t], eg_s[t], eg_s[t]);
             }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) sk[c] = warp_sum(sk[c]);
-            float so[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float delta = (vj[c] - sk[c]) * beta;
-                M[c].x += delta * k4.x;
-                M[c].y += delta * k4.y;
-                M[c].z += delta * k4.z;
-                M[c].w += delta * k4.w;
-                so[c] = M[c].x * q4.x + M[c].y * q4.y + M[c].z * q4.z + M[c].w * q4.w;
-            }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) so[c] = warp_sum(so[c]);
-            if (lane < 4) {
-                float o = so[0];
-#pragma unroll
-                for (int c = 1; c < 4; ++c)
-                    if (lane == c) o = so[c];
-                os[t][4 * warp + lane] = o * scale;
-            }
+            const float o = gdn_token(M, k, q, e, vs[t][col - j_base], beta_s[t]);
+            if ((lane & 7) == 0) os[t][col - j_base] = o * scale;
             const int slot = T - 1 - t;
             if (slot < p.K) {
                 char* base = slot == 0 ? reinterpret_cast<char*>(p.state) : p.snap + (int64_t) (slot - 1) * p.snap_stride;
-                const int type = slot == 0 ? 0 : p.snap_type;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) store4(base, type, e0 + (int64_t) (j0 + c) * S + 4 * lane, M[c]);
+                gdn_store_col(base, slot == 0 ? 0 : p.snap_type, elem, r8, M);
             }
         }
     }
@@ -319,7 +280,10 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS) gdn_s
             }
         }
     }
-    if (last && warp < 2) write_conv_slots<T>(p, cl, win, xs);
+    if (last) {
+        write_conv_slots<T>(p, cq, winq, xq);
+        write_conv_slots<T>(p, ck, wink, xk);
+    }
     // no CTA of the cluster reads this one's shared memory, and every push into it has landed before its norm warps
     // finish: the CTA leaves without a cluster barrier
 }

@@ -1020,7 +1020,7 @@ kb_status kb_gdn_step(const kb_tensor* qkv, const kb_tensor* conv_state, const k
         const size_t es = code == 0 ? 4 : 2;
         if (ssm_snap->ne[0] != S * S * H_v || ssm_snap->ne[1] < n_written - 1 || ssm_snap->nb[0] != es)
             return KB_ERR_BAD_SHAPE;
-        if ((reinterpret_cast<uintptr_t>(ssm_snap->data) & 7) || (ssm_snap->nb[1] & 7)) return KB_ERR_UNSUPPORTED;
+        if (!aligned16(reinterpret_cast<uintptr_t>(ssm_snap->data)) || !aligned16(ssm_snap->nb[1])) return KB_ERR_UNSUPPORTED;
         p.snap = static_cast<char*>(ssm_snap->data);
         p.snap_stride = (int64_t) ssm_snap->nb[1];
         p.snap_type = code;

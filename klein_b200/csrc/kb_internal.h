@@ -200,7 +200,7 @@ struct GdnNormParams {
 cudaError_t launch_gdn_gated_norm(const GdnNormParams& p, int S, cudaStream_t stream);
 
 // One DeltaNet layer of a decode / verify pass in one launch (gdn_step.cu): S = 128, conv width 4, 1 <= T <= 4;
-// every buffer contiguous and 16-byte aligned (the snapshot rows 8-byte aligned).
+// every buffer contiguous and 16-byte aligned.
 struct GdnStepParams {
     const float* qkv;                // [T][qkv_ld]: q heads, k heads, v heads
     int64_t qkv_ld;
