@@ -57,7 +57,7 @@ def ncu_traffic(name: str):
         with open(path) as f:
             for line in f:
                 if line.startswith("traffic_bytes:"):
-                    return int(float(line.split(":", 1)[1]))
+                    return int(float(line.split(":", 1)[1].split()[0]))  # the number; a note may follow it
     except OSError:
         pass
     return None

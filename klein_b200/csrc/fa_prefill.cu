@@ -3,15 +3,19 @@
 // the f16 widening of a q8_0 / q4_0 cache (kv_widen.cu writes it; Q is then rounded to q8_0 first, as ggml's CPU op
 // rounds it to the vec_dot type of a q8_0 or q4_0 K, ops.cpp:8960).
 //
-// One CTA computes a 128-query tile of one head. Roles (8 warps):
-//   warps 0-3  softmax, one thread per query row (row r = TMEM lane r, all 64 cells of a block): stage Q, run the
-//              online softmax (unmasked blocks on the packed f32x2 pipe), rescale O when needed, write the
-//              normalised output. One thread per row needs no exchange of row maxima between warps.
-//   warps 4-5  TMA producers for K and for V (independent chains): 64 cells x 256 dims, 128-byte swizzle, rings
+// One CTA computes a 128-query tile of one head. Roles (12 warps):
+//   warps 0-7  softmax in two warpgroups that take alternate 64-cell blocks of the same 128 rows (group g the
+//              blocks j with j % 2 == g), one thread per query row and group (row r = TMEM lane r, all 64 cells of
+//              its blocks): stage Q, run the online softmax (unmasked blocks on the packed f32x2 pipe), rescale O
+//              when needed, write the normalised output. One warp per scheduler could not keep up with the tensor
+//              core (one block's softmax took longer than its MMAs); with two, one group's exponentials overlap the
+//              other's TMEM reads and waits. The running row max passes from block to block, and so from group to
+//              group, through shared memory (an mbarrier per group); each group keeps its own row sum.
+//   warps 8-9  TMA producers for K and for V (independent chains): 64 cells x 256 dims, 128-byte swizzle, rings
 //              of 3 tiles each
-//   warp 6     S issuer (one thread): S_j = Q K_j^T, 16 MMAs of K = 16 into S buffer j % 3, once PV_{j-3} (the
+//   warp 10    S issuer (one thread): S_j = Q K_j^T, 16 MMAs of K = 16 into S buffer j % 3, once PV_{j-3} (the
 //              last reader of that buffer) has completed
-//   warp 7     PV issuer (one thread): O += P_j V_j (TS form: P from TMEM) as soon as the softmax has written P_j.
+//   warp 11    PV issuer (one thread): O += P_j V_j (TS form: P from TMEM) as soon as the softmax has written P_j.
 //              The tensor core accepts only a few MMAs ahead of the one executing, so one thread issuing both
 //              would hold PV back behind the 16 S MMAs.
 // TMEM (512 columns): O 128 x 256 f32 at [0, 256), S_0..S_2 128 x 64 f32 at [256, 448), Q dims 0-127 (f16|bf16
@@ -40,10 +44,10 @@ constexpr int KVTILE = BN * D * 2;            // 32 KiB: 4 chunks of [64 cells][
 constexpr int KSTAGE = 3;                     // K ring depth (the K chain is latency-bound: depth sets the rate)
 constexpr int VSTAGE = 3;                     // V ring depth
 constexpr int NSTAGE = 3;                     // S / P buffers: S_{j+3} may start once PV_j has read P_j
-constexpr int SOFTMAX_WGS = 1;                 // softmax warpgroups: each owns 64 / SOFTMAX_WGS cells of a row
+constexpr int SOFTMAX_WGS = 2;                 // softmax warpgroups: group g takes the blocks j with j % 2 == g
 constexpr int SOFTMAX_WARPS = 4 * SOFTMAX_WGS;
-constexpr int CPT = BN / SOFTMAX_WGS;           // cells per softmax thread per block
-constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread (rescale / epilogue)
+constexpr int CPT = BN;                         // cells per softmax thread per block (the whole row of the block)
+constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread in the epilogue
 constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // + K producer, V producer, S issuer, PV issuer
 constexpr int W_KPROD = SOFTMAX_WARPS, W_VPROD = SOFTMAX_WARPS + 1, W_SMMA = SOFTMAX_WARPS + 2, W_PVMMA = SOFTMAX_WARPS + 3;
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_Q = 448;  // Q: dims 0-127 (the other half is in shared memory)
@@ -56,7 +60,8 @@ struct Smem {
     uint8_t v[VSTAGE][KVTILE];
     uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[VSTAGE], v_empty[VSTAGE];
     uint64_t s_full[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
-    __half xmax[2][SOFTMAX_WGS][BM];           // [block parity][group][row]: partial row maxima exchanged per block
+    float mx[SOFTMAX_WGS][BM];                  // [group][row]: the running max after the group's latest block
+    uint64_t m_ready[SOFTMAX_WGS];             // group g has published mx[g] for its block (4 warp arrivals)
     uint32_t tmem_base;
     int failed;
 };
@@ -131,9 +136,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.p_full[s], SOFTMAX_WARPS);
+            mbar_init(&sm.p_full[s], 4);  // the 4 warps of the group that owns the block
             mbar_init(&sm.o_done[s], 1);
         }
+        for (int g = 0; g < SOFTMAX_WGS; ++g) mbar_init(&sm.m_ready[g], 4);
         sm.failed = 0;
         fence_barrier_init();
     }
@@ -285,9 +291,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // -------------------------------------------------------------------------------- softmax
-        // row r = TMEM lane (warp % 4) * 32 + lane; group g = warp / 4 owns cells [CPT g, CPT g + CPT) of each
-        // 64-cell block and dims [OPT g, OPT g + OPT) of O. The groups of a row agree on its max through shared
-        // memory once per block. Every thread reaches every named barrier, failed or not.
+        // row r = TMEM lane (warp % 4) * 32 + lane; group g = warp / 4 takes blocks g, g + 2, ... (all 64 cells) and
+        // dims [OPT g, OPT g + OPT) of O in the epilogue. Every thread reaches every named barrier, failed or not.
         const int grp = warp >> 2;
         const int r = (warp & 3) * 32 + lane;
         const int qi = q0 + r;
@@ -300,9 +305,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             slope = h < p.n_head_log2 ? powf(p.m0, (float) (h + 1)) : powf(p.m1, (float) (2 * (h - p.n_head_log2) + 1));
         const int64_t row_pos = p.pos0 + q0;  // position of the tile's first query
         const float scl = p.scale_log2;
-        float m = -INFINITY, l = 0.0f;
+        float m = -INFINITY;   // the row's running max after the previous block (O's reference)
+        float mg = -INFINITY;  // the reference of this group's row sum l
+        float l = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nb; ++j) {
+        for (int j = grp; j < nb; j += SOFTMAX_WGS) {
             const int s = j % NSTAGE;
             ok = ok && wait_or_fail(&sm.s_full[s], (j / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
             ok = __all_sync(0xffffffffu, ok);
@@ -315,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool analytic = !mrow && !p.has_softcap;
             if (ok) {
                 tc_fence_after();
-                tmem_ld<CPT>(lane_addr + TM_S + s * BN + grp * CPT, sv);
+                tmem_ld<CPT>(lane_addr + TM_S + s * BN, sv);
                 tmem_wait_ld();
                 if (plain) {
                     // scale > 0: the max of the scaled scores is the scaled max of the raw ones (3-input max)
@@ -329,11 +336,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     bm = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * scl;
                 } else if (analytic) {
-                    const int64_t cell0 = blk0 + grp * CPT;
-                    int64_t lo = 0, hi = min((int64_t) CPT, p.n_kv - cell0);
+                    int64_t lo = 0, hi = min((int64_t) CPT, p.n_kv - blk0);
                     if (p.causal) {
-                        lo = max(lo, p.kv_lo - cell0);
-                        hi = min(hi, p.pos0 + qi + 1 - cell0);
+                        lo = max(lo, p.kv_lo - blk0);
+                        hi = min(hi, p.pos0 + qi + 1 - blk0);
                     }
                     if (qi >= p.n_q) hi = 0;
                     const int e_lo = (int) max((int64_t) 0, lo), e_hi = (int) max((int64_t) 0, hi);
@@ -344,48 +350,47 @@ __global__ void __launch_bounds__(THREADS, 1)
                         bm = fmaxf(bm, sc);
                     }
                 } else {
-                    const int64_t cell0 = blk0 + grp * CPT;
 #pragma unroll
                     for (int e = 0; e < CPT; ++e) {
-                        const float sc = prefill_score(p, __uint_as_float(sv[e]), cell0 + e, qi, mrow, slope);
+                        const float sc = prefill_score(p, __uint_as_float(sv[e]), blk0 + e, qi, mrow, slope);
                         sv[e] = __float_as_uint(sc);
                         bm = fmaxf(bm, sc);
                     }
                 }
-                // exchanged as f16 rounded up (no cell exceeds the shared reference); scores are clamped to f16's
-                // range first, a bound (6e4 in log2 units) no attention score reaches
-                if (SOFTMAX_WGS > 1) sm.xmax[j & 1][grp][r] = __float2half_ru(fminf(bm, 60000.0f));
             }
-            if (SOFTMAX_WGS > 1) named_bar_sync(1, SOFTMAX_WARPS * 32);
-            if (!ok) continue;
-            float bmax = bm;
-            if (SOFTMAX_WGS > 1) {
-                bmax = -INFINITY;
-#pragma unroll
-                for (int g2 = 0; g2 < SOFTMAX_WGS; ++g2) bmax = fmaxf(bmax, __half2float(sm.xmax[j & 1][g2][r]));
+            // the running max after block j - 1, published by the other group (block 0 starts from -inf)
+            if (j > 0) {
+                const int g2 = (j - 1) % SOFTMAX_WGS;
+                ok = ok && wait_or_fail(&sm.m_ready[g2], ((j - 1) / SOFTMAX_WGS) & 1, p, failed, DEV_ERR_WAIT_FULL);
+                ok = __all_sync(0xffffffffu, ok);
+                if (ok) m = sm.mx[g2][r];
             }
-            // lazy rescale
+            // lazy rescale: raise the reference only when the block max exceeds it by more than the threshold
             float m_use = m;
             bool rescale = false;
-            if ((bmax > m + RESCALE_THRESHOLD || m == -INFINITY) && bmax != -INFINITY) {
-                m_use = bmax;
+            if ((bm > m + RESCALE_THRESHOLD || m == -INFINITY) && bm != -INFINITY) {
+                m_use = bm;
                 rescale = m != -INFINITY;
             }
+            // publish the max after block j for the other group's next block (also when failed: no one waits in vain)
+            sm.mx[grp][r] = m_use;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.m_ready[grp]);
+            if (!ok) continue;
             const bool any_rescale = __any_sync(0xffffffffu, rescale);
             // O may only be rescaled once PV_{j-1} is complete
             if (any_rescale && j >= 1)
                 ok = wait_or_fail(&sm.o_done[(j - 1) % NSTAGE], ((j - 1) / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
-            // (P_j reuses S_j's columns; PV_{j-2}, the last reader of this buffer, ran before S_j was written)
+            // (P_j reuses S_j's columns; PV_{j-3}, the last reader of this buffer, ran before S_j was written)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) continue;
             tc_fence_after();
             if (any_rescale) {
                 const float alpha = rescale ? exp2f(m - m_use) : 1.0f;
-                l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < OPT / 32; ++c) {
+                for (int c = 0; c < D / 32; ++c) {
                     uint32_t ov[32];
-                    const uint32_t ta = lane_addr + TM_O + grp * OPT + c * 32;
+                    const uint32_t ta = lane_addr + TM_O + c * 32;
                     tmem_ld32(ta, ov);
                     tmem_wait_ld();
 #pragma unroll
@@ -394,6 +399,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tmem_wait_st();
             }
+            // this group's row sum to the new reference
+            if (mg != m_use && mg != -INFINITY) l *= exp2f(mg - m_use);
+            mg = m_use;
             m = m_use;
             const float mref = m == -INFINITY ? 0.0f : m;
             uint32_t pk[CPT / 2];
@@ -425,8 +433,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             l += (s0 + s1) + (s2 + s3);
-            // P_j into the first half of S_j's columns (every group has read its S_j: the named barrier above)
-            tmem_st<CPT / 2>(lane_addr + TM_S + s * BN + grp * (CPT / 2), pk);
+            // P_j into the first half of S_j's columns (this thread has read its S_j above)
+            tmem_st<CPT / 2>(lane_addr + TM_S + s * BN, pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -437,6 +445,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (nb > 0) {
             ok = ok && wait_or_fail(&sm.o_done[(nb - 1) % NSTAGE], ((nb - 1) / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
             ok = __all_sync(0xffffffffu, ok);
+        }
+        // the row's final max (published for the last block) and this group's sum at that reference
+        if (nb > 0) {
+            const int gl = (nb - 1) % SOFTMAX_WGS;
+            ok = ok && wait_or_fail(&sm.m_ready[gl], ((nb - 1) / SOFTMAX_WGS) & 1, p, failed, DEV_ERR_WAIT_FULL);
+            ok = __all_sync(0xffffffffu, ok);
+            const float mf = ok ? sm.mx[gl][r] : -INFINITY;
+            if (ok && mg != mf && mg != -INFINITY) l *= exp2f(mg - mf);
         }
         named_bar_sync(1, SOFTMAX_WARPS * 32);  // every group has waited: no K stage is still being read
         float* xl = reinterpret_cast<float*>(sm.k[0]);  // [group][row]

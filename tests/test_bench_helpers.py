@@ -26,3 +26,17 @@ def test_clock_sampler_without_gpu_reports_no_samples():
         pass
     s = clk.summary()
     assert "reasons" in s
+
+
+def test_every_committed_profile_traffic_line_parses():
+    """bench.py reads `traffic_bytes:` from each profile summary it cites; a note after the number must not break it."""
+    import glob
+    import os
+
+    for path in glob.glob(os.path.join(os.path.dirname(bench.__file__), "profiles", "*.md")):
+        name = os.path.splitext(os.path.basename(path))[0]
+        with open(path) as f:
+            has = any(line.startswith("traffic_bytes:") for line in f)
+        if has:
+            v = bench.ncu_traffic(name)
+            assert isinstance(v, int) and v > 0, name
