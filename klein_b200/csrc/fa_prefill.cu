@@ -60,13 +60,17 @@ struct Smem {
     uint8_t v[VSTAGE][KVTILE];
     uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[VSTAGE], v_empty[VSTAGE];
     uint64_t s_full[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
+    uint64_t q_staged;                         // the Q staging buffer (V stage 2) is free again (softmax warps)
     float mx[SOFTMAX_WGS][BM];                  // [group][row]: the running max after the group's latest block
     uint64_t m_ready[SOFTMAX_WGS];             // group g has published mx[g] for its block (4 warp arrivals)
     uint32_t tmem_base;
     int failed;
 };
-// the epilogue's partial row sums [group][row] reuse the K ring, idle once the last PV has completed
-static_assert(SOFTMAX_WGS * BM * sizeof(float) <= KVTILE, "row sums fit in a K stage");
+// the epilogue's partial row sums [group][row] reuse V stage 1 and its output tile (128 rows x 1 KB) the K ring and V
+// stage 0, all idle once the last PV has completed; Q's staging image (dims 0-127 as 16-bit pairs) uses V's last stage
+static_assert(SOFTMAX_WGS * BM * sizeof(float) <= KVTILE, "row sums fit in a V stage");
+static_assert(KSTAGE == 3 && VSTAGE >= 2, "the output tile spans the K ring and V stage 0");
+static_assert(BM * QT_DIMS * 2 <= KVTILE, "Q's staging image fits in a V stage");
 
 
 __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaPrefillParams& p, volatile int* failed,
@@ -140,6 +144,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.o_done[s], 1);
         }
         for (int g = 0; g < SOFTMAX_WGS; ++g) mbar_init(&sm.m_ready[g], 4);
+        mbar_init(&sm.q_staged, SOFTMAX_WARPS);
         sm.failed = 0;
         fence_barrier_init();
     }
@@ -153,61 +158,69 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
     if (warp < SOFTMAX_WARPS) {
-        // Q rounded to the K type into TMEM (the A operand of QK^T): row r = lane, dims [OPT grp, OPT grp + OPT) as
-        // packed pairs, 32 columns (64 dims) at a time
-        const int grp = warp >> 2, r = (warp & 3) * 32 + lane, qi = q0 + r;
+        // Q rounded to the K type, read with coalesced loads (a warp reads half a row, 512 contiguous bytes): dims
+        // 128-255 go straight into their swizzled K-major image in shared memory (the A operand of QK^T); dims 0-127
+        // into a row-major staging image in V stage 2 (16-byte units XOR-swizzled by row), from which each row's
+        // thread moves them into TMEM. V stage 2 is first loaded for block 2, after this (the q_staged barrier).
+        constexpr int NT = SOFTMAX_WARPS * 32;   // threads staging Q
+        constexpr int F4 = D / 4;                // float4 per row
+        const int tid = threadIdx.x;
+        uint8_t* stage = sm.v[VSTAGE - 1];
 #pragma unroll 1
-        for (int c = 0; c < OPT / 64; ++c) {
-            uint32_t qv[32];
-            if (qi < p.n_q) {
-                const float4* src =
-                    reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3) + (grp * OPT + c * 64) / 4;
-                if constexpr (FMT == 2) {
-                    // two q8_0 blocks of 32 dims: d = amax / 127, q = round(x / d), then f16(q * f16(d))
+        for (int i0 = 0; i0 < BM * F4 / NT; i0 += 8) {
+            float4 a[8];
 #pragma unroll
-                    for (int hb = 0; hb < 2; ++hb) {
-                        float4 a[8];
-                        float amax = 0.0f;
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            a[u] = src[8 * hb + u];
-                            amax = fmaxf(amax, max3f(fabsf(a[u].x), fabsf(a[u].y), fmaxf(fabsf(a[u].z), fabsf(a[u].w))));
-                        }
-                        const float d = amax / 127.0f;
-                        const float id = d != 0.0f ? 1.0f / d : 0.0f;
-                        const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            qv[16 * hb + 2 * u] = pack_half2(roundf(a[u].x * id) * dh, roundf(a[u].y * id) * dh);
-                            qv[16 * hb + 2 * u + 1] = pack_half2(roundf(a[u].z * id) * dh, roundf(a[u].w * id) * dh);
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        const float4 a = src[u];
-                        qv[2 * u] = OPF == 0 ? pack_half2(a.x, a.y) : pack_bf162(a.x, a.y);
-                        qv[2 * u + 1] = OPF == 0 ? pack_half2(a.z, a.w) : pack_bf162(a.z, a.w);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int u = 0; u < 32; ++u) qv[u] = 0u;
+            for (int u = 0; u < 8; ++u) {
+                const int f = tid + NT * (i0 + u), row = f / F4, c4 = f % F4, qi = q0 + row;
+                a[u] = qi < p.n_q ? reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3)[c4]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            const int d0 = grp * OPT + c * 64;
-            if (d0 < QT_DIMS) {
-                tmem_st32(tmem + ((uint32_t) ((warp & 3) * 32) << 16) + TM_Q + d0 / 2, qv);
-            } else {
-                uint8_t* img = sm.q[(d0 - QT_DIMS) / 64];
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    *reinterpret_cast<uint4*>(img + r * 128 + ((u ^ (r & 7)) << 4)) =
-                        make_uint4(qv[4 * u], qv[4 * u + 1], qv[4 * u + 2], qv[4 * u + 3]);
+            for (int u = 0; u < 8; ++u) {
+                const int f = tid + NT * (i0 + u), row = f / F4, c4 = f % F4;
+                uint2 v2;
+                if constexpr (FMT == 2) {
+                    // q8_0 blocks of 32 dims = 8 float4 in 8 consecutive lanes: d = amax / 127, q = round(x / d),
+                    // then f16(q * f16(d))
+                    float amax = max3f(fabsf(a[u].x), fabsf(a[u].y), fmaxf(fabsf(a[u].z), fabsf(a[u].w)));
+#pragma unroll
+                    for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                    const float d = amax / 127.0f;
+                    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                    const float dh = __half2float(__float2half_rn(d));
+                    v2 = make_uint2(pack_half2(roundf(a[u].x * id) * dh, roundf(a[u].y * id) * dh),
+                                    pack_half2(roundf(a[u].z * id) * dh, roundf(a[u].w * id) * dh));
+                } else {
+                    v2 = OPF == 0 ? make_uint2(pack_half2(a[u].x, a[u].y), pack_half2(a[u].z, a[u].w))
+                                  : make_uint2(pack_bf162(a[u].x, a[u].y), pack_bf162(a[u].z, a[u].w));
+                }
+                if (c4 < QT_DIMS / 4) {
+                    // staging row: 16 units of 16 bytes, unit c4 / 2 at position (c4 / 2) ^ (row % 16)
+                    *reinterpret_cast<uint2*>(stage + row * 256 + (((c4 >> 1) ^ (row & 15)) << 4) + (c4 & 1) * 8) = v2;
+                } else {
+                    const int cc = c4 - QT_DIMS / 4;  // float4 index within dims 128-255
+                    uint8_t* img = sm.q[cc / 16];
+                    *reinterpret_cast<uint2*>(img + row * 128 + ((((cc % 16) >> 1) ^ (row & 7)) << 4) + (cc & 1) * 8) = v2;
+                }
             }
         }
+        named_bar_sync(1, NT);
+        // TMEM row r = this thread's lane quadrant row; group g moves dims [64 g, 64 g + 64) (32 packed columns)
+        {
+            const int grp = warp >> 2, r = (warp & 3) * 32 + lane;
+            uint32_t qv[32];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint4 x = *reinterpret_cast<const uint4*>(stage + r * 256 + (((grp * 8 + u) ^ (r & 15)) << 4));
+                qv[4 * u] = x.x, qv[4 * u + 1] = x.y, qv[4 * u + 2] = x.z, qv[4 * u + 3] = x.w;
+            }
+            tmem_st32(tmem + ((uint32_t) ((warp & 3) * 32) << 16) + TM_Q + grp * 32, qv);
+        }
         tmem_wait_st();
-        fence_proxy_async_smem();
+        fence_proxy_async_smem();  // the generic writes of sm.q before the tensor core reads it
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.q_staged);
     }
     // the S issuer starts once Q is in TMEM; the producers and the PV issuer do not wait for it
     if (warp < SOFTMAX_WARPS || warp == W_SMMA) {
@@ -230,6 +243,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 uint64_t* fullb = is_v ? &sm.v_full[s] : &sm.k_full[s];
                 uint8_t* dst = is_v ? sm.v[s] : sm.k[s];
                 if (j >= depth && !wait_or_fail(empty, ((j / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
+                // V stage 2 carries the Q staging image until the softmax warps have moved it into TMEM
+                if (is_v && j == VSTAGE - 1 && !wait_or_fail(&sm.q_staged, 0, p, failed, DEV_ERR_WAIT_EMPTY)) break;
                 mbar_arrive_expect_tx(fullb, KVTILE);
                 for (int c = 0; c < D / 64; ++c) tma_load_4d(dst + c * (BN * 128), map, fullb, c * 64, hk, cell, kb3);
             }
@@ -441,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive(&sm.p_full[s]);
         }
         // epilogue: O / sum of the groups' l for this row, each group writing its OPT dims. Once the last PV has
-        // completed every MMA has, so the K ring is free to carry the partial row sums.
+        // completed every MMA has, so the K and V rings are free to carry the row sums and the output tile.
         if (nb > 0) {
             ok = ok && wait_or_fail(&sm.o_done[(nb - 1) % NSTAGE], ((nb - 1) / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
             ok = __all_sync(0xffffffffu, ok);
@@ -454,43 +469,59 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float mf = ok ? sm.mx[gl][r] : -INFINITY;
             if (ok && mg != mf && mg != -INFINITY) l *= exp2f(mg - mf);
         }
-        named_bar_sync(1, SOFTMAX_WARPS * 32);  // every group has waited: no K stage is still being read
-        float* xl = reinterpret_cast<float*>(sm.k[0]);  // [group][row]
+        named_bar_sync(1, SOFTMAX_WARPS * 32);  // every group has waited: no K / V stage is still being read
+        float* xl = reinterpret_cast<float*>(sm.v[1]);  // [group][row]
         xl[grp * BM + r] = l;
         named_bar_sync(1, SOFTMAX_WARPS * 32);
         float lt = 0.0f;
 #pragma unroll
         for (int g2 = 0; g2 < SOFTMAX_WGS; ++g2) lt += xl[g2 * BM + r];
-        float* out = reinterpret_cast<float*>(p.dst + h * p.d_nb1 + (int64_t) qi * p.d_nb2 + b * p.d_nb3) + grp * OPT;
-        if (ok && nb > 0) {
-            tc_fence_after();
-            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+        // the normalised rows into a [128 rows][1 KB] tile (16-byte units XOR-swizzled by row % 8), then written out
+        // with coalesced stores (a warp writes half a row); rows that see no cell are zeros
+        uint8_t* ost = sm.k[0];
+        {
+            const bool have = ok && nb > 0;
+            const float inv = have && lt > 0.0f ? 1.0f / lt : 0.0f;
+            if (have) tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < OPT / 32; ++c) {
                 uint32_t ov[32];
-                tmem_ld32(lane_addr + TM_O + grp * OPT + c * 32, ov);
-                tmem_wait_ld();
-                if (qi < p.n_q) {
-                    // klein's output gate (graph.cpp:124): o * sigmoid(gate), ggml's 1 / (1 + expf(-x))
-                    const float* gr = p.gate ? reinterpret_cast<const float*>(p.gate + h * p.g_nb1 + (int64_t) qi * p.g_nb2 +
-                                                                            b * p.g_nb3) + grp * OPT + c * 32
-                                             : nullptr;
+                if (have) {
+                    tmem_ld32(lane_addr + TM_O + grp * OPT + c * 32, ov);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4) {
-                        float4 o4 = make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
-                                                __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
-                        if (gr) {
-                            o4.x *= 1.0f / (1.0f + expf(-gr[e]));
-                            o4.y *= 1.0f / (1.0f + expf(-gr[e + 1]));
-                            o4.z *= 1.0f / (1.0f + expf(-gr[e + 2]));
-                            o4.w *= 1.0f / (1.0f + expf(-gr[e + 3]));
-                        }
-                        *reinterpret_cast<float4*>(out + c * 32 + e) = o4;
-                    }
+                    for (int e = 0; e < 32; ++e) ov[e] = 0u;
+                }
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const int unit = (grp * OPT + c * 32 + e) / 4;
+                    *reinterpret_cast<float4*>(ost + r * 1024 + ((unit ^ (r & 7)) << 4)) =
+                        make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
+                                    __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
                 }
             }
-        } else if (nb == 0 && qi < p.n_q) {
-            for (int d = 0; d < OPT; d += 4) *reinterpret_cast<float4*>(out + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        named_bar_sync(1, SOFTMAX_WARPS * 32);
+        {
+            constexpr int NT = SOFTMAX_WARPS * 32, F4 = D / 4;
+            const int tid = threadIdx.x;
+#pragma unroll 4
+            for (int i = 0; i < BM * F4 / NT; ++i) {
+                const int f = tid + NT * i, row = f / F4, c4 = f % F4, q = q0 + row;
+                if (q >= p.n_q) continue;
+                float4 o4 = *reinterpret_cast<const float4*>(ost + row * 1024 + ((c4 ^ (row & 7)) << 4));
+                if (p.gate) {
+                    // klein's output gate (graph.cpp:124): o * sigmoid(gate), ggml's 1 / (1 + expf(-x))
+                    const float4 g4 = reinterpret_cast<const float4*>(p.gate + h * p.g_nb1 + (int64_t) q * p.g_nb2 +
+                                                                      b * p.g_nb3)[c4];
+                    o4.x *= 1.0f / (1.0f + expf(-g4.x));
+                    o4.y *= 1.0f / (1.0f + expf(-g4.y));
+                    o4.z *= 1.0f / (1.0f + expf(-g4.z));
+                    o4.w *= 1.0f / (1.0f + expf(-g4.w));
+                }
+                reinterpret_cast<float4*>(p.dst + h * p.d_nb1 + (int64_t) q * p.d_nb2 + b * p.d_nb3)[c4] = o4;
+            }
         }
     }
     tc_fence_before();
