@@ -4,13 +4,14 @@
 // rounds it to the vec_dot type of a q8_0 or q4_0 K, ops.cpp:8960).
 //
 // One CTA computes a 128-query tile of one head. Roles (12 warps):
-//   warps 0-7  softmax in two warpgroups that take alternate 64-cell blocks of the same 128 rows (group g the
-//              blocks j with j % 2 == g), one thread per query row and group (row r = TMEM lane r, all 64 cells of
-//              its blocks): stage Q, run the online softmax (unmasked blocks on the packed f32x2 pipe), rescale O
-//              when needed, write the normalised output. One warp per scheduler could not keep up with the tensor
-//              core (one block's softmax took longer than its MMAs); with two, one group's exponentials overlap the
-//              other's TMEM reads and waits. The running row max passes from block to block, and so from group to
-//              group, through shared memory (an mbarrier per group); each group keeps its own row sum.
+//   warps 0-7  softmax in two warpgroups that share every 64-cell block: group g takes cells [32 g, 32 g + 32) of
+//              each row (row r = TMEM lane r, one thread per row and group) and dims [128 g, 128 g + 128) of O.
+//              Stage Q, run the online softmax (unmasked blocks on the packed f32x2 pipe), rescale O when needed,
+//              write the normalised output. The groups agree on each block's row max through shared memory (f32,
+//              one named barrier per block); each keeps its part of the row sum. The block's softmax latency is the
+//              S -> softmax -> PV -> S_{j+3} cycle's longest step: halving the cells per thread shortens it (one
+//              thread per row over all 64 cells took 1.0 us of a 1.09 us block; groups taking alternate blocks
+//              overlapped their work but left each block's latency, and so the cycle, unchanged).
 //   warps 8-9  TMA producers for K and for V (independent chains): 64 cells x 256 dims, 128-byte swizzle, rings
 //              of 3 tiles each
 //   warp 10    S issuer (one thread): S_j = Q K_j^T, 16 MMAs of K = 16 into S buffer j % 3, once PV_{j-3} (the
@@ -44,10 +45,10 @@ constexpr int KVTILE = BN * D * 2;            // 32 KiB: 4 chunks of [64 cells][
 constexpr int KSTAGE = 3;                     // K ring depth (the K chain is latency-bound: depth sets the rate)
 constexpr int VSTAGE = 3;                     // V ring depth
 constexpr int NSTAGE = 3;                     // S / P buffers: S_{j+3} may start once PV_j has read P_j
-constexpr int SOFTMAX_WGS = 2;                 // softmax warpgroups: group g takes the blocks j with j % 2 == g
+constexpr int SOFTMAX_WGS = 2;                 // softmax warpgroups, sharing every block's cells
 constexpr int SOFTMAX_WARPS = 4 * SOFTMAX_WGS;
-constexpr int CPT = BN;                         // cells per softmax thread per block (the whole row of the block)
-constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread in the epilogue
+constexpr int CPT = BN / SOFTMAX_WGS;           // cells per softmax thread per block
+constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread (rescale and epilogue)
 constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // + K producer, V producer, S issuer, PV issuer
 constexpr int W_KPROD = SOFTMAX_WARPS, W_VPROD = SOFTMAX_WARPS + 1, W_SMMA = SOFTMAX_WARPS + 2, W_PVMMA = SOFTMAX_WARPS + 3;
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_Q = 448;  // Q: dims 0-127 (the other half is in shared memory)
@@ -61,8 +62,7 @@ struct Smem {
     uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[VSTAGE], v_empty[VSTAGE];
     uint64_t s_full[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
     uint64_t q_staged;                         // the Q staging buffer (V stage 2) is free again (softmax warps)
-    float mx[SOFTMAX_WGS][BM];                  // [group][row]: the running max after the group's latest block
-    uint64_t m_ready[SOFTMAX_WGS];             // group g has published mx[g] for its block (4 warp arrivals)
+    float xmax[2][SOFTMAX_WGS][BM];            // [block parity][group][row]: the groups' block maxima
     uint32_t tmem_base;
     int failed;
 };
@@ -140,10 +140,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.p_full[s], 4);  // the 4 warps of the group that owns the block
+            mbar_init(&sm.p_full[s], SOFTMAX_WARPS);
             mbar_init(&sm.o_done[s], 1);
         }
-        for (int g = 0; g < SOFTMAX_WGS; ++g) mbar_init(&sm.m_ready[g], 4);
         mbar_init(&sm.q_staged, SOFTMAX_WARPS);
         sm.failed = 0;
         fence_barrier_init();
@@ -166,17 +165,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         constexpr int F4 = D / 4;                // float4 per row
         const int tid = threadIdx.x;
         uint8_t* stage = sm.v[VSTAGE - 1];
+        constexpr int QB = 16;  // float4 loads in flight per thread
 #pragma unroll 1
-        for (int i0 = 0; i0 < BM * F4 / NT; i0 += 8) {
-            float4 a[8];
+        for (int i0 = 0; i0 < BM * F4 / NT; i0 += QB) {
+            float4 a[QB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < QB; ++u) {
                 const int f = tid + NT * (i0 + u), row = f / F4, c4 = f % F4, qi = q0 + row;
                 a[u] = qi < p.n_q ? reinterpret_cast<const float4*>(p.q + qi * p.q_nb1 + h * p.q_nb2 + b * p.q_nb3)[c4]
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < QB; ++u) {
                 const int f = tid + NT * (i0 + u), row = f / F4, c4 = f % F4;
                 uint2 v2;
                 if constexpr (FMT == 2) {
@@ -306,8 +306,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // -------------------------------------------------------------------------------- softmax
-        // row r = TMEM lane (warp % 4) * 32 + lane; group g = warp / 4 takes blocks g, g + 2, ... (all 64 cells) and
-        // dims [OPT g, OPT g + OPT) of O in the epilogue. Every thread reaches every named barrier, failed or not.
+        // row r = TMEM lane (warp % 4) * 32 + lane; group g = warp / 4 owns cells [CPT g, CPT g + CPT) of each
+        // 64-cell block and dims [OPT g, OPT g + OPT) of O. Every thread reaches every named barrier, failed or not.
         const int grp = warp >> 2;
         const int r = (warp & 3) * 32 + lane;
         const int qi = q0 + r;
@@ -320,24 +320,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             slope = h < p.n_head_log2 ? powf(p.m0, (float) (h + 1)) : powf(p.m1, (float) (2 * (h - p.n_head_log2) + 1));
         const int64_t row_pos = p.pos0 + q0;  // position of the tile's first query
         const float scl = p.scale_log2;
-        float m = -INFINITY;   // the row's running max after the previous block (O's reference)
-        float mg = -INFINITY;  // the reference of this group's row sum l
-        float l = 0.0f;
+        float m = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int j = grp; j < nb; j += SOFTMAX_WGS) {
+        for (int j = 0; j < nb; ++j) {
             const int s = j % NSTAGE;
             ok = ok && wait_or_fail(&sm.s_full[s], (j / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
             ok = __all_sync(0xffffffffu, ok);
             uint32_t sv[CPT];
             float bm = -INFINITY;
             const int64_t blk0 = block_cell(j);
+            const int64_t cell0 = blk0 + grp * CPT;
             const bool plain = !mrow && !p.has_softcap && blk0 + BN <= p.n_kv &&
                                (!p.causal || (blk0 >= p.kv_lo && blk0 + BN - 1 <= row_pos)) && q0 + BM <= p.n_q;
             // without a mask tensor or softcap the visible cells of a row form one range [e_lo, e_hi) of the block
             const bool analytic = !mrow && !p.has_softcap;
             if (ok) {
                 tc_fence_after();
-                tmem_ld<CPT>(lane_addr + TM_S + s * BN, sv);
+                tmem_ld<CPT>(lane_addr + TM_S + s * BN + grp * CPT, sv);
                 tmem_wait_ld();
                 if (plain) {
                     // scale > 0: the max of the scaled scores is the scaled max of the raw ones (3-input max)
@@ -351,10 +350,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     bm = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * scl;
                 } else if (analytic) {
-                    int64_t lo = 0, hi = min((int64_t) CPT, p.n_kv - blk0);
+                    int64_t lo = 0, hi = min((int64_t) CPT, p.n_kv - cell0);
                     if (p.causal) {
-                        lo = max(lo, p.kv_lo - blk0);
-                        hi = min(hi, p.pos0 + qi + 1 - blk0);
+                        lo = max(lo, p.kv_lo - cell0);
+                        hi = min(hi, p.pos0 + qi + 1 - cell0);
                     }
                     if (qi >= p.n_q) hi = 0;
                     const int e_lo = (int) max((int64_t) 0, lo), e_hi = (int) max((int64_t) 0, hi);
@@ -367,31 +366,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                 } else {
 #pragma unroll
                     for (int e = 0; e < CPT; ++e) {
-                        const float sc = prefill_score(p, __uint_as_float(sv[e]), blk0 + e, qi, mrow, slope);
+                        const float sc = prefill_score(p, __uint_as_float(sv[e]), cell0 + e, qi, mrow, slope);
                         sv[e] = __float_as_uint(sc);
                         bm = fmaxf(bm, sc);
                     }
                 }
+                sm.xmax[j & 1][grp][r] = bm;
             }
-            // the running max after block j - 1, published by the other group (block 0 starts from -inf)
-            if (j > 0) {
-                const int g2 = (j - 1) % SOFTMAX_WGS;
-                ok = ok && wait_or_fail(&sm.m_ready[g2], ((j - 1) / SOFTMAX_WGS) & 1, p, failed, DEV_ERR_WAIT_FULL);
-                ok = __all_sync(0xffffffffu, ok);
-                if (ok) m = sm.mx[g2][r];
-            }
+            // both groups have read their S_j (P_j overwrites its first half below) and published their maxima
+            named_bar_sync(1, SOFTMAX_WARPS * 32);
+            if (!ok) continue;
+            float bmax = -INFINITY;
+#pragma unroll
+            for (int g2 = 0; g2 < SOFTMAX_WGS; ++g2) bmax = fmaxf(bmax, sm.xmax[j & 1][g2][r]);
             // lazy rescale: raise the reference only when the block max exceeds it by more than the threshold
             float m_use = m;
             bool rescale = false;
-            if ((bm > m + RESCALE_THRESHOLD || m == -INFINITY) && bm != -INFINITY) {
-                m_use = bm;
+            if ((bmax > m + RESCALE_THRESHOLD || m == -INFINITY) && bmax != -INFINITY) {
+                m_use = bmax;
                 rescale = m != -INFINITY;
             }
-            // publish the max after block j for the other group's next block (also when failed: no one waits in vain)
-            sm.mx[grp][r] = m_use;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.m_ready[grp]);
-            if (!ok) continue;
             const bool any_rescale = __any_sync(0xffffffffu, rescale);
             // O may only be rescaled once PV_{j-1} is complete
             if (any_rescale && j >= 1)
@@ -402,10 +396,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             if (any_rescale) {
                 const float alpha = rescale ? exp2f(m - m_use) : 1.0f;
+                l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c = 0; c < OPT / 32; ++c) {
                     uint32_t ov[32];
-                    const uint32_t ta = lane_addr + TM_O + c * 32;
+                    const uint32_t ta = lane_addr + TM_O + grp * OPT + c * 32;
                     tmem_ld32(ta, ov);
                     tmem_wait_ld();
 #pragma unroll
@@ -414,9 +409,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tmem_wait_st();
             }
-            // this group's row sum to the new reference
-            if (mg != m_use && mg != -INFINITY) l *= exp2f(mg - m_use);
-            mg = m_use;
             m = m_use;
             const float mref = m == -INFINITY ? 0.0f : m;
             uint32_t pk[CPT / 2];
@@ -448,8 +440,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             l += (s0 + s1) + (s2 + s3);
-            // P_j into the first half of S_j's columns (this thread has read its S_j above)
-            tmem_st<CPT / 2>(lane_addr + TM_S + s * BN, pk);
+            // P_j into the first half of S_j's columns (every group has read its S_j: the named barrier above)
+            tmem_st<CPT / 2>(lane_addr + TM_S + s * BN + grp * (CPT / 2), pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -460,14 +452,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (nb > 0) {
             ok = ok && wait_or_fail(&sm.o_done[(nb - 1) % NSTAGE], ((nb - 1) / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL);
             ok = __all_sync(0xffffffffu, ok);
-        }
-        // the row's final max (published for the last block) and this group's sum at that reference
-        if (nb > 0) {
-            const int gl = (nb - 1) % SOFTMAX_WGS;
-            ok = ok && wait_or_fail(&sm.m_ready[gl], ((nb - 1) / SOFTMAX_WGS) & 1, p, failed, DEV_ERR_WAIT_FULL);
-            ok = __all_sync(0xffffffffu, ok);
-            const float mf = ok ? sm.mx[gl][r] : -INFINITY;
-            if (ok && mg != mf && mg != -INFINITY) l *= exp2f(mg - mf);
         }
         named_bar_sync(1, SOFTMAX_WARPS * 32);  // every group has waited: no K / V stage is still being read
         float* xl = reinterpret_cast<float*>(sm.v[1]);  // [group][row]
