@@ -855,17 +855,26 @@ cudaError_t set_smem(Kern kern, size_t smem, bool (&done)[64]) {
 
 }  // namespace
 
-cudaError_t launch_gdn_chunked(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream) {
-    static bool prep_done[64] = {}, state_done[64] = {};
+cudaError_t launch_gdn_prep(const GdnChunkParams& p, cudaStream_t stream) {
+    static bool prep_done[64] = {};
     cudaError_t e = set_smem(gdn_chunk_prep_kernel, sizeof(PrepSmem), prep_done);
     if (e != cudaSuccess) return e;
-    e = set_smem(gdn_chunk_state_kernel, sizeof(StateSmem), state_done);
-    if (e != cudaSuccess) return e;
     gdn_chunk_prep_kernel<<<dim3(p.in.H_v, p.n_chunks, p.in.n_seqs), PREP_THREADS, sizeof(PrepSmem), stream>>>(p);
-    e = cudaGetLastError();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_state(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream) {
+    static bool state_done[64] = {};
+    cudaError_t e = set_smem(gdn_chunk_state_kernel, sizeof(StateSmem), state_done);
     if (e != cudaSuccess) return e;
     gdn_chunk_state_kernel<<<dim3(p.in.H_v, p.in.n_seqs), ST_THREADS, sizeof(StateSmem), stream>>>(tmO, p);
     return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_chunked(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream) {
+    cudaError_t e = launch_gdn_prep(p, stream);
+    if (e != cudaSuccess) return e;
+    return launch_gdn_state(p, tmO, stream);
 }
 
 }  // namespace kb

@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/klein_b200.h"
 #include "kb_gdn.h"
@@ -690,6 +691,40 @@ bool encode_attn_map(const kb::GdnParams& p, int64_t tok_end, CUtensorMap* map) 
                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A side stream per device and a set of events for the overlapped chunked schedule below, created on first use
+// and kept for the process (streams and events, no device memory). The mutex keeps two host threads from
+// interleaving their records of the shared events.
+constexpr int GDN_MAX_PARTS = 16;
+constexpr int64_t GDN_PART_CHUNKS = 16;  // chunks per part (64 tokens each)
+struct GdnOverlap {
+    cudaStream_t side = nullptr;   // the records, lowest priority
+    cudaStream_t chain = nullptr;  // the state chain, highest priority: a part's chain, once its records are ready,
+                                   // takes SMs ahead of the next part's records
+    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaEvent_t part[GDN_MAX_PARTS] = {};
+    bool ok = false;
+};
+std::mutex g_overlap_mu;
+
+GdnOverlap* gdn_overlap() {
+    static GdnOverlap per_dev[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    GdnOverlap& o = per_dev[dev];
+    if (!o.ok) {
+        int lo = 0, hi = 0;
+        if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) return nullptr;
+        if (cudaStreamCreateWithPriority(&o.side, cudaStreamNonBlocking, lo) != cudaSuccess) return nullptr;
+        if (cudaStreamCreateWithPriority(&o.chain, cudaStreamNonBlocking, hi) != cudaSuccess) return nullptr;
+        if (cudaEventCreateWithFlags(&o.fork, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        if (cudaEventCreateWithFlags(&o.join, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        for (cudaEvent_t& e : o.part)
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        o.ok = true;
+    }
+    return &o;
+}
+
 kb_status gdn_run(const kb::GdnParams& p, bool packed, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
     const int64_t S = p.S, T = p.T, n_w = std::min<int64_t>(T, p.K), Tc = gdn_chunked_tokens(T, p.K);
     const int64_t per_chunk = (int64_t) p.n_seqs * p.H_v * kb::GDN_REC_BYTES;
@@ -718,7 +753,42 @@ kb_status gdn_run(const kb::GdnParams& p, bool packed, void* scratch, size_t scr
     c.wait_ns = g_wait_ns;
     const int64_t n_chunks = (Tc + kb::GDN_CHUNK - 1) / kb::GDN_CHUNK;
     const int64_t per_pass = std::min<int64_t>(n_chunks, (int64_t) scratch_bytes / per_chunk);
-    for (int64_t c0 = 0; c0 < n_chunks; c0 += per_pass) {
+    const int64_t n_parts = (n_chunks + GDN_PART_CHUNKS - 1) / GDN_PART_CHUNKS;
+    GdnOverlap* ov = per_pass == n_chunks && n_parts >= 2 && n_parts <= GDN_MAX_PARTS ? gdn_overlap() : nullptr;
+    if (ov) {
+        // Overlapped schedule: the state chain runs on 48 SMs (one CTA per head) while the rest would idle, so the
+        // records of part k + 1 are prepared on a side stream while part k's chain runs; part k's chain waits only
+        // for part k's records (stream order and events; no kernel waits on another). Every part's records have
+        // their own region of the scratch.
+        std::lock_guard<std::mutex> lock(g_overlap_mu);
+        if (cudaEventRecord(ov->fork, stream) != cudaSuccess || cudaStreamWaitEvent(ov->side, ov->fork, 0) != cudaSuccess ||
+            cudaStreamWaitEvent(ov->chain, ov->fork, 0) != cudaSuccess)
+            return KB_ERR_CUDA;
+        std::vector<kb::GdnChunkParams> parts;
+        for (int64_t k = 0; k < n_parts; ++k) {
+            const int64_t c0 = k * GDN_PART_CHUNKS, nc = std::min(GDN_PART_CHUNKS, n_chunks - c0);
+            kb::GdnChunkParams c2 = c;
+            c2.rec = static_cast<char*>(scratch) + c0 * per_chunk;
+            c2.tok0 = c0 * kb::GDN_CHUNK;
+            c2.n_tok = std::min(nc * kb::GDN_CHUNK, Tc - c2.tok0);
+            c2.n_chunks = (int) nc;
+            c2.s0 = c0 == 0 ? p.s0 : s_out;
+            c2.s0_seq_stride = c0 == 0 ? p.s0_seq_stride : state_stride;
+            c2.snap = k == n_parts - 1 ? snap : nullptr;
+            if (kb::launch_gdn_prep(c2, ov->side) != cudaSuccess) return KB_ERR_CUDA;
+            if (cudaEventRecord(ov->part[k], ov->side) != cudaSuccess) return KB_ERR_CUDA;
+            parts.push_back(c2);
+        }
+        for (int64_t k = 0; k < n_parts; ++k) {
+            CUtensorMap tmO;
+            if (!encode_attn_map(p, parts[k].tok0 + parts[k].n_tok, &tmO)) return KB_ERR_CUDA;
+            if (cudaStreamWaitEvent(ov->chain, ov->part[k], 0) != cudaSuccess) return KB_ERR_CUDA;
+            if (kb::launch_gdn_state(parts[k], tmO, ov->chain) != cudaSuccess) return KB_ERR_CUDA;
+        }
+        if (cudaEventRecord(ov->join, ov->chain) != cudaSuccess || cudaStreamWaitEvent(stream, ov->join, 0) != cudaSuccess)
+            return KB_ERR_CUDA;
+    }
+    for (int64_t c0 = 0; !ov && c0 < n_chunks; c0 += per_pass) {
         const int64_t nc = std::min(per_pass, n_chunks - c0);
         c.tok0 = c0 * kb::GDN_CHUNK;
         c.n_tok = std::min(nc * kb::GDN_CHUNK, Tc - c.tok0);

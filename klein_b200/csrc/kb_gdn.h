@@ -61,6 +61,9 @@ struct GdnChunkParams {
 // tmO: 4-d f32 map over the attention output (value dim, head, token, sequence) with box {128, 1, 64, 1}, its
 // token extent ending at tok0 + n_tok
 cudaError_t launch_gdn_chunked(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream);
+// the two halves of launch_gdn_chunked: the records of the pass's chunks, then the state chain over them
+cudaError_t launch_gdn_prep(const GdnChunkParams& p, cudaStream_t stream);
+cudaError_t launch_gdn_state(const GdnChunkParams& p, const CUtensorMap& tmO, cudaStream_t stream);
 
 // Cache row write (ggml_set_rows): dst row idx[r] of every (i2, i3) <- src row r converted to dst_type.
 struct SetRowsParams {
