@@ -63,7 +63,7 @@ def test_noalloc_matches_allocating_entry_point_twice(kb, cuda):
 
 
 def test_noalloc_buffer_covers_every_split_plan(kb, cuda):
-    """The split plan keeps the partials of one call at most (SM count x 24 rows x (256 + 2) floats), so the
+    """The split plan keeps the partials of one call at most (SM count x 32 rows x (256 + 2) floats), so the
     built-in buffer covers every shape on this GPU; a 64-token call (many row chunks) matches the allocating
     entry point."""
     import torch
