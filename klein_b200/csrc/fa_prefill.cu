@@ -41,36 +41,65 @@ constexpr float LOG2E = 1.4426950408889634f;
 constexpr int D = 256;
 constexpr int BM = 128;                       // query rows per CTA
 constexpr int BN = 64;                        // cells per K/V block
-constexpr int KVTILE = BN * D * 2;            // 32 KiB: 4 chunks of [64 cells][128 B]
-constexpr int KSTAGE = 3;                     // K ring depth (the K chain is latency-bound: depth sets the rate)
-constexpr int VSTAGE = 3;                     // V ring depth
-constexpr int NSTAGE = 3;                     // S / P buffers: S_{j+3} may start once PV_j has read P_j
+constexpr int KVTILE = BN * D * 2;            // 32 KiB: a whole K or V tile, 4 chunks of [64 cells][128 B]
 constexpr int SOFTMAX_WGS = 2;                 // softmax warpgroups, sharing every block's cells
 constexpr int SOFTMAX_WARPS = 4 * SOFTMAX_WGS;
 constexpr int CPT = BN / SOFTMAX_WGS;           // cells per softmax thread per block
 constexpr int OPT = D / SOFTMAX_WGS;            // O columns per softmax thread (rescale and epilogue)
 constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // + K producer, V producer, S issuer, PV issuer
 constexpr int W_KPROD = SOFTMAX_WARPS, W_VPROD = SOFTMAX_WARPS + 1, W_SMMA = SOFTMAX_WARPS + 2, W_PVMMA = SOFTMAX_WARPS + 3;
-constexpr uint32_t TM_O = 0, TM_S = 256, TM_Q = 448;  // Q: dims 0-127 (the other half is in shared memory)
-constexpr int QT_DIMS = 128;                           // Q dims held in TMEM
+constexpr uint32_t TM_O = 0, TM_S = 256;              // O, then the S / P buffers (then Q's TMEM part, if any)
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 units: rescale O only when the max grows by > 2^8
 
+// The K / V rings. One CTA holds whole tiles in 3-deep rings. A pair of CTAs (PAIR: two heads of a GQA group on the
+// same query tile, M = 256 MMAs issued by CTA 0) splits every tile: each CTA holds 32 of a K tile's 64 cells and 2 of
+// a V tile's 4 dim chunks, so the same shared memory carries 6-deep rings. The K ring's depth is what sets the
+// steady state (K_{j+depth}'s load can start only when S_j's MMAs have freed its stage, and takes ~2.5 us).
+//
+// S / P buffers (NSTAGE): S_{j+NSTAGE} may start once PV_j has read P_j, so the loop S -> softmax -> PV spans NSTAGE
+// blocks. O 256 + 3 x 64 S columns + Q dims 0-127 (64 packed columns) fill TMEM; Q dims 128-255 sit in shared memory.
+// (A pair with all of Q in shared memory, 5-deep rings and a fourth S / P buffer measured slower: every S MMA then
+// reads its A operand from shared memory as well, 3.4 us from issue to completion against 0.8.)
+template <bool PAIR>
+struct Ring {
+    static constexpr int KROWS = PAIR ? BN / 2 : BN;     // cells of a K tile held here
+    static constexpr int VCHUNKS = PAIR ? 2 : 4;         // 64-dim chunks of a V tile held here
+    static constexpr int KST = KROWS * D * 2;            // bytes of a K stage
+    static constexpr int VST = VCHUNKS * BN * 128;       // bytes of a V stage
+    static constexpr int KSTAGE = PAIR ? 6 : 3, VSTAGE = PAIR ? 6 : 3;
+    static constexpr int QT_DIMS = 128;                  // Q dims held in TMEM (the rest in shared memory)
+    static constexpr int NSTAGE = 3;
+    static constexpr uint32_t TM_Q = TM_S + NSTAGE * BN;
+    static constexpr int OUT_V = (BM * D * 4 - KSTAGE * KST) / VST;  // V stages the output tile needs beyond the K ring
+    static constexpr int QSTG = BM * QT_DIMS * 2 / VST;              // V stages (the last ones) of Q's staging image
+    static_assert(TM_Q + QT_DIMS / 2 <= 512, "TMEM");
+};
+
+template <bool PAIR>
 struct Smem {
-    uint8_t q[(D - QT_DIMS) / 64][BM * 128];   // Q dims 128-255: K-major, 128B-swizzled [chunk][128 rows][128 B]
-    uint8_t k[KSTAGE][KVTILE];                 // (1024-aligned offsets)
-    uint8_t v[VSTAGE][KVTILE];
-    uint64_t k_full[KSTAGE], k_empty[KSTAGE], v_full[VSTAGE], v_empty[VSTAGE];
-    uint64_t s_full[NSTAGE], p_full[NSTAGE], o_done[NSTAGE];
-    uint64_t q_staged;                         // the Q staging buffer (V stage 2) is free again (softmax warps)
+    using R = Ring<PAIR>;
+    uint8_t q[(D - R::QT_DIMS) / 64][BM * 128];  // Q's shared-memory dims: K-major, 128B-swizzled [chunk][128 rows][128 B]
+    uint8_t k[R::KSTAGE][R::KST];              // (1024-aligned offsets)
+    uint8_t v[R::VSTAGE][R::VST];
+    uint64_t k_full[R::KSTAGE], k_empty[R::KSTAGE], v_full[R::VSTAGE], v_empty[R::VSTAGE];
+    uint64_t s_full[R::NSTAGE], p_full[R::NSTAGE], o_done[R::NSTAGE];
+    uint64_t q_staged;                         // the Q staging stages of the V ring are free again (softmax warps)
+    uint64_t q_ready;                          // Q is in place (in both CTAs of a pair): the S issuer may start
     float xmax[2][SOFTMAX_WGS][BM];            // [block parity][group][row]: the groups' block maxima
     uint32_t tmem_base;
     int failed;
 };
-// the epilogue's partial row sums [group][row] reuse V stage 1 and its output tile (128 rows x 1 KB) the K ring and V
-// stage 0, all idle once the last PV has completed; Q's staging image (dims 0-127 as 16-bit pairs) uses V's last stage
-static_assert(SOFTMAX_WGS * BM * sizeof(float) <= KVTILE, "row sums fit in a V stage");
-static_assert(KSTAGE == 3 && VSTAGE >= 2, "the output tile spans the K ring and V stage 0");
-static_assert(BM * QT_DIMS * 2 <= KVTILE, "Q's staging image fits in a V stage");
+// the epilogue's output tile (128 rows x 1 KB) spans the K ring and the first OUT_V V stages and its partial row sums
+// [group][row] the next V stage, all idle once the last PV has completed; Q's staging image (dims 0-127 as 16-bit
+// pairs) uses the last QSTG V stages
+template <bool PAIR>
+constexpr bool ring_fits() {
+    using R = Ring<PAIR>;
+    return R::KSTAGE * R::KST + R::OUT_V * R::VST == BM * D * 4 && R::OUT_V + 1 <= R::VSTAGE - R::QSTG &&
+           SOFTMAX_WGS * BM * (int) sizeof(float) <= R::VST && R::QSTG * R::VST == BM * R::QT_DIMS * 2 &&
+           sizeof(Smem<PAIR>) <= 232448;
+}
+static_assert(ring_fits<false>() && ring_fits<true>(), "ring layout");
 
 
 __device__ __forceinline__ bool wait_or_fail(uint64_t* bar, uint32_t parity, const FaPrefillParams& p, volatile int* failed,
@@ -98,10 +127,17 @@ __device__ __forceinline__ float prefill_score(const FaPrefillParams& p, float x
 
 // FMT: 0 = f16 K/V, 1 = bf16 K/V (the type of K, V, and of the rounding of Q and P); 2 = f16 K/V widened from a
 // q8_0 / q4_0 cache, with Q quantised to q8_0 (quantize_row_q8_0_ref's rule) and widened to f16(q * d)
-template <int FMT>
+//
+// PAIR: launched in clusters of 2 (heads 2 i and 2 i + 1, same query tile, same KV head): the MMAs of both CTAs are one
+// cta_group::2 MMA of M = 256 issued by CTA 0's issuers, which wait on CTA 0's barriers (each CTA's half-tile loads
+// count there, and CTA 1's softmax warps arrive there) and commit to both CTAs' barriers.
+template <int FMT, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const FaPrefillParams p) {
+    using R = Ring<PAIR>;
+    constexpr int KSTAGE = R::KSTAGE, VSTAGE = R::VSTAGE, NSTAGE = R::NSTAGE, QT_DIMS = R::QT_DIMS;
+    constexpr uint32_t TM_Q = R::TM_Q;
     constexpr int OPF = FMT == 1 ? 1 : 0;  // operand format of the MMAs: f16 or bf16
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte alignment; the dynamic window starts there (checked, not assumed)
@@ -109,8 +145,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (threadIdx.x == 0) record_error(p.err, DEV_ERR_ALIGN);
         return;
     }
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+    Smem<PAIR>& sm = *reinterpret_cast<Smem<PAIR>*>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // CTA 0 of a pair issues the MMAs
+    const bool issuer_cta = rank == 0;
 
     // heavy (late) query tiles first; consecutive CTAs share the tile and walk the heads (K/V reuse in L2)
     const int tile = p.n_qtiles - 1 - (int) (blockIdx.x / p.n_head);
@@ -126,7 +164,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int nb = c_hi > c_lo ? (int) ((c_hi - c_lo + BN - 1) / BN) : 0;
     // the heads of a GQA group walk the shared K/V blocks from different starting points, so that they do not
     // all request the same L2 lines at once; block order does not change the result of the online softmax
-    const int rot = nb > 0 ? (int) (((int64_t) (h % p.gqa) * nb) / p.gqa) : 0;
+    // (a pair walks as one: its two heads share every MMA)
+    const int rot = nb > 0 ? (PAIR ? (int) (((int64_t) ((h % p.gqa) / 2) * nb) / (p.gqa / 2))
+                                   : (int) (((int64_t) (h % p.gqa) * nb) / p.gqa))
+                           : 0;
     auto block_cell = [&](int j) -> int64_t { return c_lo + (int64_t) ((j + rot) % nb) * BN; };
 
     if (threadIdx.x == 0) {
@@ -140,19 +181,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.p_full[s], SOFTMAX_WARPS);
+            mbar_init(&sm.p_full[s], (PAIR ? 2 : 1) * SOFTMAX_WARPS);
             mbar_init(&sm.o_done[s], 1);
         }
         mbar_init(&sm.q_staged, SOFTMAX_WARPS);
+        mbar_init(&sm.q_ready, (PAIR ? 2 : 1) * SOFTMAX_WARPS);
         sm.failed = 0;
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(&sm.tmem_base, 512);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(&sm.tmem_base, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(&sm.tmem_base, 512);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
@@ -164,7 +212,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         constexpr int NT = SOFTMAX_WARPS * 32;   // threads staging Q
         constexpr int F4 = D / 4;                // float4 per row
         const int tid = threadIdx.x;
-        uint8_t* stage = sm.v[VSTAGE - 1];
+        uint8_t* stage = sm.v[0] + (VSTAGE - R::QSTG) * R::VST;  // (unused when all of Q is in shared memory)
         constexpr int QB = 16;  // float4 loads in flight per thread
 #pragma unroll 1
         for (int i0 = 0; i0 < BM * F4 / NT; i0 += QB) {
@@ -198,7 +246,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // staging row: 16 units of 16 bytes, unit c4 / 2 at position (c4 / 2) ^ (row % 16)
                     *reinterpret_cast<uint2*>(stage + row * 256 + (((c4 >> 1) ^ (row & 15)) << 4) + (c4 & 1) * 8) = v2;
                 } else {
-                    const int cc = c4 - QT_DIMS / 4;  // float4 index within dims 128-255
+                    const int cc = c4 - QT_DIMS / 4;  // float4 index within Q's shared-memory dims
                     uint8_t* img = sm.q[cc / 16];
                     *reinterpret_cast<uint2*>(img + row * 128 + ((((cc % 16) >> 1) ^ (row & 7)) << 4) + (cc & 1) * 8) = v2;
                 }
@@ -206,7 +254,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         named_bar_sync(1, NT);
         // TMEM row r = this thread's lane quadrant row; group g moves dims [64 g, 64 g + 64) (32 packed columns)
-        {
+        if constexpr (QT_DIMS > 0) {
             const int grp = warp >> 2, r = (warp & 3) * 32 + lane;
             uint32_t qv[32];
 #pragma unroll
@@ -220,13 +268,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_proxy_async_smem();  // the generic writes of sm.q before the tensor core reads it
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.q_staged);
+        if (lane == 0) {
+            mbar_arrive(&sm.q_staged);
+            if constexpr (PAIR)
+                mbar_arrive_cluster(smem_rank(&sm.q_ready, 0));
+            else
+                mbar_arrive(&sm.q_ready);
+        }
     }
-    // the S issuer starts once Q is in TMEM; the producers and the PV issuer do not wait for it
-    if (warp < SOFTMAX_WARPS || warp == W_SMMA) {
-        named_bar_sync(2, (SOFTMAX_WARPS + 1) * 32);
-        tc_fence_after();
-    }
+    // the S issuer starts once Q is in place (q_ready); the producers and the PV issuer do not wait for it
 
     if (warp == W_KPROD || warp == W_VPROD) {
         // -------------------------------------------------------------------------------- TMA producers
@@ -244,9 +294,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                 uint8_t* dst = is_v ? sm.v[s] : sm.k[s];
                 if (j >= depth && !wait_or_fail(empty, ((j / depth) - 1) & 1, p, failed, DEV_ERR_WAIT_EMPTY)) break;
                 // V stage 2 carries the Q staging image until the softmax warps have moved it into TMEM
-                if (is_v && j == VSTAGE - 1 && !wait_or_fail(&sm.q_staged, 0, p, failed, DEV_ERR_WAIT_EMPTY)) break;
-                mbar_arrive_expect_tx(fullb, KVTILE);
-                for (int c = 0; c < D / 64; ++c) tma_load_4d(dst + c * (BN * 128), map, fullb, c * 64, hk, cell, kb3);
+                if (R::QSTG > 0 && is_v && j == VSTAGE - R::QSTG &&
+                    !wait_or_fail(&sm.q_staged, 0, p, failed, DEV_ERR_WAIT_EMPTY))
+                    break;
+                if constexpr (PAIR) {
+                    // both halves complete on CTA 0's barrier, which expects the whole tile
+                    if (issuer_cta) mbar_arrive_expect_tx(fullb, KVTILE);
+                    const uint32_t bar0 = smem_rank(fullb, 0);
+                    if (is_v) {
+                        for (int cc = 0; cc < R::VCHUNKS; ++cc)
+                            tma_load_4d_pair(dst + cc * (BN * 128), map, bar0, (int) (rank * R::VCHUNKS + cc) * 64, hk, cell,
+                                             kb3);
+                    } else {
+                        for (int c = 0; c < D / 64; ++c)
+                            tma_load_4d_pair(dst + c * (R::KROWS * 128), map, bar0, c * 64, hk, cell + (int) rank * R::KROWS,
+                                             kb3);
+                    }
+                } else {
+                    mbar_arrive_expect_tx(fullb, KVTILE);
+                    for (int c = 0; c < D / 64; ++c) tma_load_4d(dst + c * (BN * 128), map, fullb, c * 64, hk, cell, kb3);
+                }
             }
         }
     } else if (warp == W_SMMA) {
@@ -254,8 +321,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // S_j = Q K_j^T into buffer j % 2, once PV_{j-2} (the last reader of that buffer, through P_{j-2}) has
         // completed. A separate PV issuer keeps PV from waiting behind these 16 MMAs: the tensor core accepts only
         // a few MMAs ahead of the one executing, so issuing them takes about as long as running them.
-        if (lane == 0 && nb > 0) {
-            constexpr uint32_t idS = umma_idesc_f16(OPF, BM, BN, false, false);
+        if (lane == 0 && nb > 0 && issuer_cta) {
+            constexpr uint32_t idS = umma_idesc_f16(OPF, PAIR ? 2 * BM : BM, BN, false, false);
+            wait_or_fail(&sm.q_ready, 0, p, failed, DEV_ERR_WAIT_FULL);
             for (int j = 0; j < nb; ++j) {
                 const int s = j % NSTAGE, ks_ = j % KSTAGE;
                 if (!wait_or_fail(&sm.k_full[ks_], (j / KSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
@@ -269,25 +337,38 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int kk = 0; kk < 4; ++kk) {
                         // A = Q (dims 0-127 from TMEM, 8 packed columns per step; dims 128-255 from shared
                         // memory), B = K block, K-major
-                        const uint64_t bdesc = smem_desc_sw128(k_addr + c * (BN * 128) + kk * 32, 16, 1024);
+                        const uint64_t bdesc = smem_desc_sw128(k_addr + c * (R::KROWS * 128) + kk * 32, 16, 1024);
                         if (c * 64 < QT_DIMS) {
-                            umma_ts(tmem + TM_S + s * BN, tmem + TM_Q + (c * 4 + kk) * 8, bdesc, idS, (c | kk) != 0);
+                            if constexpr (PAIR)
+                                umma_ts_pair(tmem + TM_S + s * BN, tmem + TM_Q + (c * 4 + kk) * 8, bdesc, idS, (c | kk) != 0);
+                            else
+                                umma_ts(tmem + TM_S + s * BN, tmem + TM_Q + (c * 4 + kk) * 8, bdesc, idS, (c | kk) != 0);
                         } else {
                             const uint64_t adesc =
                                 smem_desc_sw128(smem_u32(sm.q[(c * 64 - QT_DIMS) / 64]) + kk * 32, 16, 1024);
-                            umma_ss(tmem + TM_S + s * BN, adesc, bdesc, idS, true);
+                            if constexpr (PAIR)
+                                umma_ss_pair(tmem + TM_S + s * BN, adesc, bdesc, idS, (c | kk) != 0);
+                            else
+                                umma_ss(tmem + TM_S + s * BN, adesc, bdesc, idS, (c | kk) != 0);
                         }
                     }
                 }
-                umma_commit(&sm.s_full[s]);
-                umma_commit(&sm.k_empty[ks_]);
+                if constexpr (PAIR) {
+                    for (uint32_t r2 = 0; r2 < 2; ++r2) {
+                        umma_commit_pair(smem_rank(&sm.s_full[s], r2));
+                        umma_commit_pair(smem_rank(&sm.k_empty[ks_], r2));
+                    }
+                } else {
+                    umma_commit(&sm.s_full[s]);
+                    umma_commit(&sm.k_empty[ks_]);
+                }
             }
         }
     } else if (warp == W_PVMMA) {
         // -------------------------------------------------------------------------------- PV issuer
         // O += P_i V_i as soon as the softmax has written P_i (into the first half of S_i's columns)
-        if (lane == 0 && nb > 0) {
-            constexpr uint32_t idO = umma_idesc_f16(OPF, BM, D, false, true);
+        if (lane == 0 && nb > 0 && issuer_cta) {
+            constexpr uint32_t idO = umma_idesc_f16(OPF, PAIR ? 2 * BM : BM, D, false, true);
             for (int i = 0; i < nb; ++i) {
                 const int s = i % NSTAGE, vs = i % VSTAGE;
                 if (!wait_or_fail(&sm.p_full[s], (i / NSTAGE) & 1, p, failed, DEV_ERR_WAIT_FULL)) break;
@@ -298,10 +379,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int ks = 0; ks < BN / 16; ++ks) {
                     // B = V block, MN-major: 64-dim chunks 8 KiB apart (LBO), 8-cell groups 1 KiB apart (SBO)
                     const uint64_t bdesc = smem_desc_sw128(v_addr + ks * 16 * 128, BN * 128, 1024);
-                    umma_ts(tmem + TM_O, tmem + TM_S + s * BN + ks * 8, bdesc, idO, i > 0 || ks > 0);
+                    if constexpr (PAIR)
+                        umma_ts_pair(tmem + TM_O, tmem + TM_S + s * BN + ks * 8, bdesc, idO, i > 0 || ks > 0);
+                    else
+                        umma_ts(tmem + TM_O, tmem + TM_S + s * BN + ks * 8, bdesc, idO, i > 0 || ks > 0);
                 }
-                umma_commit(&sm.o_done[s]);
-                umma_commit(&sm.v_empty[vs]);
+                if constexpr (PAIR) {
+                    for (uint32_t r2 = 0; r2 < 2; ++r2) {
+                        umma_commit_pair(smem_rank(&sm.o_done[s], r2));
+                        umma_commit_pair(smem_rank(&sm.v_empty[vs], r2));
+                    }
+                } else {
+                    umma_commit(&sm.o_done[s]);
+                    umma_commit(&sm.v_empty[vs]);
+                }
             }
         }
     } else {
@@ -445,7 +536,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.p_full[s]);
+            if (lane == 0) {
+                if constexpr (PAIR)
+                    mbar_arrive_cluster(smem_rank(&sm.p_full[s], 0));
+                else
+                    mbar_arrive(&sm.p_full[s]);
+            }
         }
         // epilogue: O / sum of the groups' l for this row, each group writing its OPT dims. Once the last PV has
         // completed every MMA has, so the K and V rings are free to carry the row sums and the output tile.
@@ -454,7 +550,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = __all_sync(0xffffffffu, ok);
         }
         named_bar_sync(1, SOFTMAX_WARPS * 32);  // every group has waited: no K / V stage is still being read
-        float* xl = reinterpret_cast<float*>(sm.v[1]);  // [group][row]
+        float* xl = reinterpret_cast<float*>(sm.v[R::OUT_V]);  // [group][row]
         xl[grp * BM + r] = l;
         named_bar_sync(1, SOFTMAX_WARPS * 32);
         float lt = 0.0f;
@@ -510,31 +606,56 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
+    // a pair leaves together: CTA 0's MMAs read CTA 1's shared memory and TMEM, and CTA 1 arrives on CTA 0's barriers
+    if constexpr (PAIR) cluster_sync_all();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    if (warp == 0) {
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem, 512);
+        else
+            tmem_dealloc(tmem, 512);
+    }
 }
 
 }  // namespace
 
-size_t fa_prefill_smem_bytes() { return sizeof(Smem); }
+size_t fa_prefill_smem_bytes(bool pair) { return pair ? sizeof(Smem<true>) : sizeof(Smem<false>); }
 
-cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorMap& tmK, const CUtensorMap& tmV,
+cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, bool pair, const CUtensorMap& tmK, const CUtensorMap& tmV,
                               cudaStream_t stream) {
-    static bool attr_done[3][64] = {};
+    static bool attr_done[2][3][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
-    auto kern = fmt == 0 ? fa_prefill_kernel<0> : fmt == 1 ? fa_prefill_kernel<1> : fa_prefill_kernel<2>;
-    const size_t smem = fa_prefill_smem_bytes();
-    if (dev < 0 || dev >= 64 || !attr_done[fmt][dev]) {
+    if (pair && (p.n_head % 2 != 0 || p.gqa % 2 != 0)) return cudaErrorInvalidValue;
+    using Kern = void (*)(CUtensorMap, CUtensorMap, FaPrefillParams);
+    const Kern kern = pair ? (fmt == 0 ? fa_prefill_kernel<0, true> : fmt == 1 ? fa_prefill_kernel<1, true> : fa_prefill_kernel<2, true>)
+                           : (fmt == 0 ? fa_prefill_kernel<0, false> : fmt == 1 ? fa_prefill_kernel<1, false>
+                                                                                : fa_prefill_kernel<2, false>);
+    const size_t smem = fa_prefill_smem_bytes(pair);
+    if (dev < 0 || dev >= 64 || !attr_done[pair][fmt][dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
         if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_done[fmt][dev] = true;
+        if (dev >= 0 && dev < 64) attr_done[pair][fmt][dev] = true;
     }
-    dim3 grid(p.n_qtiles * p.n_head, p.ne3);
-    kern<<<grid, THREADS, smem, stream>>>(tmK, tmV, p);
-    return cudaGetLastError();
+    const dim3 grid(p.n_qtiles * p.n_head, p.ne3);
+    if (!pair) {
+        kern<<<grid, THREADS, smem, stream>>>(tmK, tmV, p);
+        return cudaGetLastError();
+    }
+    // clusters of 2 consecutive CTAs: heads 2 i and 2 i + 1 of the same query tile
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmK, tmV, p);
 }
 
 }  // namespace kb

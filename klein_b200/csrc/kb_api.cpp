@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -50,6 +51,13 @@ DevInfo dev_info() {
 }
 
 uint64_t g_wait_ns = 1000000000ull;  // 1 s budget for every bounded device wait
+// Prefill on CTA pairs (cta_group::2, each CTA holding half of every K / V tile) where the head shape allows it,
+// when KB_PREFILL_PAIR=1 (read per call). Off by default: correct, but 766 against 800 TFLOP/s for one CTA per tile
+// at config[2] (deeper K / V rings moved the limit to the three S / P buffers).
+bool prefill_pair_enabled() {
+    const char* e = std::getenv("KB_PREFILL_PAIR");
+    return e && e[0] == '1';
+}
 
 bool aligned16(size_t x) { return (x & 15) == 0; }
 
@@ -152,7 +160,7 @@ FaPlan plan_fa(const FaShape& s, bool push = false) {
     return pl;
 }
 
-kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
+kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map, int box_cells = kb::FA_TILE) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return KB_ERR_CUDA;
     if (t->type == KB_TYPE_Q8_0 || t->type == KB_TYPE_Q4_0) {
@@ -171,7 +179,7 @@ kb_status encode_kv_map(const kb_tensor* t, CUtensorMap* map) {
     // dims (innermost first): head dim, KV head, cell, batch; box = 64 dims x 1 head x 64 cells
     const cuuint64_t dims[4] = {(cuuint64_t) t->ne[0], (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[3]};
     const cuuint64_t strides[3] = {(cuuint64_t) t->nb[2], (cuuint64_t) t->nb[1], (cuuint64_t) t->nb[3]};
-    const cuuint32_t box[4] = {64, 1, (cuuint32_t) kb::FA_TILE, 1};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t) box_cells, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUtensorMapDataType dt = t->type == KB_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = enc(map, dt, 4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -255,6 +263,8 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         pp.q_nb1 = (int64_t) q->nb[1], pp.q_nb2 = (int64_t) q->nb[2], pp.q_nb3 = (int64_t) q->nb[3];
         pp.n_q = s.n_q, pp.n_head = s.H, pp.n_head_kv = s.H_kv, pp.gqa = s.gqa, pp.ne3 = s.ne3, pp.rk3 = s.ne3 / s.ne3k;
         pp.n_qtiles = (s.n_q + 127) / 128;
+        // CTA pairs share each MMA when the heads of a GQA group pair up (klein's 24 / 4 heads do)
+        const bool pair = prefill_pair_enabled() && s.H % 2 == 0 && s.gqa % 2 == 0;
         pp.n_kv = s.n_kv;
         if (mask) {
             pp.mask = static_cast<const char*>(mask->data);
@@ -309,13 +319,13 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
                     if (kb::launch_kv_widen(wp, s.kv_type, cs) != cudaSuccess) return KB_ERR_CUDA;
                 }
             }
-            if ((st = encode_kv_map(&fv[0], &tK)) != KB_OK) return st;
+            if ((st = encode_kv_map(&fv[0], &tK, pair ? kb::FA_PAIR_KROWS : kb::FA_TILE)) != KB_OK) return st;
             if ((st = encode_kv_map(&fv[1], &tV)) != KB_OK) return st;
-            return kb::launch_fa_prefill(pp, 2, tK, tV, cs) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
+            return kb::launch_fa_prefill(pp, 2, pair, tK, tV, cs) == cudaSuccess ? KB_OK : KB_ERR_CUDA;
         }
-        if ((st = encode_kv_map(k, &tK)) != KB_OK) return st;
+        if ((st = encode_kv_map(k, &tK, pair ? kb::FA_PAIR_KROWS : kb::FA_TILE)) != KB_OK) return st;
         if ((st = encode_kv_map(v, &tV)) != KB_OK) return st;
-        cudaError_t e = kb::launch_fa_prefill(pp, s.kv_type == KB_TYPE_BF16 ? 1 : 0, tK, tV, cs);
+        cudaError_t e = kb::launch_fa_prefill(pp, s.kv_type == KB_TYPE_BF16 ? 1 : 0, pair, tK, tV, cs);
         return e == cudaSuccess ? KB_OK : KB_ERR_CUDA;
     }
     if (s.kv_type == KB_TYPE_BF16) return KB_ERR_UNSUPPORTED;  // bf16 caches: prefill shapes only

@@ -95,10 +95,12 @@ struct FaPrefillParams {
     uint64_t wait_ns;
 };
 
-size_t fa_prefill_smem_bytes();
-// fmt: 0 = f16 K/V, 1 = bf16 K/V, 2 = f16 K/V widened from q8_0 / q4_0 (Q rounded to q8_0 first)
-cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, const CUtensorMap& tmK, const CUtensorMap& tmV,
+size_t fa_prefill_smem_bytes(bool pair);
+// fmt: 0 = f16 K/V, 1 = bf16 K/V, 2 = f16 K/V widened from q8_0 / q4_0 (Q rounded to q8_0 first). pair: clusters of 2
+// CTAs sharing each MMA (n_head and gqa even; tmK's box 32 cells instead of 64)
+cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, bool pair, const CUtensorMap& tmK, const CUtensorMap& tmV,
                               cudaStream_t stream);
+constexpr int FA_PAIR_KROWS = 32;  // cells of a K tile each CTA of a pair loads
 
 // Widening of cells [c0, c1) of a q8_0 / q4_0 cache view [D = 256, n_kv, H_kv, ne3] (kv_widen.cu) into a contiguous
 // f16 copy [ne3][n_kv][H_kv][256] (cells outside [c0, c1) are not written).

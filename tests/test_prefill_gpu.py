@@ -74,3 +74,21 @@ def test_prefill_dense_mask_matches_analytic(kb, cuda):
 def test_prefill_config2_bf16_4096(kb, cuda):
     """config[2]: 4,096-token causal prefill, 24 Q / 4 KV heads, D 256, bf16 Q/K/V."""
     case(kb, cuda, kb.BF16, 4096, 4096, 0, seed=2)
+
+
+@pytest.fixture
+def pair_mode(monkeypatch):
+    """The CTA-pair form of the prefill kernel (cta_group::2: two heads of a GQA group on one query tile, each CTA
+    loading half of every K / V tile), selected per call by KB_PREFILL_PAIR=1."""
+    monkeypatch.setenv("KB_PREFILL_PAIR", "1")
+
+
+@pytest.mark.parametrize("kvt_name", ["F16", "BF16"])
+@pytest.mark.parametrize("n_q,n_kv,pos0", [(128, 128, 0), (300, 300, 0), (256, 1256, 1000), (640, 700, 60)])
+def test_prefill_pairs(kb, cuda, pair_mode, kvt_name, n_q, n_kv, pos0):
+    case(kb, cuda, getattr(kb, kvt_name), n_q, n_kv, pos0, seed=11)
+
+
+def test_prefill_pairs_dense_mask_and_config2(kb, cuda, pair_mode):
+    case(kb, cuda, kb.F16, 256, 700, 444, dense=True)
+    case(kb, cuda, kb.BF16, 4096, 4096, 0)

@@ -84,9 +84,12 @@ def test_prefill_quant_chunk_2048(kb, cuda, name, gt):
     check_attention(gpu[rows], exact_rows(O.q_round_q8_0(q), kd, vd, rows, pos0))
 
 
+@pytest.mark.parametrize("pair", ["0", "1"], ids=["one_cta", "cta_pairs"])
 @pytest.mark.parametrize("n_q,n_kv,pos0,kv_lo", [(300, 1300, 1000, 37), (128, 4000, 3872, 0), (640, 700, 60, 0)])
-def test_prefill_quant_ragged(kb, cuda, n_q, n_kv, pos0, kv_lo):
-    """ragged tiles, a kv_lo window that starts inside a 64-cell block, and cells past the last query's position"""
+def test_prefill_quant_ragged(kb, cuda, monkeypatch, pair, n_q, n_kv, pos0, kv_lo):
+    """ragged tiles, a kv_lo window that starts inside a 64-cell block, and cells past the last query's position; on
+    one CTA per tile and on CTA pairs (KB_PREFILL_PAIR=1)"""
+    monkeypatch.setenv("KB_PREFILL_PAIR", pair)
     q, kc, vc, kd, vd = O.make_fa_inputs(700 + n_q + n_kv, n_q, n_kv, kv_type=O.GGML_Q8_0)
     gpu = run(kb, cuda, q, kc, vc, kb.Q8_0, causal=True, pos0=pos0, kv_lo=kv_lo)
     check_attention(gpu, exact_rows(O.q_round_q8_0(q), kd, vd, np.arange(n_q), pos0, kv_lo=kv_lo))
