@@ -1053,12 +1053,20 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
                                        f2pack(nr.z, nr.w)),
                                  x[r + 2], x[r + 3]);
                     }
-                } else if (!p.mask && !p.has_softcap && p.ring == 0) {
-                    // causal bounds only: row r sees cells [kv_lo, pos0 + qi_r] below the split's end
-                    const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
+                } else if (!p.mask && !p.has_softcap) {
+                    // causal bounds only: row r sees cells [kv_lo, pos0 + qi_r] below the split's end; with the MTP
+                    // head's ring, slot `key` holds cell end - ((end - key) mod ring) (one mapping per slot, not per
+                    // row) and row r also needs that cell inside its window (> pos0 + qi_r - ring)
+                    int64_t cell = key;
+                    if (p.causal && p.ring > 0) {
+                        const int64_t end = p.pos0 + p.n_q - 1;
+                        cell = end - (((end - key) % p.ring) + p.ring) % p.ring;
+                    }
+                    const bool in = key < key_end && (!p.causal || cell >= p.kv_lo);
 #pragma unroll
                     for (int r = 0; r < N; ++r) {
-                        const bool vis = r < rows && in && (!p.causal || key <= p.pos0 + sm.row_qi[r]);
+                        const int64_t pos = p.pos0 + sm.row_qi[r];
+                        const bool vis = r < rows && in && (!p.causal || (cell <= pos && (p.ring == 0 || cell > pos - p.ring)));
                         x[r] = vis ? fmaf(__uint_as_float(sv[r]), scl, with_ref ? sm.nref[r] : 0.0f) : -INFINITY;
                     }
                 } else {
