@@ -516,6 +516,7 @@ struct Smem {
     float alpha[N];                 // rescale factors of the last raise
     int row_qi[N], row_h[N];
     float row_slope[N];
+    const __half* row_mask[N];      // each row's mask row (dense mask), or null
     uint64_t kfull[KRAW], kempty[KRAW], vfull[VRAW], vempty[VRAW];
     uint64_t k_full[2], k_free[2], s_full[2], p_full[2], p_free[2], v_full[2], v_free[2], o_done, s_done;
     uint32_t tmem_base;
@@ -725,6 +726,9 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
             sm.row_qi[r] = qi;
             sm.row_h[r] = h;
             sm.row_slope[r] = slope_of(p, h);
+            sm.row_mask[r] = p.mask ? reinterpret_cast<const __half*>(p.mask + qi * p.m_nb1 + (h % p.m_ne2) * p.m_nb2 +
+                                                                        (b % p.m_ne3) * p.m_nb3)
+                                    : nullptr;
         }
         fence_proxy_async_smem();
         named_bar_sync(2, THREADS - 64);
@@ -1020,6 +1024,17 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
         const int c = 32 * warp + lane;  // cell of the block = TMEM lane
         const uint32_t lane_addr = tmem + ((uint32_t) (32 * warp) << 16);
         const float scl = p.scale_log2;
+        // a dense mask broadcast over the heads whose rows for this chunk are <= 4 consecutive queries: their row
+        // pointers, so that each cell loads those few values once per block (not one per row)
+        const int q_first = sm.row_qi[0], q_last = sm.row_qi[max(rows - 1, 0)];
+        const int dm_n = p.mask && p.m_ne2 == 1 && q_last - q_first < 4 ? q_last - q_first + 1 : 0;
+        const int dm_q0 = q_first;
+        const __half* dm_row[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            dm_row[u] = u < dm_n ? reinterpret_cast<const __half*>(p.mask + (int64_t) (q_first + u) * p.m_nb1 +
+                                                                   (b % p.m_ne3) * p.m_nb3)
+                                 : nullptr;
         const int64_t min_pos = p.pos0 + sm.row_qi[0];
         float l[N];
 #pragma unroll
@@ -1068,6 +1083,63 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
                         const int64_t pos = p.pos0 + sm.row_qi[r];
                         const bool vis = r < rows && in && (!p.causal || (cell <= pos && (p.ring == 0 || cell > pos - p.ring)));
                         x[r] = vis ? fmaf(__uint_as_float(sv[r]), scl, with_ref ? sm.nref[r] : 0.0f) : -INFINITY;
+                    }
+                } else if (!p.has_softcap && p.ring == 0 && dm_n > 0) {
+                    // a dense mask broadcast over the heads (klein's graph passes one): its values for this cell in
+                    // the chunk's <= 4 query rows, 0 almost everywhere (then only the scale applies), plus the causal
+                    // bounds when given; masked_score's arithmetic
+                    const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
+                    float mq[4];
+                    bool zero = true;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        mq[u] = (u < dm_n && in) ? __half2float(dm_row[u][key]) : 0.0f;
+                        zero = zero && mq[u] == 0.0f;
+                    }
+                    if (zero && in && with_ref && (!p.causal || key <= min_pos)) {
+                        // visible to every row with nothing added: the unmasked form (rows past the chunk's end have
+                        // a reference of -inf)
+                        const uint64_t sc2 = f2pack(scl, scl);
+#pragma unroll
+                        for (int r = 0; r < N; r += 4) {
+                            const float4 nr = *reinterpret_cast<const float4*>(sm.nref + r);
+                            f2unpack(ffma2(f2pack(__uint_as_float(sv[r]), __uint_as_float(sv[r + 1])), sc2, f2pack(nr.x, nr.y)),
+                                     x[r], x[r + 1]);
+                            f2unpack(ffma2(f2pack(__uint_as_float(sv[r + 2]), __uint_as_float(sv[r + 3])), sc2,
+                                           f2pack(nr.z, nr.w)),
+                                     x[r + 2], x[r + 3]);
+                        }
+                        return;
+                    }
+#pragma unroll
+                    for (int r = 0; r < N; ++r) {
+                        float v = -INFINITY;
+                        if (r < rows && in && (!p.causal || key <= p.pos0 + sm.row_qi[r])) {
+                            v = __uint_as_float(sv[r]) * scl;
+                            if (!zero) {
+                                const int u = sm.row_qi[r] - dm_q0;
+                                const float m = u == 0 ? mq[0] : u == 1 ? mq[1] : u == 2 ? mq[2] : mq[3];
+                                const float mv = sm.row_slope[r] * m;
+                                if (mv == -INFINITY) v = -INFINITY;
+                                else v += mv * LOG2E;
+                            }
+                        }
+                        x[r] = (v == -INFINITY || !with_ref) ? v : v + sm.nref[r];
+                    }
+                } else if (!p.has_softcap && p.ring == 0) {
+                    // a dense mask of another shape: one f16 load per (cell, row) through the row's mask pointer
+                    const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
+#pragma unroll
+                    for (int r = 0; r < N; ++r) {
+                        float v = -INFINITY;
+                        if (r < rows && in && (!p.causal || key <= p.pos0 + sm.row_qi[r])) {
+                            const float mv = sm.row_slope[r] * __half2float(sm.row_mask[r][key]);
+                            if (mv != -INFINITY) {
+                                v = __uint_as_float(sv[r]) * scl;
+                                v += mv * LOG2E;
+                            }
+                        }
+                        x[r] = (v == -INFINITY || !with_ref) ? v : v + sm.nref[r];
                     }
                 } else {
                     const bool in = key < key_end;
