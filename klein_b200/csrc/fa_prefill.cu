@@ -161,6 +161,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         c_hi = min(c_hi, p.pos0 + q0 + BM);
         c_lo = max((int64_t) 0, p.kv_lo) / BN * BN;
     }
+    if (p.mask_cls) {
+        // a classified mask: leading and trailing blocks hidden from the whole tile are not visited
+        const uint8_t* cls = p.mask_cls + (int64_t) tile * p.cls_ld;
+        int first = -1, last = -1;
+        for (int bi = (int) (c_lo / BN); bi < p.cls_ld && (int64_t) bi * BN < c_hi; ++bi)
+            if (cls[bi] != FA_MASK_HIDDEN) {
+                if (first < 0) first = bi;
+                last = bi;
+            }
+        if (first < 0) {
+            c_hi = c_lo;
+        } else {
+            c_lo = max(c_lo, (int64_t) first * BN);
+            c_hi = min(c_hi, (int64_t) (last + 1) * BN);
+        }
+    }
     const int nb = c_hi > c_lo ? (int) ((c_hi - c_lo + BN - 1) / BN) : 0;
     // the heads of a GQA group walk the shared K/V blocks from different starting points, so that they do not
     // all request the same L2 lines at once; block order does not change the result of the online softmax
@@ -421,7 +437,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             float bm = -INFINITY;
             const int64_t blk0 = block_cell(j);
             const int64_t cell0 = blk0 + grp * CPT;
-            const bool plain = !mrow && !p.has_softcap && blk0 + BN <= p.n_kv &&
+            // a block the mask leaves untouched (classified all 0) is computed as an unmasked one
+            const bool mask_free = !mrow || (p.mask_cls && p.mask_cls[(int64_t) tile * p.cls_ld + blk0 / BN] == FA_MASK_ZERO);
+            const bool plain = mask_free && !p.has_softcap && blk0 + BN <= p.n_kv &&
                                (!p.causal || (blk0 >= p.kv_lo && blk0 + BN - 1 <= row_pos)) && q0 + BM <= p.n_q;
             // without a mask tensor or softcap the visible cells of a row form one range [e_lo, e_hi) of the block
             const bool analytic = !mrow && !p.has_softcap;
@@ -451,6 +469,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < CPT; ++e) {
                         const float sc = (e >= e_lo && e < e_hi) ? __uint_as_float(sv[e]) * scl : -INFINITY;
+                        sv[e] = __float_as_uint(sc);
+                        bm = fmaxf(bm, sc);
+                    }
+                } else if (mrow && !p.has_softcap && cell0 + CPT <= p.n_kv && qi < p.n_q &&
+                           (reinterpret_cast<uintptr_t>(mrow + cell0) & 15) == 0) {
+                    // the row's CPT mask values in 16-byte loads, then masked_score's arithmetic per cell
+                    uint4 mw[CPT / 8];
+#pragma unroll
+                    for (int u = 0; u < CPT / 8; ++u) mw[u] = reinterpret_cast<const uint4*>(mrow + cell0)[u];
+                    const __half* mh = reinterpret_cast<const __half*>(mw);
+#pragma unroll
+                    for (int e = 0; e < CPT; ++e) {
+                        const int64_t key = cell0 + e;
+                        float sc = -INFINITY;
+                        if (!p.causal || (key >= p.kv_lo && key <= p.pos0 + qi)) {
+                            const float mv = slope * __half2float(mh[e]);
+                            if (mv != -INFINITY) sc = __uint_as_float(sv[e]) * scl + mv * LOG2E;
+                        }
                         sv[e] = __float_as_uint(sc);
                         bm = fmaxf(bm, sc);
                     }
@@ -618,6 +654,77 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 }  // namespace
+
+namespace {
+
+// One CTA of 128 threads per (128-query tile, 64-cell block), 128 bytes of each of the tile's rows. Aligned rows:
+// thread t reads 16-byte unit t % 8 of rows t / 8 + 16 i (i < 8; a warp instruction covers 4 whole 128-byte row
+// pieces, all 8 loads in flight); otherwise warp w reads rows 32 w .. + 31 in 4-byte or 2-byte pieces. Cells past
+// n_kv count as -inf, rows past n_q are ignored.
+__global__ void __launch_bounds__(128) fa_mask_classify_kernel(const char* mask, int64_t m_nb1, int n_q, int64_t n_kv,
+                                                               int n_blocks, uint8_t* out) {
+    const int blk = blockIdx.x, tile = blockIdx.y;
+    const int64_t c0 = (int64_t) blk * BN;
+    bool nonzero = false, visible = false;
+    auto look = [&](uint16_t a) {
+        nonzero = nonzero || (a & 0x7FFFu) != 0;  // +-0 is zero
+        visible = visible || a != 0xFC00u;        // anything but -inf
+    };
+    if (((reinterpret_cast<uintptr_t>(mask) | (uintptr_t) m_nb1) & 15) == 0 && c0 + BN <= n_kv) {
+        const int u = threadIdx.x & 7;
+        uint4 w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int qi = tile * BM + (threadIdx.x >> 3) + 16 * i;
+            w[i] = qi < n_q ? *reinterpret_cast<const uint4*>(mask + (int64_t) qi * m_nb1 + (c0 + 8 * u) * 2)
+                            : make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t x[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int qi = tile * BM + (threadIdx.x >> 3) + 16 * i;
+                if (qi < n_q) {
+                    look((uint16_t) (x[e] & 0xFFFFu));
+                    look((uint16_t) (x[e] >> 16));
+                }
+            }
+        }
+    } else {
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        const int64_t cell = c0 + 2 * l;
+        const bool pairs = ((reinterpret_cast<uintptr_t>(mask) | (uintptr_t) m_nb1) & 3) == 0 && cell + 1 < n_kv;
+#pragma unroll 8
+        for (int rr = 0; rr < 32; ++rr) {
+            const int qi = tile * BM + w * 32 + rr;
+            if (qi < n_q) {
+                const uint16_t* row = reinterpret_cast<const uint16_t*>(mask + (int64_t) qi * m_nb1);
+                uint16_t a, b;
+                if (pairs) {
+                    const uint32_t ab = *reinterpret_cast<const uint32_t*>(row + cell);
+                    a = (uint16_t) (ab & 0xFFFFu), b = (uint16_t) (ab >> 16);
+                } else {
+                    a = cell < n_kv ? row[cell] : (uint16_t) 0xFC00u;
+                    b = cell + 1 < n_kv ? row[cell + 1] : (uint16_t) 0xFC00u;
+                }
+                look(a);
+                look(b);
+            }
+        }
+    }
+    const int nz = __syncthreads_or(nonzero), vis = __syncthreads_or(visible);
+    if (threadIdx.x == 0) out[(int64_t) tile * n_blocks + blk] = !vis ? FA_MASK_HIDDEN : !nz ? FA_MASK_ZERO : FA_MASK_MIXED;
+}
+
+}  // namespace
+
+cudaError_t launch_fa_mask_classify(const char* mask, int64_t m_nb1, int n_q, int64_t n_kv, int n_blocks, uint8_t* out,
+                                    cudaStream_t stream) {
+    if (n_q <= 0 || n_blocks <= 0) return cudaSuccess;
+    fa_mask_classify_kernel<<<dim3(n_blocks, (n_q + BM - 1) / BM), 128, 0, stream>>>(mask, m_nb1, n_q, n_kv, n_blocks, out);
+    return cudaGetLastError();
+}
 
 size_t fa_prefill_smem_bytes(bool pair) { return pair ? sizeof(Smem<true>) : sizeof(Smem<false>); }
 

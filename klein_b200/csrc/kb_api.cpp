@@ -79,6 +79,12 @@ constexpr int PREFILL_MIN_Q = 128;
 bool prefill_shape(const FaShape& s, const kb_fa_params* prm, bool partial) {
     return !partial && s.n_q >= PREFILL_MIN_Q && !(prm && prm->causal && prm->ring > 0);
 }
+// the class table of a dense mask for the prefill kernel: one byte per (128-query tile, 64-cell block)
+size_t mask_cls_bytes(const FaShape& s) {
+    const size_t n = (size_t) ((s.n_q + 127) / 128) * (size_t) ((s.n_kv + 63) / 64);
+    return (n + 255) / 256 * 256;
+}
+
 bool use_prefill(const FaShape& s, const kb_fa_params* prm, bool partial) {
     return prefill_shape(s, prm, partial) && (s.kv_type == KB_TYPE_F16 || s.kv_type == KB_TYPE_BF16);
 }
@@ -200,7 +206,8 @@ size_t kb_flash_attn_ext_scratch_bytes(const kb_tensor* q, const kb_tensor* k, c
     // the streaming kernel's split partials: what kb_flash_attn_ext_partial needs for any shape (the f16 / bf16
     // prefill kernel takes none), plus, for prefill shapes over a q8_0 / q4_0 cache, the two f16 views
     const size_t stream_need = plan_fa(s).scratch;
-    if (prefill_quant_shape(s, params, false)) return std::max(2 * widen_view_bytes(s), stream_need);
+    if (prefill_quant_shape(s, params, false)) return std::max(2 * widen_view_bytes(s) + mask_cls_bytes(s), stream_need);
+    if (use_prefill(s, params, false)) return std::max(mask_cls_bytes(s), stream_need);
     return stream_need;
 }
 
@@ -292,6 +299,18 @@ kb_status fa_impl(const kb_tensor* q, const kb_tensor* k, const kb_tensor* v, co
         pp.wait_ns = g_wait_ns;
         CUtensorMap tK, tV;
         cudaStream_t cs = static_cast<cudaStream_t>(stream);
+        // a dense mask broadcast over the heads (klein's): classify its (query tile, 64-cell block) pieces first, so
+        // that the kernel skips the hidden leading / trailing blocks and computes untouched blocks as unmasked ones
+        const size_t cls_off = quant_prefill ? 2 * widen_view_bytes(s) : 0;
+        if (mask && pp.m_ne2 == 1 && (pp.m_ne3 == 1 || s.ne3 == 1) && scratch &&
+            scratch_bytes >= cls_off + mask_cls_bytes(s)) {
+            uint8_t* cls = static_cast<uint8_t*>(scratch) + cls_off;
+            const int n_blocks = (int) ((s.n_kv + 63) / 64);
+            if (kb::launch_fa_mask_classify(pp.mask, pp.m_nb1, s.n_q, s.n_kv, n_blocks, cls, cs) != cudaSuccess)
+                return KB_ERR_CUDA;
+            pp.mask_cls = cls;
+            pp.cls_ld = n_blocks;
+        }
         if (quant_prefill) {
             // widen the cells the query tiles read (whole 64-cell blocks from kv_lo's block up to the last tile's
             // causal bound; every cell without causal bounds) into f16 views [ne3k][n_kv][H_kv][256] in the scratch

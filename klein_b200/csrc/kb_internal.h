@@ -91,11 +91,20 @@ struct FaPrefillParams {
     int64_t d_nb1, d_nb2, d_nb3;
     const char* gate;                // null, or f32 [D, H, n_q, ne3]: the output is o * sigmoid(gate)
     int64_t g_nb1, g_nb2, g_nb3;
+    // a dense mask broadcast over the heads, classified per (128-query tile, 64-cell block) by
+    // launch_fa_mask_classify: FA_MASK_MIXED, FA_MASK_ZERO (every value 0) or FA_MASK_HIDDEN (every value -inf); null
+    // when not classified
+    const uint8_t* mask_cls;
+    int cls_ld;                      // blocks per tile row of the table
     int* err;
     uint64_t wait_ns;
 };
+constexpr uint8_t FA_MASK_MIXED = 0, FA_MASK_ZERO = 1, FA_MASK_HIDDEN = 2;
 
 size_t fa_prefill_smem_bytes(bool pair);
+// classes of mask rows [0, n_q) (row stride m_nb1) x cells [0, n_kv) into out[tile * n_blocks + block]
+cudaError_t launch_fa_mask_classify(const char* mask, int64_t m_nb1, int n_q, int64_t n_kv, int n_blocks, uint8_t* out,
+                                    cudaStream_t stream);
 // fmt: 0 = f16 K/V, 1 = bf16 K/V, 2 = f16 K/V widened from q8_0 / q4_0 (Q rounded to q8_0 first). pair: clusters of 2
 // CTAs sharing each MMA (n_head and gqa even; tmK's box 32 cells instead of 64)
 cudaError_t launch_fa_prefill(const FaPrefillParams& p, int fmt, bool pair, const CUtensorMap& tmK, const CUtensorMap& tmV,

@@ -92,3 +92,25 @@ def test_prefill_pairs(kb, cuda, pair_mode, kvt_name, n_q, n_kv, pos0):
 def test_prefill_pairs_dense_mask_and_config2(kb, cuda, pair_mode):
     case(kb, cuda, kb.F16, 256, 700, 444, dense=True)
     case(kb, cuda, kb.BF16, 4096, 4096, 0)
+
+
+@pytest.mark.parametrize("kvt_name", ["F16", "BF16"])
+def test_prefill_mask_classes(kb, cuda, kvt_name):
+    """A dense mask whose 64-cell blocks are, per 128-query tile, all 0 (computed as unmasked), all -inf (the leading
+    and trailing ones skipped, those in between computed), or mixed, plus finite nonzero values: every class of the
+    mask classification against the exact f64 attention with the same mask."""
+    kvt = getattr(kb, kvt_name)
+    n_q, n_kv, H_kv = 384, 1000, 4
+    ggml_t = O.GGML_F16 if kvt == kb.F16 else O.GGML_BF16
+    q, kc, vc, kd, vd = O.make_fa_inputs(4242, n_q, n_kv, H_kv=H_kv, kv_type=ggml_t)
+    rng = np.random.default_rng(7)
+    mask = np.zeros((n_q, n_kv), dtype=np.float32)
+    mask[:, :128] = -np.inf                      # hidden leading blocks (every tile)
+    mask[:128, 640:] = -np.inf                   # hidden trailing blocks of the first tile
+    mask[128:256, 320:384] = -np.inf             # a hidden block between visible ones
+    mask[256:, 448:512] = rng.choice([0.0, -np.inf, -0.5], size=(128, 64))  # mixed values
+    mask[:, 900:] = -rng.random((n_q, 100)).astype(np.float32)  # finite, nonzero
+    mask = mask.astype(np.float16).astype(np.float32)
+    gpu = run(kb, cuda, q, kc, vc, kvt, H_kv, mask=mask)
+    qr = O.q_round_f16(q) if kvt == kb.F16 else O.q_round_bf16(q)
+    check_attention(gpu, exact_np(qr, kd, vd, mask), None)
