@@ -476,6 +476,70 @@ def bench_gdn_layer(kb, torch, dev, steps, warmup):
     return res
 
 
+def bench_dense_mask(kb, torch, dev, steps, warmup):
+    """The two attention kernels with klein's dense f16 mask (engine.cpp:308-326, what klein's graph passes through
+    ggml) instead of the analytic bounds: the 4-token verify step over 262,144 f16 cells (4 layers, inputs > L2) and a
+    2,048-token bf16 prompt chunk over 4,096 cells, each beside the same call with analytic bounds."""
+    def causal_mask(n_q, n_kv, pos0):
+        # klein's mask for a prompt chunk at positions pos0 .. pos0 + n_q - 1 (engine.cpp:308-326): 0 where the cell is
+        # at or before the row's position, -inf after it
+        c = torch.arange(n_kv, device=dev)[None, :]
+        p = pos0 + torch.arange(n_q, device=dev)[:, None]
+        return torch.where(c <= p, 0.0, float("-inf")).half()
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17)
+    pk, _ = measured_peaks()
+
+    def time_calls(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / steps
+
+    res = {}
+    n_kv, n_q, n_layers = N_KV, N_Q, 4
+    layers = []
+    for _ in range(n_layers):
+        kc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
+        vc = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).half()
+        layers.append((kc, vc, kb.kv_cache_view(kc, kb.F16, H_KV, D), kb.kv_cache_view(vc, kb.F16, H_KV, D)))
+    q = torch.randn(1, n_q, H, D, device=dev, generator=gen)
+    mask = causal_mask(n_q, n_kv, n_kv - n_q)
+    t = {}
+    for name, kw in (("analytic", dict(causal=True, pos0=n_kv - n_q)), ("dense", dict(mask=mask))):
+        t[name] = time_calls(lambda: [kb.flash_attn_ext(q, l[2], l[3], SCALE, **kw) for l in layers]) / n_layers
+    gbs = 2 * n_kv * H_KV * D * 2 / (t["dense"] * 1e-6) / 1e9
+    res["verify_f16_dense_mask"] = {
+        "value": round(t["dense"], 2), "unit": "us/layer", "analytic_bounds_us": round(t["analytic"], 2),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / pk["hbm_gbs"], 4)}}
+    del layers, mask
+    torch.cuda.empty_cache()
+    T, n_kv = 2048, 4096
+    q = torch.randn(1, T, H, D, device=dev, generator=gen).bfloat16().float()
+    k = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).bfloat16()
+    v = torch.randn(n_kv, H_KV * D, device=dev, generator=gen).bfloat16()
+    kv, vv = kb.kv_cache_view(k, kb.BF16, H_KV, D), kb.kv_cache_view(v, kb.BF16, H_KV, D)
+    mask = causal_mask(T, n_kv, n_kv - T)
+    t = {}
+    for name, kw in (("analytic", dict(causal=True, pos0=n_kv - T)), ("dense", dict(mask=mask))):
+        t[name] = time_calls(lambda: kb.flash_attn_ext(q, kv, vv, SCALE, **kw))
+    flops = 4 * D * H * (T * (T + 1) // 2 + T * (n_kv - T))
+    tf = flops / (t["dense"] * 1e-6) / 1e12
+    res["prefill_bf16_2048_dense_mask"] = {
+        "value": round(tf, 1), "unit": "TFLOP/s", "us": round(t["dense"], 1), "analytic_bounds_us": round(t["analytic"], 1),
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tf / pk["bf16_tflops"], 4)}}
+    return res
+
+
 def bench_io_ops(kb, torch, dev, steps, warmup):
     """The ops around the two attention kinds at config[2]'s 4,096-token prefill (qwen35 shapes, f16 cache):
     kb_attn_prologue (Q/gate split, RMS norms, M-RoPE, K/V cache writes), kb_gdn_input (conv, SiLU, L2 norms, gates,
@@ -1365,6 +1429,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                                        kv="q8_0", T=2048, n_kv=4096)
         secondary["gdn_verify"] = bench_gdn(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary.update(bench_gdn_layer(kb, torch, dev, max(3, args.steps // 20), args.warmup))
+        secondary.update(bench_dense_mask(kb, torch, dev, max(3, args.steps // 20), args.warmup))
         secondary["gdn_prefill_4096"] = bench_gdn_prefill(kb, torch, dev, max(3, args.steps // 20), args.warmup)
         secondary["io_ops"] = bench_io_ops(kb, torch, dev, max(20, args.steps // 2), args.warmup)
         if not args.no_stack:
