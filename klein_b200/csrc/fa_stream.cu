@@ -1024,17 +1024,11 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
         const int c = 32 * warp + lane;  // cell of the block = TMEM lane
         const uint32_t lane_addr = tmem + ((uint32_t) (32 * warp) << 16);
         const float scl = p.scale_log2;
-        // a dense mask broadcast over the heads whose rows for this chunk are <= 4 consecutive queries: their row
-        // pointers, so that each cell loads those few values once per block (not one per row)
+        // a dense mask broadcast over the heads whose rows for this chunk are <= 4 consecutive queries: each cell
+        // loads those few values once per block (not one per row); the row addresses are formed in the branch that
+        // reads them, so that they hold no registers across the loop
         const int q_first = sm.row_qi[0], q_last = sm.row_qi[max(rows - 1, 0)];
         const int dm_n = p.mask && p.m_ne2 == 1 && q_last - q_first < 4 ? q_last - q_first + 1 : 0;
-        const int dm_q0 = q_first;
-        const __half* dm_row[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-            dm_row[u] = u < dm_n ? reinterpret_cast<const __half*>(p.mask + (int64_t) (q_first + u) * p.m_nb1 +
-                                                                   (b % p.m_ne3) * p.m_nb3)
-                                 : nullptr;
         const int64_t min_pos = p.pos0 + sm.row_qi[0];
         float l[N];
 #pragma unroll
@@ -1089,11 +1083,14 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
                     // the chunk's <= 4 query rows, 0 almost everywhere (then only the scale applies), plus the causal
                     // bounds when given; masked_score's arithmetic
                     const bool in = key < key_end && (!p.causal || key >= p.kv_lo);
+                    const int dm_q0 = sm.row_qi[0];
+                    const char* dm_cell = p.mask + (int64_t) dm_q0 * p.m_nb1 + (b % p.m_ne3) * p.m_nb3 + key * 2;
                     float mq[4];
                     bool zero = true;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        mq[u] = (u < dm_n && in) ? __half2float(dm_row[u][key]) : 0.0f;
+                        mq[u] = (u < dm_n && in) ? __half2float(*reinterpret_cast<const __half*>(dm_cell + u * p.m_nb1))
+                                                 : 0.0f;
                         zero = zero && mq[u] == 0.0f;
                     }
                     if (zero && in && with_ref && (!p.causal || key <= min_pos)) {
