@@ -734,6 +734,15 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
         named_bar_sync(2, THREADS - 64);
     }
 
+    // Registers (quantised caches): the producer / issuer warpgroup (warps 12-15) gives 48 of its 128 per thread to
+    // the three compute warpgroups (softmax, K and V dequantisation: 144 each); 3 x 144 + 80 = 4 x 128, the launch's
+    // total. Both calls are made once per warp, by all 32 lanes together (every warp is converged after the Q-staging
+    // barriers), and the counts are kept to the end: the common tail runs within the smaller share.
+    if (warp >= W_KTMA) {
+    if constexpr (Q8) {
+        __syncwarp();
+        reg_lower<80>();
+    }
     if (warp == W_KTMA || warp == W_VTMA) {
         // ------------------------------------------------------------------------ TMA producers
         const bool is_v = warp == W_VTMA;
@@ -838,7 +847,13 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
             }
             umma_commit(&sm.o_done);  // on every path
         }
-    } else if (Q8 && warp >= W_KDQ && warp < W_VDQ) {
+    }
+    } else {
+    if constexpr (Q8) {
+        __syncwarp();
+        reg_raise<144>();
+    }
+    if (Q8 && warp >= W_KDQ && warp < W_VDQ) {
         // ------------------------------------------------------------------------ K dequantisation -> TMEM
         const int i = warp - W_KDQ;
         const int half = i >> 1, cell = 32 * (i & 1) + lane;
@@ -1281,6 +1296,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
                 }
             }
         }
+    }
     }
     // every MMA has completed before the columns are released (o_done is committed on every path)
     if (warp == W_SMMA) {

@@ -22,6 +22,22 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------ registers
+
+// Moves registers between the warpgroups of a CTA (every warp of a warpgroup executes the same call): lower gives
+// back all above R per thread, raise waits until the CTA's pool (threads x registers at launch) holds enough. The
+// counts of all warpgroups must add up to the launch's total, or a raise waits for ever.
+template <uint32_t R>
+__device__ __forceinline__ void reg_lower() {
+    static_assert(R % 8 == 0 && R >= 24 && R <= 256, "setmaxnreg counts are multiples of 8 in [24, 256]");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R) : "memory");
+}
+template <uint32_t R>
+__device__ __forceinline__ void reg_raise() {
+    static_assert(R % 8 == 0 && R >= 24 && R <= 256, "setmaxnreg counts are multiples of 8 in [24, 256]");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
