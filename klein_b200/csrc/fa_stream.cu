@@ -497,6 +497,10 @@ struct Roles {
     static constexpr int KTMA = Q8 ? 12 : 4, VTMA = Q8 ? 13 : 5, SMMA = Q8 ? 14 : 6, PVMMA = Q8 ? 15 : 7;
     static constexpr int THREADS = (Q8 ? 16 : 8) * 32;
     static constexpr uint32_t TMEM_COLS = Q8 ? 512 : 128;
+    // quantised: registers per thread at launch (the whole register file over THREADS), and the shares the producer /
+    // issuer warpgroup and each of the three compute warpgroups move to with setmaxnreg
+    static constexpr uint32_t REG_LAUNCH = 65536 / THREADS, REG_PRODUCERS = 80, REG_COMPUTE = 144;
+    static_assert(!Q8 || 3 * REG_COMPUTE + REG_PRODUCERS == 4 * REG_LAUNCH, "the shares add up to the launch's total");
 };
 constexpr uint32_t TM_S = 0, TM_O = 64, TM_K = 128;
 constexpr float THRESH = 8.0f;  // log2 units
@@ -741,7 +745,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
     if (warp >= W_KTMA) {
     if constexpr (Q8) {
         __syncwarp();
-        reg_lower<80>();
+        reg_lower<R_::REG_PRODUCERS>();
     }
     if (warp == W_KTMA || warp == W_VTMA) {
         // ------------------------------------------------------------------------ TMA producers
@@ -851,7 +855,7 @@ __global__ void __launch_bounds__(Roles<KT != KT_F16>::THREADS, 1)
     } else {
     if constexpr (Q8) {
         __syncwarp();
-        reg_raise<144>();
+        reg_raise<R_::REG_COMPUTE>();
     }
     if (Q8 && warp >= W_KDQ && warp < W_VDQ) {
         // ------------------------------------------------------------------------ K dequantisation -> TMEM
@@ -1330,6 +1334,20 @@ cudaError_t launch_tc(const FaStreamParams& p, const CUtensorMap& tmK, const CUt
     static bool attr_done[64] = {};
     auto kern = tc::fa_stream_tc_kernel<N, KT>;
     const size_t smem = sizeof(tc::Smem<N, KT>);
+    const bool first = [&] {
+        int dev = 0;
+        return cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !attr_done[dev];
+    }();
+    if constexpr (KT != tc::KT_F16) {
+        // the register split assumes the launch holds exactly REG_LAUNCH per thread: with fewer, a warpgroup's raise
+        // would wait for registers that never come, so such a build is refused before its first launch
+        if (first) {
+            cudaFuncAttributes fa{};
+            const cudaError_t ea = cudaFuncGetAttributes(&fa, kern);
+            if (ea != cudaSuccess) return ea;
+            if (fa.numRegs != (int) tc::Roles<true>::REG_LAUNCH) return cudaErrorInvalidConfiguration;
+        }
+    }
     cudaError_t e = set_smem_once(kern, smem, attr_done);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_splits, p.n_head_kv, p.n_row_chunks * p.ne3);
