@@ -217,6 +217,47 @@ def test_gdn_io_validates(kb):
     assert status(lambda: kb.gdn_gated_norm(y, y, torch.ones(S), 1e-6, stream=0)) == kb.KB_ERR_BAD_SHAPE
 
 
+def test_gdn_step_validates(kb):
+    """kb_gdn_step refuses malformed layers before touching the device; a well-formed one reaches the launch, which
+    fails without a GPU."""
+    import torch
+
+    S, H_k, H_v, KC = 128, 16, 48, 4
+    ch = 2 * S * H_k + S * H_v
+
+    def layer(n=4, K=4, conv_w_width=KC, conv_rows=None, snap_dtype=torch.float16, snap_rows=None):
+        return dict(qkv=torch.zeros(n, ch), conv_state=torch.zeros(K, conv_rows or (KC - 1) * ch),
+                    conv_w=torch.zeros(ch, conv_w_width), beta_raw=torch.zeros(n, H_v), alpha=torch.zeros(n, H_v),
+                    dt_bias=torch.zeros(H_v), a=torch.zeros(H_v), ssm=torch.zeros(H_v, S, S),
+                    snap=torch.zeros(snap_rows if snap_rows is not None else K - 1, S * S * H_v, dtype=snap_dtype)
+                    if K > 1 else None,
+                    n_snapshots=K, z=torch.zeros(n, H_v * S), ssm_norm=torch.ones(S), rms_eps=1e-6,
+                    sync=torch.zeros(H_k, dtype=torch.int32))
+
+    def status(**kw):
+        try:
+            kb.gdn_step(**kw, stream=0)
+        except kb.KbError as e:
+            return e.status
+        return kb.KB_OK
+
+    assert status(**layer()) == kb.KB_ERR_CUDA  # well-formed: fails only at the launch
+    assert status(**layer(n=1, K=1)) == kb.KB_ERR_CUDA
+    assert status(**layer(n=5)) == kb.KB_ERR_UNSUPPORTED  # 1-4 tokens per launch
+    assert status(**layer(conv_w_width=3)) == kb.KB_ERR_UNSUPPORTED  # conv kernel width 4 only
+    assert status(**layer(conv_rows=3 * ch - 4)) == kb.KB_ERR_BAD_SHAPE
+    assert status(**dict(layer(), n_snapshots=0)) == kb.KB_ERR_ARG
+    assert status(**dict(layer(), snap=None)) == kb.KB_ERR_ARG  # 4 snapshots need the snapshot rows
+    assert status(**layer(n=2, snap_rows=1)) == kb.KB_ERR_CUDA  # 2 tokens write slots 0 and 1 only
+    assert status(**layer(snap_rows=2)) == kb.KB_ERR_BAD_SHAPE  # 4 tokens write 3 snapshot rows
+    assert status(**layer(snap_dtype=torch.int32)) == kb.KB_ERR_UNSUPPORTED  # f32 / f16 / bf16 snapshots only
+    odd = torch.zeros(4 * H_k + 4, dtype=torch.uint8)[1:]  # a counter array off its 4-byte alignment
+    assert status(**dict(layer(), sync=odd)) == kb.KB_ERR_ARG
+    bad_z = layer()
+    bad_z["z"] = torch.zeros(4, H_v * S - 4)
+    assert status(**bad_z) == kb.KB_ERR_BAD_SHAPE
+
+
 def test_plain_c_caller(tmp_path):
     """tests/abi_check.c: the header compiles as C11 with warnings as errors, links against the library, and the
     calls' validation answers a C caller without a device."""
