@@ -217,6 +217,27 @@ def test_gdn_io_validates(kb):
     assert status(lambda: kb.gdn_gated_norm(y, y, torch.ones(S), 1e-6, stream=0)) == kb.KB_ERR_BAD_SHAPE
 
 
+def test_scratch_bytes_cover_the_prefill_mask_table(kb):
+    """For prompt chunks the scratch a caller sizes with kb_flash_attn_ext_scratch_bytes holds the dense mask's class
+    table (one byte per 128-query tile and 64-cell block, rounded up to 256 bytes), and for a quantised cache the two
+    f16 views before it; the verify shape keeps its split partials."""
+    D, H, H_kv = 256, 24, 4
+    L = kb.lib()
+    by = ctypes.byref
+    prm = kb.fa_params(1 / 16)
+    for n_q, n_kv in ((4096, 8192), (2048, 4096), (300, 1000)):
+        q = kb.kb_tensor(1 << 20, kb.F32, [D, n_q, H, 1], [4, H * D * 4, D * 4, n_q * H * D * 4])
+        table = -(-(-(-n_q // 128) * -(-n_kv // 64)) // 256) * 256
+        k = kb.kb_tensor(1 << 20, kb.F16, [D, n_kv, H_kv, 1], [2, 2048, 512, 2048 * n_kv])
+        assert L.kb_flash_attn_ext_scratch_bytes(by(q), by(k), by(k), by(prm)) >= table
+        kq = kb.kb_tensor(1 << 20, kb.Q8_0, [D, n_kv, H_kv, 1], [34, 1088, 272, 1088 * n_kv])
+        views = 2 * n_kv * H_kv * D * 2
+        assert L.kb_flash_attn_ext_scratch_bytes(by(q), by(kq), by(kq), by(prm)) >= views + table
+    q = kb.kb_tensor(1 << 20, kb.F32, [D, 4, H, 1], [4, H * D * 4, D * 4, 4 * H * D * 4])
+    k = kb.kb_tensor(1 << 20, kb.F16, [D, 262144, H_kv, 1], [2, 2048, 512, 2048 * 262144])
+    assert L.kb_flash_attn_ext_scratch_bytes(by(q), by(k), by(k), by(prm)) > 0
+
+
 def test_gdn_step_validates(kb):
     """kb_gdn_step refuses malformed layers before touching the device; a well-formed one reaches the launch, which
     fails without a GPU."""
