@@ -1506,6 +1506,22 @@ def run_case(case: str):
         kc, vc, kv, vv = make_layers(kb, torch, dev, gen, n_kv, case[len("verify_"):])[0]
         q = torch.randn(1, 4, H, D, device=dev, generator=gen)
         run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, causal=True, pos0=n_kv - 4)
+    elif case in ("verify_f16_dense_mask", "prefill_bf16_2048_dense_mask"):
+        # klein's dense f16 mask instead of the analytic bounds (0 at or before the row's position, -inf after)
+        T, n_kv = (4, 262144) if case.startswith("verify") else (2048, 4096)
+        bf = case.startswith("prefill")
+        k = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        v = torch.randn(n_kv, H_KV * D, device=dev, generator=gen)
+        k, v = (k.bfloat16(), v.bfloat16()) if bf else (k.half(), v.half())
+        t = kb.BF16 if bf else kb.F16
+        kv, vv = kb.kv_cache_view(k, t, H_KV, D), kb.kv_cache_view(v, t, H_KV, D)
+        q = torch.randn(1, T, H, D, device=dev, generator=gen)
+        if bf:
+            q = q.bfloat16().float()
+        c = torch.arange(n_kv, device=dev)[None, :]
+        pos = n_kv - T + torch.arange(T, device=dev)[:, None]
+        mask = torch.where(c <= pos, 0.0, float("-inf")).half()
+        run = lambda: kb.flash_attn_ext(q, kv, vv, SCALE, mask=mask)
     elif case in ("gdn_step_1", "gdn_step_4"):
         # one DeltaNet layer of the decode / verify step in one launch (kb_gdn_step), K = 4 f16 snapshots
         T, S, Hk, Hv = int(case[-1]), 128, 16, 48
@@ -1556,7 +1572,8 @@ def main():
                          "itself (fused), or an NCCL all-gather")
     ap.add_argument("--case", default=None,
                     choices=["prefill_bf16_4096", "prefill_q8_0_2048", "gdn_prefill_4096", "gdn_verify", "verify_f16", "verify_q8_0",
-                             "verify_q4_0", "gdn_input_4096", "gdn_step_1", "gdn_step_4"],
+                             "verify_q4_0", "gdn_input_4096", "gdn_step_1", "gdn_step_4", "verify_f16_dense_mask",
+                             "prefill_bf16_2048_dense_mask"],
                     help="run one small untimed invocation of a workload (for profiler captures) and exit")
     args = ap.parse_args()
     if args.case:
